@@ -1,0 +1,318 @@
+"""Decode benchmark of the B200 Llama token loop (BASELINE config 1 by default).
+
+Workload: Llama-3.2-1B-architecture Q8_0 GGUF, random-init from seed 0 (the real
+GGUF is not available; seeded synthetic weights with the same shapes stand in),
+batch 1, a 32-token prompt of uniform random ids in [0, 128000), then greedy
+decode. One step = one decoded token (forward of one token through all 16 layers,
+LM head, device argmax fed back as the next input).
+
+  value : decode tok/s with everything resident in HBM (sq_decode_steps: steps
+          chained on the device, CUDA-event timed on the context's stream)
+  e2e   : the same tokens through the host-facing C ABI, one sq_forward call per
+          token (H2D of the token id, D2H of the argmax) — wall-clock timed
+  roofline: algorithmic bytes per step / event-timed step duration vs the measured
+          HBM copy bandwidth (MEASURED_PEAKS.json)
+  cpu_baseline: the CPU oracle (C restatement of the reference's x86 scalar path)
+          on the host cores, on a bounded sample of the same workload
+
+`--impl reference` times that CPU restatement alone on this workload (the Rust
+reference cannot be built here: no Rust toolchain).
+Multi-GPU (torchrun): each rank runs an independent replica of the workload (the
+1B model does not shard: "replicas only"); value = all ranks' tokens / max time.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "squirrel-rs_b200"))
+
+WORKLOADS = {
+    # name: (spec, weight type, prompt length, metric label)
+    "1b-q8_0": ("1b", "q8_0", 32),
+    "1b-q4_0": ("1b", "q4_0", 32),
+    "1b-bf16": ("1b", "bf16", 32),
+    "1b-q4_0-long": ("1b", "q4_0", 2048),
+}
+METRIC = "decode tok/s (Llama-3.2-1B Q8_0, bs1)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="1b-q8_0", choices=sorted(WORKLOADS))
+    ap.add_argument("--acts", default="f32", choices=["f32", "q8"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-decode-steps", type=int, default=4)
+    return ap.parse_args()
+
+
+def bytes_per_step(cfg, wtype, kv_len):
+    """Algorithmic HBM bytes of one decode step: every weight once (LM head = tied
+    token_embd), norm weights, the embedding row, K/V read at kv_len positions plus
+    the new K/V row, and the logits written."""
+    bb = {8: 34, 2: 18, 30: 64}[wtype]
+    E, F, H, KV, hd, L, V = (cfg.embed_dim, cfg.ffn_dim, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                             cfg.n_blocks, cfg.vocab_size)
+    per_layer = (E * H * hd + 2 * E * KV * hd + H * hd * E + 3 * E * F) // 32 * bb
+    weights = L * per_layer + V * E // 32 * bb
+    norms = (2 * L + 1) * E * 4
+    kv = L * 2 * KV * hd * 4 * (kv_len + 1)
+    return weights + norms + kv + E // 32 * bb + V * 4
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_for(workload):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(workload)
+    return None
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sample(path, prompt, decode_steps, threads):
+    """The oracle on the host cores: prefill the prompt, then `decode_steps` timed
+    decode tokens. Returns (tok/s over the decode steps, ids)."""
+    from oracle import oracle as O
+    m = O.Model(path)
+    ids, ms, _ = m.generate(prompt, decode_steps + 1, nthreads=threads)
+    m.close()
+    dec = ms[1:]
+    return float(len(dec) / (dec.sum() / 1e3)), ids
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from sqb200 import gguf_synth as G
+    spec, wt, plen = WORKLOADS[args.workload]
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(plen, seed=1234)
+    threads = cpu_threads()
+    from oracle import oracle as O
+    m = O.Model(path)
+    # untimed prefill, warm-up decode steps, then K timed decode steps (one token each)
+    logits = m.forward(prompt, nthreads=threads)
+    tok = np.array([O.greedy(logits)], np.uint32)
+    for _ in range(args.warmup):
+        tok = np.array([O.greedy(m.forward(tok, nthreads=threads))], np.uint32)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = np.array([O.greedy(m.forward(tok, nthreads=threads))], np.uint32)
+    dt = time.perf_counter() - t0
+    m.close()
+    v = args.steps / dt
+    sample = (f"{spec} {wt} W8A32 scalar x86 path (C restatement, -O2 -ffp-contract=off), {plen}-token prompt "
+              f"untimed, {args.warmup} warm-up + {args.steps} timed decode tokens")
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init GGUF, random prompt ids)",
+            "config": {"workload": args.workload, "prompt": plen, "batch": 1},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from sqb200 import gguf_synth as G
+    from sqb200 import lib
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    spec, wt, plen = WORKLOADS[args.workload]
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(plen, seed=1234)
+    acts = lib.ACTS_Q8 if args.acts == "q8" else lib.ACTS_F32
+    model = lib.Model(path, device=local, acts=acts)
+    cfg = model.config
+    max_ctx = plen + 2 * (args.warmup + args.steps) + 8
+    ctx = model.new_context(max_ctx)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+
+    # prefill (timed separately: prefill tok/s is a secondary number of the metric)
+    t0 = time.perf_counter()
+    first = ctx.forward(prompt)
+    prefill_s = time.perf_counter() - t0
+    ctx.decode_steps(args.warmup)
+    kv0 = ctx.seq_len
+
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        ids = ctx.decode_steps(args.steps)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = world * args.steps / (ms / 1e3)
+    step_ms = ms / args.steps
+
+    # e2e through the host-facing ABI: one sq_forward per token from host memory
+    ctx.reset()
+    tok = ctx.forward(prompt)
+    for _ in range(args.warmup):
+        tok = ctx.forward(np.array([tok], np.uint32))
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    host_tok = np.zeros(1, np.uint32)
+    for _ in range(args.steps):
+        host_tok[0] = tok
+        tok = ctx.forward(host_tok)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * args.steps / e2e_s
+
+    # roofline of the decode step (one persistent-kernel launch per token when available)
+    mean_kv = kv0 + (args.steps - 1) / 2
+    algo = bytes_per_step(cfg, cfg.weight_type, mean_kv)
+    achieved = algo / (step_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        th = cpu_threads()
+        tps, cpu_ids = cpu_sample(path, prompt, args.cpu_decode_steps, th)
+        cpu = {"value": tps, "unit": "tok/s", "cores": th, "kind": "port",
+               "sample": f"{plen}-token prompt prefill untimed, then {args.cpu_decode_steps} timed decode tokens "
+                         f"({spec} {wt}, W8A32 scalar x86 path, C restatement, {th} threads)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC if args.workload == "1b-q8_0" else f"decode tok/s ({args.workload}, bs1)",
+            "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if args.acts == "f32" else "int8",
+            "data": "synthetic (seeded random-init GGUF N(0,0.02) quantized; uniform random prompt ids)",
+            "config": {"workload": args.workload, "model": f"llama-3.2-{spec}-arch {wt}", "prompt": plen,
+                       "batch": 1, "decode_steps": args.steps, "acts": args.acts,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "weights %.2f GB > 126 MB L2 per step; no flush needed" % (algo / 1e9),
+                       "prefill_tok_s": plen / prefill_s, "kv_len_start": kv0},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic_for(args.workload),
+                         "algorithmic_bytes_per_step": algo, "kernel": "decode step"},
+            "gpu_launches": args.steps * launches_per_step(ctx, cfg),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "first_ids": [int(first)] + [int(i) for i in ids[:8]],
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def launches_per_step(ctx, cfg):
+    from sqb200 import lib
+    n = lib.load().sq_decode_launches_per_step(ctx._h) if hasattr(lib.load(), "sq_decode_launches_per_step") else -1
+    if n and n > 0:
+        return n
+    # op path: embed + per layer 18 + final norm, LM head, argmax (2), feedback
+    return 1 + 18 * cfg.n_blocks + 5
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

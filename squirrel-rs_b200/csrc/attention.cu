@@ -1,0 +1,160 @@
+// attention.cu — causal GQA attention for the op-level ABI and prefill
+// (kernels/attention.rs:11-70 semantics: scores = (q.k) * 1/sqrt(hd) over keys
+// 0..=offset+t, max-subtracted softmax, probability-weighted sum of V).
+//
+// One CTA per (query row t, head h, key split). Each of the 4 warps walks a
+// strided subset of the split's keys with an online softmax (running max m,
+// running sum l, accumulator a[d]); lanes own head_dim/32 dimensions each, so K
+// and V rows are read coalesced. Warp states are merged in shared memory; with
+// one split the CTA writes out = a * (1/l), otherwise it writes (m, l, a) and
+// k_sdpa_combine merges the splits.
+#include <math.h>
+
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace sq {
+
+constexpr int SDPA_WARPS = 4;
+constexpr int SDPA_MAX_HD = 256;
+
+template <int DPL>  // dims per lane = head_dim / 32
+__global__ void __launch_bounds__(SDPA_WARPS * 32)
+    k_sdpa(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+           float *__restrict__ out, float *__restrict__ part, int seq_q, int seq_k, int n_heads,
+           int group, long long kps, long long khs, int split_len, float scale) {
+  const int hd = DPL * 32;
+  const int row = blockIdx.x;  // t * n_heads + h
+  const int split = blockIdx.y, n_split = gridDim.y;
+  const int t = row / n_heads, h = row % n_heads, g = h / group;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int live = seq_k - seq_q + t + 1;
+  const int k0 = split * split_len;
+  const int k1 = min(live, k0 + split_len);
+
+  float qv[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; i++) qv[i] = q[(size_t)row * hd + lane + 32 * i];
+
+  float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; i++) acc[i] = 0.f;
+
+  const float *kb = k + g * khs, *vb = v + g * khs;
+  for (int s = k0 + wid; s < k1; s += SDPA_WARPS) {
+    const float *kr = kb + (size_t)s * kps;
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) d = fmaf(qv[i], kr[lane + 32 * i], d);
+    const float sc = warp_sum(d) * scale;
+    const float mn = fmaxf(m, sc);
+    const float corr = expf(m - mn);  // 0 on the first key (m = -inf)
+    const float p = expf(sc - mn);
+    l = l * corr + p;
+    const float *vr = vb + (size_t)s * kps;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) acc[i] = fmaf(p, vr[lane + 32 * i], acc[i] * corr);
+    m = mn;
+  }
+
+  __shared__ float sm_m[SDPA_WARPS], sm_l[SDPA_WARPS];
+  __shared__ float sm_a[SDPA_WARPS][SDPA_MAX_HD];
+  if (lane == 0) {
+    sm_m[wid] = m;
+    sm_l[wid] = l;
+  }
+#pragma unroll
+  for (int i = 0; i < DPL; i++) sm_a[wid][lane + 32 * i] = acc[i];
+  __syncthreads();
+  if (wid == 0) {
+    float M = -INFINITY;
+    for (int w = 0; w < SDPA_WARPS; w++) M = fmaxf(M, sm_m[w]);
+    float L = 0.f, A[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) A[i] = 0.f;
+    for (int w = 0; w < SDPA_WARPS; w++) {
+      const float f = (sm_l[w] > 0.f) ? expf(sm_m[w] - M) : 0.f;
+      L = fmaf(sm_l[w], f, L);
+#pragma unroll
+      for (int i = 0; i < DPL; i++) A[i] = fmaf(sm_a[w][lane + 32 * i], f, A[i]);
+    }
+    if (n_split == 1) {
+      const float inv = 1.0f / L;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) out[(size_t)row * hd + lane + 32 * i] = A[i] * inv;
+    } else {
+      float *pp = part + ((size_t)row * n_split + split) * (hd + 2);
+      if (lane == 0) {
+        pp[0] = M;
+        pp[1] = L;
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; i++) pp[2 + lane + 32 * i] = A[i];
+    }
+  }
+}
+
+__global__ void k_sdpa_combine(const float *__restrict__ part, float *__restrict__ out, int n_split, int hd) {
+  const int row = blockIdx.x;
+  const float *pp = part + (size_t)row * n_split * (hd + 2);
+  float M = -INFINITY;
+  for (int i = 0; i < n_split; i++)
+    if (pp[i * (hd + 2) + 1] > 0.f) M = fmaxf(M, pp[i * (hd + 2)]);
+  float L = 0.f;
+  for (int i = 0; i < n_split; i++) {
+    const float l = pp[i * (hd + 2) + 1];
+    if (l > 0.f) L = fmaf(l, expf(pp[i * (hd + 2)] - M), L);
+  }
+  const float inv = 1.0f / L;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float a = 0.f;
+    for (int i = 0; i < n_split; i++) {
+      const float l = pp[i * (hd + 2) + 1];
+      if (l > 0.f) a = fmaf(pp[i * (hd + 2) + 2 + d], expf(pp[i * (hd + 2)] - M), a);
+    }
+    out[(size_t)row * hd + d] = a * inv;
+  }
+}
+
+// Splits per query row: enough CTAs to fill the GPU when there are few rows, and
+// never more than SDPA_MAX_ROW_SPLITS (row, split) pairs in total, so one scratch
+// buffer of sdpa_max_partials_floats(head_dim) floats serves every call.
+int sdpa_num_splits(int seq_q, int seq_k, int n_heads) {
+  const long long rows = (long long)seq_q * n_heads;
+  if (rows >= 2 * 148) return 1;
+  int ns = (seq_k + 255) / 256;
+  const int want = (int)((4 * 148 + rows - 1) / rows);
+  if (ns > want) ns = want;
+  if (ns > 64) ns = 64;
+  if ((long long)ns * rows > SDPA_MAX_ROW_SPLITS) ns = (int)(SDPA_MAX_ROW_SPLITS / rows);
+  return ns < 1 ? 1 : ns;
+}
+
+size_t sdpa_partials_floats(int seq_q, int n_heads, int head_dim, int n_split) {
+  return (size_t)seq_q * n_heads * n_split * (head_dim + 2);
+}
+
+size_t sdpa_max_partials_floats(int head_dim) { return (size_t)SDPA_MAX_ROW_SPLITS * (head_dim + 2); }
+
+cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
+                        int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
+                        int n_split, float *part) {
+  const int group = n_heads / n_kv_heads;
+  const float scale = 1.0f / sqrtf((float)head_dim);  // attention.rs:37
+  const int split_len = (seq_k + n_split - 1) / n_split;
+  dim3 grid(seq_q * n_heads, n_split);
+  switch (head_dim / 32) {
+    case 1: k_sdpa<1><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 2: k_sdpa<2><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 3: k_sdpa<3><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 4: k_sdpa<4><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 5: k_sdpa<5><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 6: k_sdpa<6><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 7: k_sdpa<7><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    default: k_sdpa<8><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+  }
+  if (n_split > 1) k_sdpa_combine<<<seq_q * n_heads, 64, 0, s>>>(part, out, n_split, head_dim);
+  return cudaGetLastError();
+}
+
+}  // namespace sq

@@ -1,0 +1,677 @@
+// ops.cu — op-level kernels for sm_100a and the C-ABI entry points that replace
+// squirrel-rs's `src/ops` functions. Decode of one token runs in the persistent
+// decode kernel (decode.cu); these kernels serve the op-level ABI and prefill.
+#include <math.h>
+#include <stdio.h>
+
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace sq {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+int fail(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char *what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return SQ_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------------------------
+// linear, f32 activations (W8A32 / W4A32 / BF16): dot_prod.rs:86-96, 255-270, 464-472.
+// One warp per output row; lanes take the row's blocks; up to MT activation rows reuse
+// each decoded block from registers. Per block the 32 products are summed first and
+// scaled once (the reference's block_acc * scale), with FMA accumulation.
+// ------------------------------------------------------------------------------------
+template <int T>
+__device__ __forceinline__ void load_block_f32(const uint8_t *blk, float (&q)[32], float &scale) {
+  if constexpr (T == SQ_Q8_0) {
+    scale = h2f(ld_u16(blk));
+    const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      uint16_t v = p[i];
+      q[2 * i] = (float)(int8_t)(v & 0xFF);
+      q[2 * i + 1] = (float)(int8_t)(v >> 8);
+    }
+  } else if constexpr (T == SQ_Q4_0) {
+    scale = h2f(ld_u16(blk));
+    const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      uint16_t v = p[i];
+      uint8_t b0 = v & 0xFF, b1 = v >> 8;
+      q[2 * i] = (float)((b0 & 15) - 8);
+      q[2 * i + 16] = (float)((b0 >> 4) - 8);
+      q[2 * i + 1] = (float)((b1 & 15) - 8);
+      q[2 * i + 17] = (float)((b1 >> 4) - 8);
+    }
+  } else {
+    scale = 1.0f;
+    const uint4 *p = reinterpret_cast<const uint4 *>(blk);  // BF16 blocks are 64-byte aligned rows
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      uint4 u = p[i];
+      uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        q[8 * i + 2 * k] = __uint_as_float(w[k] << 16);
+        q[8 * i + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+      }
+    }
+  }
+}
+
+template <int T, int MT>
+__global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x, int m, int in_dim,
+                                                     const uint8_t *__restrict__ w, int out_dim,
+                                                     float *__restrict__ y) {
+  constexpr int BB = type_bytes<T>();
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int bpr = in_dim / QK;
+  for (int n = gw; n < out_dim; n += nw) {
+    const uint8_t *wr = w + (size_t)n * bpr * BB;
+    for (int m0 = 0; m0 < m; m0 += MT) {
+      float acc[MT];
+#pragma unroll
+      for (int r = 0; r < MT; r++) acc[r] = 0.f;
+      for (int b = lane; b < bpr; b += 32) {
+        float q[32], scale;
+        load_block_f32<T>(wr + (size_t)b * BB, q, scale);
+#pragma unroll
+        for (int r = 0; r < MT; r++) {
+          if (m0 + r < m) {
+            const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)(m0 + r) * in_dim + b * QK);
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+              float4 v = __ldg(xr + k);
+              s = fmaf(v.x, q[4 * k], s);
+              s = fmaf(v.y, q[4 * k + 1], s);
+              s = fmaf(v.z, q[4 * k + 2], s);
+              s = fmaf(v.w, q[4 * k + 3], s);
+            }
+            acc[r] = (T == SQ_BF16) ? acc[r] + s : fmaf(s, scale, acc[r]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < MT; r++) {
+        float v = warp_sum(acc[r]);
+        if (lane == 0 && m0 + r < m) y[(size_t)(m0 + r) * out_dim + n] = v;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// linear, Q8_0 activations (W8A8 / W4A8): dot_prod.rs:378-403 (scalar twins). The
+// integer block sums are exact (dp4a); each block adds (isum * sa) * sb.
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void load_q8_words(const uint8_t *blk, int (&w)[8], float &scale) {
+  scale = h2f(ld_u16(blk));
+  const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2);
+#pragma unroll
+  for (int i = 0; i < 8; i++) w[i] = (int)((uint32_t)p[2 * i] | ((uint32_t)p[2 * i + 1] << 16));
+}
+
+template <int T, int MT>
+__global__ void __launch_bounds__(256) k_linear_q8(const uint8_t *__restrict__ xq, int m, int in_dim,
+                                                    const uint8_t *__restrict__ w, int out_dim,
+                                                    float *__restrict__ y) {
+  constexpr int BB = type_bytes<T>();
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int bpr = in_dim / QK;
+  for (int n = gw; n < out_dim; n += nw) {
+    const uint8_t *wr = w + (size_t)n * bpr * BB;
+    for (int m0 = 0; m0 < m; m0 += MT) {
+      float acc[MT];
+#pragma unroll
+      for (int r = 0; r < MT; r++) acc[r] = 0.f;
+      for (int b = lane; b < bpr; b += 32) {
+        const uint8_t *blk = wr + (size_t)b * BB;
+        int wq[8];
+        float sb;
+        if constexpr (T == SQ_Q8_0) {
+          load_q8_words(blk, wq, sb);
+        } else {
+          sb = h2f(ld_u16(blk));
+          const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2);
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            uint32_t v = (uint32_t)p[2 * i] | ((uint32_t)p[2 * i + 1] << 16);
+            wq[i] = (int)__vsub4(v & 0x0F0F0F0Fu, 0x08080808u);             // elements 4i..4i+3
+            wq[i + 4] = (int)__vsub4((v >> 4) & 0x0F0F0F0Fu, 0x08080808u);  // elements 16+4i..
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < MT; r++) {
+          if (m0 + r < m) {
+            int aw[8];
+            float sa;
+            load_q8_words(xq + ((size_t)(m0 + r) * bpr + b) * Q8_BYTES, aw, sa);
+            int isum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) isum = __dp4a(aw[i], wq[i], isum);
+            acc[r] += ((float)isum * sa) * sb;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < MT; r++) {
+        float v = warp_sum(acc[r]);
+        if (lane == 0 && m0 + r < m) y[(size_t)(m0 + r) * out_dim + n] = v;
+      }
+    }
+  }
+}
+
+// quantize_row_q8_0_scalar (dot_prod.rs:21-31), one warp per block, bit-exact.
+__global__ void k_quantize_q8_0(const float *__restrict__ x, size_t nblocks, uint8_t *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  size_t b = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const size_t stride = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (; b < nblocks; b += stride) {
+    float v = x[b * QK + lane];
+    float amax = warp_max(fabsf(v));
+    float scale = __fdiv_rn(amax, 127.0f);
+    float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    float r = roundf(__fmul_rn(v, inv));  // ties away from zero, like f32::round
+    int8_t q = (r != r) ? 0 : (int8_t)fminf(fmaxf(r, -127.0f), 127.0f);
+    uint8_t *blk = out + b * Q8_BYTES;
+    blk[2 + lane] = (uint8_t)q;
+    if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = __half_as_ushort(__float2half_rn(scale));
+  }
+}
+
+// embed (ops/embedding.rs:10-52): exact dequantized rows. A token id >= vocab (the
+// reference panics on the slice) yields a NaN row instead of an out-of-bounds read.
+template <int T>
+__global__ void k_embed(const uint32_t *__restrict__ tokens, const uint8_t *__restrict__ w, int dim, int vocab,
+                        float *__restrict__ out) {
+  constexpr int BB = type_bytes<T>();
+  const int t = blockIdx.y;
+  const uint32_t tok = tokens[t];
+  const uint8_t *row = w + (size_t)(tok < (uint32_t)vocab ? tok : 0) * (dim / QK) * BB;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+    out[(size_t)t * dim + i] = tok < (uint32_t)vocab ? dequant_elem<T>(row + (i / QK) * BB, i % QK) : __int_as_float(0x7fc00000);
+}
+
+template <int T>
+__global__ void k_dequant(const uint8_t *__restrict__ blocks, size_t n, float *__restrict__ out) {
+  constexpr int BB = type_bytes<T>();
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = dequant_elem<T>(blocks + (i / QK) * BB, (int)(i % QK));
+}
+
+// rms_norm_f32_into (kernels/rms_norm.rs:40-56): y = (x*w) / sqrt(mean(x^2) + eps), one CTA per row.
+__global__ void __launch_bounds__(256) k_rms_norm(const float *__restrict__ x, const float *__restrict__ w,
+                                                  float *y, int dim, float eps) {
+  __shared__ float red[8];
+  const float *xr = x + (size_t)blockIdx.x * dim;
+  float *yr = y + (size_t)blockIdx.x * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)dim), eps));
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fdiv_rn(__fmul_rn(xr[i], w[i]), rms);
+}
+
+// rope_f32_interleaved (kernels/rope.rs:7-36): rotate (x[2j], x[2j+1]) by pos*inv_freq[j].
+// sin/cos are evaluated in double and rounded once to float.
+__global__ void k_rope(float *x, int seq, int row_dim, int base_pos, const float *__restrict__ inv_freq,
+                       int half) {
+  const int pairs = row_dim / 2;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < (long long)seq * pairs;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(idx / pairs), p = (int)(idx % pairs), j = p % half;
+    const float theta = __fmul_rn((float)(base_pos + r), inv_freq[j]);
+    double sd, cd;
+    sincos((double)theta, &sd, &cd);
+    const float s = (float)sd, c = (float)cd;
+    float *e = x + (size_t)r * row_dim + 2 * p;
+    const float a = e[0], b = e[1];
+    e[0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    e[1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  }
+}
+
+__global__ void k_rope_table(float *x, int seq, int row_dim, int base_pos, const float *__restrict__ cos_t,
+                             const float *__restrict__ sin_t, int half) {
+  const int pairs = row_dim / 2;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < (long long)seq * pairs;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(idx / pairs), p = (int)(idx % pairs), j = p % half;
+    const size_t t = (size_t)(base_pos + r) * half + j;
+    const float c = cos_t[t], s = sin_t[t];
+    float *e = x + (size_t)r * row_dim + 2 * p;
+    const float a = e[0], b = e[1];
+    e[0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    e[1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  }
+}
+
+// sigmoid_f32 (kernels/sigmoid.rs:2-9) and silu (silu.rs:4-8).
+__device__ __forceinline__ float sigmoid_ref(float x) {
+  if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+  const float z = expf(x);
+  return __fdiv_rn(z, __fadd_rn(1.0f, z));
+}
+__device__ __forceinline__ float silu_ref(float x) { return __fmul_rn(x, sigmoid_ref(x)); }
+
+__global__ void k_silu(float *x, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = silu_ref(x[i]);
+}
+__global__ void k_mul(const float *a, const float *b, float *out, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __fmul_rn(a[i], b[i]);
+}
+__global__ void k_add(float *a, const float *b, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    a[i] = __fadd_rn(a[i], b[i]);
+}
+__global__ void k_silu_mul(const float *g, const float *u, float *out, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __fmul_rn(silu_ref(g[i]), u[i]);
+}
+
+// GreedySampler (greedy.rs:6-15): per-CTA ordered reduction of a contiguous chunk,
+// then one CTA combines the chunk states in index order.
+constexpr int ARGMAX_THREADS = 256;
+constexpr int ARGMAX_CHUNK = 4096;
+
+__device__ ArgState block_arg_reduce(ArgState s) {
+  __shared__ ArgState sh[ARGMAX_THREADS / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {  // combine with the neighbour range to the right
+    ArgState r;
+    r.v = __shfl_down_sync(0xffffffffu, s.v, o);
+    r.best = __shfl_down_sync(0xffffffffu, s.best, o);
+    r.nan = __shfl_down_sync(0xffffffffu, s.nan, o);
+    if ((lane & (2 * o - 1)) == 0) s = arg_combine(s, r);
+  }
+  if (lane == 0) sh[wid] = s;
+  __syncthreads();
+  ArgState t = arg_empty();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t = arg_combine(t, sh[i]);
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax_partial(const float *__restrict__ x, size_t n,
+                                                                   ArgState *part) {
+  const size_t lo = (size_t)blockIdx.x * ARGMAX_CHUNK;
+  const size_t hi = lo + ARGMAX_CHUNK < n ? lo + ARGMAX_CHUNK : n;
+  // each thread scans a contiguous sub-range so its sequential fold keeps index order
+  const size_t per = (ARGMAX_CHUNK + ARGMAX_THREADS - 1) / ARGMAX_THREADS;
+  ArgState s = arg_empty();
+  for (size_t i = lo + threadIdx.x * per; i < lo + (threadIdx.x + 1) * per && i < hi; i++)
+    s = arg_combine(s, arg_elem(x[i], (long long)i));
+  s = block_arg_reduce(s);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+__global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax_final(const ArgState *part, int np, long long *out) {
+  const int per = (np + ARGMAX_THREADS - 1) / ARGMAX_THREADS;
+  ArgState s = arg_empty();
+  for (int i = threadIdx.x * per; i < (threadIdx.x + 1) * per && i < np; i++) s = arg_combine(s, part[i]);
+  s = block_arg_reduce(s);
+  if (threadIdx.x == 0) *out = arg_result(s);
+}
+
+// ------------------------------------------------------------------------------------
+// launchers
+// ------------------------------------------------------------------------------------
+static int g_num_sms = 0;
+static int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+static inline int grid_for(size_t work, int per_block, int cap) {
+  size_t g = (work + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > (size_t)cap) g = cap;
+  return (int)g;
+}
+
+cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out) {
+  size_t nb = n / QK;
+  k_quantize_q8_0<<<grid_for(nb, 8, 65535), 256, 0, s>>>(x, nb, (uint8_t *)out);
+  return cudaGetLastError();
+}
+
+template <int T>
+static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, const uint8_t *w, int out_dim,
+                         float *y) {
+  const int grid = grid_for((size_t)out_dim, 8, num_sms() * 8);
+  if (m <= 1)
+    k_linear_f32<T, 1><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
+  else if (m <= 4)
+    k_linear_f32<T, 4><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
+  else
+    k_linear_f32<T, 8><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
+}
+
+template <int T>
+static void linear_q8_t(cudaStream_t s, const uint8_t *xq, int m, int in_dim, const uint8_t *w, int out_dim,
+                        float *y) {
+  const int grid = grid_for((size_t)out_dim, 8, num_sms() * 8);
+  if (m <= 1)
+    k_linear_q8<T, 1><<<grid, 256, 0, s>>>(xq, m, in_dim, w, out_dim, y);
+  else if (m <= 4)
+    k_linear_q8<T, 4><<<grid, 256, 0, s>>>(xq, m, in_dim, w, out_dim, y);
+  else
+    k_linear_q8<T, 8><<<grid, 256, 0, s>>>(xq, m, in_dim, w, out_dim, y);
+}
+
+cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, const void *w, int wtype,
+                          int out_dim, float *y, int acts_q8, void *xq) {
+  const uint8_t *wb = (const uint8_t *)w;
+  if (acts_q8 && wtype != SQ_BF16) {
+    if (x) {
+      cudaError_t e = launch_quantize_q8_0(s, x, (size_t)m * in_dim, xq);
+      if (e != cudaSuccess) return e;
+    }
+    if (wtype == SQ_Q8_0) linear_q8_t<SQ_Q8_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
+    else linear_q8_t<SQ_Q4_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
+  } else {
+    if (wtype == SQ_Q8_0) linear_f32_t<SQ_Q8_0>(s, x, m, in_dim, wb, out_dim, y);
+    else if (wtype == SQ_Q4_0) linear_f32_t<SQ_Q4_0>(s, x, m, in_dim, wb, out_dim, y);
+    else linear_f32_t<SQ_BF16>(s, x, m, in_dim, wb, out_dim, y);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype, int dim, int vocab,
+                         float *out) {
+  dim3 grid(grid_for((size_t)dim, 256, 64), n);
+  const uint8_t *wb = (const uint8_t *)w;
+  if (wtype == SQ_Q8_0) k_embed<SQ_Q8_0><<<grid, 256, 0, s>>>(tokens, wb, dim, vocab, out);
+  else if (wtype == SQ_Q4_0) k_embed<SQ_Q4_0><<<grid, 256, 0, s>>>(tokens, wb, dim, vocab, out);
+  else k_embed<SQ_BF16><<<grid, 256, 0, s>>>(tokens, wb, dim, vocab, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(cudaStream_t s, const void *blocks, int wtype, size_t n, float *out) {
+  const int grid = grid_for(n, 256, num_sms() * 16);
+  const uint8_t *b = (const uint8_t *)blocks;
+  if (wtype == SQ_Q8_0) k_dequant<SQ_Q8_0><<<grid, 256, 0, s>>>(b, n, out);
+  else if (wtype == SQ_Q4_0) k_dequant<SQ_Q4_0><<<grid, 256, 0, s>>>(b, n, out);
+  else k_dequant<SQ_BF16><<<grid, 256, 0, s>>>(b, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm(cudaStream_t s, const float *x, const float *w, float *y, int rows, int dim,
+                            float eps) {
+  k_rms_norm<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_rows(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
+                             const float *inv_freq, int half) {
+  k_rope<<<grid_for((size_t)seq * row_dim / 2, 256, num_sms() * 8), 256, 0, s>>>(x, seq, row_dim, base_pos,
+                                                                                 inv_freq, half);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_rows_table(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
+                                   const float *cos_t, const float *sin_t, int half) {
+  k_rope_table<<<grid_for((size_t)seq * row_dim / 2, 256, num_sms() * 8), 256, 0, s>>>(
+      x, seq, row_dim, base_pos, cos_t, sin_t, half);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu(cudaStream_t s, float *x, size_t n) {
+  k_silu<<<grid_for(n, 256, num_sms() * 8), 256, 0, s>>>(x, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_mul(cudaStream_t s, const float *a, const float *b, float *out, size_t n) {
+  k_mul<<<grid_for(n, 256, num_sms() * 8), 256, 0, s>>>(a, b, out, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_add(cudaStream_t s, float *a, const float *b, size_t n) {
+  k_add<<<grid_for(n, 256, num_sms() * 8), 256, 0, s>>>(a, b, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_silu_mul(cudaStream_t s, const float *g, const float *u, float *out, size_t n) {
+  k_silu_mul<<<grid_for(n, 256, num_sms() * 8), 256, 0, s>>>(g, u, out, n);
+  return cudaGetLastError();
+}
+
+int argmax_partials(size_t n) { return (int)((n + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK); }
+
+cudaError_t launch_argmax(cudaStream_t s, const float *x, size_t n, void *partials, long long *out) {
+  const int np = argmax_partials(n);
+  k_argmax_partial<<<np, ARGMAX_THREADS, 0, s>>>(x, n, (ArgState *)partials);
+  k_argmax_final<<<1, ARGMAX_THREADS, 0, s>>>((const ArgState *)partials, np, out);
+  return cudaGetLastError();
+}
+
+}  // namespace sq
+
+// =====================================================================================
+// C ABI, op level. Validation mirrors the reference's checks before any launch.
+// =====================================================================================
+using namespace sq;
+
+static inline bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+extern "C" const char *sq_last_error(void) { return g_last_error.c_str(); }
+extern "C" const char *sq_version(void) { return "squirrel-b200 0.1 (sm_100a)"; }
+
+static int check_linear(const float *input, int m, int in_dim, const void *weight, int wtype, int out_dim,
+                        float *output) {
+  if (!input || !weight || !output) return fail(SQ_ERR_ARG, "linear: null pointer");
+  if (!is_weight_type(wtype)) return fail(SQ_ERR_INVALID_TYPE, "linear: weight type must be Q8_0, Q4_0 or BF16");
+  if (m <= 0 || in_dim <= 0 || out_dim <= 0 || in_dim % QK)
+    return fail(SQ_ERR_SHAPE, "linear: in_dim must be a positive multiple of 32 and m, out_dim positive");
+  if (!aligned16(input) || ((uintptr_t)weight & 1) || (wtype == SQ_BF16 && !aligned16(weight)))
+    return fail(SQ_ERR_ALIGN, "linear: input must be 16-byte aligned, blocks 2-byte aligned (BF16: 16)");
+  return SQ_OK;
+}
+
+extern "C" int sq_linear(void *stream, const float *input, int m, int in_dim, const void *weight, int wtype,
+                         int out_dim, float *output, int acts) {
+  int st = check_linear(input, m, in_dim, weight, wtype, out_dim, output);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  void *xq = nullptr;
+  const bool q8 = acts == SQ_ACTS_Q8 && wtype != SQ_BF16;
+  if (q8) SQ_CUDA(cudaMallocAsync(&xq, (size_t)m * (in_dim / QK) * Q8_BYTES, s));
+  cudaError_t e = launch_linear(s, input, m, in_dim, weight, wtype, out_dim, output, q8, xq);
+  if (xq) cudaFreeAsync(xq, s);
+  if (e != cudaSuccess) return cuda_fail(e, "sq_linear");
+  return SQ_OK;
+}
+
+extern "C" int sq_linear_shared(void *stream, const float *input, int m, int in_dim, int n,
+                                const void *const *weights, const int *out_dims, int wtype,
+                                float *const *outputs, int acts, void *act_scratch) {
+  if (n <= 0 || !weights || !out_dims || !outputs) return fail(SQ_ERR_SHAPE, "linear_shared: no projections");
+  for (int i = 0; i < n; i++) {
+    int st = check_linear(input, m, in_dim, weights[i], wtype, out_dims[i], outputs[i]);
+    if (st) return st;
+  }
+  const bool q8 = acts == SQ_ACTS_Q8 && wtype != SQ_BF16;
+  if (q8 && !act_scratch) return fail(SQ_ERR_ARG, "linear_shared: Q8 activations need act_scratch");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (q8) {  // quantize the shared input once (linear.rs:117-127)
+    cudaError_t e = launch_quantize_q8_0(s, input, (size_t)m * in_dim, act_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "linear_shared quantize");
+  }
+  for (int i = 0; i < n; i++) {
+    cudaError_t e = launch_linear(s, q8 ? nullptr : input, m, in_dim, weights[i], wtype, out_dims[i],
+                                  outputs[i], q8, act_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "sq_linear_shared");
+  }
+  return SQ_OK;
+}
+
+extern "C" int sq_embed(void *stream, const uint32_t *tokens, int n_tokens, const void *weight, int wtype,
+                        int embed_dim, int vocab, float *out) {
+  if (!tokens || !weight || !out) return fail(SQ_ERR_ARG, "embed: null pointer");
+  if (!is_weight_type(wtype)) return fail(SQ_ERR_INVALID_TYPE, "embed: weight type must be Q8_0, Q4_0 or BF16");
+  if (n_tokens <= 0) return fail(SQ_ERR_EMPTY, "embed: no tokens");
+  if (embed_dim <= 0 || embed_dim % QK || vocab <= 0) return fail(SQ_ERR_SHAPE, "embed: embed_dim must be a multiple of 32");
+  cudaError_t e = launch_embed((cudaStream_t)stream, tokens, n_tokens, weight, wtype, embed_dim, vocab, out);
+  if (e != cudaSuccess) return cuda_fail(e, "sq_embed");
+  return SQ_OK;
+}
+
+extern "C" int sq_rms_norm(void *stream, const float *input, const float *weight, float *output, int rows,
+                           int dim, float eps) {
+  if (!input || !weight || !output) return fail(SQ_ERR_ARG, "rms_norm: null pointer");
+  if (rows < 0 || dim <= 0) return fail(SQ_ERR_SHAPE, "rms_norm: bad shape");
+  if (rows == 0) return SQ_OK;
+  cudaError_t e = launch_rms_norm((cudaStream_t)stream, input, weight, output, rows, dim, eps);
+  if (e != cudaSuccess) return cuda_fail(e, "sq_rms_norm");
+  return SQ_OK;
+}
+
+extern "C" int sq_rms_norm_inplace(void *stream, float *x, const float *weight, int rows, int dim, float eps) {
+  return sq_rms_norm(stream, x, weight, x, rows, dim, eps);
+}
+
+extern "C" int sq_rope_rows(void *stream, float *x, int seq, int row_dim, int base_pos, const float *inv_freq,
+                            int half) {
+  if (!x || !inv_freq) return fail(SQ_ERR_ARG, "rope_rows: null pointer");
+  if (half <= 0 || seq <= 0 || row_dim <= 0 || row_dim % (2 * half) || base_pos < 0)
+    return fail(SQ_ERR_SHAPE, "rope_rows: row width must be a multiple of head_dim = 2*half");
+  cudaError_t e = launch_rope_rows((cudaStream_t)stream, x, seq, row_dim, base_pos, inv_freq, half);
+  if (e != cudaSuccess) return cuda_fail(e, "sq_rope_rows");
+  return SQ_OK;
+}
+
+extern "C" int sq_silu(void *stream, float *x, size_t n) {
+  if (!x) return fail(SQ_ERR_ARG, "silu: null pointer");
+  if (!n) return SQ_OK;
+  cudaError_t e = launch_silu((cudaStream_t)stream, x, n);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_silu");
+}
+extern "C" int sq_elementwise_mul(void *stream, const float *a, const float *b, float *out, size_t n) {
+  if (!a || !b || !out) return fail(SQ_ERR_ARG, "elementwise_mul: null pointer");
+  if (!n) return SQ_OK;
+  cudaError_t e = launch_mul((cudaStream_t)stream, a, b, out, n);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_elementwise_mul");
+}
+extern "C" int sq_elementwise_add(void *stream, float *a, const float *b, size_t n) {
+  if (!a || !b) return fail(SQ_ERR_ARG, "elementwise_add: null pointer");
+  if (!n) return SQ_OK;
+  cudaError_t e = launch_add((cudaStream_t)stream, a, b, n);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_elementwise_add");
+}
+extern "C" int sq_silu_mul(void *stream, const float *gate, const float *up, float *out, size_t n) {
+  if (!gate || !up || !out) return fail(SQ_ERR_ARG, "silu_mul: null pointer");
+  if (!n) return SQ_OK;
+  cudaError_t e = launch_silu_mul((cudaStream_t)stream, gate, up, out, n);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_silu_mul");
+}
+
+extern "C" int sq_quantize_row_q8_0(void *stream, const float *src, size_t n, void *out_blocks) {
+  if (!src || !out_blocks) return fail(SQ_ERR_ARG, "quantize_row_q8_0: null pointer");
+  if (n % QK) return fail(SQ_ERR_SHAPE, "quantize_row_q8_0: length must be a multiple of 32");
+  if ((uintptr_t)out_blocks & 1) return fail(SQ_ERR_ALIGN, "quantize_row_q8_0: output must be 2-byte aligned");
+  if (!n) return SQ_OK;
+  cudaError_t e = launch_quantize_q8_0((cudaStream_t)stream, src, n, out_blocks);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_quantize_row_q8_0");
+}
+
+extern "C" int sq_dequantize(void *stream, const void *blocks, int wtype, size_t n_elems, float *out) {
+  if (!blocks || !out) return fail(SQ_ERR_ARG, "dequantize: null pointer");
+  if (!is_weight_type(wtype)) return fail(SQ_ERR_INVALID_TYPE, "dequantize: type must be Q8_0, Q4_0 or BF16");
+  if (n_elems % QK) return fail(SQ_ERR_SHAPE, "dequantize: length must be a multiple of 32");
+  if ((uintptr_t)blocks & 1) return fail(SQ_ERR_ALIGN, "dequantize: blocks must be 2-byte aligned");
+  if (!n_elems) return SQ_OK;
+  cudaError_t e = launch_dequantize((cudaStream_t)stream, blocks, wtype, n_elems, out);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_dequantize");
+}
+
+extern "C" int sq_argmax(void *stream, const float *logits, size_t n, int64_t *out_index) {
+  if (!logits || !out_index) return fail(SQ_ERR_ARG, "argmax: null pointer");
+  if (!n) return fail(SQ_ERR_EMPTY, "argmax: empty logits");
+  cudaStream_t s = (cudaStream_t)stream;
+  void *part = nullptr;
+  SQ_CUDA(cudaMallocAsync(&part, (size_t)argmax_partials(n) * sizeof(ArgState), s));
+  cudaError_t e = launch_argmax(s, logits, n, part, (long long *)out_index);
+  cudaFreeAsync(part, s);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_argmax");
+}
+
+extern "C" int sq_sdpa_cached(void *stream, const float *q, const float *k, const float *v, float *out,
+                              int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim) {
+  if (!q || !k || !v || !out) return fail(SQ_ERR_ARG, "sdpa_cached: null pointer");
+  if (n_kv_heads <= 0 || head_dim <= 0 || n_heads <= 0 || n_heads % n_kv_heads)
+    return fail(SQ_ERR_SHAPE, "sdpa_cached: n_heads must be a positive multiple of n_kv_heads");
+  if (seq_q <= 0 || seq_k < seq_q) return fail(SQ_ERR_SHAPE, "sdpa_cached: need 0 < seq_q <= seq_k");
+  if (head_dim > 256 || head_dim % 32) return fail(SQ_ERR_SHAPE, "sdpa_cached: head_dim must be a multiple of 32, <= 256");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int ns = sdpa_num_splits(seq_q, seq_k, n_heads);
+  float *part = nullptr;
+  if (ns > 1) SQ_CUDA(cudaMallocAsync((void **)&part, sdpa_partials_floats(seq_q, n_heads, head_dim, ns) * 4, s));
+  cudaError_t e = launch_sdpa(s, q, k, v, out, seq_q, seq_k, n_heads, n_kv_heads, head_dim,
+                              (long long)n_kv_heads * head_dim, head_dim, ns, part);
+  if (part) cudaFreeAsync(part, s);
+  return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_sdpa_cached");
+}
+
+namespace sq {
+__global__ void k_kv_append(const float *__restrict__ k, const float *__restrict__ v, float *kc, float *vc, int n,
+                            int n_kv, int hd, int pos, int max_ctx) {
+  const long long total = (long long)n * n_kv * hd;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % hd);
+    const int g = (int)((i / hd) % n_kv);
+    const int r = (int)(i / ((long long)hd * n_kv));
+    const size_t dst = ((size_t)g * max_ctx + pos + r) * hd + d;
+    kc[dst] = k[i];
+    vc[dst] = v[i];
+  }
+}
+
+cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, float *kc, float *vc, int n,
+                             int n_kv, int hd, int pos, int max_ctx) {
+  k_kv_append<<<grid_for((size_t)n * n_kv * hd, 256, num_sms() * 8), 256, 0, s>>>(k, v, kc, vc, n, n_kv, hd,
+                                                                                  pos, max_ctx);
+  return cudaGetLastError();
+}
+
+__global__ void k_feedback(const long long *argmax, uint32_t *tok, uint32_t *out_ids, int step) {
+  const uint32_t t = (uint32_t)argmax[0];
+  tok[0] = t;
+  if (out_ids) out_ids[step] = t;
+}
+
+cudaError_t launch_feedback(cudaStream_t s, const long long *argmax, uint32_t *tok, uint32_t *out_ids, int step) {
+  k_feedback<<<1, 1, 0, s>>>(argmax, tok, out_ids, step);
+  return cudaGetLastError();
+}
+}  // namespace sq

@@ -1,0 +1,54 @@
+// ops.cuh — internal launchers of the op-level kernels (used by the C ABI in ops.cu
+// and by the model orchestration in host/model.cpp). No validation here: callers
+// validate shapes first.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sq {
+
+// out[m][out_dim] = x[m][in_dim] @ w; acts_q8 uses `xq` (m*in/32 Q8_0 blocks) when non-null.
+cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, const void *w, int wtype,
+                          int out_dim, float *y, int acts_q8, void *xq);
+cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out);
+cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype,
+                         int embed_dim, int vocab, float *out);
+cudaError_t launch_rms_norm(cudaStream_t s, const float *x, const float *w, float *y, int rows, int dim,
+                            float eps);
+// RoPE with on-device double-precision sin/cos of pos*inv_freq[j].
+cudaError_t launch_rope_rows(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
+                             const float *inv_freq, int half);
+// RoPE from a host-computed (C library sinf/cosf) table [n_pos][half].
+cudaError_t launch_rope_rows_table(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
+                                   const float *cos_t, const float *sin_t, int half);
+cudaError_t launch_silu(cudaStream_t s, float *x, size_t n);
+cudaError_t launch_mul(cudaStream_t s, const float *a, const float *b, float *out, size_t n);
+cudaError_t launch_add(cudaStream_t s, float *a, const float *b, size_t n);
+cudaError_t launch_silu_mul(cudaStream_t s, const float *g, const float *u, float *out, size_t n);
+cudaError_t launch_dequantize(cudaStream_t s, const void *blocks, int wtype, size_t n, float *out);
+// Two-stage greedy argmax; `partials` holds at least argmax_partials(n) states (16 bytes each).
+int argmax_partials(size_t n);
+cudaError_t launch_argmax(cudaStream_t s, const float *x, size_t n, void *partials, long long *out);
+
+// Causal GQA attention. q/out rows: [seq_q][n_heads*hd]; key s of kv head g lives at
+// k + s*k_pos_stride + g*k_head_stride (same for v). `part` is scratch for split-KV
+// partials of sdpa_partials_floats(...) floats (may be null when n_split == 1).
+constexpr long long SDPA_MAX_ROW_SPLITS = 1024;
+int sdpa_num_splits(int seq_q, int seq_k, int n_heads);
+size_t sdpa_partials_floats(int seq_q, int n_heads, int head_dim, int n_split);
+size_t sdpa_max_partials_floats(int head_dim);
+cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out,
+                        int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim,
+                        long long k_pos_stride, long long k_head_stride, int n_split, float *part);
+
+}  // namespace sq
+
+namespace sq {
+// KV append into the head-major cache [n_kv][max_ctx][hd] of one layer:
+// cache[g][pos + r][d] = src[r][g*hd + d] for r < n (kv_cache.rs:38-53 semantics).
+cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, float *kc, float *vc, int n,
+                             int n_kv, int hd, int pos, int max_ctx);
+// dst_tok[0] = (uint32)argmax[0]; out_ids[step] = dst_tok[0]  (device-side token feedback)
+cudaError_t launch_feedback(cudaStream_t s, const long long *argmax, uint32_t *tok, uint32_t *out_ids, int step);
+}  // namespace sq

@@ -1,0 +1,66 @@
+// model.h — host-side structs behind the opaque sq_model / sq_ctx handles.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/squirrel_cuda.h"
+
+namespace sq {
+struct DevTensor {
+  void *ptr = nullptr;
+  int type = 0;
+  std::vector<uint64_t> dims;
+  size_t nbytes = 0;
+};
+struct DecodeState;  // persistent decode kernel resources (decode.cu)
+void rope_inv_freq(const sq_llama_config &c, std::vector<float> &out);
+int forward_device(sq_ctx *c, const uint32_t *d_ids, int n);
+}  // namespace sq
+
+// LlamaWeights (models/llama/weights.rs:18-47) resolved to device pointers.
+struct sq_model {
+  sq_llama_config cfg{};
+  int device = 0;
+  int acts = SQ_ACTS_F32;
+  bool finalized = false;
+  std::unordered_map<std::string, sq::DevTensor> tensors;
+  struct Layer {
+    const float *attn_norm = nullptr, *ffn_norm = nullptr;
+    const void *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr,
+               *down = nullptr;
+  };
+  std::vector<Layer> layers;
+  const void *embd = nullptr, *out_w = nullptr;
+  int embd_type = 0, out_type = 0;
+  const float *out_norm = nullptr;
+  std::vector<float> inv_freq;
+  float *d_inv_freq = nullptr;
+  ~sq_model();
+};
+
+// ModelContext (models/common/context.rs:9-28): KV cache + workspace, on one stream.
+struct sq_ctx {
+  sq_model *m = nullptr;
+  int max_ctx = 0;
+  int seq_len = 0;  // KvCache::seq_len: position of the next token
+  bool have_logits = false;
+  cudaStream_t stream = nullptr;
+  // head-major KV cache: [layer][kv_head][max_ctx][head_dim] f32
+  float *kc = nullptr, *vc = nullptr;
+  int ws_rows = 0;
+  float *hidden = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr,
+        *attn_out = nullptr, *gate = nullptr, *up = nullptr, *act = nullptr, *ffn_out = nullptr, *logits = nullptr;
+  void *xq = nullptr;  // Q8_0 activation scratch (the reference's act_q)
+  float *sdpa_part = nullptr;
+  size_t sdpa_part_floats = 0;
+  void *argmax_part = nullptr;
+  long long *d_argmax = nullptr;
+  uint32_t *d_tokens = nullptr;
+  float *d_cos = nullptr, *d_sin = nullptr;  // RoPE table [max_ctx][head_dim/2]
+  sq::DecodeState *dec = nullptr;
+  std::vector<void *> allocs;
+  ~sq_ctx();
+};

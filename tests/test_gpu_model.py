@@ -1,0 +1,133 @@
+"""Model-level parity: sq_forward / sq_generate / sq_decode_steps on the B200
+against the CPU oracle's Llama3_2::forward on the same seeded GGUF and token ids.
+Bar: identical greedy ids, logits within max-abs 1e-2 and
+max-abs / max|logit| <= 1e-3."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from sqb200 import gguf_synth as G
+
+pytestmark = pytest.mark.gpu
+
+ABS_TOL, REL_TOL = 1e-2, 1e-3
+
+
+def assert_logits_close(got, want):
+    err = float(np.max(np.abs(got - want)))
+    assert err <= ABS_TOL, err
+    assert err / float(np.max(np.abs(want))) <= REL_TOL, err
+
+
+@pytest.fixture(scope="module")
+def models():
+    return {}
+
+
+def gpu_model(models, spec, wt, acts):
+    from sqb200 import lib
+    key = (spec, wt, acts)
+    if key not in models:
+        models[key] = lib.Model(G.ensure_gguf(spec, wt), acts=acts)
+    return models[key]
+
+
+@pytest.mark.parametrize("wt", ["q8_0", "q4_0", "bf16"])
+@pytest.mark.parametrize("acts", [0, 1])
+@pytest.mark.parametrize("spec", ["tiny", "small"])
+def test_generate_matches_oracle(gpu_lib, models, spec, wt, acts):
+    if wt == "bf16" and acts == 1:
+        pytest.skip("BF16 always uses f32 activations (ops/linear.rs:34)")
+    path = G.ensure_gguf(spec, wt)
+    vocab = G.SPECS[spec]["vocab"]
+    prompt = G.prompt_ids(8, seed=11, high=vocab)
+    ref = O.Model(path, acts_q8=bool(acts))
+    ids_ref, _, logits_ref = ref.generate(prompt, 20, want_logits=True)
+    m = gpu_model(models, spec, wt, acts)
+    ctx = m.new_context(256)
+    ids, ms = ctx.generate(prompt, 20)
+    assert np.array_equal(ids, ids_ref)
+    # step-by-step logits through the same boundary
+    ctx.reset()
+    inp = prompt
+    for step in range(20):
+        nxt = ctx.forward(inp)
+        assert nxt == ids_ref[step]
+        assert_logits_close(ctx.logits(), logits_ref[step])
+        inp = np.array([nxt], np.uint32)
+    ctx.close()
+
+
+def test_chunked_prefill_and_decode_steps(gpu_lib, models):
+    """A prompt longer than the prefill chunk, then device-chained decode steps."""
+    spec, wt = "tiny", "q8_0"
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(300, seed=5, high=G.SPECS[spec]["vocab"])
+    ref = O.Model(path)
+    ids_ref, _, logits_ref = ref.generate(prompt, 12, want_logits=True)
+    m = gpu_model(models, spec, wt, 0)
+    ctx = m.new_context(512)
+    first = ctx.forward(prompt)
+    assert first == ids_ref[0]
+    assert_logits_close(ctx.logits(), logits_ref[0])
+    rest = ctx.decode_steps(11)
+    assert np.array_equal(rest, ids_ref[1:12])
+    assert_logits_close(ctx.logits(), logits_ref[11])
+    assert ctx.seq_len == 300 + 11
+    ctx.close()
+
+
+def test_upload_path_equals_gguf_path(gpu_lib, models):
+    """sq_model_create + sq_model_upload_tensor + finalize (the reference-side parser
+    path) gives the same model as sq_model_load_gguf."""
+    from sqb200 import lib
+    import struct
+    spec, wt = "tiny", "q4_0"
+    path = G.ensure_gguf(spec, wt)
+    ref_m = gpu_model(models, spec, wt, 0)
+    cfg = ref_m.config
+    tensors = []
+    raw = open(path, "rb").read()
+    data_start = None
+    # walk the file the way the writer laid it out
+    from sqb200.gguf_synth import tensor_list, tensor_nbytes
+    off = 0
+    entries = []
+    for name, dims, ttype in tensor_list(G.SPECS[spec], G.TYPE_NAMES[wt]):
+        n = tensor_nbytes(int(np.prod(dims)), ttype)
+        entries.append((name, ttype, dims, off, n))
+        off = (off + n + 255) // 256 * 256
+    data_start = len(raw) - off  # the writer pads the last tensor to 256 bytes too
+    for name, ttype, dims, o, n in entries:
+        tensors.append((name, ttype, dims, np.frombuffer(raw, np.uint8, n, data_start + o)))
+    m2 = lib.Model.from_tensors(cfg, tensors)
+    prompt = G.prompt_ids(6, seed=3, high=cfg.vocab_size)
+    a = ref_m.new_context(64)
+    b = m2.new_context(64)
+    ia, _ = a.generate(prompt, 8)
+    ib, _ = b.generate(prompt, 8)
+    assert np.array_equal(ia, ib)
+    assert np.array_equal(a.logits(), b.logits())
+    a.close(); b.close(); m2.close()
+
+
+def test_model_errors(gpu_lib, models):
+    from sqb200 import lib
+    m = gpu_model(models, "tiny", "q8_0", 0)
+    ctx = m.new_context(16)
+    with pytest.raises(lib.KernelError) as e:
+        ctx.forward(np.array([], np.uint32))
+    assert e.value.kind == "EmptyInput"  # model.rs:57-61
+    with pytest.raises(lib.KernelError) as e:
+        ctx.forward(np.array([m.config.vocab_size], np.uint32))
+    assert e.value.kind == "ShapeMismatch"
+    with pytest.raises(lib.KernelError) as e:
+        ctx.forward(np.zeros(17, np.uint32))
+    assert e.value.kind == "CacheFull"
+    with pytest.raises(lib.KernelError) as e:
+        ctx.logits()
+    assert e.value.kind == "EmptyInput"
+    with pytest.raises(lib.KernelError) as e:
+        lib.Model("/nonexistent.gguf")
+    assert e.value.kind == "Io"
+    ctx.close()
