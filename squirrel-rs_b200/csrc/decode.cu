@@ -1,12 +1,976 @@
-// decode.cu — persistent single-token decode kernel (placeholder until enabled).
+// decode.cu — the persistent single-token decode kernel for sm_100a.
+//
+// One cooperative launch per token runs the whole of Llama3_2::forward for one
+// token (models/llama/model.rs:45-97 with layers.rs:81-109) plus GreedySampler
+// (greedy.rs:6-15): embedding, 16 x [RMSNorm + QKV + RoPE + KV append, GQA
+// attention, O + residual, RMSNorm + gate/up + SiLU*up, down + residual], final
+// RMSNorm, LM head, argmax — and feeds the argmax back as the next token id.
+//
+// Layout: one CTA per SM. Warp NC is the producer: one lane streams every weight
+// row this CTA owns, for the whole token, through a ring of NSLOT shared-memory
+// slots with 1-D bulk async copies (cp.async.bulk ... mbarrier::complete_tx),
+// never waiting on the activations. Warps 0..NC-1 are consumers: they decode the
+// GGUF blocks straight from shared memory (native 34/18/64-byte layout) against
+// activations held in registers, and meet the other CTAs at grid barriers only
+// where the math needs a whole vector (after QKV, attention, O, gate/up, down).
+// Because the producer runs ahead across those barriers, HBM keeps streaming
+// while the consumers wait.
+//
+// Every wait (mbarrier, grid barrier) is bounded by a clock limit; on expiry the
+// kernel records an error, drains its in-flight copies and returns, and the host
+// reports SQ_ERR_TIMEOUT.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <algorithm>
+#include <vector>
+
 #include "../host/model.h"
 #include "common.cuh"
 #include "decode.cuh"
+#include "ops.cuh"
 
 namespace sq {
-int decode_prepare(sq_ctx *) { return SQ_OK; }
-bool decode_available(const sq_ctx *) { return false; }
-int decode_launch(sq_ctx *, uint32_t *, uint32_t *, int) { return fail(SQ_ERR_ARG, "decode kernel unavailable"); }
-int decode_check(sq_ctx *) { return SQ_OK; }
-void decode_release(sq_ctx *) {}
+namespace dk {
+
+constexpr int NC = 8;                    // consumer warps
+constexpr int NTHREADS = (NC + 1) * 32;  // + one producer warp
+constexpr int SLOT = 36864;              // bytes per ring slot
+constexpr int NSLOT = 5;
+constexpr int MAX_LAYERS = 128;
+constexpr int MAX_TILE_ITEMS = 512;      // rows x segments per tile
+constexpr int GROUP = 4;                 // q heads per kv head supported here
+constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
+
+enum { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DOWN = 3, ST_LM = 4 };
+
+struct LayerW {
+  const uint8_t *q, *k, *v, *o, *gate, *up, *down;
+  const float *attn_norm, *ffn_norm;
+};
+
+struct Params {
+  int L, E, Q, KVd, F, V, H, KVH, hd, max_ctx, G;
+  int nseg_E, nseg_Q, nseg_F;
+  int rb_E, rb_Q, rb_F;        // bytes per weight row with in_dim = E / Q / F
+  int tile_rows[5];            // rows per tile per stage kind (gate/up: per matrix)
+  int max_chunks;
+  float eps, attn_scale;
+  const uint8_t *embd, *out_w;
+  const float *out_norm, *cos_t, *sin_t;
+  float *kc, *vc, *hidden, *qbuf, *attn_out, *act, *logits, *attn_part;
+  unsigned *attn_cnt, *bar, *ticket, *err;
+  ArgState *arg_part;
+  long long *argmax;
+  int *pos;
+  LayerW layers[MAX_LAYERS];
+};
+
+// ---------------------------------------------------------------------------------
+// PTX helpers: mbarrier, bulk copy, grid barrier
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
+  return *(const volatile unsigned *)p;
+}
+// Bounded wait on an mbarrier phase; false (and the error flag set) on timeout or
+// when another CTA already failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, unsigned *err) {
+  if (mbar_try_wait(b, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(b, parity)) {
+    if (ld_volatile(err)) return false;
+    if (clock64() - t0 > WAIT_LIMIT) {
+      atomicExch(err, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory"); }
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier among the consumer warps of all CTAs (the producer never joins).
+__device__ void grid_barrier(const Params &p, unsigned target) {
+  consumers_sync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(p.bar, 1u);
+    const long long t0 = clock64();
+    while (ld_acquire(p.bar) < target) {
+      if (ld_volatile(p.err)) break;
+      if (clock64() - t0 > WAIT_LIMIT) {
+        atomicExch(p.err, 2u);
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence();
+  }
+  consumers_sync();
+}
+
+// ---------------------------------------------------------------------------------
+// work split (identical in producer and consumers)
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void unit_range(int units, int stage, int cta, int G, int &u0, int &u1) {
+  const int c = (cta + stage * 61) % G;  // rotate which CTAs get the larger shares
+  u0 = (int)((long long)units * c / G);
+  u1 = (int)((long long)units * (c + 1) / G);
+}
+
+// rows of stage `kind` of layer l owned by this CTA, in the stage's row space
+__device__ __forceinline__ void stage_rows(const Params &p, int kind, int l, int cta, int &r0, int &r1) {
+  const int stage = l * 5 + kind;
+  int u0, u1;
+  switch (kind) {
+    case ST_QKV:
+      unit_range((p.Q + 2 * p.KVd) / 2, stage, cta, p.G, u0, u1);
+      r0 = 2 * u0;
+      r1 = 2 * u1;
+      return;
+    case ST_O: unit_range(p.E, stage, cta, p.G, r0, r1); return;
+    case ST_GU: unit_range(p.F, stage, cta, p.G, r0, r1); return;
+    case ST_DOWN: unit_range(p.E, stage, cta, p.G, r0, r1); return;
+    default: unit_range(p.V, stage, cta, p.G, r0, r1); return;
+  }
+}
+
+__device__ __forceinline__ int stage_rb(const Params &p, int kind) {
+  return kind == ST_O ? p.rb_Q : (kind == ST_DOWN ? p.rb_F : p.rb_E);
+}
+__device__ __forceinline__ int stage_nseg(const Params &p, int kind) {
+  return kind == ST_O ? p.nseg_Q : (kind == ST_DOWN ? p.nseg_F : p.nseg_E);
+}
+
+// ---------------------------------------------------------------------------------
+// producer: stream this CTA's weight rows for the whole token
+// ---------------------------------------------------------------------------------
+struct Ring {
+  uint8_t *slots;
+  uint64_t *full, *empty;
+};
+
+__device__ void producer(const Params &p, const Ring &ring) {
+  const int cta = blockIdx.x;
+  int slot = 0;
+  unsigned phase = 0;
+  int issued = 0;
+  bool ok = true;
+  auto next_slot = [&]() -> uint8_t * {
+    if (!mbar_wait(&ring.empty[slot], phase ^ 1u, p.err)) ok = false;
+    return ring.slots + (size_t)slot * SLOT;
+  };
+  auto advance = [&]() {
+    issued++;
+    if (++slot == NSLOT) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  };
+  for (int l = 0; l <= p.L && ok; l++) {
+    const int kinds_lo = l < p.L ? ST_QKV : ST_LM, kinds_hi = l < p.L ? ST_DOWN : ST_LM;
+    for (int kind = kinds_lo; kind <= kinds_hi && ok; kind++) {
+      int r0, r1;
+      stage_rows(p, kind, l, cta, r0, r1);
+      const int rb = stage_rb(p, kind), T = p.tile_rows[kind];
+      for (int r = r0; r < r1 && ok; r += T) {
+        const int n = min(T, r1 - r);
+        uint8_t *dst = next_slot();
+        if (!ok) break;
+        const LayerW &W = p.layers[l < p.L ? l : 0];
+        if (kind == ST_GU) {
+          mbar_expect_tx(&ring.full[slot], 2u * n * rb);
+          bulk_g2s(dst, W.gate + (size_t)r * rb, n * rb, &ring.full[slot]);
+          bulk_g2s(dst + (size_t)n * rb, W.up + (size_t)r * rb, n * rb, &ring.full[slot]);
+        } else if (kind == ST_QKV) {
+          mbar_expect_tx(&ring.full[slot], (unsigned)n * rb);
+          // rows [r, r+n) of the concatenation [Wq; Wk; Wv]
+          int a = r, off = 0;
+          const int bounds[3] = {p.Q, p.Q + p.KVd, p.Q + 2 * p.KVd};
+          const uint8_t *base[3] = {W.q, W.k, W.v};
+          const int start[3] = {0, p.Q, p.Q + p.KVd};
+          for (int t = 0; t < 3; t++) {
+            const int hi = min(r + n, bounds[t]);
+            if (a < hi) {
+              bulk_g2s(dst + (size_t)off * rb, base[t] + (size_t)(a - start[t]) * rb, (hi - a) * rb, &ring.full[slot]);
+              off += hi - a;
+              a = hi;
+            }
+          }
+        } else {
+          const uint8_t *src = kind == ST_O ? W.o : (kind == ST_DOWN ? W.down : p.out_w);
+          mbar_expect_tx(&ring.full[slot], (unsigned)n * rb);
+          bulk_g2s(dst, src + (size_t)r * rb, n * rb, &ring.full[slot]);
+        }
+        advance();
+      }
+    }
+  }
+  // Drain: on the normal path the consumers have consumed every issued slot;
+  // after an error wait (bounded) for the copies still in flight before exiting.
+  if (!ok || ld_volatile(p.err)) {
+    // slots issued but maybe not consumed: the last min(issued, NSLOT) slots
+    int s = slot;
+    unsigned ph = phase;
+    for (int i = 0; i < min(issued, NSLOT); i++) {
+      if (--s < 0) {
+        s = NSLOT - 1;
+        ph ^= 1u;
+      }
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&ring.full[s], ph) && clock64() - t0 < WAIT_LIMIT) {
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// consumers: block decode against register-resident activations
+// ---------------------------------------------------------------------------------
+// Element index of activation register i (0..63) of `lane` in segment `seg`.
+// Q8_0 / Q4_0: each lane owns one pair of consecutive 32-element blocks of the
+// segment (the segment = 32 pairs = 2048 elements). BF16: each lane owns 8
+// consecutive elements of each 256-element stripe (16-byte shared-memory reads).
+template <int T>
+__device__ __forceinline__ int xelem(int seg, int lane, int i) {
+  if constexpr (T == SQ_BF16) return seg * 2048 + (i >> 3) * 256 + lane * 8 + (i & 7);
+  return seg * 2048 + lane * 64 + i;
+}
+
+__device__ __forceinline__ float q8f(uint32_t wx, int byte) {  // wx = word ^ 0x80808080
+  return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388736.0f;
+}
+__device__ __forceinline__ float nibf(uint32_t nib4, int byte) {  // nib4 = 4 nibbles in byte lanes
+  return __uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388616.0f;
+}
+
+// Dot of this lane's 64 activations with its 64 weights of one row. `rowp` is the
+// row in shared memory; `seg` selects the 2048-element segment.
+template <int T>
+__device__ __forceinline__ float lane_dot(const uint8_t *rowp, int seg, int lane, const float (&x)[64]) {
+  if constexpr (T == SQ_Q8_0) {
+    const uint32_t *wp = reinterpret_cast<const uint32_t *>(rowp + (size_t)(seg * 32 + lane) * 68);
+    uint32_t w[17];
+#pragma unroll
+    for (int i = 0; i < 17; i++) w[i] = wp[i];
+    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
+    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 32; i++) {  // block 0: bytes 2..33
+      const int byte = 2 + i;
+      a[i & 3] = fmaf(x[i], q8f(w[byte >> 2] ^ 0x80808080u, byte & 3), a[i & 3]);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i++) {  // block 1: bytes 36..67
+      const int byte = 36 + i;
+      b[i & 3] = fmaf(x[32 + i], q8f(w[byte >> 2] ^ 0x80808080u, byte & 3), b[i & 3]);
+    }
+    return fmaf((a[0] + a[1]) + (a[2] + a[3]), s0, ((b[0] + b[1]) + (b[2] + b[3])) * s1);
+  } else if constexpr (T == SQ_Q4_0) {
+    const uint32_t *wp = reinterpret_cast<const uint32_t *>(rowp + (size_t)(seg * 32 + lane) * 36);
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; i++) w[i] = wp[i];
+    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
+    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[4] >> 16)));
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 16; j++) {  // block 0: quant bytes at 2..17
+      const int byte = 2 + j;
+      const uint32_t word = w[byte >> 2];
+      a[j & 3] = fmaf(x[j], nibf(word & 0x0F0F0F0Fu, byte & 3), a[j & 3]);
+      a[(j + 2) & 3] = fmaf(x[16 + j], nibf((word >> 4) & 0x0F0F0F0Fu, byte & 3), a[(j + 2) & 3]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) {  // block 1: quant bytes at 20..35
+      const int byte = 20 + j;
+      const uint32_t word = w[byte >> 2];
+      b[j & 3] = fmaf(x[32 + j], nibf(word & 0x0F0F0F0Fu, byte & 3), b[j & 3]);
+      b[(j + 2) & 3] = fmaf(x[48 + j], nibf((word >> 4) & 0x0F0F0F0Fu, byte & 3), b[(j + 2) & 3]);
+    }
+    return fmaf((a[0] + a[1]) + (a[2] + a[3]), s0, ((b[0] + b[1]) + (b[2] + b[3])) * s1);
+  } else {
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const uint4 u = *reinterpret_cast<const uint4 *>(rowp + (size_t)(seg * 2048 + k * 256 + lane * 8) * 2);
+      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        a[(2 * j) & 3] = fmaf(x[8 * k + 2 * j], __uint_as_float(ws[j] << 16), a[(2 * j) & 3]);
+        a[(2 * j + 1) & 3] = fmaf(x[8 * k + 2 * j + 1], __uint_as_float(ws[j] & 0xFFFF0000u), a[(2 * j + 1) & 3]);
+      }
+    }
+    return (a[0] + a[1]) + (a[2] + a[3]);
+  }
+}
+
+// Whether lane's elements in segment seg exist for a row of `in_dim` elements.
+template <int T>
+__device__ __forceinline__ bool lane_active(int seg, int lane, int in_dim) {
+  if constexpr (T == SQ_BF16) return seg * 2048 + lane * 8 < in_dim;  // in_dim % 256 == 0 checked on host
+  return seg * 2048 + lane * 64 < in_dim;
+}
+
+// Load this lane's activations of segment seg from a global vector written in this
+// kernel (L2 reads: other SMs wrote it).
+template <int T>
+__device__ __forceinline__ void load_x(float (&x)[64], const float *v, int seg, int lane, int in_dim) {
+  if (!lane_active<T>(seg, lane, in_dim)) {
+#pragma unroll
+    for (int i = 0; i < 64; i++) x[i] = 0.f;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 64; i += 4) {
+    const float4 f = __ldcg(reinterpret_cast<const float4 *>(v + xelem<T>(seg, lane, i)));
+    x[i] = f.x;
+    x[i + 1] = f.y;
+    x[i + 2] = f.z;
+    x[i + 3] = f.w;
+  }
+}
+
+// x = rms_norm(h) restricted to this lane's elements (rms_norm.rs:40-56): the
+// squared sum covers all E elements of h; y = (h*w)/rms per element.
+template <int T>
+__device__ __forceinline__ void load_x_norm(float (&x)[64], const float *h, const float *w, int seg, int lane,
+                                            int E, float eps) {
+  float ss = 0.f;
+  for (int e = lane * 4; e < E; e += 128) {
+    const float4 f = __ldcg(reinterpret_cast<const float4 *>(h + e));
+    ss = fmaf(f.x, f.x, ss);
+    ss = fmaf(f.y, f.y, ss);
+    ss = fmaf(f.z, f.z, ss);
+    ss = fmaf(f.w, f.w, ss);
+  }
+  ss = warp_sum(ss);
+  const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), eps));
+  load_x<T>(x, h, seg, lane, E);
+  if (!lane_active<T>(seg, lane, E)) return;
+#pragma unroll
+  for (int i = 0; i < 64; i++) x[i] = __fdiv_rn(__fmul_rn(x[i], __ldg(w + xelem<T>(seg, lane, i))), rms);
+}
+
+__device__ __forceinline__ float sigmoid_ref(float v) {  // kernels/sigmoid.rs:2-9
+  if (v >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+  const float z = expf(v);
+  return __fdiv_rn(z, __fadd_rn(1.0f, z));
+}
+
+struct Smem {
+  float red[2][MAX_TILE_ITEMS];
+  float att_m[NC][GROUP], att_l[NC][GROUP];
+  float att_a[NC][GROUP][128];
+  int flag;
+};
+
+// Process one matvec stage of this CTA: wait for each tile, dot every (row, segment)
+// item this warp owns, then finish rows in the epilogue.
+template <int T, int KIND>
+__device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, int l, const float (&x)[64], int &slot,
+                             unsigned &phase, int &tile_ctr, int pos) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int nseg = stage_nseg(p, KIND), rb = stage_rb(p, KIND), Tr = p.tile_rows[KIND];
+  const int in_dim = KIND == ST_O ? p.Q : (KIND == ST_DOWN ? p.F : p.E);
+  const int seg = warp % nseg;
+  const bool active = lane_active<T>(seg, lane, in_dim);
+  int r0, r1;
+  stage_rows(p, KIND, l, blockIdx.x, r0, r1);
+  const LayerW &W = p.layers[l < p.L ? l : 0];
+  for (int r = r0; r < r1; r += Tr) {
+    const int n = min(Tr, r1 - r);
+    const int rows = KIND == ST_GU ? 2 * n : n;
+    const uint8_t *tile = rg.slots + (size_t)slot * SLOT;
+    float *red = sm.red[tile_ctr & 1];
+    const bool ok = mbar_wait(&rg.full[slot], phase, p.err);
+    if (ok) {
+      for (int it = warp; it < rows * nseg; it += NC) {  // it % nseg == seg for every it of this warp
+        const int row = it / nseg;
+        float v = active ? lane_dot<T>(tile + (size_t)row * rb, seg, lane, x) : 0.f;
+        v = warp_sum(v);
+        if (lane == 0) red[it] = v;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rg.empty[slot]);
+    if (++slot == NSLOT) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    tile_ctr++;
+    consumers_sync();
+    if (!ok) continue;
+    // epilogue
+    if (KIND == ST_QKV) {
+      const int half = p.hd / 2;
+      for (int t = tid; t < n / 2; t += NC * 32) {
+        const int row = r + 2 * t;  // even row of the pair, in [Wq; Wk; Wv] row space
+        float a = 0.f, b = 0.f;
+        for (int s = 0; s < nseg; s++) {
+          a += red[(2 * t) * nseg + s];
+          b += red[(2 * t + 1) * nseg + s];
+        }
+        if (row < p.Q + p.KVd) {  // q or k: RoPE from the host-computed table (rope.rs:25-31)
+          const int j = (row % p.hd) / 2;
+          const float c = p.cos_t[(size_t)pos * half + j], s = p.sin_t[(size_t)pos * half + j];
+          const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+          const float rbv = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+          if (row < p.Q) {
+            p.qbuf[row] = ra;
+            p.qbuf[row + 1] = rbv;
+          } else {
+            const int kr = row - p.Q, g = kr / p.hd, d = kr % p.hd;
+            float *dst = p.kc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
+            dst[0] = ra;
+            dst[1] = rbv;
+          }
+        } else {
+          const int vr = row - p.Q - p.KVd, g = vr / p.hd, d = vr % p.hd;
+          float *dst = p.vc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
+          dst[0] = a;
+          dst[1] = b;
+        }
+      }
+    } else {
+      for (int t = tid; t < n; t += NC * 32) {
+        float v = 0.f;
+        for (int s = 0; s < nseg; s++) v += red[t * nseg + s];
+        const int row = r + t;
+        if (KIND == ST_O || KIND == ST_DOWN) {
+          p.hidden[row] = __fadd_rn(__ldcg(p.hidden + row), v);  // residual (elementwise_add.rs:47-61)
+        } else if (KIND == ST_GU) {
+          float u = 0.f;
+          for (int s = 0; s < nseg; s++) u += red[(n + t) * nseg + s];
+          p.act[row] = __fmul_rn(__fmul_rn(v, sigmoid_ref(v)), u);  // silu(gate) * up
+        } else {
+          p.logits[row] = v;
+        }
+      }
+    }
+  }
+  (void)W;
+}
+
+// Causal GQA attention for one token at position pos (attention.rs:11-70): split-KV
+// over (kv head, chunk) items; the last CTA to finish a kv head merges its chunks.
+template <int DPL>
+__device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Lk = pos + 1;
+  int n_chunks = (Lk + 31) / 32;
+  const int cap = max(1, (2 * p.G) / p.KVH);
+  if (n_chunks > cap) n_chunks = cap;
+  if (n_chunks > p.max_chunks) n_chunks = p.max_chunks;
+  const int CH = (Lk + n_chunks - 1) / n_chunks;
+  const int items = p.KVH * n_chunks;
+  const int hd = p.hd;
+  for (int item = blockIdx.x; item < items; item += p.G) {
+    const int g = item / n_chunks, c = item % n_chunks;
+    const int s0 = c * CH, s1 = min(Lk, s0 + CH);
+    float qv[GROUP][DPL], m[GROUP], lsum[GROUP], acc[GROUP][DPL];
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+      m[h] = -INFINITY;
+      lsum[h] = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) {
+        qv[h][i] = __ldcg(p.qbuf + (size_t)(g * GROUP + h) * hd + lane + 32 * i);
+        acc[h][i] = 0.f;
+      }
+    }
+    const float *kb = p.kc + ((size_t)l * p.KVH + g) * p.max_ctx * hd;
+    const float *vb = p.vc + ((size_t)l * p.KVH + g) * p.max_ctx * hd;
+    for (int s = s0 + warp; s < s1; s += NC) {
+      float kr[DPL], vr[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) {
+        kr[i] = __ldcg(kb + (size_t)s * hd + lane + 32 * i);
+        vr[i] = __ldcg(vb + (size_t)s * hd + lane + 32 * i);
+      }
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) {
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) d = fmaf(qv[h][i], kr[i], d);
+        const float sc = warp_sum(d) * p.attn_scale;
+        const float mn = fmaxf(m[h], sc);
+        const float corr = expf(m[h] - mn);
+        const float pr = expf(sc - mn);
+        lsum[h] = fmaf(lsum[h], corr, pr);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) acc[h][i] = fmaf(pr, vr[i], acc[h][i] * corr);
+        m[h] = mn;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+      if (lane == 0) {
+        sm.att_m[warp][h] = m[h];
+        sm.att_l[warp][h] = lsum[h];
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; i++) sm.att_a[warp][h][lane + 32 * i] = acc[h][i];
+    }
+    consumers_sync();
+    if (warp < GROUP) {  // merge the warps' states of head `warp` into this chunk's partial
+      const int h = warp;
+      float M = -INFINITY;
+      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.att_m[w][h]);
+      float Ls = 0.f, A[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) A[i] = 0.f;
+      for (int w = 0; w < NC; w++) {
+        const float f = sm.att_l[w][h] > 0.f ? expf(sm.att_m[w][h] - M) : 0.f;
+        Ls = fmaf(sm.att_l[w][h], f, Ls);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.att_a[w][h][lane + 32 * i], f, A[i]);
+      }
+      float *pp = p.attn_part + (((size_t)g * p.max_chunks + c) * GROUP + h) * (hd + 2);
+      if (lane == 0) {
+        pp[0] = M;
+        pp[1] = Ls;
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; i++) pp[2 + lane + 32 * i] = A[i];
+      __threadfence();
+    }
+    consumers_sync();
+    if (threadIdx.x == 0) {
+      const unsigned old = atomicAdd(p.attn_cnt + g, 1u);
+      sm.flag = old == (unsigned)(n_chunks - 1);
+    }
+    consumers_sync();
+    if (sm.flag) {
+      __threadfence();
+      if (warp < GROUP) {  // combine all chunks of head g*GROUP+warp
+        const int h = warp;
+        float M = -INFINITY;
+        for (int cc = 0; cc < n_chunks; cc++) {
+          const float *pp = p.attn_part + (((size_t)g * p.max_chunks + cc) * GROUP + h) * (hd + 2);
+          if (__ldcg(pp + 1) > 0.f) M = fmaxf(M, __ldcg(pp));
+        }
+        float Ls = 0.f, A[DPL];
+#pragma unroll
+        for (int i = 0; i < DPL; i++) A[i] = 0.f;
+        for (int cc = 0; cc < n_chunks; cc++) {
+          const float *pp = p.attn_part + (((size_t)g * p.max_chunks + cc) * GROUP + h) * (hd + 2);
+          const float lc = __ldcg(pp + 1);
+          if (lc > 0.f) {
+            const float f = expf(__ldcg(pp) - M);
+            Ls = fmaf(lc, f, Ls);
+#pragma unroll
+            for (int i = 0; i < DPL; i++) A[i] = fmaf(__ldcg(pp + 2 + lane + 32 * i), f, A[i]);
+          }
+        }
+        const float inv = 1.0f / Ls;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) p.attn_out[(size_t)(g * GROUP + h) * hd + lane + 32 * i] = A[i] * inv;
+      }
+      if (threadIdx.x == 0) p.attn_cnt[g] = 0;
+    }
+    consumers_sync();
+  }
+}
+
+// Ordered greedy fold over a contiguous range by one warp (lanes take contiguous
+// sub-ranges, combined left to right).
+__device__ ArgState warp_argmax(const float *v, long long lo, long long hi, bool from_l2) {
+  const int lane = threadIdx.x & 31;
+  const long long n = hi - lo, per = (n + 31) / 32;
+  ArgState s = arg_empty();
+  for (long long i = lo + lane * per; i < lo + (lane + 1) * per && i < hi; i++)
+    s = arg_combine(s, arg_elem(from_l2 ? __ldcg(v + i) : v[i], i));
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    ArgState r;
+    r.v = __shfl_down_sync(0xffffffffu, s.v, o);
+    r.best = __shfl_down_sync(0xffffffffu, s.best, o);
+    r.nan = __shfl_down_sync(0xffffffffu, s.nan, o);
+    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) s = arg_combine(s, r);
+  }
+  return s;  // valid in lane 0
+}
+
+__device__ ArgState warp_argmax_states(const ArgState *st, int n) {
+  const int lane = threadIdx.x & 31;
+  const int per = (n + 31) / 32;
+  ArgState s = arg_empty();
+  for (int i = lane * per; i < (lane + 1) * per && i < n; i++) {
+    ArgState x;
+    x.v = __ldcg(&st[i].v);
+    x.best = __ldcg(&st[i].best);
+    x.nan = __ldcg(&st[i].nan);
+    s = arg_combine(s, x);
+  }
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    ArgState r;
+    r.v = __shfl_down_sync(0xffffffffu, s.v, o);
+    r.best = __shfl_down_sync(0xffffffffu, s.best, o);
+    r.nan = __shfl_down_sync(0xffffffffu, s.nan, o);
+    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) s = arg_combine(s, r);
+  }
+  return s;
+}
+
+template <int T, int DPL>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_decode(const Params *__restrict__ pp, const uint32_t *tok_in, uint32_t *tok_out, uint32_t *out_ids,
+             int step) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  const Params &p = *pp;
+  Ring rg;
+  rg.slots = dsm;
+  rg.full = reinterpret_cast<uint64_t *>(dsm + (size_t)NSLOT * SLOT);
+  rg.empty = rg.full + NSLOT;
+  Smem &sm = *reinterpret_cast<Smem *>(rg.empty + NSLOT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSLOT; s++) {
+      mbar_init(&rg.full[s], 1);
+      mbar_init(&rg.empty[s], NC);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == NC) {  // producer warp: one lane issues everything
+    if (lane == 0) producer(p, rg);
+    return;
+  }
+  const int pos = *p.pos;
+  const uint32_t tok = *tok_in;
+  int slot = 0, tile_ctr = 0;
+  unsigned phase = 0, bar_target = 0;
+  float x[64];
+  for (int l = 0; l < p.L; l++) {
+    const LayerW &W = p.layers[l];
+    // ---- RMSNorm + QKV + RoPE + KV append
+    const int segE = warp % p.nseg_E;
+    if (l == 0) {
+      // embed (ops/embedding.rs:10-52) straight into registers; CTA 0 also writes hidden
+      const uint8_t *row = p.embd + (size_t)tok * (p.E / QK) * type_bytes<T>();
+      float ss = 0.f;
+      for (int e = lane; e < p.E; e += 32) {
+        const float v = dequant_elem<T>(row + (e / QK) * type_bytes<T>(), e % QK);
+        ss = fmaf(v, v, ss);
+        if (blockIdx.x == 0 && warp == 0) p.hidden[e] = v;
+      }
+      ss = warp_sum(ss);
+      const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.E), p.eps));
+      const bool act = lane_active<T>(segE, lane, p.E);
+#pragma unroll
+      for (int i = 0; i < 64; i++) {
+        const int e = xelem<T>(segE, lane, i);
+        const float v = act ? dequant_elem<T>(row + (e / QK) * type_bytes<T>(), e % QK) : 0.f;
+        x[i] = act ? __fdiv_rn(__fmul_rn(v, __ldg(W.attn_norm + e)), rms) : 0.f;
+      }
+    } else {
+      load_x_norm<T>(x, p.hidden, W.attn_norm, segE, lane, p.E, p.eps);
+    }
+    matvec_stage<T, ST_QKV>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    bar_target += p.G;
+    grid_barrier(p, bar_target);
+    // ---- attention
+    attention_stage<DPL>(p, sm, l, pos);
+    bar_target += p.G;
+    grid_barrier(p, bar_target);
+    // ---- O projection + residual
+    load_x<T>(x, p.attn_out, warp % p.nseg_Q, lane, p.Q);
+    matvec_stage<T, ST_O>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    bar_target += p.G;
+    grid_barrier(p, bar_target);
+    // ---- RMSNorm + gate/up + SiLU*up
+    load_x_norm<T>(x, p.hidden, W.ffn_norm, segE, lane, p.E, p.eps);
+    matvec_stage<T, ST_GU>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    bar_target += p.G;
+    grid_barrier(p, bar_target);
+    // ---- down + residual
+    load_x<T>(x, p.act, warp % p.nseg_F, lane, p.F);
+    matvec_stage<T, ST_DOWN>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    bar_target += p.G;
+    grid_barrier(p, bar_target);
+  }
+  // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
+  load_x_norm<T>(x, p.hidden, p.out_norm, warp % p.nseg_E, lane, p.E, p.eps);
+  matvec_stage<T, ST_LM>(p, rg, sm, p.L, x, slot, phase, tile_ctr, pos);
+  consumers_sync();
+  // ---- greedy argmax: this CTA's rows in order, then the last CTA folds all CTAs
+  if (warp == 0) {
+    int r0, r1;
+    stage_rows(p, ST_LM, p.L, blockIdx.x, r0, r1);
+    const ArgState s = warp_argmax(p.logits, r0, r1, true);
+    unsigned last = 0;
+    if (lane == 0) {
+      p.arg_part[blockIdx.x] = s;
+      __threadfence();
+      last = atomicAdd(p.ticket, 1u) == (unsigned)(p.G - 1);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      // stage_rows rotates ownership, so fold the CTAs in row order
+      const ArgState f = [&]() {
+        ArgState acc = arg_empty();
+        for (int base = 0; base < p.G; base += 32) {
+          ArgState mine = arg_empty();
+          const int i = base + lane;
+          if (i < p.G) {
+            const int owner = ((i - (p.L * 5 + ST_LM) * 61) % p.G + p.G) % p.G;  // CTA whose rotated index is i
+            mine.v = __ldcg(&p.arg_part[owner].v);
+            mine.best = __ldcg(&p.arg_part[owner].best);
+            mine.nan = __ldcg(&p.arg_part[owner].nan);
+          }
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            ArgState r;
+            r.v = __shfl_down_sync(0xffffffffu, mine.v, o);
+            r.best = __shfl_down_sync(0xffffffffu, mine.best, o);
+            r.nan = __shfl_down_sync(0xffffffffu, mine.nan, o);
+            if ((lane & (2 * o - 1)) == 0 && lane + o < 32) mine = arg_combine(mine, r);
+          }
+          if (lane == 0) acc = arg_combine(acc, mine);
+        }
+        return acc;
+      }();
+      if (lane == 0) {
+        const long long id = arg_result(f);
+        *p.argmax = id;
+        *tok_out = (uint32_t)id;
+        if (out_ids) out_ids[step] = (uint32_t)id;
+        *p.pos = pos + 1;
+        *p.bar = 0;  // every CTA has passed its last grid barrier
+        *p.ticket = 0;
+      }
+    }
+  }
+}
+
+}  // namespace dk
+
+// ---------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------
+struct DecodeState {
+  bool available = false;
+  int dev_pos = 0;  // position the device counter holds once queued launches finish
+  dk::Params *d_params = nullptr;
+  void *kernel = nullptr;
+  size_t smem = 0;
+  int grid = 0;
+  unsigned *d_err = nullptr;
+  int *d_pos = nullptr;
+  std::vector<void *> allocs;
+};
+
+template <int T, int DPL>
+static void *pick_kernel() {
+  return (void *)dk::k_decode<T, DPL>;
+}
+
+static int nseg_for(int in_dim) {
+  const int s = (in_dim + 2047) / 2048;
+  for (int c : {1, 2, 4, 8})
+    if (s <= c) return c;
+  return 0;
+}
+
+int decode_prepare(sq_ctx *c) {
+  const sq_model *m = c->m;
+  const sq_llama_config &cf = m->cfg;
+  auto *st = new DecodeState();
+  c->dec = st;
+  if (getenv("SQ_DISABLE_DECODE_KERNEL")) return SQ_OK;
+  const int E = cf.embed_dim, Q = cf.n_heads * cf.head_dim, KVd = cf.n_kv_heads * cf.head_dim, F = cf.ffn_dim;
+  const int wt = cf.weight_type, bb = block_bytes(wt);
+  // supported shapes: same type everywhere, rows multiple of 16 bytes, <= 8 segments, GQA group 4
+  bool ok = m->out_type == wt && m->embd_type == wt && cf.n_blocks <= dk::MAX_LAYERS &&
+            cf.n_heads == dk::GROUP * cf.n_kv_heads && (cf.head_dim == 64 || cf.head_dim == 128);
+  const int nE = nseg_for(E), nQ = nseg_for(Q), nF = nseg_for(F);
+  ok = ok && nE && nQ && nF;
+  ok = ok && m->acts == SQ_ACTS_F32;  // Q8_0 activations run on the op-level kernels
+  for (int d : {E, Q, F}) {
+    ok = ok && (d / QK) % 8 == 0 && ((size_t)(d / QK) * bb) % 16 == 0;  // pairs, 16-byte rows
+    if (wt == SQ_BF16) ok = ok && d % 2048 == 0;  // BF16 lanes stripe whole 2048-element segments
+  }
+  const int rbE = E / QK * bb, rbQ = Q / QK * bb, rbF = F / QK * bb;
+  auto rows_fit = [&](int rb, int mult) {
+    int t = dk::SLOT / (rb * mult);
+    if (t >= 2) t &= ~1;
+    return t;
+  };
+  dk::Params h{};
+  h.tile_rows[dk::ST_QKV] = rows_fit(rbE, 1);
+  h.tile_rows[dk::ST_O] = rows_fit(rbQ, 1);
+  h.tile_rows[dk::ST_GU] = rows_fit(rbE, 2);
+  h.tile_rows[dk::ST_DOWN] = rows_fit(rbF, 1);
+  h.tile_rows[dk::ST_LM] = rows_fit(rbE, 1);
+  for (int k = 0; k < 5; k++) {
+    const int nseg = k == dk::ST_O ? nQ : (k == dk::ST_DOWN ? nF : nE);
+    ok = ok && h.tile_rows[k] >= 2 && h.tile_rows[k] * (k == dk::ST_GU ? 2 : 1) * nseg <= dk::MAX_TILE_ITEMS;
+  }
+  if (!ok) return SQ_OK;  // the op-level path serves this model
+  int dev = m->device, nsm = 0;
+  SQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  void *kern = nullptr;
+  if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
+  else if (wt == SQ_Q4_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q4_0, 2>() : pick_kernel<SQ_Q4_0, 4>();
+  else kern = cf.head_dim == 64 ? pick_kernel<SQ_BF16, 2>() : pick_kernel<SQ_BF16, 4>();
+  const size_t smem = (size_t)dk::NSLOT * dk::SLOT + 2 * dk::NSLOT * sizeof(uint64_t) + sizeof(dk::Smem);
+  SQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  SQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, dk::NTHREADS, smem));
+  if (per_sm < 1) return SQ_OK;
+  h.L = cf.n_blocks;
+  h.E = E;
+  h.Q = Q;
+  h.KVd = KVd;
+  h.F = F;
+  h.V = cf.vocab_size;
+  h.H = cf.n_heads;
+  h.KVH = cf.n_kv_heads;
+  h.hd = cf.head_dim;
+  h.max_ctx = c->max_ctx;
+  h.G = nsm;
+  h.nseg_E = nE;
+  h.nseg_Q = nQ;
+  h.nseg_F = nF;
+  h.rb_E = rbE;
+  h.rb_Q = rbQ;
+  h.rb_F = rbF;
+  h.max_chunks = std::max(1, (2 * nsm) / cf.n_kv_heads);
+  h.eps = cf.rms_eps;
+  h.attn_scale = 1.0f / sqrtf((float)cf.head_dim);
+  h.embd = (const uint8_t *)m->embd;
+  h.out_w = (const uint8_t *)m->out_w;
+  h.out_norm = m->out_norm;
+  h.cos_t = c->d_cos;
+  h.sin_t = c->d_sin;
+  h.kc = c->kc;
+  h.vc = c->vc;
+  h.hidden = c->hidden;
+  h.qbuf = c->q;
+  h.attn_out = c->attn;
+  h.act = c->act;
+  h.logits = c->logits;
+  h.argmax = c->d_argmax;
+  for (int l = 0; l < cf.n_blocks; l++) {
+    const auto &Lw = m->layers[l];
+    h.layers[l] = {(const uint8_t *)Lw.q, (const uint8_t *)Lw.k, (const uint8_t *)Lw.v, (const uint8_t *)Lw.o,
+                   (const uint8_t *)Lw.gate, (const uint8_t *)Lw.up, (const uint8_t *)Lw.down, Lw.attn_norm,
+                   Lw.ffn_norm};
+  }
+  auto alloc = [&](void **p, size_t bytes) -> cudaError_t {
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e == cudaSuccess) {
+      st->allocs.push_back(*p);
+      e = cudaMemset(*p, 0, bytes);
+    }
+    return e;
+  };
+  SQ_CUDA(alloc((void **)&h.attn_part, (size_t)cf.n_kv_heads * h.max_chunks * dk::GROUP * (cf.head_dim + 2) * 4));
+  SQ_CUDA(alloc((void **)&h.attn_cnt, (size_t)cf.n_kv_heads * 4));
+  SQ_CUDA(alloc((void **)&h.bar, 4));
+  SQ_CUDA(alloc((void **)&h.ticket, 4));
+  SQ_CUDA(alloc((void **)&h.err, 4));
+  SQ_CUDA(alloc((void **)&h.arg_part, (size_t)nsm * sizeof(ArgState)));
+  SQ_CUDA(alloc((void **)&h.pos, 4));
+  SQ_CUDA(alloc((void **)&st->d_params, sizeof(dk::Params)));
+  SQ_CUDA(cudaMemcpy(st->d_params, &h, sizeof(dk::Params), cudaMemcpyHostToDevice));
+  st->d_err = h.err;
+  st->d_pos = h.pos;
+  st->kernel = kern;
+  st->smem = smem;
+  st->grid = nsm;
+  st->available = true;
+  return SQ_OK;
+}
+
+bool decode_available(const sq_ctx *c) { return c->dec && c->dec->available; }
+
+__global__ void k_set_int(int *p, int v) { *p = v; }
+
+int decode_launch(sq_ctx *c, uint32_t *d_tok, uint32_t *out_ids, int step) {
+  DecodeState *st = c->dec;
+  // the kernel reads the position from device memory and advances it itself; resync
+  // only after prefill or reset moved the host's count
+  if (st->dev_pos != c->seq_len) {
+    k_set_int<<<1, 1, 0, c->stream>>>(st->d_pos, c->seq_len);
+    SQ_CHECK_LAUNCH("decode pos");
+    st->dev_pos = c->seq_len;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(st->grid);
+  cfg.blockDim = dim3(dk::NTHREADS);
+  cfg.dynamicSmemBytes = st->smem;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void *args[] = {&st->d_params, &d_tok, &d_tok, &out_ids, &step};
+  SQ_CUDA(cudaLaunchKernelExC(&cfg, st->kernel, args));
+  c->seq_len += 1;
+  st->dev_pos += 1;
+  return SQ_OK;
+}
+
+int decode_check(sq_ctx *c) {
+  DecodeState *st = c->dec;
+  if (!st || !st->available) return SQ_OK;
+  unsigned err = 0;
+  SQ_CUDA(cudaMemcpy(&err, st->d_err, 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    // reset the kernel's flag and counters so the context stays usable
+    cudaMemset(st->d_err, 0, 4);
+    for (void *p : st->allocs) (void)p;
+    st->dev_pos = -1;  // force a position resync
+    return fail(SQ_ERR_TIMEOUT, "decode kernel: a bounded wait expired (code " + std::to_string(err) + ")");
+  }
+  return SQ_OK;
+}
+
+void decode_release(sq_ctx *c) {
+  if (!c->dec) return;
+  for (void *p : c->dec->allocs) cudaFree(p);
+  delete c->dec;
+  c->dec = nullptr;
+}
+
 }  // namespace sq

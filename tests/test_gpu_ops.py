@@ -237,8 +237,8 @@ def test_silu_mul_add(gpu_lib):
     a = dev(g.copy())
     lib.elementwise_add(a, dev(u))
     assert np.array_equal(host(a), g + u)
-    sm = host(lib.silu_mul(dev(g), dev(u)))
-    assert np.all(np.abs(sm - want * u) <= 3e-7 * np.abs(want * u) + 1e-30)
+    sm = host(lib.silu_mul(dev(g), dev(u)))  # silu's 2 ulp plus one rounding of the product
+    assert np.all(np.abs(sm - want * u) <= 5e-7 * np.abs(want * u) + 1e-30)
 
 
 @pytest.mark.parametrize("case", ["known", "nan", "ties", "random", "vocab", "all_nan_tail"])
