@@ -219,6 +219,7 @@ def run_ours(args):
     prefill_s = time.perf_counter() - t0
     ctx.decode_steps(args.warmup)
     kv0 = ctx.seq_len
+    lpt = ctx.launches_per_token
 
     if dist:
         dist.barrier()
@@ -285,7 +286,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic_for(args.workload),
                          "algorithmic_bytes_per_step": algo, "kernel": "decode step"},
-            "gpu_launches": args.steps * launches_per_step(ctx, cfg),
+            "gpu_launches": args.steps * lpt,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "first_ids": [int(first)] + [int(i) for i in ids[:8]],
@@ -296,15 +297,6 @@ def run_ours(args):
     if dist:
         dist.destroy_process_group()
     return 0
-
-
-def launches_per_step(ctx, cfg):
-    from sqb200 import lib
-    n = lib.load().sq_decode_launches_per_step(ctx._h) if hasattr(lib.load(), "sq_decode_launches_per_step") else -1
-    if n and n > 0:
-        return n
-    # op path: embed + per layer 18 + final norm, LM head, argmax (2), feedback
-    return 1 + 18 * cfg.n_blocks + 5
 
 
 def main():

@@ -161,6 +161,9 @@ int sq_generate(sq_ctx *c, const uint32_t *prompt, size_t n_prompt, int max_toke
 int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids);
 /* Device stream of the context (cudaStream_t), for timing with events. */
 void *sq_ctx_stream(sq_ctx *c);
+/* Kernel launches one decode step of this context issues: 1 when the persistent
+ * decode kernel serves the model, else the count of the op-level sequence. */
+int sq_ctx_launches_per_token(const sq_ctx *c, int *out);
 
 #ifdef __cplusplus
 }

@@ -2,27 +2,32 @@
 //
 // One cooperative launch per token runs the whole of Llama3_2::forward for one
 // token (models/llama/model.rs:45-97 with layers.rs:81-109) plus GreedySampler
-// (greedy.rs:6-15): embedding, 16 x [RMSNorm + QKV + RoPE + KV append, GQA
+// (greedy.rs:6-15): embedding, L x [RMSNorm + QKV + RoPE + KV append, GQA
 // attention, O + residual, RMSNorm + gate/up + SiLU*up, down + residual], final
 // RMSNorm, LM head, argmax — and feeds the argmax back as the next token id.
 //
-// Layout: one CTA per SM. Warp NC is the producer: one lane streams every weight
-// row this CTA owns, for the whole token, through a ring of NSLOT shared-memory
-// slots with 1-D bulk async copies (cp.async.bulk ... mbarrier::complete_tx),
-// never waiting on the activations. Warps 0..NC-1 are consumers: they decode the
-// GGUF blocks straight from shared memory (native 34/18/64-byte layout) against
-// activations held in registers, and meet the other CTAs at grid barriers only
-// where the math needs a whole vector (after QKV, attention, O, gate/up, down).
-// Because the producer runs ahead across those barriers, HBM keeps streaming
-// while the consumers wait.
+// Layout: one CTA of NC warps per SM. Every weight row the CTA owns for the whole
+// token streams through a ring of NSLOT shared-memory slots with 1-D bulk async
+// copies (cp.async.bulk ... mbarrier::complete_tx): the last warp to finish with a
+// slot immediately refills it with the tile NSLOT positions ahead in the CTA's tile
+// table (built once per context), so NSLOT tiles are always in flight — also while
+// the warps wait at a grid barrier. The warps decode the GGUF blocks straight from
+// shared memory (native 34/18/64-byte layout) against activations held in
+// registers, two weight rows per warp at a time, and finish each row inside the
+// warp (RoPE, residual add, SiLU*up, logits). They meet the other CTAs at grid
+// barriers only where the math needs a whole vector (after QKV, attention, O,
+// gate/up, down).
 //
 // Every wait (mbarrier, grid barrier) is bounded by a clock limit; on expiry the
 // kernel records an error, drains its in-flight copies and returns, and the host
 // reports SQ_ERR_TIMEOUT.
 #include <cuda_runtime.h>
 #include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
 
 #include <algorithm>
+#include <string>
 #include <vector>
 
 #include "../host/model.h"
@@ -33,12 +38,13 @@
 namespace sq {
 namespace dk {
 
-constexpr int NC = 8;                    // consumer warps
-constexpr int NTHREADS = (NC + 1) * 32;  // + one producer warp
+constexpr int NC = 8;                    // warps per CTA (2 per SM sub-partition: 255 registers each)
+constexpr int NTHREADS = NC * 32;
 constexpr int SLOT = 36864;              // bytes per ring slot
 constexpr int NSLOT = 5;
 constexpr int MAX_LAYERS = 128;
 constexpr int MAX_TILE_ITEMS = 512;      // rows x segments per tile
+constexpr int MAX_LM_ROWS = 1024;        // LM-head rows per CTA kept in shared memory
 constexpr int GROUP = 4;                 // q heads per kv head supported here
 constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
 
@@ -63,11 +69,16 @@ struct Params {
   ArgState *arg_part;
   long long *argmax;
   int *pos;
+  unsigned long long *timeline;  // optional per-CTA stage timestamps (SQ_DECODE_TIMELINE)
+  int tl_stride;
+  int2 *tiles;                   // [G][max_tiles] tile table: {row, layer<<16 | kind<<12 | rows}
+  int *ntiles;                   // [G]
+  int max_tiles;
   LayerW layers[MAX_LAYERS];
 };
 
 // ---------------------------------------------------------------------------------
-// PTX helpers: mbarrier, bulk copy, grid barrier
+// PTX helpers: mbarrier, bulk copy, shared loads, grid barrier
 // ---------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -76,9 +87,6 @@ __device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count) {
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *b, unsigned parity) {
   unsigned ok;
@@ -115,36 +123,66 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory"); }
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory"); }
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
-// Grid barrier among the consumer warps of all CTAs (the producer never joins).
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Timeline slot k of this CTA: 0 = start; for stage s (5 per layer, the LM head is
+// stage 5L) 6s+2 = activations loaded, 6s+3 / 6s+4 = first / last tile landed,
+// 6s+5 / 6s+6 = grid-barrier arrive / leave; stride-2 = LM head done, stride-1 = end.
+__device__ __forceinline__ void stamp(const Params &p, int k) {
+  if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = global_ns();
+}
+
+// Grid barrier among all CTAs. Thread 0 publishes the CTA's writes with a release
+// add and spins on an acquire load; the CTA barriers on both sides order the other
+// threads.
 __device__ void grid_barrier(const Params &p, unsigned target) {
-  consumers_sync();
+  cta_sync();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(p.bar, 1u);
+    const int b = (int)(target / p.G) - 1;
+    stamp(p, 6 * b + 5);
+    red_release_add(p.bar, 1u);
     const long long t0 = clock64();
+    unsigned it = 0;
     while (ld_acquire(p.bar) < target) {
-      if (ld_volatile(p.err)) break;
-      if (clock64() - t0 > WAIT_LIMIT) {
-        atomicExch(p.err, 2u);
-        break;
+      if ((++it & 255u) == 0) {
+        if (ld_volatile(p.err)) break;
+        if (clock64() - t0 > WAIT_LIMIT) {
+          atomicExch(p.err, 2u);
+          break;
+        }
       }
-      __nanosleep(32);
     }
-    __threadfence();
+    stamp(p, 6 * b + 6);
   }
-  consumers_sync();
+  cta_sync();
 }
 
 // ---------------------------------------------------------------------------------
-// work split (identical in producer and consumers)
+// work split (the same in the tile tables and in the consumers)
 // ---------------------------------------------------------------------------------
 __device__ __forceinline__ void unit_range(int units, int stage, int cta, int G, int &u0, int &u1) {
   const int c = (cta + stage * 61) % G;  // rotate which CTAs get the larger shares
@@ -177,90 +215,15 @@ __device__ __forceinline__ int stage_nseg(const Params &p, int kind) {
 }
 
 // ---------------------------------------------------------------------------------
-// producer: stream this CTA's weight rows for the whole token
-// ---------------------------------------------------------------------------------
-struct Ring {
-  uint8_t *slots;
-  uint64_t *full, *empty;
-};
-
-__device__ void producer(const Params &p, const Ring &ring) {
-  const int cta = blockIdx.x;
-  int slot = 0;
-  unsigned phase = 0;
-  int issued = 0;
-  bool ok = true;
-  auto next_slot = [&]() -> uint8_t * {
-    if (!mbar_wait(&ring.empty[slot], phase ^ 1u, p.err)) ok = false;
-    return ring.slots + (size_t)slot * SLOT;
-  };
-  auto advance = [&]() {
-    issued++;
-    if (++slot == NSLOT) {
-      slot = 0;
-      phase ^= 1u;
-    }
-  };
-  for (int l = 0; l <= p.L && ok; l++) {
-    const int kinds_lo = l < p.L ? ST_QKV : ST_LM, kinds_hi = l < p.L ? ST_DOWN : ST_LM;
-    for (int kind = kinds_lo; kind <= kinds_hi && ok; kind++) {
-      int r0, r1;
-      stage_rows(p, kind, l, cta, r0, r1);
-      const int rb = stage_rb(p, kind), T = p.tile_rows[kind];
-      for (int r = r0; r < r1 && ok; r += T) {
-        const int n = min(T, r1 - r);
-        uint8_t *dst = next_slot();
-        if (!ok) break;
-        const LayerW &W = p.layers[l < p.L ? l : 0];
-        if (kind == ST_GU) {
-          mbar_expect_tx(&ring.full[slot], 2u * n * rb);
-          bulk_g2s(dst, W.gate + (size_t)r * rb, n * rb, &ring.full[slot]);
-          bulk_g2s(dst + (size_t)n * rb, W.up + (size_t)r * rb, n * rb, &ring.full[slot]);
-        } else if (kind == ST_QKV) {
-          mbar_expect_tx(&ring.full[slot], (unsigned)n * rb);
-          // rows [r, r+n) of the concatenation [Wq; Wk; Wv]
-          int a = r, off = 0;
-          const int bounds[3] = {p.Q, p.Q + p.KVd, p.Q + 2 * p.KVd};
-          const uint8_t *base[3] = {W.q, W.k, W.v};
-          const int start[3] = {0, p.Q, p.Q + p.KVd};
-          for (int t = 0; t < 3; t++) {
-            const int hi = min(r + n, bounds[t]);
-            if (a < hi) {
-              bulk_g2s(dst + (size_t)off * rb, base[t] + (size_t)(a - start[t]) * rb, (hi - a) * rb, &ring.full[slot]);
-              off += hi - a;
-              a = hi;
-            }
-          }
-        } else {
-          const uint8_t *src = kind == ST_O ? W.o : (kind == ST_DOWN ? W.down : p.out_w);
-          mbar_expect_tx(&ring.full[slot], (unsigned)n * rb);
-          bulk_g2s(dst, src + (size_t)r * rb, n * rb, &ring.full[slot]);
-        }
-        advance();
-      }
-    }
-  }
-  // Drain: on the normal path the consumers have consumed every issued slot;
-  // after an error wait (bounded) for the copies still in flight before exiting.
-  if (!ok || ld_volatile(p.err)) {
-    // slots issued but maybe not consumed: the last min(issued, NSLOT) slots
-    int s = slot;
-    unsigned ph = phase;
-    for (int i = 0; i < min(issued, NSLOT); i++) {
-      if (--s < 0) {
-        s = NSLOT - 1;
-        ph ^= 1u;
-      }
-      const long long t0 = clock64();
-      while (!mbar_try_wait(&ring.full[s], ph) && clock64() - t0 < WAIT_LIMIT) {
-      }
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------------
 // consumers: block decode against register-resident activations
 // ---------------------------------------------------------------------------------
+constexpr unsigned FULL = 0xffffffffu;
+
+struct Ring {
+  uint8_t *slots;
+  uint64_t *full;  // full[s]: the bytes of the tile in slot s have landed
+};
+
 // Element index of activation register i (0..63) of `lane` in segment `seg`.
 // Q8_0 / Q4_0: each lane owns one pair of consecutive 32-element blocks of the
 // segment (the segment = 32 pairs = 2048 elements). BF16: each lane owns 8
@@ -271,79 +234,10 @@ __device__ __forceinline__ int xelem(int seg, int lane, int i) {
   return seg * 2048 + lane * 64 + i;
 }
 
-__device__ __forceinline__ float q8f(uint32_t wx, int byte) {  // wx = word ^ 0x80808080
-  return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388736.0f;
-}
-__device__ __forceinline__ float nibf(uint32_t nib4, int byte) {  // nib4 = 4 nibbles in byte lanes
-  return __uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388616.0f;
-}
-
-// Dot of this lane's 64 activations with its 64 weights of one row. `rowp` is the
-// row in shared memory; `seg` selects the 2048-element segment.
-template <int T>
-__device__ __forceinline__ float lane_dot(const uint8_t *rowp, int seg, int lane, const float (&x)[64]) {
-  if constexpr (T == SQ_Q8_0) {
-    const uint32_t *wp = reinterpret_cast<const uint32_t *>(rowp + (size_t)(seg * 32 + lane) * 68);
-    uint32_t w[17];
-#pragma unroll
-    for (int i = 0; i < 17; i++) w[i] = wp[i];
-    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
-    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
-    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < 32; i++) {  // block 0: bytes 2..33
-      const int byte = 2 + i;
-      a[i & 3] = fmaf(x[i], q8f(w[byte >> 2] ^ 0x80808080u, byte & 3), a[i & 3]);
-    }
-#pragma unroll
-    for (int i = 0; i < 32; i++) {  // block 1: bytes 36..67
-      const int byte = 36 + i;
-      b[i & 3] = fmaf(x[32 + i], q8f(w[byte >> 2] ^ 0x80808080u, byte & 3), b[i & 3]);
-    }
-    return fmaf((a[0] + a[1]) + (a[2] + a[3]), s0, ((b[0] + b[1]) + (b[2] + b[3])) * s1);
-  } else if constexpr (T == SQ_Q4_0) {
-    const uint32_t *wp = reinterpret_cast<const uint32_t *>(rowp + (size_t)(seg * 32 + lane) * 36);
-    uint32_t w[9];
-#pragma unroll
-    for (int i = 0; i < 9; i++) w[i] = wp[i];
-    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
-    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[4] >> 16)));
-    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < 16; j++) {  // block 0: quant bytes at 2..17
-      const int byte = 2 + j;
-      const uint32_t word = w[byte >> 2];
-      a[j & 3] = fmaf(x[j], nibf(word & 0x0F0F0F0Fu, byte & 3), a[j & 3]);
-      a[(j + 2) & 3] = fmaf(x[16 + j], nibf((word >> 4) & 0x0F0F0F0Fu, byte & 3), a[(j + 2) & 3]);
-    }
-#pragma unroll
-    for (int j = 0; j < 16; j++) {  // block 1: quant bytes at 20..35
-      const int byte = 20 + j;
-      const uint32_t word = w[byte >> 2];
-      b[j & 3] = fmaf(x[32 + j], nibf(word & 0x0F0F0F0Fu, byte & 3), b[j & 3]);
-      b[(j + 2) & 3] = fmaf(x[48 + j], nibf((word >> 4) & 0x0F0F0F0Fu, byte & 3), b[(j + 2) & 3]);
-    }
-    return fmaf((a[0] + a[1]) + (a[2] + a[3]), s0, ((b[0] + b[1]) + (b[2] + b[3])) * s1);
-  } else {
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-      const uint4 u = *reinterpret_cast<const uint4 *>(rowp + (size_t)(seg * 2048 + k * 256 + lane * 8) * 2);
-      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        a[(2 * j) & 3] = fmaf(x[8 * k + 2 * j], __uint_as_float(ws[j] << 16), a[(2 * j) & 3]);
-        a[(2 * j + 1) & 3] = fmaf(x[8 * k + 2 * j + 1], __uint_as_float(ws[j] & 0xFFFF0000u), a[(2 * j + 1) & 3]);
-      }
-    }
-    return (a[0] + a[1]) + (a[2] + a[3]);
-  }
-}
-
 // Whether lane's elements in segment seg exist for a row of `in_dim` elements.
 template <int T>
 __device__ __forceinline__ bool lane_active(int seg, int lane, int in_dim) {
-  if constexpr (T == SQ_BF16) return seg * 2048 + lane * 8 < in_dim;  // in_dim % 256 == 0 checked on host
+  if constexpr (T == SQ_BF16) return seg * 2048 < in_dim;  // BF16 rows are whole segments (host check)
   return seg * 2048 + lane * 64 < in_dim;
 }
 
@@ -393,98 +287,355 @@ __device__ __forceinline__ float sigmoid_ref(float v) {  // kernels/sigmoid.rs:2
   return __fdiv_rn(z, __fadd_rn(1.0f, z));
 }
 
+// int8 / nibble -> exact float: place the byte under the exponent of 2^23 and
+// subtract the bias (2^23 + 128 for sign-flipped int8, 2^23 + 8 for Q4_0's -8).
+__device__ __forceinline__ float q8f(uint32_t wx, int byte) {  // wx = word ^ 0x80808080
+  return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388736.0f;
+}
+__device__ __forceinline__ float nibf(uint32_t nib4, int byte) {  // nib4 = 4 nibbles in byte lanes
+  return __uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388616.0f;
+}
+
+template <int T>
+constexpr int nwords() {
+  return T == SQ_Q8_0 ? 17 : (T == SQ_Q4_0 ? 9 : 32);
+}
+
+// This lane's weight words of one row: Q8_0 / Q4_0 one 68 / 36-byte block pair
+// (4-byte aligned, conflict-free: odd word stride), BF16 eight 16-byte chunks.
+template <int T>
+__device__ __forceinline__ void lane_load(uint32_t row, int seg, int lane, uint32_t (&w)[nwords<T>()]) {
+  if constexpr (T == SQ_Q8_0) {
+    const uint32_t a = row + (uint32_t)(seg * 32 + lane) * 68u;
+#pragma unroll
+    for (int i = 0; i < 17; i++) w[i] = lds32(a + 4 * i);
+  } else if constexpr (T == SQ_Q4_0) {
+    const uint32_t a = row + (uint32_t)(seg * 32 + lane) * 36u;
+#pragma unroll
+    for (int i = 0; i < 9; i++) w[i] = lds32(a + 4 * i);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const uint4 u = lds128(row + (uint32_t)(seg * 2048 + k * 256 + lane * 8) * 2u);
+      w[4 * k] = u.x;
+      w[4 * k + 1] = u.y;
+      w[4 * k + 2] = u.z;
+      w[4 * k + 3] = u.w;
+    }
+  }
+}
+
+// Dot of the lane's 64 activations with its 64 weights (f32 activations: W8A32 /
+// W4A32 / BF16 — dot_prod.rs:86-96, 255-270, 464-472; per block the products are
+// summed first and scaled once).
+template <int T>
+__device__ __forceinline__ float lane_dot(const uint32_t (&w)[nwords<T>()], const float (&x)[64]) {
+  if constexpr (T == SQ_Q8_0) {
+    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
+    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 32; i++) {  // block 0: bytes 2..33
+      const int byte = 2 + i;
+      a[i & 3] = fmaf(x[i], q8f(w[byte >> 2] ^ 0x80808080u, byte & 3), a[i & 3]);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i++) {  // block 1: bytes 36..67
+      const int byte = 36 + i;
+      b[i & 3] = fmaf(x[32 + i], q8f(w[byte >> 2] ^ 0x80808080u, byte & 3), b[i & 3]);
+    }
+    return fmaf((a[0] + a[1]) + (a[2] + a[3]), s0, ((b[0] + b[1]) + (b[2] + b[3])) * s1);
+  } else if constexpr (T == SQ_Q4_0) {
+    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
+    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[4] >> 16)));
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 16; j++) {  // block 0: quant bytes at 2..17 (element j low nibble, j+16 high)
+      const int byte = 2 + j;
+      const uint32_t word = w[byte >> 2];
+      a[j & 3] = fmaf(x[j], nibf(word & 0x0F0F0F0Fu, byte & 3), a[j & 3]);
+      a[(j + 2) & 3] = fmaf(x[16 + j], nibf((word >> 4) & 0x0F0F0F0Fu, byte & 3), a[(j + 2) & 3]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) {  // block 1: quant bytes at 20..35
+      const int byte = 20 + j;
+      const uint32_t word = w[byte >> 2];
+      b[j & 3] = fmaf(x[32 + j], nibf(word & 0x0F0F0F0Fu, byte & 3), b[j & 3]);
+      b[(j + 2) & 3] = fmaf(x[48 + j], nibf((word >> 4) & 0x0F0F0F0Fu, byte & 3), b[(j + 2) & 3]);
+    }
+    return fmaf((a[0] + a[1]) + (a[2] + a[3]), s0, ((b[0] + b[1]) + (b[2] + b[3])) * s1);
+  } else {
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t u = w[4 * k + j];
+        a[(2 * j) & 3] = fmaf(x[8 * k + 2 * j], __uint_as_float(u << 16), a[(2 * j) & 3]);
+        a[(2 * j + 1) & 3] = fmaf(x[8 * k + 2 * j + 1], __uint_as_float(u & 0xFFFF0000u), a[(2 * j + 1) & 3]);
+      }
+    }
+    return (a[0] + a[1]) + (a[2] + a[3]);
+  }
+}
+
+// Sum two values over the warp with one butterfly: afterwards every lane holds
+// both totals (x = a's, y = b's).
+__device__ __forceinline__ float2 warp_sum2(float a, float b) {
+  const int lane = threadIdx.x & 31;
+  float keep = (lane & 16) ? b : a;
+  const float send = (lane & 16) ? a : b;
+  keep += __shfl_xor_sync(FULL, send, 16);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(FULL, keep, o);
+  return make_float2(__shfl_sync(FULL, keep, 0), __shfl_sync(FULL, keep, 16));
+}
+
 struct Smem {
   float red[2][MAX_TILE_ITEMS];
   float att_m[NC][GROUP], att_l[NC][GROUP];
   float att_a[NC][GROUP][128];
+  float lm[MAX_LM_ROWS];
+  int rel[NSLOT];     // warps done with the tile in each slot
+  int issued[NSLOT];  // copies issued into each slot (for the error-path drain)
+  int ntiles;
   int flag;
 };
+static_assert(sizeof(Smem) % 16 == 0, "the tile table after Smem is a bulk-copy target (16-byte aligned)");
 
-// Process one matvec stage of this CTA: wait for each tile, dot every (row, segment)
-// item this warp owns, then finish rows in the epilogue.
+// Issue tile j of this CTA's table into `slot`: one or more bulk copies completing
+// on full[slot]. Rows of a QKV tile may span Wq / Wk / Wv; a gate/up tile carries
+// its gate rows, then the same rows of Wup.
+__device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
+  const int2 d = tbl[j];
+  const int r = d.x, n = d.y & 0xFFF, kind = (d.y >> 12) & 0xF, l = d.y >> 16;
+  const int rb = stage_rb(p, kind);
+  uint8_t *dst = rg.slots + (size_t)slot * SLOT;
+  uint64_t *bar = &rg.full[slot];
+  const LayerW &W = p.layers[l < p.L ? l : 0];
+  sm.issued[slot]++;
+  if (kind == ST_GU) {
+    mbar_expect_tx(bar, 2u * n * rb);
+    bulk_g2s(dst, W.gate + (size_t)r * rb, n * rb, bar);
+    bulk_g2s(dst + (size_t)n * rb, W.up + (size_t)r * rb, n * rb, bar);
+  } else if (kind == ST_QKV) {
+    mbar_expect_tx(bar, (unsigned)n * rb);
+    int a = r, off = 0;
+    const int bounds[3] = {p.Q, p.Q + p.KVd, p.Q + 2 * p.KVd};
+    const uint8_t *base[3] = {W.q, W.k, W.v};
+    const int start[3] = {0, p.Q, p.Q + p.KVd};
+#pragma unroll
+    for (int t = 0; t < 3; t++) {
+      const int hi = min(r + n, bounds[t]);
+      if (a < hi) {
+        bulk_g2s(dst + (size_t)off * rb, base[t] + (size_t)(a - start[t]) * rb, (hi - a) * rb, bar);
+        off += hi - a;
+        a = hi;
+      }
+    }
+  } else {
+    const uint8_t *src = kind == ST_O ? W.o : (kind == ST_DOWN ? W.down : p.out_w);
+    mbar_expect_tx(bar, (unsigned)n * rb);
+    bulk_g2s(dst, src + (size_t)r * rb, n * rb, bar);
+  }
+}
+
+// A warp is done reading tile `k` in `slot`; the last of the NC warps refills the
+// slot with tile k + NSLOT.
+__device__ __forceinline__ void release_slot(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int slot,
+                                             int k) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    if (atomicAdd(&sm.rel[slot], 1) == NC - 1) {
+      sm.rel[slot] = 0;
+      if (k + NSLOT < sm.ntiles) issue_tile(p, rg, sm, tbl, k + NSLOT, slot);
+    }
+  }
+}
+
+// Per-stage values each warp holds in registers: RoPE cos/sin of the token's
+// position for frequency index lane and lane+32, and hidden[r0 + lane] (the
+// residual of this CTA's rows of the O / down stages).
+struct StageRegs {
+  float c0, c1, s0, s1, hres;
+};
+
+// Finish output row(s) of a stage (warp-uniform arguments; lane 0 stores).
+// rows a / b are absolute rows of the stage's row space; vb is ignored when !hasb.
+template <int KIND>
+__device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, int pos, int r0, int a, float va, int b,
+                                            float vb, bool hasb, const StageRegs &sr) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (KIND == ST_QKV) {  // a even, b = a + 1: RoPE pair (rope.rs:25-31), then q / K / V
+    const int j = (a % p.hd) >> 1;
+    const float c = __shfl_sync(FULL, j < 32 ? sr.c0 : sr.c1, j & 31);
+    const float s = __shfl_sync(FULL, j < 32 ? sr.s0 : sr.s1, j & 31);
+    if (lane == 0) {
+      if (a < p.Q + p.KVd) {
+        const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+        const float rb = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
+        if (a < p.Q) {
+          p.qbuf[a] = ra;
+          p.qbuf[a + 1] = rb;
+        } else {
+          const int kr = a - p.Q, g = kr / p.hd, d = kr % p.hd;
+          float *dst = p.kc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
+          dst[0] = ra;
+          dst[1] = rb;
+        }
+      } else {
+        const int vr = a - p.Q - p.KVd, g = vr / p.hd, d = vr % p.hd;
+        float *dst = p.vc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
+        dst[0] = va;
+        dst[1] = vb;
+      }
+    }
+  } else if constexpr (KIND == ST_O || KIND == ST_DOWN) {  // residual (elementwise_add.rs:47-61)
+    const float ha = __shfl_sync(FULL, sr.hres, (a - r0) & 31);
+    const float hb = __shfl_sync(FULL, sr.hres, (b - r0) & 31);
+    if (lane == 0) {
+      p.hidden[a] = __fadd_rn(ha, va);
+      if (hasb) p.hidden[b] = __fadd_rn(hb, vb);
+    }
+  } else if constexpr (KIND == ST_GU) {  // a = gate row, vb = up (silu.rs:4-8, elementwise_mul.rs:3-17)
+    if (lane == 0) p.act[a] = __fmul_rn(__fmul_rn(va, sigmoid_ref(va)), vb);
+  } else {  // LM head logits
+    if (lane == 0) {
+      p.logits[a] = va;
+      sm.lm[a - r0] = va;
+      if (hasb) {
+        p.logits[b] = vb;
+        sm.lm[b - r0] = vb;
+      }
+    }
+  }
+}
+
+// One matvec stage of this CTA: for each tile of its rows, wait for the slot,
+// dot two rows at a time per warp, finish the rows, release the slot.
 template <int T, int KIND>
-__device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, int l, const float (&x)[64], int &slot,
-                             unsigned &phase, int &tile_ctr, int pos) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+__device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int l,
+                             const float (&x)[64], int &slot, unsigned &phase, int &tile_ctr, int pos,
+                             const StageRegs &sr) {
+  constexpr int NW = nwords<T>();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nseg = stage_nseg(p, KIND), rb = stage_rb(p, KIND), Tr = p.tile_rows[KIND];
   const int in_dim = KIND == ST_O ? p.Q : (KIND == ST_DOWN ? p.F : p.E);
-  const int seg = warp % nseg;
+  const int seg = warp % nseg, rpw = NC / nseg, rs = warp / nseg;
   const bool active = lane_active<T>(seg, lane, in_dim);
+  const uint32_t slots = smem_u32(rg.slots);
   int r0, r1;
   stage_rows(p, KIND, l, blockIdx.x, r0, r1);
-  const LayerW &W = p.layers[l < p.L ? l : 0];
+  const int stage_id = KIND == ST_LM ? 5 * p.L : 5 * l + (KIND == ST_QKV ? 0 : KIND + 1);
+  stamp(p, 6 * stage_id + 2);
   for (int r = r0; r < r1; r += Tr) {
     const int n = min(Tr, r1 - r);
     const int rows = KIND == ST_GU ? 2 * n : n;
-    const uint8_t *tile = rg.slots + (size_t)slot * SLOT;
+    const uint32_t tile = slots + (uint32_t)slot * SLOT;
     float *red = sm.red[tile_ctr & 1];
     const bool ok = mbar_wait(&rg.full[slot], phase, p.err);
+    if (r == r0) stamp(p, 6 * stage_id + 3);
+    if (r + Tr >= r1) stamp(p, 6 * stage_id + 4);
     if (ok) {
-      for (int it = warp; it < rows * nseg; it += NC) {  // it % nseg == seg for every it of this warp
-        const int row = it / nseg;
-        float v = active ? lane_dot<T>(tile + (size_t)row * rb, seg, lane, x) : 0.f;
-        v = warp_sum(v);
-        if (lane == 0) red[it] = v;
+      if (nseg == 1) {
+        // warp-owned row pairs: (2i, 2i+1), or (gate i, up i)
+        const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
+        for (int i = warp; i < npairs; i += NC) {
+          const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
+          const bool hasb = b < rows;
+          float va = 0.f, vb = 0.f;
+          if (active) {
+            uint32_t wa[NW], wb[NW];
+            lane_load<T>(tile + (uint32_t)a * rb, 0, lane, wa);
+            if (hasb) lane_load<T>(tile + (uint32_t)b * rb, 0, lane, wb);
+            va = lane_dot<T>(wa, x);
+            if (hasb) vb = lane_dot<T>(wb, x);
+          }
+          const float2 v = warp_sum2(va, vb);
+          if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, v.x, r + i, v.y, true, sr);
+          else finish_rows<KIND>(p, sm, l, pos, r0, r + a, v.x, r + b, v.y, hasb, sr);
+        }
+      } else {
+        // segment-split rows: partial sums per (row, segment) meet in shared memory
+        for (int i = rs; i < rows; i += 2 * rpw) {
+          const int a = i, b = i + rpw;
+          const bool hasb = b < rows;
+          float va = 0.f, vb = 0.f;
+          if (active) {
+            uint32_t wa[NW], wb[NW];
+            lane_load<T>(tile + (uint32_t)a * rb, seg, lane, wa);
+            if (hasb) lane_load<T>(tile + (uint32_t)b * rb, seg, lane, wb);
+            va = lane_dot<T>(wa, x);
+            if (hasb) vb = lane_dot<T>(wb, x);
+          }
+          const float2 v = warp_sum2(va, vb);
+          if (lane == 0) {
+            red[a * nseg + seg] = v.x;
+            if (hasb) red[b * nseg + seg] = v.y;
+          }
+        }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&rg.empty[slot]);
+    release_slot(p, rg, sm, tbl, slot, tile_ctr);
     if (++slot == NSLOT) {
       slot = 0;
       phase ^= 1u;
     }
     tile_ctr++;
-    consumers_sync();
-    if (!ok) continue;
-    // epilogue
-    if (KIND == ST_QKV) {
-      const int half = p.hd / 2;
-      for (int t = tid; t < n / 2; t += NC * 32) {
-        const int row = r + 2 * t;  // even row of the pair, in [Wq; Wk; Wv] row space
-        float a = 0.f, b = 0.f;
-        for (int s = 0; s < nseg; s++) {
-          a += red[(2 * t) * nseg + s];
-          b += red[(2 * t + 1) * nseg + s];
-        }
-        if (row < p.Q + p.KVd) {  // q or k: RoPE from the host-computed table (rope.rs:25-31)
-          const int j = (row % p.hd) / 2;
-          const float c = p.cos_t[(size_t)pos * half + j], s = p.sin_t[(size_t)pos * half + j];
-          const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-          const float rbv = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
-          if (row < p.Q) {
-            p.qbuf[row] = ra;
-            p.qbuf[row + 1] = rbv;
-          } else {
-            const int kr = row - p.Q, g = kr / p.hd, d = kr % p.hd;
-            float *dst = p.kc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
-            dst[0] = ra;
-            dst[1] = rbv;
+    if (nseg > 1) {
+      cta_sync();
+      if (ok && warp == 0) {
+        const int units = KIND == ST_QKV ? n / 2 : n;
+        for (int t0 = 0; t0 < units; t0 += 32) {
+          const int t = min(t0 + lane, units - 1);  // every lane joins the shuffles
+          float va = 0.f, vb = 0.f;
+          const int a = KIND == ST_QKV ? 2 * t : t, b = KIND == ST_QKV ? 2 * t + 1 : (KIND == ST_GU ? n + t : t);
+          for (int s = 0; s < nseg; s++) {
+            va += red[a * nseg + s];
+            vb += red[b * nseg + s];
           }
-        } else {
-          const int vr = row - p.Q - p.KVd, g = vr / p.hd, d = vr % p.hd;
-          float *dst = p.vc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
-          dst[0] = a;
-          dst[1] = b;
-        }
-      }
-    } else {
-      for (int t = tid; t < n; t += NC * 32) {
-        float v = 0.f;
-        for (int s = 0; s < nseg; s++) v += red[t * nseg + s];
-        const int row = r + t;
-        if (KIND == ST_O || KIND == ST_DOWN) {
-          p.hidden[row] = __fadd_rn(__ldcg(p.hidden + row), v);  // residual (elementwise_add.rs:47-61)
-        } else if (KIND == ST_GU) {
-          float u = 0.f;
-          for (int s = 0; s < nseg; s++) u += red[(n + t) * nseg + s];
-          p.act[row] = __fmul_rn(__fmul_rn(v, sigmoid_ref(v)), u);  // silu(gate) * up
-        } else {
-          p.logits[row] = v;
+          const bool mine = t0 + lane < units;
+          if (KIND == ST_QKV) {
+            const int row = r + a;
+            const int j = (row % p.hd) >> 1;
+            const float c0 = __shfl_sync(FULL, sr.c0, j & 31), c1 = __shfl_sync(FULL, sr.c1, j & 31);
+            const float s0 = __shfl_sync(FULL, sr.s0, j & 31), s1 = __shfl_sync(FULL, sr.s1, j & 31);
+            const float c = j < 32 ? c0 : c1, s = j < 32 ? s0 : s1;
+            if (mine) {
+              if (row < p.Q + p.KVd) {
+                const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+                const float rbv = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
+                if (row < p.Q) {
+                  p.qbuf[row] = ra;
+                  p.qbuf[row + 1] = rbv;
+                } else {
+                  const int kr = row - p.Q, g = kr / p.hd, d = kr % p.hd;
+                  float *dst = p.kc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
+                  dst[0] = ra;
+                  dst[1] = rbv;
+                }
+              } else {
+                const int vr = row - p.Q - p.KVd, g = vr / p.hd, d = vr % p.hd;
+                float *dst = p.vc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
+                dst[0] = va;
+                dst[1] = vb;
+              }
+            }
+          } else if (KIND == ST_O || KIND == ST_DOWN) {
+            const float h = __shfl_sync(FULL, sr.hres, (r + t - r0) & 31);
+            if (mine) p.hidden[r + t] = __fadd_rn(h, va);
+          } else if (KIND == ST_GU) {
+            if (mine) p.act[r + t] = __fmul_rn(__fmul_rn(va, sigmoid_ref(va)), vb);
+          } else {
+            if (mine) {
+              p.logits[r + t] = va;
+              sm.lm[r + t - r0] = va;
+            }
+          }
         }
       }
     }
   }
-  (void)W;
 }
 
 // Causal GQA attention for one token at position pos (attention.rs:11-70): split-KV
@@ -547,7 +698,7 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
 #pragma unroll
       for (int i = 0; i < DPL; i++) sm.att_a[warp][h][lane + 32 * i] = acc[h][i];
     }
-    consumers_sync();
+    cta_sync();
     if (warp < GROUP) {  // merge the warps' states of head `warp` into this chunk's partial
       const int h = warp;
       float M = -INFINITY;
@@ -570,12 +721,12 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
       for (int i = 0; i < DPL; i++) pp[2 + lane + 32 * i] = A[i];
       __threadfence();
     }
-    consumers_sync();
+    cta_sync();
     if (threadIdx.x == 0) {
       const unsigned old = atomicAdd(p.attn_cnt + g, 1u);
       sm.flag = old == (unsigned)(n_chunks - 1);
     }
-    consumers_sync();
+    cta_sync();
     if (sm.flag) {
       __threadfence();
       if (warp < GROUP) {  // combine all chunks of head g*GROUP+warp
@@ -604,49 +755,42 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
       }
       if (threadIdx.x == 0) p.attn_cnt[g] = 0;
     }
-    consumers_sync();
+    cta_sync();
   }
 }
 
-// Ordered greedy fold over a contiguous range by one warp (lanes take contiguous
-// sub-ranges, combined left to right).
-__device__ ArgState warp_argmax(const float *v, long long lo, long long hi, bool from_l2) {
-  const int lane = threadIdx.x & 31;
-  const long long n = hi - lo, per = (n + 31) / 32;
-  ArgState s = arg_empty();
-  for (long long i = lo + lane * per; i < lo + (lane + 1) * per && i < hi; i++)
-    s = arg_combine(s, arg_elem(from_l2 ? __ldcg(v + i) : v[i], i));
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    ArgState r;
-    r.v = __shfl_down_sync(0xffffffffu, s.v, o);
-    r.best = __shfl_down_sync(0xffffffffu, s.best, o);
-    r.nan = __shfl_down_sync(0xffffffffu, s.nan, o);
-    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) s = arg_combine(s, r);
-  }
-  return s;  // valid in lane 0
-}
-
-__device__ ArgState warp_argmax_states(const ArgState *st, int n) {
+// Ordered greedy fold (greedy.rs:6-15) over n values in shared memory by one warp:
+// lanes take contiguous sub-ranges, combined left to right. Valid in lane 0.
+__device__ ArgState warp_argmax_smem(const float *v, int n, long long base) {
   const int lane = threadIdx.x & 31;
   const int per = (n + 31) / 32;
   ArgState s = arg_empty();
-  for (int i = lane * per; i < (lane + 1) * per && i < n; i++) {
-    ArgState x;
-    x.v = __ldcg(&st[i].v);
-    x.best = __ldcg(&st[i].best);
-    x.nan = __ldcg(&st[i].nan);
-    s = arg_combine(s, x);
-  }
+  for (int i = lane * per; i < (lane + 1) * per && i < n; i++) s = arg_combine(s, arg_elem(v[i], base + i));
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     ArgState r;
-    r.v = __shfl_down_sync(0xffffffffu, s.v, o);
-    r.best = __shfl_down_sync(0xffffffffu, s.best, o);
-    r.nan = __shfl_down_sync(0xffffffffu, s.nan, o);
-    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) s = arg_combine(s, r);
+    r.v = __shfl_down_sync(FULL, s.v, o);
+    r.best = __shfl_down_sync(FULL, s.best, o);
+    r.nan = __shfl_down_sync(FULL, s.nan, o);
+    if ((lane & (2 * o - 1)) == 0) s = arg_combine(s, r);
   }
   return s;
+}
+
+__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr) {
+  const int lane = threadIdx.x & 31;
+  if (kind == ST_QKV) {
+    const int half = p.hd >> 1;
+    const size_t base = (size_t)pos * half;
+    sr.c0 = lane < half ? __ldg(p.cos_t + base + lane) : 0.f;
+    sr.s0 = lane < half ? __ldg(p.sin_t + base + lane) : 0.f;
+    sr.c1 = lane + 32 < half ? __ldg(p.cos_t + base + 32 + lane) : 0.f;
+    sr.s1 = lane + 32 < half ? __ldg(p.sin_t + base + 32 + lane) : 0.f;
+  } else if (kind == ST_O || kind == ST_DOWN) {
+    int r0, r1;
+    stage_rows(p, kind, l, blockIdx.x, r0, r1);
+    sr.hres = lane < r1 - r0 ? __ldcg(p.hidden + r0 + lane) : 0.f;
+  }
 }
 
 template <int T, int DPL>
@@ -658,30 +802,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   Ring rg;
   rg.slots = dsm;
   rg.full = reinterpret_cast<uint64_t *>(dsm + (size_t)NSLOT * SLOT);
-  rg.empty = rg.full + NSLOT;
-  Smem &sm = *reinterpret_cast<Smem *>(rg.empty + NSLOT);
+  uint64_t *tbl_bar = rg.full + NSLOT;
+  Smem &sm = *reinterpret_cast<Smem *>(tbl_bar + 1);  // 16-byte aligned: 5 + 1 barriers of 8 bytes
+  int2 *tbl = reinterpret_cast<int2 *>(&sm + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  stamp(p, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; s++) {
       mbar_init(&rg.full[s], 1);
-      mbar_init(&rg.empty[s], NC);
+      sm.rel[s] = 0;
+      sm.issued[s] = 0;
     }
+    mbar_init(tbl_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // this CTA's tile table (8 bytes a tile, padded to 16) into shared memory, then the first NSLOT tiles
+    const int nt = p.ntiles[blockIdx.x];
+    sm.ntiles = nt;
+    const unsigned tb = (unsigned)((nt * 8 + 15) & ~15);
+    mbar_expect_tx(tbl_bar, tb);
+    bulk_g2s(tbl, p.tiles + (size_t)blockIdx.x * p.max_tiles, tb, tbl_bar);
+    if (mbar_wait(tbl_bar, 0, p.err))
+      for (int j = 0; j < NSLOT && j < nt; j++) issue_tile(p, rg, sm, tbl, j, j);
   }
   __syncthreads();
-  if (warp == NC) {  // producer warp: one lane issues everything
-    if (lane == 0) producer(p, rg);
-    return;
-  }
   const int pos = *p.pos;
   const uint32_t tok = *tok_in;
   int slot = 0, tile_ctr = 0;
   unsigned phase = 0, bar_target = 0;
   float x[64];
+  StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
   for (int l = 0; l < p.L; l++) {
     const LayerW &W = p.layers[l];
     // ---- RMSNorm + QKV + RoPE + KV append
     const int segE = warp % p.nseg_E;
+    load_stage_regs(p, ST_QKV, l, pos, sr);
     if (l == 0) {
       // embed (ops/embedding.rs:10-52) straight into registers; CTA 0 also writes hidden
       const uint8_t *row = p.embd + (size_t)tok * (p.E / QK) * type_bytes<T>();
@@ -703,7 +857,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else {
       load_x_norm<T>(x, p.hidden, W.attn_norm, segE, lane, p.E, p.eps);
     }
-    matvec_stage<T, ST_QKV>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
     // ---- attention
@@ -711,65 +865,66 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bar_target += p.G;
     grid_barrier(p, bar_target);
     // ---- O projection + residual
+    load_stage_regs(p, ST_O, l, pos, sr);
     load_x<T>(x, p.attn_out, warp % p.nseg_Q, lane, p.Q);
-    matvec_stage<T, ST_O>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
     // ---- RMSNorm + gate/up + SiLU*up
     load_x_norm<T>(x, p.hidden, W.ffn_norm, segE, lane, p.E, p.eps);
-    matvec_stage<T, ST_GU>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
     // ---- down + residual
+    load_stage_regs(p, ST_DOWN, l, pos, sr);
     load_x<T>(x, p.act, warp % p.nseg_F, lane, p.F);
-    matvec_stage<T, ST_DOWN>(p, rg, sm, l, x, slot, phase, tile_ctr, pos);
+    matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
   }
   // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
   load_x_norm<T>(x, p.hidden, p.out_norm, warp % p.nseg_E, lane, p.E, p.eps);
-  matvec_stage<T, ST_LM>(p, rg, sm, p.L, x, slot, phase, tile_ctr, pos);
-  consumers_sync();
-  // ---- greedy argmax: this CTA's rows in order, then the last CTA folds all CTAs
+  matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr);
+  cta_sync();
+  stamp(p, p.tl_stride - 2);
+  // ---- greedy argmax: this CTA's rows (kept in shared memory) in order, then the
+  // last CTA to finish folds the per-CTA states in row order
   if (warp == 0) {
     int r0, r1;
     stage_rows(p, ST_LM, p.L, blockIdx.x, r0, r1);
-    const ArgState s = warp_argmax(p.logits, r0, r1, true);
+    const ArgState s = warp_argmax_smem(sm.lm, r1 - r0, r0);
     unsigned last = 0;
     if (lane == 0) {
       p.arg_part[blockIdx.x] = s;
       __threadfence();
       last = atomicAdd(p.ticket, 1u) == (unsigned)(p.G - 1);
     }
-    last = __shfl_sync(0xffffffffu, last, 0);
+    last = __shfl_sync(FULL, last, 0);
     if (last) {
       __threadfence();
-      // stage_rows rotates ownership, so fold the CTAs in row order
-      const ArgState f = [&]() {
-        ArgState acc = arg_empty();
-        for (int base = 0; base < p.G; base += 32) {
-          ArgState mine = arg_empty();
-          const int i = base + lane;
-          if (i < p.G) {
-            const int owner = ((i - (p.L * 5 + ST_LM) * 61) % p.G + p.G) % p.G;  // CTA whose rotated index is i
-            mine.v = __ldcg(&p.arg_part[owner].v);
-            mine.best = __ldcg(&p.arg_part[owner].best);
-            mine.nan = __ldcg(&p.arg_part[owner].nan);
-          }
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            ArgState r;
-            r.v = __shfl_down_sync(0xffffffffu, mine.v, o);
-            r.best = __shfl_down_sync(0xffffffffu, mine.best, o);
-            r.nan = __shfl_down_sync(0xffffffffu, mine.nan, o);
-            if ((lane & (2 * o - 1)) == 0 && lane + o < 32) mine = arg_combine(mine, r);
-          }
-          if (lane == 0) acc = arg_combine(acc, mine);
+      ArgState acc = arg_empty();
+      const int stage = p.L * 5 + ST_LM;
+      for (int base = 0; base < p.G; base += 32) {
+        ArgState mine = arg_empty();
+        const int i = base + lane;  // rotated index i owns the i-th row range
+        if (i < p.G) {
+          const int owner = ((i - stage * 61) % p.G + p.G) % p.G;
+          mine.v = __ldcg(&p.arg_part[owner].v);
+          mine.best = __ldcg(&p.arg_part[owner].best);
+          mine.nan = __ldcg(&p.arg_part[owner].nan);
         }
-        return acc;
-      }();
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          ArgState r;
+          r.v = __shfl_down_sync(FULL, mine.v, o);
+          r.best = __shfl_down_sync(FULL, mine.best, o);
+          r.nan = __shfl_down_sync(FULL, mine.nan, o);
+          if ((lane & (2 * o - 1)) == 0) mine = arg_combine(mine, r);
+        }
+        if (lane == 0) acc = arg_combine(acc, mine);
+      }
       if (lane == 0) {
-        const long long id = arg_result(f);
+        const long long id = arg_result(acc);
         *p.argmax = id;
         *tok_out = (uint32_t)id;
         if (out_ids) out_ids[step] = (uint32_t)id;
@@ -779,6 +934,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
   }
+  // after a failed wait, let every copy this CTA issued land before the CTA exits
+  if (threadIdx.x == 0 && ld_volatile(p.err)) {
+    for (int s = 0; s < NSLOT; s++) {
+      if (!sm.issued[s]) continue;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&rg.full[s], (unsigned)(sm.issued[s] - 1) & 1u) && clock64() - t0 < WAIT_LIMIT) {
+      }
+    }
+  }
+  stamp(p, p.tl_stride - 1);
+}
+
+// Per-CTA tile tables, built once per context with the same row split the kernel
+// uses: the tiles of every stage of every layer in consumption order.
+__global__ void k_build_tiles(const Params *__restrict__ pp, int2 *tiles, int *ntiles, int max_tiles) {
+  const Params &p = *pp;
+  if (threadIdx.x != 0) return;
+  const int cta = blockIdx.x;
+  int nt = 0;
+  for (int l = 0; l <= p.L; l++) {
+    const int lo = l < p.L ? ST_QKV : ST_LM, hi = l < p.L ? ST_DOWN : ST_LM;
+    for (int kind = lo; kind <= hi; kind++) {
+      int r0, r1;
+      stage_rows(p, kind, l, cta, r0, r1);
+      for (int r = r0; r < r1; r += p.tile_rows[kind]) {
+        const int n = min(p.tile_rows[kind], r1 - r);
+        if (nt < max_tiles) tiles[(size_t)cta * max_tiles + nt] = make_int2(r, (l << 16) | (kind << 12) | n);
+        nt++;
+      }
+    }
+  }
+  ntiles[cta] = nt;
 }
 
 }  // namespace dk
@@ -793,8 +980,12 @@ struct DecodeState {
   void *kernel = nullptr;
   size_t smem = 0;
   int grid = 0;
-  unsigned *d_err = nullptr;
+  unsigned *d_err = nullptr, *d_bar = nullptr, *d_ticket = nullptr, *d_attn_cnt = nullptr;
   int *d_pos = nullptr;
+  int n_kv_heads = 0;
+  unsigned long long *d_timeline = nullptr;  // SQ_DECODE_TIMELINE=<file>: stage stamps of the last launch
+  int tl_stride = 0;
+  std::string tl_path;
   std::vector<void *> allocs;
 };
 
@@ -844,18 +1035,15 @@ int decode_prepare(sq_ctx *c) {
     const int nseg = k == dk::ST_O ? nQ : (k == dk::ST_DOWN ? nF : nE);
     ok = ok && h.tile_rows[k] >= 2 && h.tile_rows[k] * (k == dk::ST_GU ? 2 : 1) * nseg <= dk::MAX_TILE_ITEMS;
   }
-  if (!ok) return SQ_OK;  // the op-level path serves this model
   int dev = m->device, nsm = 0;
   SQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  // residual rows per CTA live in one register per lane; LM rows per CTA in shared memory
+  ok = ok && (E + nsm - 1) / nsm <= 32 && (cf.vocab_size + nsm - 1) / nsm <= dk::MAX_LM_ROWS;
+  if (!ok) return SQ_OK;  // the op-level path serves this model
   void *kern = nullptr;
   if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
   else if (wt == SQ_Q4_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q4_0, 2>() : pick_kernel<SQ_Q4_0, 4>();
   else kern = cf.head_dim == 64 ? pick_kernel<SQ_BF16, 2>() : pick_kernel<SQ_BF16, 4>();
-  const size_t smem = (size_t)dk::NSLOT * dk::SLOT + 2 * dk::NSLOT * sizeof(uint64_t) + sizeof(dk::Smem);
-  SQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  int per_sm = 0;
-  SQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, dk::NTHREADS, smem));
-  if (per_sm < 1) return SQ_OK;
   h.L = cf.n_blocks;
   h.E = E;
   h.Q = Q;
@@ -911,8 +1099,40 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(alloc((void **)&h.arg_part, (size_t)nsm * sizeof(ArgState)));
   SQ_CUDA(alloc((void **)&h.pos, 4));
   SQ_CUDA(alloc((void **)&st->d_params, sizeof(dk::Params)));
+  if (const char *tl = getenv("SQ_DECODE_TIMELINE")) {  // opt-in stage timestamps
+    st->tl_path = tl;
+    st->tl_stride = 6 * (5 * cf.n_blocks + 1) + 4;
+    SQ_CUDA(alloc((void **)&st->d_timeline, (size_t)nsm * st->tl_stride * 8));
+    h.timeline = st->d_timeline;
+    h.tl_stride = st->tl_stride;
+  }
+  // tile tables: count pass, then fill (same row split as the kernel)
+  SQ_CUDA(alloc((void **)&h.ntiles, (size_t)nsm * sizeof(int)));
   SQ_CUDA(cudaMemcpy(st->d_params, &h, sizeof(dk::Params), cudaMemcpyHostToDevice));
+  dk::k_build_tiles<<<nsm, 32>>>(st->d_params, nullptr, h.ntiles, 0);
+  SQ_CHECK_LAUNCH("build tiles");
+  std::vector<int> counts(nsm);
+  SQ_CUDA(cudaMemcpy(counts.data(), h.ntiles, nsm * sizeof(int), cudaMemcpyDeviceToHost));
+  h.max_tiles = (*std::max_element(counts.begin(), counts.end()) + 1) & ~1;
+  SQ_CUDA(alloc((void **)&h.tiles, (size_t)nsm * h.max_tiles * sizeof(int2)));
+  SQ_CUDA(cudaMemcpy(st->d_params, &h, sizeof(dk::Params), cudaMemcpyHostToDevice));
+  dk::k_build_tiles<<<nsm, 32>>>(st->d_params, h.tiles, h.ntiles, h.max_tiles);
+  SQ_CHECK_LAUNCH("build tiles");
+  SQ_CUDA(cudaDeviceSynchronize());
+  const size_t smem = (size_t)dk::NSLOT * dk::SLOT + (dk::NSLOT + 1) * sizeof(uint64_t) + sizeof(dk::Smem) +
+                      (size_t)h.max_tiles * sizeof(int2);
+  int smem_max = 0;
+  SQ_CUDA(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (smem > (size_t)smem_max) return SQ_OK;  // tile table too long: the op-level path serves this model
+  SQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  SQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, dk::NTHREADS, smem));
+  if (per_sm < 1) return SQ_OK;
   st->d_err = h.err;
+  st->d_bar = h.bar;
+  st->d_ticket = h.ticket;
+  st->d_attn_cnt = h.attn_cnt;
+  st->n_kv_heads = cf.n_kv_heads;
   st->d_pos = h.pos;
   st->kernel = kern;
   st->smem = smem;
@@ -956,10 +1176,22 @@ int decode_check(sq_ctx *c) {
   if (!st || !st->available) return SQ_OK;
   unsigned err = 0;
   SQ_CUDA(cudaMemcpy(&err, st->d_err, 4, cudaMemcpyDeviceToHost));
+  if (st->d_timeline) {
+    std::vector<unsigned long long> tl((size_t)st->grid * st->tl_stride);
+    SQ_CUDA(cudaMemcpy(tl.data(), st->d_timeline, tl.size() * 8, cudaMemcpyDeviceToHost));
+    if (FILE *f = fopen(st->tl_path.c_str(), "wb")) {
+      const int hdr[2] = {st->grid, st->tl_stride};
+      fwrite(hdr, sizeof hdr, 1, f);
+      fwrite(tl.data(), 8, tl.size(), f);
+      fclose(f);
+    }
+  }
   if (err) {
     // reset the kernel's flag and counters so the context stays usable
     cudaMemset(st->d_err, 0, 4);
-    for (void *p : st->allocs) (void)p;
+    cudaMemset(st->d_bar, 0, 4);
+    cudaMemset(st->d_ticket, 0, 4);
+    cudaMemset(st->d_attn_cnt, 0, (size_t)st->n_kv_heads * 4);
     st->dev_pos = -1;  // force a position resync
     return fail(SQ_ERR_TIMEOUT, "decode kernel: a bounded wait expired (code " + std::to_string(err) + ")");
   }

@@ -484,6 +484,25 @@ using namespace sq;
 
 static inline bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+// Stream-ordered scratch for the op-level calls. The device's default memory pool
+// is told to keep freed memory, so repeated calls reuse it instead of returning
+// it to the driver at every synchronization.
+static cudaError_t scratch_alloc(void **p, size_t bytes, cudaStream_t s) {
+  static bool pool_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && !pool_set[dev]) {
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pool_set[dev] = true;
+  }
+  return cudaMallocAsync(p, bytes, s);
+}
+
 extern "C" const char *sq_last_error(void) { return g_last_error.c_str(); }
 extern "C" const char *sq_version(void) { return "squirrel-b200 0.1 (sm_100a)"; }
 
@@ -505,7 +524,7 @@ extern "C" int sq_linear(void *stream, const float *input, int m, int in_dim, co
   cudaStream_t s = (cudaStream_t)stream;
   void *xq = nullptr;
   const bool q8 = acts == SQ_ACTS_Q8 && wtype != SQ_BF16;
-  if (q8) SQ_CUDA(cudaMallocAsync(&xq, (size_t)m * (in_dim / QK) * Q8_BYTES, s));
+  if (q8) SQ_CUDA(scratch_alloc(&xq, (size_t)m * (in_dim / QK) * Q8_BYTES, s));
   cudaError_t e = launch_linear(s, input, m, in_dim, weight, wtype, out_dim, output, q8, xq);
   if (xq) cudaFreeAsync(xq, s);
   if (e != cudaSuccess) return cuda_fail(e, "sq_linear");
@@ -619,7 +638,7 @@ extern "C" int sq_argmax(void *stream, const float *logits, size_t n, int64_t *o
   if (!n) return fail(SQ_ERR_EMPTY, "argmax: empty logits");
   cudaStream_t s = (cudaStream_t)stream;
   void *part = nullptr;
-  SQ_CUDA(cudaMallocAsync(&part, (size_t)argmax_partials(n) * sizeof(ArgState), s));
+  SQ_CUDA(scratch_alloc(&part, (size_t)argmax_partials(n) * sizeof(ArgState), s));
   cudaError_t e = launch_argmax(s, logits, n, part, (long long *)out_index);
   cudaFreeAsync(part, s);
   return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_argmax");
@@ -635,7 +654,7 @@ extern "C" int sq_sdpa_cached(void *stream, const float *q, const float *k, cons
   cudaStream_t s = (cudaStream_t)stream;
   const int ns = sdpa_num_splits(seq_q, seq_k, n_heads);
   float *part = nullptr;
-  if (ns > 1) SQ_CUDA(cudaMallocAsync((void **)&part, sdpa_partials_floats(seq_q, n_heads, head_dim, ns) * 4, s));
+  if (ns > 1) SQ_CUDA(scratch_alloc((void **)&part, sdpa_partials_floats(seq_q, n_heads, head_dim, ns) * 4, s));
   cudaError_t e = launch_sdpa(s, q, k, v, out, seq_q, seq_k, n_heads, n_kv_heads, head_dim,
                               (long long)n_kv_heads * head_dim, head_dim, ns, part);
   if (part) cudaFreeAsync(part, s);

@@ -415,6 +415,7 @@ sq_ctx::~sq_ctx() {
   cudaSetDevice(m->device);
   if (stream) cudaStreamSynchronize(stream);
   decode_release(this);
+  cudaFree(d_out_ids);
   for (void *p : allocs) cudaFree(p);
   if (stream) cudaStreamDestroy(stream);
   cudaSetDevice(prev);
@@ -497,6 +498,20 @@ extern "C" int sq_ctx_seq_len(const sq_ctx *c, int *out) {
 }
 
 extern "C" void *sq_ctx_stream(sq_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+extern "C" int sq_ctx_launches_per_token(const sq_ctx *c, int *out) {
+  if (!c || !out) return fail(SQ_ERR_ARG, "launches_per_token: null pointer");
+  if (decode_available(c)) {
+    *out = 1;
+    return SQ_OK;
+  }
+  // the op-level sequence of forward_rows for one row, plus the token feedback kernel
+  const sq_llama_config &cf = c->m->cfg;
+  const int aq = c->m->acts == SQ_ACTS_Q8 && cf.weight_type != SQ_BF16;
+  const int split = sdpa_num_splits(1, c->seq_len + 1, cf.n_heads) > 1;
+  *out = 1 + cf.n_blocks * (16 + 2 * aq + split) + 4 + 1;
+  return SQ_OK;
+}
 
 namespace sq {
 
@@ -637,8 +652,15 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
   if (c->seq_len == 0) return fail(SQ_ERR_EMPTY, "decode_steps: context holds no position yet");
   if ((size_t)c->seq_len + n_steps > (size_t)c->max_ctx) return fail(SQ_ERR_CAPACITY, "decode_steps: KV cache full");
   SQ_CUDA(cudaSetDevice(c->m->device));
-  uint32_t *d_out = nullptr;
-  SQ_CUDA(cudaMallocAsync((void **)&d_out, n_steps * sizeof(uint32_t), c->stream));
+  if (n_steps > c->out_cap) {  // grow the context's id buffer (kept across calls)
+    SQ_CUDA(cudaStreamSynchronize(c->stream));
+    cudaFree(c->d_out_ids);
+    c->d_out_ids = nullptr;
+    c->out_cap = 0;
+    SQ_CUDA(cudaMalloc((void **)&c->d_out_ids, (size_t)n_steps * sizeof(uint32_t)));
+    c->out_cap = n_steps;
+  }
+  uint32_t *d_out = c->d_out_ids;
   // the previous forward's argmax is the first input
   cudaError_t e = launch_feedback(c->stream, c->d_argmax, c->d_tokens, nullptr, 0);
   int st = e == cudaSuccess ? SQ_OK : cuda_fail(e, "decode_steps");
@@ -655,7 +677,6 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
     cudaError_t e2 = cudaMemcpyAsync(out_ids, d_out, n_steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream);
     if (e2 != cudaSuccess) st = cuda_fail(e2, "decode_steps copy");
   }
-  cudaFreeAsync(d_out, c->stream);
   cudaError_t e3 = cudaStreamSynchronize(c->stream);
   if (!st && e3 != cudaSuccess) st = cuda_fail(e3, "decode_steps sync");
   if (!st) st = decode_check(c);

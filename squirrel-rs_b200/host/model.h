@@ -61,6 +61,8 @@ struct sq_ctx {
   uint32_t *d_tokens = nullptr;
   float *d_cos = nullptr, *d_sin = nullptr;  // RoPE table [max_ctx][head_dim/2]
   sq::DecodeState *dec = nullptr;
+  uint32_t *d_out_ids = nullptr;  // ids of sq_decode_steps
+  int out_cap = 0;
   std::vector<void *> allocs;
   ~sq_ctx();
 };

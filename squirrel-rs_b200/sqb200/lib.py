@@ -78,6 +78,7 @@ SIGNATURES = {
                          C.POINTER(_i)]),
     "sq_decode_steps": (_i, [_vp, _i, C.POINTER(C.c_uint32)]),
     "sq_ctx_stream": (_vp, [_vp]),
+    "sq_ctx_launches_per_token": (_i, [_vp, C.POINTER(_i)]),
 }
 
 
@@ -285,6 +286,12 @@ class Context:
     @property
     def stream(self):
         return load().sq_ctx_stream(self._h)
+
+    @property
+    def launches_per_token(self):
+        v = C.c_int()
+        _check(load().sq_ctx_launches_per_token(self._h, C.byref(v)))
+        return v.value
 
     def forward(self, ids):
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
