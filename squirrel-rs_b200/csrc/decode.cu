@@ -43,7 +43,8 @@ constexpr int NTHREADS = NC * 32;
 constexpr int SLOT = 36864;              // bytes per ring slot
 constexpr int NSLOT = 5;
 constexpr int MAX_LAYERS = 128;
-constexpr int MAX_TILE_ITEMS = 512;      // rows x segments per tile
+constexpr int MAX_TILE_ITEMS = 256;      // rows x segments per tile
+constexpr int MAX_X = 8192;              // longest stage input staged in shared memory (floats)
 constexpr int MAX_LM_ROWS = 1024;        // LM-head rows per CTA kept in shared memory
 constexpr int GROUP = 4;                 // q heads per kv head supported here
 constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
@@ -107,14 +108,16 @@ __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, unsigned *err) {
   if (mbar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(b, parity)) {
-    if (ld_volatile(err)) return false;
-    if (clock64() - t0 > WAIT_LIMIT) {
-      atomicExch(err, 1u);
-      return false;
+  for (unsigned it = 1;; it++) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((it & 63u) == 0) {  // the global error flag and the clock only now and then
+      if (ld_volatile(err)) return false;
+      if (clock64() - t0 > WAIT_LIMIT) {
+        atomicExch(err, 1u);
+        return false;
+      }
     }
   }
-  return true;
 }
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
   asm volatile(
@@ -150,8 +153,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 // Timeline slot k of this CTA: 0 = start; for stage s (5 per layer, the LM head is
-// stage 5L) 6s+2 = activations loaded, 6s+3 / 6s+4 = first / last tile landed,
-// 6s+5 / 6s+6 = grid-barrier arrive / leave; stride-2 = LM head done, stride-1 = end.
+// stage 5L) 8s+1 = per-stage registers loaded, 8s+2 = squared sum of the norm done,
+// 8s+3 = activations loaded, 8s+4 / 8s+5 = first / last tile landed, 8s+6 / 8s+7 =
+// grid-barrier arrive / leave; stride-2 = LM head done, stride-1 = end.
 __device__ __forceinline__ void stamp(const Params &p, int k) {
   if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = global_ns();
 }
@@ -163,7 +167,7 @@ __device__ void grid_barrier(const Params &p, unsigned target) {
   cta_sync();
   if (threadIdx.x == 0) {
     const int b = (int)(target / p.G) - 1;
-    stamp(p, 6 * b + 5);
+    stamp(p, 8 * b + 6);
     red_release_add(p.bar, 1u);
     const long long t0 = clock64();
     unsigned it = 0;
@@ -176,7 +180,7 @@ __device__ void grid_barrier(const Params &p, unsigned target) {
         }
       }
     }
-    stamp(p, 6 * b + 6);
+    stamp(p, 8 * b + 7);
   }
   cta_sync();
 }
@@ -243,42 +247,17 @@ __device__ __forceinline__ bool lane_active(int seg, int lane, int in_dim) {
 
 // Load this lane's activations of segment seg from a global vector written in this
 // kernel (L2 reads: other SMs wrote it).
-template <int T>
-__device__ __forceinline__ void load_x(float (&x)[64], const float *v, int seg, int lane, int in_dim) {
-  if (!lane_active<T>(seg, lane, in_dim)) {
-#pragma unroll
-    for (int i = 0; i < 64; i++) x[i] = 0.f;
-    return;
-  }
-#pragma unroll
-  for (int i = 0; i < 64; i += 4) {
-    const float4 f = __ldcg(reinterpret_cast<const float4 *>(v + xelem<T>(seg, lane, i)));
-    x[i] = f.x;
-    x[i + 1] = f.y;
-    x[i + 2] = f.z;
-    x[i + 3] = f.w;
-  }
+// 16-byte global loads issued as written (volatile asm keeps them ahead of their
+// uses, so a lane's whole vector is one round trip, not sixteen).
+__device__ __forceinline__ float4 ldcg4(const float *p) {  // data other SMs wrote in this kernel: L2
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
 }
-
-// x = rms_norm(h) restricted to this lane's elements (rms_norm.rs:40-56): the
-// squared sum covers all E elements of h; y = (h*w)/rms per element.
-template <int T>
-__device__ __forceinline__ void load_x_norm(float (&x)[64], const float *h, const float *w, int seg, int lane,
-                                            int E, float eps) {
-  float ss = 0.f;
-  for (int e = lane * 4; e < E; e += 128) {
-    const float4 f = __ldcg(reinterpret_cast<const float4 *>(h + e));
-    ss = fmaf(f.x, f.x, ss);
-    ss = fmaf(f.y, f.y, ss);
-    ss = fmaf(f.z, f.z, ss);
-    ss = fmaf(f.w, f.w, ss);
-  }
-  ss = warp_sum(ss);
-  const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), eps));
-  load_x<T>(x, h, seg, lane, E);
-  if (!lane_active<T>(seg, lane, E)) return;
-#pragma unroll
-  for (int i = 0; i < 64; i++) x[i] = __fdiv_rn(__fmul_rn(x[i], __ldg(w + xelem<T>(seg, lane, i))), rms);
+__device__ __forceinline__ float4 ldnc4(const float *p) {  // constant data (norm weights)
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
 }
 
 __device__ __forceinline__ float sigmoid_ref(float v) {  // kernels/sigmoid.rs:2-9
@@ -391,10 +370,24 @@ __device__ __forceinline__ float2 warp_sum2(float a, float b) {
   return make_float2(__shfl_sync(FULL, keep, 0), __shfl_sync(FULL, keep, 16));
 }
 
+__device__ __forceinline__ uint32_t ldnc32(const uint8_t *p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+struct AttScratch {
+  float m[NC][GROUP], l[NC][GROUP];
+  float a[NC][GROUP][128];
+};
+
 struct Smem {
   float red[2][MAX_TILE_ITEMS];
-  float att_m[NC][GROUP], att_l[NC][GROUP];
-  float att_a[NC][GROUP][128];
+  union {
+    float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index)
+    AttScratch at;    // attention-stage partials (a different phase of the layer)
+  };
+  float ssp[NC];      // per-warp partial squared sums of the RMS norm
   float lm[MAX_LM_ROWS];
   int rel[NSLOT];     // warps done with the tile in each slot
   int issued[NSLOT];  // copies issued into each slot (for the error-path drain)
@@ -402,6 +395,137 @@ struct Smem {
   int flag;
 };
 static_assert(sizeof(Smem) % 16 == 0, "the tile table after Smem is a bulk-copy target (16-byte aligned)");
+
+// ---- stage inputs: one cooperative load per CTA into shared memory -------------
+// Every CTA needs the whole input vector of a stage (all 2048 elements of the
+// residual for a norm, all of attn / act). Reading it once per CTA — not once per
+// warp — keeps the 148 CTAs' simultaneous reads of the same few KB from piling up
+// on a handful of L2 slices. xs stores element e of the vector where lane `lane`
+// of a warp reading segment `seg` finds its register i with one conflict-free
+// 16-byte load: xs[seg*2048 + (i/4)*128 + lane*4 + i%4].
+template <int T>
+__device__ __forceinline__ int xs_index(int e) {
+  const int seg = e >> 11, r = e & 2047;
+  int lane, i;
+  if constexpr (T == SQ_BF16) {
+    lane = (r & 255) >> 3;
+    i = ((r >> 8) << 3) | (r & 7);
+  } else {
+    lane = r >> 6;
+    i = r & 63;
+  }
+  return (seg << 11) + ((i >> 2) << 7) + (lane << 2) + (i & 3);
+}
+
+enum { XS_PLAIN = 0, XS_NORM = 1, XS_EMBED = 2 };
+
+// Stage the n-element input of a stage into sm.xs. XS_PLAIN copies v; XS_NORM
+// stages h*w for the RMS norm of h (rms_norm.rs:40-56) and returns 1/rms; XS_EMBED
+// dequantizes the embedding row (ops/embedding.rs:10-52, exact scale*q) as h,
+// optionally writing it to p.hidden, and normalizes it like XS_NORM. The squared
+// sum is combined in a fixed order, so every CTA computes the same rms.
+template <int T, int MODE>
+__device__ float stage_x(const Params &p, Smem &sm, const float *v, const float *w, int n, const uint8_t *emb_row,
+                         bool write_hidden) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float ss = 0.f;
+  if constexpr (MODE == XS_EMBED) {
+    // 8 elements (one quarter block) per thread per pass
+    for (int g0 = 0; g0 < n / 8; g0 += NC * 32) {
+      const int g = g0 + tid;
+      if (g < n / 8) {
+        const int e = g * 8, b = e >> 5, j0 = e & 31;
+        float d[8];
+        if constexpr (T == SQ_BF16) {
+          const uint8_t *a = emb_row + (size_t)b * 64 + j0 * 2;
+          const uint32_t u[4] = {ldnc32(a), ldnc32(a + 4), ldnc32(a + 8), ldnc32(a + 12)};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            d[2 * k] = __uint_as_float(u[k] << 16);
+            d[2 * k + 1] = __uint_as_float(u[k] & 0xFFFF0000u);
+          }
+        } else if constexpr (T == SQ_Q8_0) {
+          const uint8_t *blk = emb_row + (size_t)b * Q8_BYTES;
+          const float sc = h2f(ld_u16(blk));
+#pragma unroll
+          for (int k = 0; k < 8; k++) d[k] = sc * (float)(int8_t)__ldg(blk + 2 + j0 + k);
+        } else {
+          const uint8_t *blk = emb_row + (size_t)b * Q4_BYTES;
+          const float sc = h2f(ld_u16(blk));
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const uint8_t byte = __ldg(blk + 2 + ((j0 + k) & 15));
+            d[k] = sc * (float)((j0 < 16 ? (byte & 0x0F) : (byte >> 4)) - 8);
+          }
+        }
+        const float4 w0 = ldnc4(w + e), w1 = ldnc4(w + e + 4);
+        if (write_hidden) {
+          *reinterpret_cast<float4 *>(p.hidden + e) = make_float4(d[0], d[1], d[2], d[3]);
+          *reinterpret_cast<float4 *>(p.hidden + e + 4) = make_float4(d[4], d[5], d[6], d[7]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) ss = fmaf(d[k], d[k], ss);
+        *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(e)]) =
+            make_float4(__fmul_rn(d[0], w0.x), __fmul_rn(d[1], w0.y), __fmul_rn(d[2], w0.z), __fmul_rn(d[3], w0.w));
+        *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(e + 4)]) =
+            make_float4(__fmul_rn(d[4], w1.x), __fmul_rn(d[5], w1.y), __fmul_rn(d[6], w1.z), __fmul_rn(d[7], w1.w));
+      }
+    }
+  } else {
+    // float4 chunks, all of this thread's loads in flight before any use
+    constexpr int MAXC = MAX_X / 4 / (NC * 32);
+    float4 hv[MAXC], wv[MAXC];
+    const int nc = n / 4;
+#pragma unroll
+    for (int k = 0; k < MAXC; k++) {
+      const int c = k * NC * 32 + tid;
+      hv[k] = c < nc ? ldcg4(v + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (MODE == XS_NORM) wv[k] = c < nc ? ldnc4(w + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < MAXC; k++) {
+      const int c = k * NC * 32 + tid;
+      if (c < nc) {
+        float4 o = hv[k];
+        if (MODE == XS_NORM) {
+          ss = fmaf(hv[k].x, hv[k].x, ss);
+          ss = fmaf(hv[k].y, hv[k].y, ss);
+          ss = fmaf(hv[k].z, hv[k].z, ss);
+          ss = fmaf(hv[k].w, hv[k].w, ss);
+          o = make_float4(__fmul_rn(hv[k].x, wv[k].x), __fmul_rn(hv[k].y, wv[k].y), __fmul_rn(hv[k].z, wv[k].z),
+                          __fmul_rn(hv[k].w, wv[k].w));
+        }
+        *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(4 * c)]) = o;
+      }
+    }
+  }
+  if (MODE != XS_PLAIN) {
+    ss = warp_sum(ss);
+    if (lane == 0) sm.ssp[warp] = ss;
+  }
+  cta_sync();
+  if (MODE == XS_PLAIN) return 1.0f;
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; k++) tot += sm.ssp[k];
+  return 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
+}
+
+// This warp's activation registers from the staged input, times `scale` (1/rms
+// for a norm: (h*w) * (1/rms), one rounding from the reference's (h*w)/rms).
+template <int T>
+__device__ __forceinline__ void x_from_smem(float (&x)[64], const Smem &sm, int seg, int lane, int n, float scale) {
+  const bool act = lane_active<T>(seg, lane, n);
+#pragma unroll
+  for (int k = 0; k < 16; k++) {
+    const float4 f = act ? *reinterpret_cast<const float4 *>(&sm.xs[(seg << 11) + (k << 7) + (lane << 2)])
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[4 * k] = __fmul_rn(f.x, scale);
+    x[4 * k + 1] = __fmul_rn(f.y, scale);
+    x[4 * k + 2] = __fmul_rn(f.z, scale);
+    x[4 * k + 3] = __fmul_rn(f.w, scale);
+  }
+}
 
 // Issue tile j of this CTA's table into `slot`: one or more bulk copies completing
 // on full[slot]. Rows of a QKV tile may span Wq / Wk / Wv; a gate/up tile carries
@@ -527,15 +651,15 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
   int r0, r1;
   stage_rows(p, KIND, l, blockIdx.x, r0, r1);
   const int stage_id = KIND == ST_LM ? 5 * p.L : 5 * l + (KIND == ST_QKV ? 0 : KIND + 1);
-  stamp(p, 6 * stage_id + 2);
+  stamp(p, 8 * stage_id + 3);
   for (int r = r0; r < r1; r += Tr) {
     const int n = min(Tr, r1 - r);
     const int rows = KIND == ST_GU ? 2 * n : n;
     const uint32_t tile = slots + (uint32_t)slot * SLOT;
     float *red = sm.red[tile_ctr & 1];
     const bool ok = mbar_wait(&rg.full[slot], phase, p.err);
-    if (r == r0) stamp(p, 6 * stage_id + 3);
-    if (r + Tr >= r1) stamp(p, 6 * stage_id + 4);
+    if (r == r0) stamp(p, 8 * stage_id + 4);
+    if (r + Tr >= r1) stamp(p, 8 * stage_id + 5);
     if (ok) {
       if (nseg == 1) {
         // warp-owned row pairs: (2i, 2i+1), or (gate i, up i)
@@ -692,25 +816,25 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
 #pragma unroll
     for (int h = 0; h < GROUP; h++) {
       if (lane == 0) {
-        sm.att_m[warp][h] = m[h];
-        sm.att_l[warp][h] = lsum[h];
+        sm.at.m[warp][h] = m[h];
+        sm.at.l[warp][h] = lsum[h];
       }
 #pragma unroll
-      for (int i = 0; i < DPL; i++) sm.att_a[warp][h][lane + 32 * i] = acc[h][i];
+      for (int i = 0; i < DPL; i++) sm.at.a[warp][h][lane + 32 * i] = acc[h][i];
     }
     cta_sync();
     if (warp < GROUP) {  // merge the warps' states of head `warp` into this chunk's partial
       const int h = warp;
       float M = -INFINITY;
-      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.att_m[w][h]);
+      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.at.m[w][h]);
       float Ls = 0.f, A[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; i++) A[i] = 0.f;
       for (int w = 0; w < NC; w++) {
-        const float f = sm.att_l[w][h] > 0.f ? expf(sm.att_m[w][h] - M) : 0.f;
-        Ls = fmaf(sm.att_l[w][h], f, Ls);
+        const float f = sm.at.l[w][h] > 0.f ? expf(sm.at.m[w][h] - M) : 0.f;
+        Ls = fmaf(sm.at.l[w][h], f, Ls);
 #pragma unroll
-        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.att_a[w][h][lane + 32 * i], f, A[i]);
+        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.at.a[w][h][lane + 32 * i], f, A[i]);
       }
       float *pp = p.attn_part + (((size_t)g * p.max_chunks + c) * GROUP + h) * (hd + 2);
       if (lane == 0) {
@@ -836,26 +960,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ---- RMSNorm + QKV + RoPE + KV append
     const int segE = warp % p.nseg_E;
     load_stage_regs(p, ST_QKV, l, pos, sr);
+    stamp(p, 8 * (5 * l) + 1);
     if (l == 0) {
-      // embed (ops/embedding.rs:10-52) straight into registers; CTA 0 also writes hidden
-      const uint8_t *row = p.embd + (size_t)tok * (p.E / QK) * type_bytes<T>();
-      float ss = 0.f;
-      for (int e = lane; e < p.E; e += 32) {
-        const float v = dequant_elem<T>(row + (e / QK) * type_bytes<T>(), e % QK);
-        ss = fmaf(v, v, ss);
-        if (blockIdx.x == 0 && warp == 0) p.hidden[e] = v;
-      }
-      ss = warp_sum(ss);
-      const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.E), p.eps));
-      const bool act = lane_active<T>(segE, lane, p.E);
-#pragma unroll
-      for (int i = 0; i < 64; i++) {
-        const int e = xelem<T>(segE, lane, i);
-        const float v = act ? dequant_elem<T>(row + (e / QK) * type_bytes<T>(), e % QK) : 0.f;
-        x[i] = act ? __fdiv_rn(__fmul_rn(v, __ldg(W.attn_norm + e)), rms) : 0.f;
-      }
+      const float sc = stage_x<T, XS_EMBED>(p, sm, nullptr, W.attn_norm, p.E, p.embd + (size_t)tok * p.rb_E,
+                                            blockIdx.x == 0);
+      x_from_smem<T>(x, sm, segE, lane, p.E, sc);
     } else {
-      load_x_norm<T>(x, p.hidden, W.attn_norm, segE, lane, p.E, p.eps);
+      const float sc = stage_x<T, XS_NORM>(p, sm, p.hidden, W.attn_norm, p.E, nullptr, false);
+      x_from_smem<T>(x, sm, segE, lane, p.E, sc);
     }
     matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
@@ -866,24 +978,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     grid_barrier(p, bar_target);
     // ---- O projection + residual
     load_stage_regs(p, ST_O, l, pos, sr);
-    load_x<T>(x, p.attn_out, warp % p.nseg_Q, lane, p.Q);
+    stamp(p, 8 * (5 * l + 2) + 1);
+    stage_x<T, XS_PLAIN>(p, sm, p.attn_out, nullptr, p.Q, nullptr, false);
+    x_from_smem<T>(x, sm, warp % p.nseg_Q, lane, p.Q, 1.0f);
     matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
     // ---- RMSNorm + gate/up + SiLU*up
-    load_x_norm<T>(x, p.hidden, W.ffn_norm, segE, lane, p.E, p.eps);
+    {
+      const float sc = stage_x<T, XS_NORM>(p, sm, p.hidden, W.ffn_norm, p.E, nullptr, false);
+      x_from_smem<T>(x, sm, segE, lane, p.E, sc);
+    }
     matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
     // ---- down + residual
     load_stage_regs(p, ST_DOWN, l, pos, sr);
-    load_x<T>(x, p.act, warp % p.nseg_F, lane, p.F);
+    stamp(p, 8 * (5 * l + 4) + 1);
+    stage_x<T, XS_PLAIN>(p, sm, p.act, nullptr, p.F, nullptr, false);
+    x_from_smem<T>(x, sm, warp % p.nseg_F, lane, p.F, 1.0f);
     matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
     bar_target += p.G;
     grid_barrier(p, bar_target);
   }
   // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
-  load_x_norm<T>(x, p.hidden, p.out_norm, warp % p.nseg_E, lane, p.E, p.eps);
+  {
+    const float sc = stage_x<T, XS_NORM>(p, sm, p.hidden, p.out_norm, p.E, nullptr, false);
+    x_from_smem<T>(x, sm, warp % p.nseg_E, lane, p.E, sc);
+  }
   matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr);
   cta_sync();
   stamp(p, p.tl_stride - 2);
@@ -1039,6 +1161,7 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
   // residual rows per CTA live in one register per lane; LM rows per CTA in shared memory
   ok = ok && (E + nsm - 1) / nsm <= 32 && (cf.vocab_size + nsm - 1) / nsm <= dk::MAX_LM_ROWS;
+  ok = ok && std::max(std::max(E, Q), F) <= dk::MAX_X;  // stage inputs fit the shared staging buffer
   if (!ok) return SQ_OK;  // the op-level path serves this model
   void *kern = nullptr;
   if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
@@ -1101,7 +1224,7 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(alloc((void **)&st->d_params, sizeof(dk::Params)));
   if (const char *tl = getenv("SQ_DECODE_TIMELINE")) {  // opt-in stage timestamps
     st->tl_path = tl;
-    st->tl_stride = 6 * (5 * cf.n_blocks + 1) + 4;
+    st->tl_stride = 8 * (5 * cf.n_blocks + 1) + 4;
     SQ_CUDA(alloc((void **)&st->d_timeline, (size_t)nsm * st->tl_stride * 8));
     h.timeline = st->d_timeline;
     h.tl_stride = st->tl_stride;
