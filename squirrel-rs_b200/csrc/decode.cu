@@ -70,6 +70,8 @@ struct Params {
   ArgState *arg_part;
   long long *argmax;
   int *pos;
+  unsigned long long *hid_ll, *q_ll, *kv_ll, *attn_ll, *act_ll;  // tagged exchange vectors
+  unsigned *launch;              // launches so far (the high bits of every tag)
   unsigned long long *timeline;  // optional per-CTA stage timestamps (SQ_DECODE_TIMELINE)
   int tl_stride;
   int2 *tiles;                   // [G][max_tiles] tile table: {row, layer<<16 | kind<<12 | rows}
@@ -153,36 +155,10 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 // Timeline slot k of this CTA: 0 = start; for stage s (5 per layer, the LM head is
-// stage 5L) 8s+1 = per-stage registers loaded, 8s+2 = squared sum of the norm done,
-// 8s+3 = activations loaded, 8s+4 / 8s+5 = first / last tile landed, 8s+6 / 8s+7 =
-// grid-barrier arrive / leave; stride-2 = LM head done, stride-1 = end.
+// stage 5L) 8s+2 = input staged, 8s+4 / 8s+5 = first / last tile landed, 8s+6 =
+// stage done; stride-2 = LM head done, stride-1 = end.
 __device__ __forceinline__ void stamp(const Params &p, int k) {
   if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = global_ns();
-}
-
-// Grid barrier among all CTAs. Thread 0 publishes the CTA's writes with a release
-// add and spins on an acquire load; the CTA barriers on both sides order the other
-// threads.
-__device__ void grid_barrier(const Params &p, unsigned target) {
-  cta_sync();
-  if (threadIdx.x == 0) {
-    const int b = (int)(target / p.G) - 1;
-    stamp(p, 8 * b + 6);
-    red_release_add(p.bar, 1u);
-    const long long t0 = clock64();
-    unsigned it = 0;
-    while (ld_acquire(p.bar) < target) {
-      if ((++it & 255u) == 0) {
-        if (ld_volatile(p.err)) break;
-        if (clock64() - t0 > WAIT_LIMIT) {
-          atomicExch(p.err, 2u);
-          break;
-        }
-      }
-    }
-    stamp(p, 8 * b + 7);
-  }
-  cta_sync();
 }
 
 // ---------------------------------------------------------------------------------
@@ -388,6 +364,7 @@ struct Smem {
     AttScratch at;    // attention-stage partials (a different phase of the layer)
   };
   float ssp[NC];      // per-warp partial squared sums of the RMS norm
+  float qh[256];      // one q head (attention over short contexts)
   float lm[MAX_LM_ROWS];
   int rel[NSLOT];     // warps done with the tile in each slot
   int issued[NSLOT];  // copies issued into each slot (for the error-path drain)
@@ -396,13 +373,65 @@ struct Smem {
 };
 static_assert(sizeof(Smem) % 16 == 0, "the tile table after Smem is a bulk-copy target (16-byte aligned)");
 
+enum { XS_PLAIN = 0, XS_NORM = 1, XS_EMBED = 2 };
+
+// ---- tagged exchange between CTAs ------------------------------------------------
+// Every vector one stage hands to the next (the residual stream, q / the new K/V
+// row, attention output, SiLU*up) lives in 64-bit words: the float in the low half,
+// the tag of the write in the high half. A reader polls the words themselves until
+// every one carries the tag it expects, so receiving the data is the
+// synchronization — no grid barrier, no flag round trip. Tags are
+// launch << 10 | layer << 3 | kind (kind below), so a stale word never matches.
+enum { TG_EMBED = 0, TG_QKV = 1, TG_ATTN = 2, TG_POST_O = 3, TG_ACT = 4, TG_POST_DOWN = 5 };
+__device__ __forceinline__ unsigned mk_tag(unsigned launch, int l, int kind) {
+  return (launch << 10) | ((unsigned)l << 3) | (unsigned)kind;
+}
+__device__ __forceinline__ void st_ll(unsigned long long *a, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll(const unsigned long long *a) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(a));
+  return v;
+}
+__device__ __forceinline__ ulonglong2 ld_ll2(const unsigned long long *a) {  // two words, 16-byte aligned
+  ulonglong2 v;
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(a));
+  return v;
+}
+__device__ __forceinline__ bool ll_ok(unsigned long long w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
+
+// Re-read one word until it carries `tag` (bounded: on expiry the error flag is set
+// and 0 returned).
+__device__ __noinline__ unsigned long long ll_wait(const Params &p, const unsigned long long *a, unsigned tag) {
+  const long long t0 = clock64();
+  for (unsigned it = 0;; it++) {
+    const unsigned long long w = ld_ll(a);
+    if (ll_ok(w, tag)) return w;
+    if ((it & 63u) == 63u) {
+      if (ld_volatile(p.err)) return 0ull;
+      if (clock64() - t0 > WAIT_LIMIT) {
+        atomicExch(p.err, 3u);
+        return 0ull;
+      }
+    }
+  }
+}
+__device__ __forceinline__ float poll_ll(const Params &p, const unsigned long long *a, unsigned tag) {
+  unsigned long long w = ld_ll(a);
+  if (!ll_ok(w, tag)) w = ll_wait(p, a, tag);
+  return ll_val(w);
+}
+
 // ---- stage inputs: one cooperative load per CTA into shared memory -------------
-// Every CTA needs the whole input vector of a stage (all 2048 elements of the
-// residual for a norm, all of attn / act). Reading it once per CTA — not once per
-// warp — keeps the 148 CTAs' simultaneous reads of the same few KB from piling up
-// on a handful of L2 slices. xs stores element e of the vector where lane `lane`
-// of a warp reading segment `seg` finds its register i with one conflict-free
-// 16-byte load: xs[seg*2048 + (i/4)*128 + lane*4 + i%4].
+// Every CTA needs the whole input vector of a stage (all elements of the residual
+// for a norm, all of attn / act). Reading it once per CTA — not once per warp —
+// keeps the CTAs' simultaneous reads of the same few KB from piling up on a
+// handful of L2 slices. xs stores element e where lane `lane` of a warp reading
+// segment `seg` finds its register i with one conflict-free 16-byte load:
+// xs[seg*2048 + (i/4)*128 + lane*4 + i%4].
 template <int T>
 __device__ __forceinline__ int xs_index(int e) {
   const int seg = e >> 11, r = e & 2047;
@@ -417,21 +446,19 @@ __device__ __forceinline__ int xs_index(int e) {
   return (seg << 11) + ((i >> 2) << 7) + (lane << 2) + (i & 3);
 }
 
-enum { XS_PLAIN = 0, XS_NORM = 1, XS_EMBED = 2 };
-
-// Stage the n-element input of a stage into sm.xs. XS_PLAIN copies v; XS_NORM
-// stages h*w for the RMS norm of h (rms_norm.rs:40-56) and returns 1/rms; XS_EMBED
-// dequantizes the embedding row (ops/embedding.rs:10-52, exact scale*q) as h,
-// optionally writing it to p.hidden, and normalizes it like XS_NORM. The squared
-// sum is combined in a fixed order, so every CTA computes the same rms.
+// Stage the n-element input of a stage into sm.xs. XS_PLAIN copies the tagged
+// vector v; XS_NORM stages h*w for the RMS norm of h (rms_norm.rs:40-56) and
+// returns 1/rms; XS_EMBED dequantizes the embedding row (ops/embedding.rs:10-52,
+// exact scale*q) as h — optionally publishing it as the layer-0 residual — and
+// normalizes it like XS_NORM. The squared sum is combined in a fixed order, so
+// every CTA computes the same rms.
 template <int T, int MODE>
-__device__ float stage_x(const Params &p, Smem &sm, const float *v, const float *w, int n, const uint8_t *emb_row,
-                         bool write_hidden) {
+__device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
+                         const uint8_t *emb_row, bool write_hidden, unsigned emb_tag) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float ss = 0.f;
   if constexpr (MODE == XS_EMBED) {
-    // 8 elements (one quarter block) per thread per pass
-    for (int g0 = 0; g0 < n / 8; g0 += NC * 32) {
+    for (int g0 = 0; g0 < n / 8; g0 += NC * 32) {  // 8 elements (a quarter block) per thread per pass
       const int g = g0 + tid;
       if (g < n / 8) {
         const int e = g * 8, b = e >> 5, j0 = e & 31;
@@ -460,8 +487,8 @@ __device__ float stage_x(const Params &p, Smem &sm, const float *v, const float 
         }
         const float4 w0 = ldnc4(w + e), w1 = ldnc4(w + e + 4);
         if (write_hidden) {
-          *reinterpret_cast<float4 *>(p.hidden + e) = make_float4(d[0], d[1], d[2], d[3]);
-          *reinterpret_cast<float4 *>(p.hidden + e + 4) = make_float4(d[4], d[5], d[6], d[7]);
+#pragma unroll
+          for (int k = 0; k < 8; k++) st_ll(p.hid_ll + e + k, d[k], emb_tag);
         }
 #pragma unroll
         for (int k = 0; k < 8; k++) ss = fmaf(d[k], d[k], ss);
@@ -472,30 +499,31 @@ __device__ float stage_x(const Params &p, Smem &sm, const float *v, const float 
       }
     }
   } else {
-    // float4 chunks, all of this thread's loads in flight before any use
-    constexpr int MAXC = MAX_X / 4 / (NC * 32);
-    float4 hv[MAXC], wv[MAXC];
-    const int nc = n / 4;
+    // word pairs (two elements), every load of this thread in flight before any use
+    constexpr int MAXC = MAX_X / 2 / (NC * 32);
+    ulonglong2 c[MAXC];
+    float2 wv[MAXC];
+    const int nc = n / 2;
 #pragma unroll
     for (int k = 0; k < MAXC; k++) {
-      const int c = k * NC * 32 + tid;
-      hv[k] = c < nc ? ldcg4(v + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (MODE == XS_NORM) wv[k] = c < nc ? ldnc4(w + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int ci = k * NC * 32 + tid;
+      c[k] = ci < nc ? ld_ll2(v + 2 * ci) : make_ulonglong2(0ull, 0ull);
+      if (MODE == XS_NORM) wv[k] = ci < nc ? *reinterpret_cast<const float2 *>(w + 2 * ci) : make_float2(0.f, 0.f);
     }
 #pragma unroll
     for (int k = 0; k < MAXC; k++) {
-      const int c = k * NC * 32 + tid;
-      if (c < nc) {
-        float4 o = hv[k];
+      const int ci = k * NC * 32 + tid;
+      if (ci < nc) {
+        if (!ll_ok(c[k].x, tag)) c[k].x = ll_wait(p, v + 2 * ci, tag);
+        if (!ll_ok(c[k].y, tag)) c[k].y = ll_wait(p, v + 2 * ci + 1, tag);
+        float a = ll_val(c[k].x), b = ll_val(c[k].y);
         if (MODE == XS_NORM) {
-          ss = fmaf(hv[k].x, hv[k].x, ss);
-          ss = fmaf(hv[k].y, hv[k].y, ss);
-          ss = fmaf(hv[k].z, hv[k].z, ss);
-          ss = fmaf(hv[k].w, hv[k].w, ss);
-          o = make_float4(__fmul_rn(hv[k].x, wv[k].x), __fmul_rn(hv[k].y, wv[k].y), __fmul_rn(hv[k].z, wv[k].z),
-                          __fmul_rn(hv[k].w, wv[k].w));
+          ss = fmaf(a, a, ss);
+          ss = fmaf(b, b, ss);
+          a = __fmul_rn(a, wv[k].x);
+          b = __fmul_rn(b, wv[k].y);
         }
-        *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(4 * c)]) = o;
+        *reinterpret_cast<float2 *>(&sm.xs[xs_index<T>(2 * ci)]) = make_float2(a, b);
       }
     }
   }
@@ -586,9 +614,11 @@ struct StageRegs {
 
 // Finish output row(s) of a stage (warp-uniform arguments; lane 0 stores).
 // rows a / b are absolute rows of the stage's row space; vb is ignored when !hasb.
+// Outputs other CTAs read go out as tagged words (`tag`); the K/V row also lands
+// in the cache for later tokens.
 template <int KIND>
 __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, int pos, int r0, int a, float va, int b,
-                                            float vb, bool hasb, const StageRegs &sr) {
+                                            float vb, bool hasb, const StageRegs &sr, unsigned tag) {
   const int lane = threadIdx.x & 31;
   if constexpr (KIND == ST_QKV) {  // a even, b = a + 1: RoPE pair (rope.rs:25-31), then q / K / V
     const int j = (a % p.hd) >> 1;
@@ -599,30 +629,34 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, in
         const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
         const float rb = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
         if (a < p.Q) {
-          p.qbuf[a] = ra;
-          p.qbuf[a + 1] = rb;
+          st_ll(p.q_ll + a, ra, tag);
+          st_ll(p.q_ll + a + 1, rb, tag);
         } else {
           const int kr = a - p.Q, g = kr / p.hd, d = kr % p.hd;
           float *dst = p.kc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
           dst[0] = ra;
           dst[1] = rb;
+          st_ll(p.kv_ll + kr, ra, tag);
+          st_ll(p.kv_ll + kr + 1, rb, tag);
         }
       } else {
         const int vr = a - p.Q - p.KVd, g = vr / p.hd, d = vr % p.hd;
         float *dst = p.vc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
         dst[0] = va;
         dst[1] = vb;
+        st_ll(p.kv_ll + p.KVd + vr, va, tag);
+        st_ll(p.kv_ll + p.KVd + vr + 1, vb, tag);
       }
     }
   } else if constexpr (KIND == ST_O || KIND == ST_DOWN) {  // residual (elementwise_add.rs:47-61)
     const float ha = __shfl_sync(FULL, sr.hres, (a - r0) & 31);
     const float hb = __shfl_sync(FULL, sr.hres, (b - r0) & 31);
     if (lane == 0) {
-      p.hidden[a] = __fadd_rn(ha, va);
-      if (hasb) p.hidden[b] = __fadd_rn(hb, vb);
+      st_ll(p.hid_ll + a, __fadd_rn(ha, va), tag);
+      if (hasb) st_ll(p.hid_ll + b, __fadd_rn(hb, vb), tag);
     }
   } else if constexpr (KIND == ST_GU) {  // a = gate row, vb = up (silu.rs:4-8, elementwise_mul.rs:3-17)
-    if (lane == 0) p.act[a] = __fmul_rn(__fmul_rn(va, sigmoid_ref(va)), vb);
+    if (lane == 0) st_ll(p.act_ll + a, __fmul_rn(__fmul_rn(va, sigmoid_ref(va)), vb), tag);
   } else {  // LM head logits
     if (lane == 0) {
       p.logits[a] = va;
@@ -640,7 +674,7 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, in
 template <int T, int KIND>
 __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int l,
                              const float (&x)[64], int &slot, unsigned &phase, int &tile_ctr, int pos,
-                             const StageRegs &sr) {
+                             const StageRegs &sr, unsigned tag) {
   constexpr int NW = nwords<T>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nseg = stage_nseg(p, KIND), rb = stage_rb(p, KIND), Tr = p.tile_rows[KIND];
@@ -651,7 +685,6 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
   int r0, r1;
   stage_rows(p, KIND, l, blockIdx.x, r0, r1);
   const int stage_id = KIND == ST_LM ? 5 * p.L : 5 * l + (KIND == ST_QKV ? 0 : KIND + 1);
-  stamp(p, 8 * stage_id + 3);
   for (int r = r0; r < r1; r += Tr) {
     const int n = min(Tr, r1 - r);
     const int rows = KIND == ST_GU ? 2 * n : n;
@@ -676,8 +709,8 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
             if (hasb) vb = lane_dot<T>(wb, x);
           }
           const float2 v = warp_sum2(va, vb);
-          if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, v.x, r + i, v.y, true, sr);
-          else finish_rows<KIND>(p, sm, l, pos, r0, r + a, v.x, r + b, v.y, hasb, sr);
+          if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, v.x, r + i, v.y, true, sr, tag);
+          else finish_rows<KIND>(p, sm, l, pos, r0, r + a, v.x, r + b, v.y, hasb, sr, tag);
         }
       } else {
         // segment-split rows: partial sums per (row, segment) meet in shared memory
@@ -708,64 +741,134 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
     tile_ctr++;
     if (nseg > 1) {
       cta_sync();
-      if (ok && warp == 0) {
-        const int units = KIND == ST_QKV ? n / 2 : n;
-        for (int t0 = 0; t0 < units; t0 += 32) {
-          const int t = min(t0 + lane, units - 1);  // every lane joins the shuffles
+      // finish the tile's rows: warp w takes row pairs w, w+NC, ... (the same pairing as above)
+      if (ok) {
+        const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
+        for (int i = warp; i < npairs; i += NC) {
+          const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
+          const bool hasb = b < rows;
           float va = 0.f, vb = 0.f;
-          const int a = KIND == ST_QKV ? 2 * t : t, b = KIND == ST_QKV ? 2 * t + 1 : (KIND == ST_GU ? n + t : t);
           for (int s = 0; s < nseg; s++) {
             va += red[a * nseg + s];
-            vb += red[b * nseg + s];
+            if (hasb) vb += red[b * nseg + s];
           }
-          const bool mine = t0 + lane < units;
-          if (KIND == ST_QKV) {
-            const int row = r + a;
-            const int j = (row % p.hd) >> 1;
-            const float c0 = __shfl_sync(FULL, sr.c0, j & 31), c1 = __shfl_sync(FULL, sr.c1, j & 31);
-            const float s0 = __shfl_sync(FULL, sr.s0, j & 31), s1 = __shfl_sync(FULL, sr.s1, j & 31);
-            const float c = j < 32 ? c0 : c1, s = j < 32 ? s0 : s1;
-            if (mine) {
-              if (row < p.Q + p.KVd) {
-                const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
-                const float rbv = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
-                if (row < p.Q) {
-                  p.qbuf[row] = ra;
-                  p.qbuf[row + 1] = rbv;
-                } else {
-                  const int kr = row - p.Q, g = kr / p.hd, d = kr % p.hd;
-                  float *dst = p.kc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
-                  dst[0] = ra;
-                  dst[1] = rbv;
-                }
-              } else {
-                const int vr = row - p.Q - p.KVd, g = vr / p.hd, d = vr % p.hd;
-                float *dst = p.vc + (((size_t)l * p.KVH + g) * p.max_ctx + pos) * p.hd + d;
-                dst[0] = va;
-                dst[1] = vb;
-              }
-            }
-          } else if (KIND == ST_O || KIND == ST_DOWN) {
-            const float h = __shfl_sync(FULL, sr.hres, (r + t - r0) & 31);
-            if (mine) p.hidden[r + t] = __fadd_rn(h, va);
-          } else if (KIND == ST_GU) {
-            if (mine) p.act[r + t] = __fmul_rn(__fmul_rn(va, sigmoid_ref(va)), vb);
-          } else {
-            if (mine) {
-              p.logits[r + t] = va;
-              sm.lm[r + t - r0] = va;
-            }
-          }
+          if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
+          else finish_rows<KIND>(p, sm, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
         }
       }
     }
   }
+  stamp(p, 8 * stage_id + 6);
 }
 
-// Causal GQA attention for one token at position pos (attention.rs:11-70): split-KV
-// over (kv head, chunk) items; the last CTA to finish a kv head merges its chunks.
+// Causal GQA attention for one token at position pos (attention.rs:11-70), reading
+// q and the new K/V row from the tagged words of the QKV stage and the older
+// positions from the KV cache; the output goes out tagged for the O stage.
+//
+// Short contexts (head_dim 64, pos < SHORT_CTX): one item per q head. The 8 warps
+// split the cached positions 32 at a time; lane = position for q.k (q broadcast
+// from shared memory, no reductions), lane = dimension for p.V; each warp keeps a
+// running max / sum / accumulator, the warps merge in shared memory, and warp 0
+// adds the current position.
+constexpr int SHORT_CTX = 512;
+
 template <int DPL>
-__device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
+__device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsigned tag_in, unsigned tag_out) {
+  constexpr int HD = DPL * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int h = blockIdx.x; h < p.H; h += p.G) {
+    const int g = h / GROUP;
+    if (warp == 0) {
+#pragma unroll
+      for (int i = 0; i < DPL; i++) sm.qh[lane + 32 * i] = poll_ll(p, p.q_ll + (size_t)h * HD + lane + 32 * i, tag_in);
+    }
+    cta_sync();
+    const float *kb = p.kc + ((size_t)l * p.KVH + g) * p.max_ctx * HD;
+    const float *vb = p.vc + ((size_t)l * p.KVH + g) * p.max_ctx * HD;
+    float m = -INFINITY, lsum = 0.f, acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) acc[i] = 0.f;
+    for (int base = warp * 32; base < pos; base += NC * 32) {
+      const int s = base + lane;
+      const bool valid = s < pos;
+      float4 kr[HD / 4];
+#pragma unroll
+      for (int k = 0; k < HD / 4; k++)
+        kr[k] = valid ? ldcg4(kb + (size_t)s * HD + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float vv[32][DPL];
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+#pragma unroll
+        for (int i = 0; i < DPL; i++) vv[j][i] = base + j < pos ? __ldcg(vb + (size_t)(base + j) * HD + lane + 32 * i) : 0.f;
+      float d = 0.f;
+#pragma unroll
+      for (int k = 0; k < HD / 4; k++) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(&sm.qh[4 * k]);
+        d = fmaf(q4.x, kr[k].x, d);
+        d = fmaf(q4.y, kr[k].y, d);
+        d = fmaf(q4.z, kr[k].z, d);
+        d = fmaf(q4.w, kr[k].w, d);
+      }
+      const float sc = valid ? d * p.attn_scale : -INFINITY;
+      const float mn = fmaxf(m, warp_max(sc));
+      const float corr = expf(m - mn);
+      const float pj = valid ? expf(sc - mn) : 0.f;
+      lsum = fmaf(lsum, corr, warp_sum(pj));
+#pragma unroll
+      for (int i = 0; i < DPL; i++) acc[i] *= corr;
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        const float pjj = __shfl_sync(FULL, pj, j);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) acc[i] = fmaf(pjj, vv[j][i], acc[i]);
+      }
+      m = mn;
+    }
+    if (lane == 0) {
+      sm.at.m[warp][0] = m;
+      sm.at.l[warp][0] = lsum;
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; i++) sm.at.a[warp][0][lane + 32 * i] = acc[i];
+    cta_sync();
+    if (warp == 0) {
+      float M = -INFINITY;
+      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.at.m[w][0]);
+      float Ls = 0.f, A[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) A[i] = 0.f;
+      for (int w = 0; w < NC; w++) {
+        const float f = sm.at.l[w][0] > 0.f ? expf(sm.at.m[w][0] - M) : 0.f;
+        Ls = fmaf(sm.at.l[w][0], f, Ls);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.at.a[w][0][lane + 32 * i], f, A[i]);
+      }
+      // the current position
+      float kq[DPL], vq[DPL], d = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) {
+        kq[i] = poll_ll(p, p.kv_ll + (size_t)g * HD + lane + 32 * i, tag_in);
+        vq[i] = poll_ll(p, p.kv_ll + p.KVd + (size_t)g * HD + lane + 32 * i, tag_in);
+        d = fmaf(sm.qh[lane + 32 * i], kq[i], d);
+      }
+      const float sc = warp_sum(d) * p.attn_scale;
+      const float mn = fmaxf(M, sc);
+      const float corr = expf(M - mn), pp = expf(sc - mn);
+      Ls = fmaf(Ls, corr, pp);
+      const float inv = 1.0f / Ls;
+#pragma unroll
+      for (int i = 0; i < DPL; i++)
+        st_ll(p.attn_ll + (size_t)h * HD + lane + 32 * i, fmaf(pp, vq[i], A[i] * corr) * inv, tag_out);
+    }
+    cta_sync();
+  }
+}
+
+// Long contexts: split-KV over (kv head, chunk) items covering the group's GROUP
+// q heads; partial (max, sum, accumulator) per chunk, and the last CTA to finish a
+// kv head merges its chunks.
+template <int DPL>
+__device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsigned tag_in, unsigned tag_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Lk = pos + 1;
   int n_chunks = (Lk + 31) / 32;
@@ -785,7 +888,7 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
       lsum[h] = 0.f;
 #pragma unroll
       for (int i = 0; i < DPL; i++) {
-        qv[h][i] = __ldcg(p.qbuf + (size_t)(g * GROUP + h) * hd + lane + 32 * i);
+        qv[h][i] = poll_ll(p, p.q_ll + (size_t)(g * GROUP + h) * hd + lane + 32 * i, tag_in);
         acc[h][i] = 0.f;
       }
     }
@@ -795,8 +898,13 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
       float kr[DPL], vr[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; i++) {
-        kr[i] = __ldcg(kb + (size_t)s * hd + lane + 32 * i);
-        vr[i] = __ldcg(vb + (size_t)s * hd + lane + 32 * i);
+        if (s == pos) {  // the row this token's QKV stage just produced
+          kr[i] = poll_ll(p, p.kv_ll + (size_t)g * hd + lane + 32 * i, tag_in);
+          vr[i] = poll_ll(p, p.kv_ll + p.KVd + (size_t)g * hd + lane + 32 * i, tag_in);
+        } else {
+          kr[i] = __ldcg(kb + (size_t)s * hd + lane + 32 * i);
+          vr[i] = __ldcg(vb + (size_t)s * hd + lane + 32 * i);
+        }
       }
 #pragma unroll
       for (int h = 0; h < GROUP; h++) {
@@ -847,7 +955,7 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
     }
     cta_sync();
     if (threadIdx.x == 0) {
-      const unsigned old = atomicAdd(p.attn_cnt + g, 1u);
+      const unsigned old = atomicAdd(p.attn_cnt + (size_t)l * p.KVH + g, 1u);
       sm.flag = old == (unsigned)(n_chunks - 1);
     }
     cta_sync();
@@ -875,9 +983,10 @@ __device__ void attention_stage(const Params &p, Smem &sm, int l, int pos) {
         }
         const float inv = 1.0f / Ls;
 #pragma unroll
-        for (int i = 0; i < DPL; i++) p.attn_out[(size_t)(g * GROUP + h) * hd + lane + 32 * i] = A[i] * inv;
+        for (int i = 0; i < DPL; i++)
+          st_ll(p.attn_ll + (size_t)(g * GROUP + h) * hd + lane + 32 * i, A[i] * inv, tag_out);
       }
-      if (threadIdx.x == 0) p.attn_cnt[g] = 0;
+      if (threadIdx.x == 0) p.attn_cnt[(size_t)l * p.KVH + g] = 0;  // per-layer counter, ready for the next token
     }
     cta_sync();
   }
@@ -901,7 +1010,8 @@ __device__ ArgState warp_argmax_smem(const float *v, int n, long long base) {
   return s;
 }
 
-__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr) {
+__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr,
+                                                unsigned hid_tag) {
   const int lane = threadIdx.x & 31;
   if (kind == ST_QKV) {
     const int half = p.hd >> 1;
@@ -910,10 +1020,10 @@ __device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l
     sr.s0 = lane < half ? __ldg(p.sin_t + base + lane) : 0.f;
     sr.c1 = lane + 32 < half ? __ldg(p.cos_t + base + 32 + lane) : 0.f;
     sr.s1 = lane + 32 < half ? __ldg(p.sin_t + base + 32 + lane) : 0.f;
-  } else if (kind == ST_O || kind == ST_DOWN) {
+  } else if (kind == ST_O || kind == ST_DOWN) {  // the residual of this CTA's rows (<= 32)
     int r0, r1;
     stage_rows(p, kind, l, blockIdx.x, r0, r1);
-    sr.hres = lane < r1 - r0 ? __ldcg(p.hidden + r0 + lane) : 0.f;
+    sr.hres = lane < r1 - r0 ? poll_ll(p, p.hid_ll + r0 + lane, hid_tag) : 0.f;
   }
 }
 
@@ -951,62 +1061,62 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   const int pos = *p.pos;
   const uint32_t tok = *tok_in;
+  const unsigned launch = *p.launch;
   int slot = 0, tile_ctr = 0;
-  unsigned phase = 0, bar_target = 0;
+  unsigned phase = 0;
   float x[64];
   StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
   for (int l = 0; l < p.L; l++) {
     const LayerW &W = p.layers[l];
-    // ---- RMSNorm + QKV + RoPE + KV append
     const int segE = warp % p.nseg_E;
-    load_stage_regs(p, ST_QKV, l, pos, sr);
-    stamp(p, 8 * (5 * l) + 1);
-    if (l == 0) {
-      const float sc = stage_x<T, XS_EMBED>(p, sm, nullptr, W.attn_norm, p.E, p.embd + (size_t)tok * p.rb_E,
-                                            blockIdx.x == 0);
-      x_from_smem<T>(x, sm, segE, lane, p.E, sc);
-    } else {
-      const float sc = stage_x<T, XS_NORM>(p, sm, p.hidden, W.attn_norm, p.E, nullptr, false);
+    const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
+    // ---- RMSNorm + QKV + RoPE + KV append
+    load_stage_regs(p, ST_QKV, l, pos, sr, 0u);
+    {
+      const float sc = l == 0 ? stage_x<T, XS_EMBED>(p, sm, nullptr, 0u, W.attn_norm, p.E, p.embd + (size_t)tok * p.rb_E,
+                                                     blockIdx.x == 0, hid_in)
+                              : stage_x<T, XS_NORM>(p, sm, p.hid_ll, hid_in, W.attn_norm, p.E, nullptr, false, 0u);
       x_from_smem<T>(x, sm, segE, lane, p.E, sc);
     }
-    matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
-    bar_target += p.G;
-    grid_barrier(p, bar_target);
-    // ---- attention
-    attention_stage<DPL>(p, sm, l, pos);
-    bar_target += p.G;
-    grid_barrier(p, bar_target);
+    stamp(p, 8 * (5 * l) + 2);
+    matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_QKV));
+    // ---- attention (waits on q / K / V words, not on a barrier)
+    cta_sync();  // shared scratch of the staging buffer is reused below
+    if (DPL <= 2 && pos < SHORT_CTX) attention_heads<DPL <= 2 ? DPL : 2>(p, sm, l, pos, mk_tag(launch, l, TG_QKV), mk_tag(launch, l, TG_ATTN));
+    else attention_chunks<DPL>(p, sm, l, pos, mk_tag(launch, l, TG_QKV), mk_tag(launch, l, TG_ATTN));
+    stamp(p, 8 * (5 * l + 1) + 6);
     // ---- O projection + residual
-    load_stage_regs(p, ST_O, l, pos, sr);
-    stamp(p, 8 * (5 * l + 2) + 1);
-    stage_x<T, XS_PLAIN>(p, sm, p.attn_out, nullptr, p.Q, nullptr, false);
+    load_stage_regs(p, ST_O, l, pos, sr, hid_in);
+    stage_x<T, XS_PLAIN>(p, sm, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, nullptr, false, 0u);
     x_from_smem<T>(x, sm, warp % p.nseg_Q, lane, p.Q, 1.0f);
-    matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
-    bar_target += p.G;
-    grid_barrier(p, bar_target);
+    stamp(p, 8 * (5 * l + 2) + 2);
+    matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_O));
     // ---- RMSNorm + gate/up + SiLU*up
     {
-      const float sc = stage_x<T, XS_NORM>(p, sm, p.hidden, W.ffn_norm, p.E, nullptr, false);
+      cta_sync();
+      const float sc = stage_x<T, XS_NORM>(p, sm, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, nullptr,
+                                           false, 0u);
       x_from_smem<T>(x, sm, segE, lane, p.E, sc);
     }
-    matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
-    bar_target += p.G;
-    grid_barrier(p, bar_target);
+    stamp(p, 8 * (5 * l + 3) + 2);
+    matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_ACT));
     // ---- down + residual
-    load_stage_regs(p, ST_DOWN, l, pos, sr);
-    stamp(p, 8 * (5 * l + 4) + 1);
-    stage_x<T, XS_PLAIN>(p, sm, p.act, nullptr, p.F, nullptr, false);
+    load_stage_regs(p, ST_DOWN, l, pos, sr, mk_tag(launch, l, TG_POST_O));
+    cta_sync();
+    stage_x<T, XS_PLAIN>(p, sm, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, nullptr, false, 0u);
     x_from_smem<T>(x, sm, warp % p.nseg_F, lane, p.F, 1.0f);
-    matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr);
-    bar_target += p.G;
-    grid_barrier(p, bar_target);
+    stamp(p, 8 * (5 * l + 4) + 2);
+    matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_DOWN));
+    cta_sync();
   }
   // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
   {
-    const float sc = stage_x<T, XS_NORM>(p, sm, p.hidden, p.out_norm, p.E, nullptr, false);
+    const float sc = stage_x<T, XS_NORM>(p, sm, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E,
+                                         nullptr, false, 0u);
     x_from_smem<T>(x, sm, warp % p.nseg_E, lane, p.E, sc);
   }
-  matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr);
+  stamp(p, 8 * (5 * p.L) + 2);
+  matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr, 0u);
   cta_sync();
   stamp(p, p.tl_stride - 2);
   // ---- greedy argmax: this CTA's rows (kept in shared memory) in order, then the
@@ -1051,7 +1161,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         *tok_out = (uint32_t)id;
         if (out_ids) out_ids[step] = (uint32_t)id;
         *p.pos = pos + 1;
-        *p.bar = 0;  // every CTA has passed its last grid barrier
+        *p.launch = launch + 1;  // every CTA read the launch count at its start
         *p.ticket = 0;
       }
     }
@@ -1104,7 +1214,7 @@ struct DecodeState {
   int grid = 0;
   unsigned *d_err = nullptr, *d_bar = nullptr, *d_ticket = nullptr, *d_attn_cnt = nullptr;
   int *d_pos = nullptr;
-  int n_kv_heads = 0;
+  int n_kv_heads = 0, n_layers = 0;
   unsigned long long *d_timeline = nullptr;  // SQ_DECODE_TIMELINE=<file>: stage stamps of the last launch
   int tl_stride = 0;
   std::string tl_path;
@@ -1215,7 +1325,17 @@ int decode_prepare(sq_ctx *c) {
     return e;
   };
   SQ_CUDA(alloc((void **)&h.attn_part, (size_t)cf.n_kv_heads * h.max_chunks * dk::GROUP * (cf.head_dim + 2) * 4));
-  SQ_CUDA(alloc((void **)&h.attn_cnt, (size_t)cf.n_kv_heads * 4));
+  SQ_CUDA(alloc((void **)&h.attn_cnt, (size_t)cf.n_blocks * cf.n_kv_heads * 4));
+  SQ_CUDA(alloc((void **)&h.hid_ll, (size_t)E * 8));
+  SQ_CUDA(alloc((void **)&h.q_ll, (size_t)Q * 8));
+  SQ_CUDA(alloc((void **)&h.kv_ll, (size_t)2 * KVd * 8));
+  SQ_CUDA(alloc((void **)&h.attn_ll, (size_t)Q * 8));
+  SQ_CUDA(alloc((void **)&h.act_ll, (size_t)F * 8));
+  SQ_CUDA(alloc((void **)&h.launch, 4));
+  {
+    const unsigned one = 1;  // tags of launch 0 would match the zeroed words
+    SQ_CUDA(cudaMemcpy(h.launch, &one, 4, cudaMemcpyHostToDevice));
+  }
   SQ_CUDA(alloc((void **)&h.bar, 4));
   SQ_CUDA(alloc((void **)&h.ticket, 4));
   SQ_CUDA(alloc((void **)&h.err, 4));
@@ -1256,6 +1376,7 @@ int decode_prepare(sq_ctx *c) {
   st->d_ticket = h.ticket;
   st->d_attn_cnt = h.attn_cnt;
   st->n_kv_heads = cf.n_kv_heads;
+  st->n_layers = cf.n_blocks;
   st->d_pos = h.pos;
   st->kernel = kern;
   st->smem = smem;
@@ -1314,7 +1435,7 @@ int decode_check(sq_ctx *c) {
     cudaMemset(st->d_err, 0, 4);
     cudaMemset(st->d_bar, 0, 4);
     cudaMemset(st->d_ticket, 0, 4);
-    cudaMemset(st->d_attn_cnt, 0, (size_t)st->n_kv_heads * 4);
+    cudaMemset(st->d_attn_cnt, 0, (size_t)st->n_kv_heads * st->n_layers * 4);
     st->dev_pos = -1;  // force a position resync
     return fail(SQ_ERR_TIMEOUT, "decode kernel: a bounded wait expired (code " + std::to_string(err) + ")");
   }
