@@ -109,6 +109,25 @@ int sq_dequantize(void *stream, const void *blocks, int wtype, size_t n_elems, f
  * resolve like Iterator::max_by with partial_cmp (the later element wins). */
 int sq_argmax(void *stream, const float *logits, size_t n, int64_t *out_index);
 
+/* No counterpart in the reference. sq_argmax without any device allocation, for
+ * callers that must not allocate device memory on the call path: sq_argmax takes
+ * its per-chunk partial states from the stream-ordered pool (cudaMallocAsync) on
+ * every call, which can fail with out-of-memory when a caller has sized its KV
+ * caches and buffers to fill the GPU, and a caller that budgets device memory up
+ * front cannot allow it. This variant keeps the partial states in a fixed 96 KiB
+ * buffer of the library's static device memory and returns the same index as
+ * sq_argmax (same kernels).
+ *   - n up to SQ_ARGMAX_NOALLOC_MAX_N elements; larger n fails with SQ_ERR_ARG
+ *     before any launch (use sq_argmax for those).
+ *   - The buffer's device address is looked up on the first call on each device
+ *     (with that device current); make that first call before capturing the
+ *     stream into a CUDA graph.
+ *   - All calls on one device share the buffer: calls that can overlap on the
+ *     device (unordered streams, concurrent host threads) race and may return a
+ *     wrong index. Order them, e.g. on one stream. */
+#define SQ_ARGMAX_NOALLOC_MAX_N (1u << 24)
+int sq_argmax_noalloc(void *stream, const float *logits, size_t n, int64_t *out_index);
+
 /* ---- model level (host pointers) ------------------------------------------------ */
 
 typedef struct sq_model sq_model;

@@ -62,6 +62,7 @@ SIGNATURES = {
     "sq_quantize_row_q8_0": (_i, [_vp, _vp, _sz, _vp]),
     "sq_dequantize": (_i, [_vp, _vp, _i, _sz, _vp]),
     "sq_argmax": (_i, [_vp, _vp, _sz, _vp]),
+    "sq_argmax_noalloc": (_i, [_vp, _vp, _sz, _vp]),
     "sq_model_create": (_i, [C.POINTER(LlamaConfig), _i, _i, C.POINTER(_vp)]),
     "sq_model_upload_tensor": (_i, [_vp, C.c_char_p, _i, C.POINTER(C.c_uint64), _i, _vp, _sz]),
     "sq_model_finalize": (_i, [_vp]),
@@ -213,6 +214,19 @@ def argmax(logits):
     import torch
     out = torch.empty(1, dtype=torch.int64, device=logits.device)
     _check(load().sq_argmax(_stream(), _p(logits), logits.numel(), _p(out)))
+    return out
+
+
+ARGMAX_NOALLOC_MAX_N = 1 << 24
+
+
+def argmax_noalloc(logits, out=None):
+    """sq_argmax_noalloc: the argmax without device allocation inside the call
+    (n <= ARGMAX_NOALLOC_MAX_N); `out` may be a caller-owned int64 device tensor."""
+    import torch
+    if out is None:
+        out = torch.empty(1, dtype=torch.int64, device=logits.device)
+    _check(load().sq_argmax_noalloc(_stream(), _p(logits), logits.numel(), _p(out)))
     return out
 
 
