@@ -42,6 +42,7 @@ constexpr int NC = 8;                    // warps per CTA (2 per SM sub-partitio
 constexpr int NTHREADS = NC * 32;
 constexpr int SLOT = 36864;              // bytes per ring slot
 constexpr int NSLOT = 5;
+constexpr int PF_TILES = 12;             // tiles prefetched into L2 beyond the ring
 constexpr int MAX_LAYERS = 128;
 constexpr int MAX_TILE_ITEMS = 256;      // rows x segments per tile
 constexpr int MAX_X = 8192;              // longest stage input staged in shared memory (floats)
@@ -77,6 +78,7 @@ struct Params {
   int2 *tiles;                   // [G][max_tiles] tile table: {row, layer<<16 | kind<<12 | rows}
   int *ntiles;                   // [G]
   int max_tiles;
+  int pf;                        // L2 prefetch distance in tiles beyond the ring (0 = off)
   LayerW layers[MAX_LAYERS];
 };
 
@@ -127,6 +129,24 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+// The same copy with an L2 eviction-priority policy for the lines it reads.
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// Prefetch [src, src + bytes) into L2 (no completion to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ uint32_t lds32(uint32_t a) {
   uint32_t v;
@@ -360,7 +380,8 @@ struct AttScratch {
 struct Smem {
   float red[2][MAX_TILE_ITEMS];
   union {
-    float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index)
+    float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index): BF16 stages
+    uint32_t xd[MAX_X];  // the stage input as digits (see stage_digits): Q8_0 / Q4_0 stages
     AttScratch at;    // attention-stage partials (a different phase of the layer)
   };
   float ssp[NC];      // per-warp partial squared sums of the RMS norm
@@ -555,23 +576,346 @@ __device__ __forceinline__ void x_from_smem(float (&x)[64], const Smem &sm, int 
   }
 }
 
-// Issue tile j of this CTA's table into `slot`: one or more bulk copies completing
-// on full[slot]. Rows of a QKV tile may span Wq / Wk / Wv; a gate/up tile carries
-// its gate rows, then the same rows of Wup.
-__device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
-  const int2 d = tbl[j];
+// ---------------------------------------------------------------------------------
+// Q8_0 / Q4_0 stage inputs as int8 digits (integer dot products against the blocks)
+// ---------------------------------------------------------------------------------
+// Each 32-element block of the f32 input x is written as x = sx * (d0 + d1/254 +
+// d2/254^2) with int8 digits d0, d1, d2 in [-127, 127] and sx = amax/127: about 23
+// significant bits of the block's largest element, the precision of an f32 value.
+// A weight block then needs three integer dot products (dp4a, exact int32), one
+// per digit, and one float combination per block:
+//   sum_i w_i x_i = sw * (sx * I0 + (sx/254^2) * (254*I1 + I2))
+// instead of a byte-to-float conversion and an FMA per element. The reference
+// sums q_i * x_i in f32 per block, then scales (dot_prod.rs:86-96, 255-270); the
+// result here differs from that only by f32-level rounding.
+//
+// Shared-memory layout: for each lane of each 2048-element segment, XDW words:
+// the lane's digit words laid out byte for byte against the lane's weight words
+// (a Q8_0 block pair is 17 words: the first block's 32 quants start at byte 2,
+// the second's at byte 36; zero digits sit under the scale bytes), then per-block
+// constants. XDW = 60 words keeps the 16-byte loads of 8 lanes on distinct banks.
+constexpr int XDW = 60;
+constexpr float DIGIT_BASE = 254.0f;
+constexpr float INV_BASE2 = 1.0f / (254.0f * 254.0f);
+template <int T>
+constexpr int ndigw() {  // digit words per lane
+  return T == SQ_Q8_0 ? 51 : 54;
+}
+// Q8_0: digit d word k (k = 0..16) at d*17 + k; sx of block a / b at 51 / 52.
+// Q4_0: digit d low-nibble word k (k = 0..8) at d*18 + k, high-nibble word at
+// d*18 + 9 + k; sx at 54 / 55; K0 = 8*S0 at 56 / 58 and KJ = 8*(254*S1 + S2) at
+// 57 / 59, where S_d is the block's sum of digit d (Q4_0 values are q - 8, the
+// integer dots use q: sum (q-8)*d = sum q*d - 8*S_d).
+static_assert(XDW * 32 * (MAX_X / 2048) <= MAX_X, "digit staging fits the input buffer");
+
+template <int T>
+struct ActRegs;
+template <>
+struct ActRegs<SQ_BF16> {
+  float x[64];
+};
+template <>
+struct ActRegs<SQ_Q8_0> {
+  uint32_t d[51];
+  float c0a, c0b, c2a, c2b;
+};
+template <>
+struct ActRegs<SQ_Q4_0> {
+  uint32_t d[54];
+  float c0a, c0b, c2a, c2b;
+  int k0a, kja, k0b, kjb;
+};
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm((unsigned)a, (unsigned)b, 0x0040), __byte_perm((unsigned)c, (unsigned)d, 0x0040),
+                     0x5410);
+}
+
+// Stage the n-element input of a Q8_0 / Q4_0 stage as digits in sm.xd (modes as
+// stage_x: XS_PLAIN the tagged vector v, XS_NORM / XS_EMBED with the RMS norm,
+// rms_norm.rs:40-56, x = (h*w) * (1/rms)). Thread t takes 8 consecutive elements
+// per pass (four threads a block); the squared sum is combined in a fixed order,
+// so every CTA computes the same rms.
+template <int T, int MODE>
+__device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
+                             const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int nseg) {
+  constexpr int NT = NC * 32, MAXP = MAX_X / (NT * 8);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = n / 8;
+  float h[MAXP][8];
+  float ss = 0.f;
+  if constexpr (MODE == XS_EMBED) {
+#pragma unroll
+    for (int k = 0; k < MAXP; k++) {
+      const int g = k * NT + tid;
+#pragma unroll
+      for (int i = 0; i < 8; i++) h[k][i] = 0.f;
+      if (g < ng) {
+        const int e = g * 8, b = e >> 5, j0 = e & 31;
+        if constexpr (T == SQ_Q8_0) {
+          const uint8_t *blk = emb_row + (size_t)b * Q8_BYTES;
+          const float sc = h2f(ld_u16(blk));
+#pragma unroll
+          for (int i = 0; i < 8; i++) h[k][i] = sc * (float)(int8_t)__ldg(blk + 2 + j0 + i);
+        } else {
+          const uint8_t *blk = emb_row + (size_t)b * Q4_BYTES;
+          const float sc = h2f(ld_u16(blk));
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const uint8_t byte = __ldg(blk + 2 + ((j0 + i) & 15));
+            h[k][i] = sc * (float)((j0 < 16 ? (byte & 0x0F) : (byte >> 4)) - 8);
+          }
+        }
+        if (write_hidden) {
+#pragma unroll
+          for (int i = 0; i < 8; i++) st_ll(p.hid_ll + e + i, h[k][i], emb_tag);
+        }
+      }
+    }
+  } else {
+    ulonglong2 c[MAXP][4];  // every load of this thread in flight before any use
+#pragma unroll
+    for (int k = 0; k < MAXP; k++) {
+      const int g = k * NT + tid;
+#pragma unroll
+      for (int i = 0; i < 4; i++) c[k][i] = g < ng ? ld_ll2(v + 8 * g + 2 * i) : make_ulonglong2(0ull, 0ull);
+    }
+#pragma unroll
+    for (int k = 0; k < MAXP; k++) {
+      const int g = k * NT + tid;
+#pragma unroll
+      for (int i = 0; i < 8; i++) h[k][i] = 0.f;
+      if (g < ng) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          if (!ll_ok(c[k][i].x, tag)) c[k][i].x = ll_wait(p, v + 8 * g + 2 * i, tag);
+          if (!ll_ok(c[k][i].y, tag)) c[k][i].y = ll_wait(p, v + 8 * g + 2 * i + 1, tag);
+          h[k][2 * i] = ll_val(c[k][i].x);
+          h[k][2 * i + 1] = ll_val(c[k][i].y);
+        }
+      }
+    }
+  }
+  if constexpr (MODE != XS_PLAIN) {
+#pragma unroll
+    for (int k = 0; k < MAXP; k++) {
+      const int g = k * NT + tid;
+      if (g < ng) {
+        const float4 w0 = ldnc4(w + 8 * g), w1 = ldnc4(w + 8 * g + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          ss = fmaf(h[k][i], h[k][i], ss);
+          h[k][i] = __fmul_rn(h[k][i], wv[i]);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) sm.ssp[warp] = ss;
+  }
+  cta_sync();  // the squared sums are in; every warp is done with the previous input
+  float scale = 1.0f;
+  if constexpr (MODE != XS_PLAIN) {
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NC; k++) tot += sm.ssp[k];
+    scale = 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
+  }
+  const int ngs = nseg * 256;  // groups of the staged segments (the tail is zero-filled)
+  const int q = tid & 3;       // quarter of the block
+#pragma unroll
+  for (int k = 0; k < MAXP; k++) {
+    const int g = k * NT + tid;
+    if (k * NT >= ngs) break;  // warp-uniform: whole passes
+    float x[8], amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      x[i] = MODE == XS_PLAIN ? h[k][i] : __fmul_rn(h[k][i], scale);
+      amax = fmaxf(amax, fabsf(x[i]));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 2));
+    const float sx = __fdiv_rn(amax, 127.0f);
+    const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+    int dg[3][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float t = x[i] * inv;
+      const float r0 = rintf(t);
+      const float t1 = (t - r0) * DIGIT_BASE;
+      const float r1 = rintf(t1);
+      const float r2 = rintf((t1 - r1) * DIGIT_BASE);
+      dg[0][i] = (int)r0;
+      dg[1][i] = (int)r1;
+      dg[2][i] = (int)r2;
+    }
+    uint32_t D[3][2], prev[3];
+#pragma unroll
+    for (int d = 0; d < 3; d++) {
+      D[d][0] = pack4(dg[d][0], dg[d][1], dg[d][2], dg[d][3]);
+      D[d][1] = pack4(dg[d][4], dg[d][5], dg[d][6], dg[d][7]);
+      prev[d] = __shfl_up_sync(FULL, D[d][1], 1);
+    }
+    int S[3] = {0, 0, 0};
+    if constexpr (T == SQ_Q4_0) {
+#pragma unroll
+      for (int d = 0; d < 3; d++) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) S[d] += dg[d][i];
+        S[d] += __shfl_xor_sync(FULL, S[d], 1);
+        S[d] += __shfl_xor_sync(FULL, S[d], 2);
+      }
+    }
+    if (g < ngs) {
+      const int b = g >> 2, seg = b >> 6, ln = (b & 63) >> 1, par = b & 1;
+      uint32_t *reg = sm.xd + (seg * 32 + ln) * XDW;
+      if constexpr (T == SQ_Q8_0) {
+#pragma unroll
+        for (int d = 0; d < 3; d++) {
+          uint32_t *r = reg + d * 17;
+          if (par) {
+            r[9 + 2 * q] = D[d][0];
+            r[10 + 2 * q] = D[d][1];
+          } else {
+            r[2 * q] = __byte_perm(q ? prev[d] : 0u, D[d][0], 0x5432);
+            r[2 * q + 1] = __byte_perm(D[d][0], D[d][1], 0x5432);
+            if (q == 3) r[8] = __byte_perm(D[d][1], 0u, 0x5432);
+          }
+        }
+        if (q == 0) reg[51 + par] = __float_as_uint(sx);
+      } else {
+        const int half = q & 1;  // which 8 of the 16 bytes; q >= 2: the high nibbles
+#pragma unroll
+        for (int d = 0; d < 3; d++) {
+          uint32_t *r = reg + d * 18 + (q >= 2 ? 9 : 0);
+          if (par) {
+            r[5 + 2 * half] = D[d][0];
+            r[6 + 2 * half] = D[d][1];
+          } else {
+            r[2 * half] = __byte_perm(half ? prev[d] : 0u, D[d][0], 0x5432);
+            r[2 * half + 1] = __byte_perm(D[d][0], D[d][1], 0x5432);
+            if (half) r[4] = __byte_perm(D[d][1], 0u, 0x5432);
+          }
+        }
+        if (q == 0) {
+          reg[54 + par] = __float_as_uint(sx);
+          reg[56 + 2 * par] = (uint32_t)(8 * S[0]);
+          reg[57 + 2 * par] = (uint32_t)(8 * (254 * S[1] + S[2]));
+        }
+      }
+    }
+  }
+  cta_sync();
+}
+
+// This warp's activation registers from the staged input.
+template <int T>
+__device__ __forceinline__ void act_from_smem(ActRegs<T> &a, const Smem &sm, int seg, int lane, int n, float scale) {
+  if constexpr (T == SQ_BF16) {
+    x_from_smem<T>(a.x, sm, seg, lane, n, scale);
+  } else {
+    const uint4 *src = reinterpret_cast<const uint4 *>(sm.xd + (seg * 32 + lane) * XDW);
+    uint32_t wv[XDW];
+#pragma unroll
+    for (int k = 0; k < XDW / 4; k++) {
+      const uint4 u = src[k];
+      wv[4 * k] = u.x;
+      wv[4 * k + 1] = u.y;
+      wv[4 * k + 2] = u.z;
+      wv[4 * k + 3] = u.w;
+    }
+    constexpr int ND = ndigw<T>();
+#pragma unroll
+    for (int k = 0; k < ND; k++) a.d[k] = wv[k];
+    a.c0a = __uint_as_float(wv[ND]);
+    a.c0b = __uint_as_float(wv[ND + 1]);
+    a.c2a = a.c0a * INV_BASE2;
+    a.c2b = a.c0b * INV_BASE2;
+    if constexpr (T == SQ_Q4_0) {
+      a.k0a = (int)wv[56];
+      a.kja = (int)wv[57];
+      a.k0b = (int)wv[58];
+      a.kjb = (int)wv[59];
+    }
+  }
+}
+
+// Stage a stage's input and load this warp's activation registers: f32 values for
+// BF16 weights, digits for Q8_0 / Q4_0.
+template <int T, int MODE>
+__device__ __forceinline__ void stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
+                                         unsigned tag, const float *w, int n, int nseg, const uint8_t *emb_row = nullptr,
+                                         bool write_hidden = false, unsigned emb_tag = 0u) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (T == SQ_BF16) {
+    const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag);
+    x_from_smem<T>(x.x, sm, warp % nseg, lane, n, sc);
+  } else {
+    stage_digits<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, nseg);
+    act_from_smem<T>(x, sm, warp % nseg, lane, n, 1.0f);
+  }
+}
+
+// Dot of the lane's block pair of one weight row with the digit registers.
+__device__ __forceinline__ float lane_dot_digits(const uint32_t (&w)[17], const ActRegs<SQ_Q8_0> &a) {
+  int i0 = 0, i1 = 0, i2 = 0, j0 = 0, j1 = 0, j2 = 0;
+#pragma unroll
+  for (int k = 0; k < 9; k++) {  // block a: words 0..8 (scale bytes meet zero digits)
+    i0 = __dp4a((int)w[k], (int)a.d[k], i0);
+    i1 = __dp4a((int)w[k], (int)a.d[17 + k], i1);
+    i2 = __dp4a((int)w[k], (int)a.d[34 + k], i2);
+  }
+#pragma unroll
+  for (int k = 9; k < 17; k++) {  // block b: words 9..16
+    j0 = __dp4a((int)w[k], (int)a.d[k], j0);
+    j1 = __dp4a((int)w[k], (int)a.d[17 + k], j1);
+    j2 = __dp4a((int)w[k], (int)a.d[34 + k], j2);
+  }
+  const float sa = h2f((uint16_t)(w[0] & 0xFFFF)), sb = h2f((uint16_t)(w[8] >> 16));
+  const float ba = fmaf((float)(254 * i1 + i2), a.c2a, (float)i0 * a.c0a);
+  const float bb = fmaf((float)(254 * j1 + j2), a.c2b, (float)j0 * a.c0b);
+  return fmaf(ba, sa, bb * sb);
+}
+__device__ __forceinline__ float lane_dot_digits(const uint32_t (&w)[9], const ActRegs<SQ_Q4_0> &a) {
+  int i0 = 0, i1 = 0, i2 = 0, j0 = 0, j1 = 0, j2 = 0;
+#pragma unroll
+  for (int k = 0; k < 9; k++) {
+    const int lo = (int)(w[k] & 0x0F0F0F0Fu), hi = (int)((w[k] >> 4) & 0x0F0F0F0Fu);
+    if (k < 5) {  // block a: words 0..4
+      i0 = __dp4a(lo, (int)a.d[k], __dp4a(hi, (int)a.d[9 + k], i0));
+      i1 = __dp4a(lo, (int)a.d[18 + k], __dp4a(hi, (int)a.d[27 + k], i1));
+      i2 = __dp4a(lo, (int)a.d[36 + k], __dp4a(hi, (int)a.d[45 + k], i2));
+    } else {      // block b: words 5..8
+      j0 = __dp4a(lo, (int)a.d[k], __dp4a(hi, (int)a.d[9 + k], j0));
+      j1 = __dp4a(lo, (int)a.d[18 + k], __dp4a(hi, (int)a.d[27 + k], j1));
+      j2 = __dp4a(lo, (int)a.d[36 + k], __dp4a(hi, (int)a.d[45 + k], j2));
+    }
+  }
+  const float sa = h2f((uint16_t)(w[0] & 0xFFFF)), sb = h2f((uint16_t)(w[4] >> 16));
+  const float ba = fmaf((float)(254 * i1 + i2 - a.kja), a.c2a, (float)(i0 - a.k0a) * a.c0a);
+  const float bb = fmaf((float)(254 * j1 + j2 - a.kjb), a.c2b, (float)(j0 - a.k0b) * a.c0b);
+  return fmaf(ba, sa, bb * sb);
+}
+template <int T>
+__device__ __forceinline__ float lane_dot(const uint32_t (&w)[nwords<T>()], const ActRegs<T> &a) {
+  if constexpr (T == SQ_BF16) return lane_dot<T>(w, a.x);
+  else return lane_dot_digits(w, a);
+}
+
+// The bulk copies of tile entry d: f(byte offset in the slot, global source, bytes).
+// Rows of a QKV tile may span Wq / Wk / Wv; a gate/up tile carries its gate rows,
+// then the same rows of Wup. Returns the tile's total bytes.
+template <class F>
+__device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) {
   const int r = d.x, n = d.y & 0xFFF, kind = (d.y >> 12) & 0xF, l = d.y >> 16;
   const int rb = stage_rb(p, kind);
-  uint8_t *dst = rg.slots + (size_t)slot * SLOT;
-  uint64_t *bar = &rg.full[slot];
   const LayerW &W = p.layers[l < p.L ? l : 0];
-  sm.issued[slot]++;
   if (kind == ST_GU) {
-    mbar_expect_tx(bar, 2u * n * rb);
-    bulk_g2s(dst, W.gate + (size_t)r * rb, n * rb, bar);
-    bulk_g2s(dst + (size_t)n * rb, W.up + (size_t)r * rb, n * rb, bar);
-  } else if (kind == ST_QKV) {
-    mbar_expect_tx(bar, (unsigned)n * rb);
+    f(0u, W.gate + (size_t)r * rb, (unsigned)(n * rb));
+    f((unsigned)(n * rb), W.up + (size_t)r * rb, (unsigned)(n * rb));
+    return 2u * n * rb;
+  }
+  if (kind == ST_QKV) {
     int a = r, off = 0;
     const int bounds[3] = {p.Q, p.Q + p.KVd, p.Q + 2 * p.KVd};
     const uint8_t *base[3] = {W.q, W.k, W.v};
@@ -580,16 +924,39 @@ __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2
     for (int t = 0; t < 3; t++) {
       const int hi = min(r + n, bounds[t]);
       if (a < hi) {
-        bulk_g2s(dst + (size_t)off * rb, base[t] + (size_t)(a - start[t]) * rb, (hi - a) * rb, bar);
+        f((unsigned)(off * rb), base[t] + (size_t)(a - start[t]) * rb, (unsigned)((hi - a) * rb));
         off += hi - a;
         a = hi;
       }
     }
-  } else {
-    const uint8_t *src = kind == ST_O ? W.o : (kind == ST_DOWN ? W.down : p.out_w);
-    mbar_expect_tx(bar, (unsigned)n * rb);
-    bulk_g2s(dst, src + (size_t)r * rb, n * rb, bar);
+    return (unsigned)(n * rb);
   }
+  const uint8_t *src = kind == ST_O ? W.o : (kind == ST_DOWN ? W.down : p.out_w);
+  f(0u, src + (size_t)r * rb, (unsigned)(n * rb));
+  return (unsigned)(n * rb);
+}
+
+// Issue tile j of this CTA's table into `slot`: bulk copies completing on full[slot].
+// The weights are read once per token, so the copies mark their L2 lines
+// evict-first; what the L2 keeps is the prefetched tiles not yet consumed.
+__device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
+  const int2 d = tbl[j];
+  uint8_t *dst = rg.slots + (size_t)slot * SLOT;
+  uint64_t *bar = &rg.full[slot];
+  sm.issued[slot]++;
+  const int n = d.y & 0xFFF, kind = (d.y >> 12) & 0xF;
+  mbar_expect_tx(bar, (kind == ST_GU ? 2u : 1u) * n * stage_rb(p, kind));
+  const uint64_t pol = policy_evict_first();
+  tile_copies(p, d, [&](unsigned off, const uint8_t *src, unsigned bytes) { bulk_g2s_hint(dst + off, src, bytes, bar, pol); });
+}
+
+// Bring tile j (modulo the table: past the end come the next token's first tiles)
+// into L2 ahead of its ring copy, so HBM keeps streaming while the warps wait for
+// other CTAs between stages.
+__device__ __forceinline__ void prefetch_tile(const Params &p, const Smem &sm, const int2 *tbl, int j) {
+  if (j >= sm.ntiles) j -= sm.ntiles;
+  if (j < 0 || j >= sm.ntiles) return;
+  tile_copies(p, tbl[j], [&](unsigned, const uint8_t *src, unsigned bytes) { bulk_prefetch_l2(src, bytes); });
 }
 
 // A warp is done reading tile `k` in `slot`; the last of the NC warps refills the
@@ -601,6 +968,7 @@ __device__ __forceinline__ void release_slot(const Params &p, const Ring &rg, Sm
     if (atomicAdd(&sm.rel[slot], 1) == NC - 1) {
       sm.rel[slot] = 0;
       if (k + NSLOT < sm.ntiles) issue_tile(p, rg, sm, tbl, k + NSLOT, slot);
+      if (p.pf > 0) prefetch_tile(p, sm, tbl, k + NSLOT + p.pf);
     }
   }
 }
@@ -673,7 +1041,7 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, in
 // dot two rows at a time per warp, finish the rows, release the slot.
 template <int T, int KIND>
 __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int l,
-                             const float (&x)[64], int &slot, unsigned &phase, int &tile_ctr, int pos,
+                             const ActRegs<T> &x, int &slot, unsigned &phase, int &tile_ctr, int pos,
                              const StageRegs &sr, unsigned tag) {
   constexpr int NW = nwords<T>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1055,8 +1423,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const unsigned tb = (unsigned)((nt * 8 + 15) & ~15);
     mbar_expect_tx(tbl_bar, tb);
     bulk_g2s(tbl, p.tiles + (size_t)blockIdx.x * p.max_tiles, tb, tbl_bar);
-    if (mbar_wait(tbl_bar, 0, p.err))
+    if (mbar_wait(tbl_bar, 0, p.err)) {
       for (int j = 0; j < NSLOT && j < nt; j++) issue_tile(p, rg, sm, tbl, j, j);
+      for (int j = NSLOT; j < NSLOT + p.pf && j < nt; j++) prefetch_tile(p, sm, tbl, j);
+    }
   }
   __syncthreads();
   const int pos = *p.pos;
@@ -1064,20 +1434,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const unsigned launch = *p.launch;
   int slot = 0, tile_ctr = 0;
   unsigned phase = 0;
-  float x[64];
+  ActRegs<T> x;
   StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
   for (int l = 0; l < p.L; l++) {
     const LayerW &W = p.layers[l];
-    const int segE = warp % p.nseg_E;
     const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
     // ---- RMSNorm + QKV + RoPE + KV append
     load_stage_regs(p, ST_QKV, l, pos, sr, 0u);
-    {
-      const float sc = l == 0 ? stage_x<T, XS_EMBED>(p, sm, nullptr, 0u, W.attn_norm, p.E, p.embd + (size_t)tok * p.rb_E,
-                                                     blockIdx.x == 0, hid_in)
-                              : stage_x<T, XS_NORM>(p, sm, p.hid_ll, hid_in, W.attn_norm, p.E, nullptr, false, 0u);
-      x_from_smem<T>(x, sm, segE, lane, p.E, sc);
-    }
+    if (l == 0)
+      stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, p.embd + (size_t)tok * p.rb_E,
+                            blockIdx.x == 0, hid_in);
+    else
+      stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E);
     stamp(p, 8 * (5 * l) + 2);
     matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_QKV));
     // ---- attention (waits on q / K / V words, not on a barrier)
@@ -1087,34 +1455,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     stamp(p, 8 * (5 * l + 1) + 6);
     // ---- O projection + residual
     load_stage_regs(p, ST_O, l, pos, sr, hid_in);
-    stage_x<T, XS_PLAIN>(p, sm, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, nullptr, false, 0u);
-    x_from_smem<T>(x, sm, warp % p.nseg_Q, lane, p.Q, 1.0f);
+    stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q);
     stamp(p, 8 * (5 * l + 2) + 2);
     matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_O));
     // ---- RMSNorm + gate/up + SiLU*up
-    {
-      cta_sync();
-      const float sc = stage_x<T, XS_NORM>(p, sm, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, nullptr,
-                                           false, 0u);
-      x_from_smem<T>(x, sm, segE, lane, p.E, sc);
-    }
+    cta_sync();
+    stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, p.nseg_E);
     stamp(p, 8 * (5 * l + 3) + 2);
     matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_ACT));
     // ---- down + residual
     load_stage_regs(p, ST_DOWN, l, pos, sr, mk_tag(launch, l, TG_POST_O));
     cta_sync();
-    stage_x<T, XS_PLAIN>(p, sm, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, nullptr, false, 0u);
-    x_from_smem<T>(x, sm, warp % p.nseg_F, lane, p.F, 1.0f);
+    stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F);
     stamp(p, 8 * (5 * l + 4) + 2);
     matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_DOWN));
     cta_sync();
   }
   // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
-  {
-    const float sc = stage_x<T, XS_NORM>(p, sm, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E,
-                                         nullptr, false, 0u);
-    x_from_smem<T>(x, sm, warp % p.nseg_E, lane, p.E, sc);
-  }
+  stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E, p.nseg_E);
   stamp(p, 8 * (5 * p.L) + 2);
   matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr, 0u);
   cta_sync();
@@ -1342,6 +1700,8 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(alloc((void **)&h.arg_part, (size_t)nsm * sizeof(ArgState)));
   SQ_CUDA(alloc((void **)&h.pos, 4));
   SQ_CUDA(alloc((void **)&st->d_params, sizeof(dk::Params)));
+  h.pf = dk::PF_TILES;
+  if (const char *pf = getenv("SQ_DECODE_L2_PREFETCH")) h.pf = std::max(0, std::min(atoi(pf), 256));  // tuning
   if (const char *tl = getenv("SQ_DECODE_TIMELINE")) {  // opt-in stage timestamps
     st->tl_path = tl;
     st->tl_stride = 8 * (5 * cf.n_blocks + 1) + 4;
