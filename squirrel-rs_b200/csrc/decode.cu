@@ -175,10 +175,24 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 // Timeline slot k of this CTA: 0 = start; for stage s (5 per layer, the LM head is
-// stage 5L) 8s+2 = input staged, 8s+4 / 8s+5 = first / last tile landed, 8s+6 =
-// stage done; stride-2 = LM head done, stride-1 = end.
+// stage 5L) 8s+1 = input words arrived, 8s+3 = input digits written, 8s+2 = input
+// staged in registers, 8s+4 / 8s+5 = first / last tile landed, 8s+6 = stage done;
+// stride-2 = LM head done, stride-1 = end. Stamps are SM clock counts; each CTA
+// also records one (global ns, clock) pair at a tick of the global timer at start
+// and at end (slots stride-6..stride-3), which maps its clocks onto global time
+// more finely than the timer's own resolution.
 __device__ __forceinline__ void stamp(const Params &p, int k) {
-  if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = global_ns();
+  if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = (unsigned long long)clock64();
+}
+__device__ __forceinline__ void stamp_sync(const Params &p, int k) {
+  if (p.timeline && threadIdx.x == 0) {
+    const unsigned long long g0 = global_ns();
+    unsigned long long g = g0;
+    for (int it = 0; it < 1000000 && g == g0; it++) g = global_ns();  // the next tick
+    const long long c = clock64();
+    p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = g;
+    p.timeline[(size_t)blockIdx.x * p.tl_stride + k + 1] = (unsigned long long)c;
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -424,6 +438,17 @@ __device__ __forceinline__ ulonglong2 ld_ll2(const unsigned long long *a) {  // 
 __device__ __forceinline__ bool ll_ok(unsigned long long w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
 __device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
 
+// A bounded poll gives up when another CTA failed or after WAIT_LIMIT clocks (then
+// it sets the error flag).
+__device__ __forceinline__ bool poll_expired(const Params &p, long long t0) {
+  if (ld_volatile(p.err)) return true;
+  if (clock64() - t0 > WAIT_LIMIT) {
+    atomicExch(p.err, 3u);
+    return true;
+  }
+  return false;
+}
+
 // Re-read one word until it carries `tag` (bounded: on expiry the error flag is set
 // and 0 returned).
 __device__ __noinline__ unsigned long long ll_wait(const Params &p, const unsigned long long *a, unsigned tag) {
@@ -444,6 +469,28 @@ __device__ __forceinline__ float poll_ll(const Params &p, const unsigned long lo
   unsigned long long w = ld_ll(a);
   if (!ll_ok(w, tag)) w = ll_wait(p, a, tag);
   return ll_val(w);
+}
+// N words at once: every stale word is re-read in the same pass, so a retry costs
+// one L2 round trip however many words are still missing.
+template <int N>
+__device__ __forceinline__ void poll_ll_n(const Params &p, const unsigned long long *const (&a)[N], unsigned tag,
+                                          float (&out)[N]) {
+  unsigned long long w[N];
+#pragma unroll
+  for (int i = 0; i < N; i++) w[i] = ld_ll(a[i]);
+  const long long t0 = clock64();
+  for (unsigned it = 0;; it++) {
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; i++) all = all && ll_ok(w[i], tag);
+    if (all) break;
+#pragma unroll
+    for (int i = 0; i < N; i++)
+      if (!ll_ok(w[i], tag)) w[i] = ld_ll(a[i]);
+    if ((it & 15u) == 15u && poll_expired(p, t0)) break;
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++) out[i] = ll_val(w[i]);
 }
 
 // ---- stage inputs: one cooperative load per CTA into shared memory -------------
@@ -531,12 +578,24 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
       c[k] = ci < nc ? ld_ll2(v + 2 * ci) : make_ulonglong2(0ull, 0ull);
       if (MODE == XS_NORM) wv[k] = ci < nc ? *reinterpret_cast<const float2 *>(w + 2 * ci) : make_float2(0.f, 0.f);
     }
+    const long long t0 = clock64();
+    for (unsigned it = 0;; it++) {  // re-read all stale pairs together
+      bool all = true;
+#pragma unroll
+      for (int k = 0; k < MAXC; k++)
+        if (k * NC * 32 + tid < nc && !(ll_ok(c[k].x, tag) && ll_ok(c[k].y, tag))) all = false;
+      if (all) break;
+#pragma unroll
+      for (int k = 0; k < MAXC; k++) {
+        const int ci = k * NC * 32 + tid;
+        if (ci < nc && !(ll_ok(c[k].x, tag) && ll_ok(c[k].y, tag))) c[k] = ld_ll2(v + 2 * ci);
+      }
+      if ((it & 15u) == 15u && poll_expired(p, t0)) break;
+    }
 #pragma unroll
     for (int k = 0; k < MAXC; k++) {
       const int ci = k * NC * 32 + tid;
       if (ci < nc) {
-        if (!ll_ok(c[k].x, tag)) c[k].x = ll_wait(p, v + 2 * ci, tag);
-        if (!ll_ok(c[k].y, tag)) c[k].y = ll_wait(p, v + 2 * ci + 1, tag);
         float a = ll_val(c[k].x), b = ll_val(c[k].y);
         if (MODE == XS_NORM) {
           ss = fmaf(a, a, ss);
@@ -626,9 +685,9 @@ struct ActRegs<SQ_Q4_0> {
   int k0a, kja, k0b, kjb;
 };
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return __byte_perm(__byte_perm((unsigned)a, (unsigned)b, 0x0040), __byte_perm((unsigned)c, (unsigned)d, 0x0040),
-                     0x5410);
+// The low bytes of four words, in order.
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // Stage the n-element input of a Q8_0 / Q4_0 stage as digits in sm.xd (modes as
@@ -638,7 +697,7 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 // so every CTA computes the same rms.
 template <int T, int MODE>
 __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
-                             const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int nseg) {
+                             const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int nseg, int stamp_at) {
   constexpr int NT = NC * 32, MAXP = MAX_X / (NT * 8);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ng = n / 8;
@@ -680,19 +739,33 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
 #pragma unroll
       for (int i = 0; i < 4; i++) c[k][i] = g < ng ? ld_ll2(v + 8 * g + 2 * i) : make_ulonglong2(0ull, 0ull);
     }
+    // until every word carries the tag: re-read all stale pairs together (one L2
+    // round trip per retry, not one per word)
+    const long long t0 = clock64();
+    for (unsigned it = 0;; it++) {
+      bool all = true;
+#pragma unroll
+      for (int k = 0; k < MAXP; k++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          if (k * NT + tid < ng && !(ll_ok(c[k][i].x, tag) && ll_ok(c[k][i].y, tag))) all = false;
+      if (all) break;
+#pragma unroll
+      for (int k = 0; k < MAXP; k++) {
+        const int g = k * NT + tid;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          if (g < ng && !(ll_ok(c[k][i].x, tag) && ll_ok(c[k][i].y, tag))) c[k][i] = ld_ll2(v + 8 * g + 2 * i);
+      }
+      if ((it & 15u) == 15u && poll_expired(p, t0)) break;
+    }
 #pragma unroll
     for (int k = 0; k < MAXP; k++) {
       const int g = k * NT + tid;
 #pragma unroll
-      for (int i = 0; i < 8; i++) h[k][i] = 0.f;
-      if (g < ng) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          if (!ll_ok(c[k][i].x, tag)) c[k][i].x = ll_wait(p, v + 8 * g + 2 * i, tag);
-          if (!ll_ok(c[k][i].y, tag)) c[k][i].y = ll_wait(p, v + 8 * g + 2 * i + 1, tag);
-          h[k][2 * i] = ll_val(c[k][i].x);
-          h[k][2 * i + 1] = ll_val(c[k][i].y);
-        }
+      for (int i = 0; i < 4; i++) {
+        h[k][2 * i] = g < ng ? ll_val(c[k][i].x) : 0.f;
+        h[k][2 * i + 1] = g < ng ? ll_val(c[k][i].y) : 0.f;
       }
     }
   }
@@ -714,6 +787,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
     if (lane == 0) sm.ssp[warp] = ss;
   }
   cta_sync();  // the squared sums are in; every warp is done with the previous input
+  if (stamp_at >= 0) stamp(p, stamp_at);
   float scale = 1.0f;
   if constexpr (MODE != XS_PLAIN) {
     float tot = 0.f;
@@ -735,25 +809,28 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
     }
     amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 2));
-    const float sx = __fdiv_rn(amax, 127.0f);
-    const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-    int dg[3][8];
+    // t = x/sx in [-127, 127]; each digit is rounded to nearest by adding 1.5*2^23
+    // (the sum's low mantissa bits are the integer, its low byte the int8 digit)
+    const float sx = amax * (1.0f / 127.0f);
+    const float inv = amax > 0.f ? 127.0f * __frcp_rn(amax) : 0.f;
+    constexpr float MAGIC = 12582912.0f;
+    uint32_t mg[3][8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       const float t = x[i] * inv;
-      const float r0 = rintf(t);
-      const float t1 = (t - r0) * DIGIT_BASE;
-      const float r1 = rintf(t1);
-      const float r2 = rintf((t1 - r1) * DIGIT_BASE);
-      dg[0][i] = (int)r0;
-      dg[1][i] = (int)r1;
-      dg[2][i] = (int)r2;
+      const float m0 = t + MAGIC, r0 = m0 - MAGIC;
+      const float t1 = fmaf(t, DIGIT_BASE, r0 * -DIGIT_BASE);  // (t - r0) * 254, one rounding
+      const float m1 = t1 + MAGIC, r1 = m1 - MAGIC;
+      const float m2 = fmaf(t1 - r1, DIGIT_BASE, MAGIC);
+      mg[0][i] = __float_as_uint(m0);
+      mg[1][i] = __float_as_uint(m1);
+      mg[2][i] = __float_as_uint(m2);
     }
     uint32_t D[3][2], prev[3];
 #pragma unroll
     for (int d = 0; d < 3; d++) {
-      D[d][0] = pack4(dg[d][0], dg[d][1], dg[d][2], dg[d][3]);
-      D[d][1] = pack4(dg[d][4], dg[d][5], dg[d][6], dg[d][7]);
+      D[d][0] = pack4(mg[d][0], mg[d][1], mg[d][2], mg[d][3]);
+      D[d][1] = pack4(mg[d][4], mg[d][5], mg[d][6], mg[d][7]);
       prev[d] = __shfl_up_sync(FULL, D[d][1], 1);
     }
     int S[3] = {0, 0, 0};
@@ -761,7 +838,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
 #pragma unroll
       for (int d = 0; d < 3; d++) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) S[d] += dg[d][i];
+        for (int i = 0; i < 8; i++) S[d] += (int)(mg[d][i] - 0x4B400000u);
         S[d] += __shfl_xor_sync(FULL, S[d], 1);
         S[d] += __shfl_xor_sync(FULL, S[d], 2);
       }
@@ -806,6 +883,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
     }
   }
   cta_sync();
+  if (stamp_at >= 0) stamp(p, stamp_at + 2);
 }
 
 // This warp's activation registers from the staged input.
@@ -844,14 +922,15 @@ __device__ __forceinline__ void act_from_smem(ActRegs<T> &a, const Smem &sm, int
 // BF16 weights, digits for Q8_0 / Q4_0.
 template <int T, int MODE>
 __device__ __forceinline__ void stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
-                                         unsigned tag, const float *w, int n, int nseg, const uint8_t *emb_row = nullptr,
-                                         bool write_hidden = false, unsigned emb_tag = 0u) {
+                                         unsigned tag, const float *w, int n, int nseg, int stamp_at,
+                                         const uint8_t *emb_row = nullptr, bool write_hidden = false,
+                                         unsigned emb_tag = 0u) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if constexpr (T == SQ_BF16) {
     const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag);
     x_from_smem<T>(x.x, sm, warp % nseg, lane, n, sc);
   } else {
-    stage_digits<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, nseg);
+    stage_digits<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, nseg, stamp_at);
     act_from_smem<T>(x, sm, warp % nseg, lane, n, 1.0f);
   }
 }
@@ -1250,14 +1329,23 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
     const int g = item / n_chunks, c = item % n_chunks;
     const int s0 = c * CH, s1 = min(Lk, s0 + CH);
     float qv[GROUP][DPL], m[GROUP], lsum[GROUP], acc[GROUP][DPL];
+    {
+      const unsigned long long *qa[GROUP * DPL];
+      float qf[GROUP * DPL];
 #pragma unroll
-    for (int h = 0; h < GROUP; h++) {
-      m[h] = -INFINITY;
-      lsum[h] = 0.f;
+      for (int h = 0; h < GROUP; h++)
 #pragma unroll
-      for (int i = 0; i < DPL; i++) {
-        qv[h][i] = poll_ll(p, p.q_ll + (size_t)(g * GROUP + h) * hd + lane + 32 * i, tag_in);
-        acc[h][i] = 0.f;
+        for (int i = 0; i < DPL; i++) qa[h * DPL + i] = p.q_ll + (size_t)(g * GROUP + h) * hd + lane + 32 * i;
+      poll_ll_n<GROUP * DPL>(p, qa, tag_in, qf);
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) {
+        m[h] = -INFINITY;
+        lsum[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) {
+          qv[h][i] = qf[h * DPL + i];
+          acc[h][i] = 0.f;
+        }
       }
     }
     const float *kb = p.kc + ((size_t)l * p.KVH + g) * p.max_ctx * hd;
@@ -1267,8 +1355,12 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
 #pragma unroll
       for (int i = 0; i < DPL; i++) {
         if (s == pos) {  // the row this token's QKV stage just produced
-          kr[i] = poll_ll(p, p.kv_ll + (size_t)g * hd + lane + 32 * i, tag_in);
-          vr[i] = poll_ll(p, p.kv_ll + p.KVd + (size_t)g * hd + lane + 32 * i, tag_in);
+          const unsigned long long *kva[2] = {p.kv_ll + (size_t)g * hd + lane + 32 * i,
+                                              p.kv_ll + p.KVd + (size_t)g * hd + lane + 32 * i};
+          float kv2[2];
+          poll_ll_n<2>(p, kva, tag_in, kv2);
+          kr[i] = kv2[0];
+          vr[i] = kv2[1];
         } else {
           kr[i] = __ldcg(kb + (size_t)s * hd + lane + 32 * i);
           vr[i] = __ldcg(vb + (size_t)s * hd + lane + 32 * i);
@@ -1408,6 +1500,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   Smem &sm = *reinterpret_cast<Smem *>(tbl_bar + 1);  // 16-byte aligned: 5 + 1 barriers of 8 bytes
   int2 *tbl = reinterpret_cast<int2 *>(&sm + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  stamp_sync(p, p.tl_stride - 6);
   stamp(p, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; s++) {
@@ -1442,10 +1535,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ---- RMSNorm + QKV + RoPE + KV append
     load_stage_regs(p, ST_QKV, l, pos, sr, 0u);
     if (l == 0)
-      stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, p.embd + (size_t)tok * p.rb_E,
-                            blockIdx.x == 0, hid_in);
+      stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1,
+                            p.embd + (size_t)tok * p.rb_E, blockIdx.x == 0, hid_in);
     else
-      stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E);
+      stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1);
     stamp(p, 8 * (5 * l) + 2);
     matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_QKV));
     // ---- attention (waits on q / K / V words, not on a barrier)
@@ -1455,24 +1548,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     stamp(p, 8 * (5 * l + 1) + 6);
     // ---- O projection + residual
     load_stage_regs(p, ST_O, l, pos, sr, hid_in);
-    stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q);
+    stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q, 8 * (5 * l + 2) + 1);
     stamp(p, 8 * (5 * l + 2) + 2);
     matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_O));
     // ---- RMSNorm + gate/up + SiLU*up
     cta_sync();
-    stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, p.nseg_E);
+    stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, p.nseg_E, 8 * (5 * l + 3) + 1);
     stamp(p, 8 * (5 * l + 3) + 2);
     matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_ACT));
     // ---- down + residual
     load_stage_regs(p, ST_DOWN, l, pos, sr, mk_tag(launch, l, TG_POST_O));
     cta_sync();
-    stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F);
+    stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F, 8 * (5 * l + 4) + 1);
     stamp(p, 8 * (5 * l + 4) + 2);
     matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_DOWN));
     cta_sync();
   }
   // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
-  stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E, p.nseg_E);
+  stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E, p.nseg_E,
+                       8 * (5 * p.L) + 1);
   stamp(p, 8 * (5 * p.L) + 2);
   matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr, 0u);
   cta_sync();
@@ -1534,6 +1628,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
   stamp(p, p.tl_stride - 1);
+  stamp_sync(p, p.tl_stride - 4);
 }
 
 // Per-CTA tile tables, built once per context with the same row split the kernel
@@ -1704,7 +1799,7 @@ int decode_prepare(sq_ctx *c) {
   if (const char *pf = getenv("SQ_DECODE_L2_PREFETCH")) h.pf = std::max(0, std::min(atoi(pf), 256));  // tuning
   if (const char *tl = getenv("SQ_DECODE_TIMELINE")) {  // opt-in stage timestamps
     st->tl_path = tl;
-    st->tl_stride = 8 * (5 * cf.n_blocks + 1) + 4;
+    st->tl_stride = 8 * (5 * cf.n_blocks + 1) + 6;
     SQ_CUDA(alloc((void **)&st->d_timeline, (size_t)nsm * st->tl_stride * 8));
     h.timeline = st->d_timeline;
     h.tl_stride = st->tl_stride;
