@@ -40,6 +40,7 @@ namespace dk {
 
 constexpr int NC = 8;                    // warps per CTA (2 per SM sub-partition: 255 registers each)
 constexpr int NTHREADS = NC * 32;
+constexpr int NG = NC / 2;               // warps per group (the groups take alternate tiles)
 constexpr int SLOT = 36864;              // bytes per ring slot
 constexpr int NSLOT = 5;
 constexpr int PF_TILES = 12;             // tiles prefetched into L2 beyond the ring
@@ -75,6 +76,7 @@ struct Params {
   unsigned *launch;              // launches so far (the high bits of every tag)
   unsigned long long *timeline;  // optional per-CTA stage timestamps (SQ_DECODE_TIMELINE)
   int tl_stride;
+  unsigned long long *tile_tl;   // with the timeline: per tile {issued, landed, done} clocks [G][max_tiles][3]
   int2 *tiles;                   // [G][max_tiles] tile table: {row, layer<<16 | kind<<12 | rows}
   int *ntiles;                   // [G]
   int max_tiles;
@@ -183,6 +185,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // more finely than the timer's own resolution.
 __device__ __forceinline__ void stamp(const Params &p, int k) {
   if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = (unsigned long long)clock64();
+}
+__device__ __forceinline__ void stamp_now(const Params &p, int k) {  // by whichever thread calls it
+  if (p.timeline) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = (unsigned long long)clock64();
 }
 __device__ __forceinline__ void stamp_sync(const Params &p, int k) {
   if (p.timeline && threadIdx.x == 0) {
@@ -392,7 +397,7 @@ struct AttScratch {
 };
 
 struct Smem {
-  float red[2][MAX_TILE_ITEMS];
+  float red[4][MAX_TILE_ITEMS];  // segment partial sums: two buffers per warp group
   union {
     float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index): BF16 stages
     uint32_t xd[MAX_X];  // the stage input as digits (see stage_digits): Q8_0 / Q4_0 stages
@@ -402,6 +407,8 @@ struct Smem {
   float qh[256];      // one q head (attention over short contexts)
   float lm[MAX_LM_ROWS];
   int rel[NSLOT];     // warps done with the tile in each slot
+  int slot_tile[NSLOT];  // tile index last issued into each slot
+  int pad_[3];
   int issued[NSLOT];  // copies issued into each slot (for the error-path drain)
   int ntiles;
   int flag;
@@ -691,12 +698,15 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
 }
 
 // Stage the n-element input of a Q8_0 / Q4_0 stage as digits in sm.xd (modes as
-// stage_x: XS_PLAIN the tagged vector v, XS_NORM / XS_EMBED with the RMS norm,
-// rms_norm.rs:40-56, x = (h*w) * (1/rms)). Thread t takes 8 consecutive elements
-// per pass (four threads a block); the squared sum is combined in a fixed order,
-// so every CTA computes the same rms.
+// stage_x: XS_PLAIN the tagged vector v; XS_NORM / XS_EMBED stage h*w of the RMS
+// norm, rms_norm.rs:40-56, and return 1/rms, which the stage applies to each dot
+// product: W.((h*w)/rms) = (W.(h*w)) * (1/rms)). Thread t takes 8 consecutive
+// elements per pass (four threads a block); the squared sum is combined in a fixed
+// order, so every CTA computes the same rms. One barrier follows the data's
+// arrival; the one that guards the buffer against the previous stage's readers
+// runs while the loads are still in flight.
 template <int T, int MODE>
-__device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
+__device__ float stage_digits(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
                              const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int nseg, int stamp_at) {
   constexpr int NT = NC * 32, MAXP = MAX_X / (NT * 8);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -704,6 +714,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
   float h[MAXP][8];
   float ss = 0.f;
   if constexpr (MODE == XS_EMBED) {
+    cta_sync();  // every warp is done with the previous input
 #pragma unroll
     for (int k = 0; k < MAXP; k++) {
       const int g = k * NT + tid;
@@ -739,6 +750,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
 #pragma unroll
       for (int i = 0; i < 4; i++) c[k][i] = g < ng ? ld_ll2(v + 8 * g + 2 * i) : make_ulonglong2(0ull, 0ull);
     }
+    cta_sync();  // every warp is done with the previous input (while these loads fly)
     // until every word carries the tag: re-read all stale pairs together (one L2
     // round trip per retry, not one per word)
     const long long t0 = clock64();
@@ -786,15 +798,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
     ss = warp_sum(ss);
     if (lane == 0) sm.ssp[warp] = ss;
   }
-  cta_sync();  // the squared sums are in; every warp is done with the previous input
   if (stamp_at >= 0) stamp(p, stamp_at);
-  float scale = 1.0f;
-  if constexpr (MODE != XS_PLAIN) {
-    float tot = 0.f;
-#pragma unroll
-    for (int k = 0; k < NC; k++) tot += sm.ssp[k];
-    scale = 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
-  }
   const int ngs = nseg * 256;  // groups of the staged segments (the tail is zero-filled)
   const int q = tid & 3;       // quarter of the block
 #pragma unroll
@@ -804,7 +808,7 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
     float x[8], amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      x[i] = MODE == XS_PLAIN ? h[k][i] : __fmul_rn(h[k][i], scale);
+      x[i] = h[k][i];
       amax = fmaxf(amax, fabsf(x[i]));
     }
     amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));
@@ -884,6 +888,11 @@ __device__ void stage_digits(const Params &p, Smem &sm, const unsigned long long
   }
   cta_sync();
   if (stamp_at >= 0) stamp(p, stamp_at + 2);
+  if constexpr (MODE == XS_PLAIN) return 1.0f;
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; k++) tot += sm.ssp[k];
+  return 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
 }
 
 // This warp's activation registers from the staged input.
@@ -919,19 +928,22 @@ __device__ __forceinline__ void act_from_smem(ActRegs<T> &a, const Smem &sm, int
 }
 
 // Stage a stage's input and load this warp's activation registers: f32 values for
-// BF16 weights, digits for Q8_0 / Q4_0.
+// BF16 weights, digits for Q8_0 / Q4_0. Returns the factor the stage's dot
+// products take (1/rms of a norm staged as digits, else 1).
 template <int T, int MODE>
-__device__ __forceinline__ void stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
+__device__ __forceinline__ float stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
                                          unsigned tag, const float *w, int n, int nseg, int stamp_at,
                                          const uint8_t *emb_row = nullptr, bool write_hidden = false,
                                          unsigned emb_tag = 0u) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if constexpr (T == SQ_BF16) {
     const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag);
-    x_from_smem<T>(x.x, sm, warp % nseg, lane, n, sc);
+    x_from_smem<T>(x.x, sm, (warp % NG) % nseg, lane, n, sc);
+    return 1.0f;
   } else {
-    stage_digits<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, nseg, stamp_at);
-    act_from_smem<T>(x, sm, warp % nseg, lane, n, 1.0f);
+    const float sc = stage_digits<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, nseg, stamp_at);
+    act_from_smem<T>(x, sm, (warp % NG) % nseg, lane, n, 1.0f);
+    return sc;
   }
 }
 
@@ -1020,9 +1032,11 @@ __device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) 
 // evict-first; what the L2 keeps is the prefetched tiles not yet consumed.
 __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
   const int2 d = tbl[j];
+  if (p.tile_tl) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + j) * 3] = (unsigned long long)clock64();
   uint8_t *dst = rg.slots + (size_t)slot * SLOT;
   uint64_t *bar = &rg.full[slot];
   sm.issued[slot]++;
+  *(volatile int *)&sm.slot_tile[slot] = j;
   const int n = d.y & 0xFFF, kind = (d.y >> 12) & 0xF;
   mbar_expect_tx(bar, (kind == ST_GU ? 2u : 1u) * n * stage_rb(p, kind));
   const uint64_t pol = policy_evict_first();
@@ -1038,13 +1052,13 @@ __device__ __forceinline__ void prefetch_tile(const Params &p, const Smem &sm, c
   tile_copies(p, tbl[j], [&](unsigned, const uint8_t *src, unsigned bytes) { bulk_prefetch_l2(src, bytes); });
 }
 
-// A warp is done reading tile `k` in `slot`; the last of the NC warps refills the
-// slot with tile k + NSLOT.
+// A warp is done reading tile `k` in `slot`; the last of the `nwarps` warps that
+// read it refills the slot with tile k + NSLOT.
 __device__ __forceinline__ void release_slot(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int slot,
-                                             int k) {
+                                             int k, int nwarps) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) {
-    if (atomicAdd(&sm.rel[slot], 1) == NC - 1) {
+    if (atomicAdd(&sm.rel[slot], 1) == nwarps - 1) {
       sm.rel[slot] = 0;
       if (k + NSLOT < sm.ntiles) issue_tile(p, rg, sm, tbl, k + NSLOT, slot);
       if (p.pf > 0) prefetch_tile(p, sm, tbl, k + NSLOT + p.pf);
@@ -1116,94 +1130,125 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, in
   }
 }
 
-// One matvec stage of this CTA: for each tile of its rows, wait for the slot,
-// dot two rows at a time per warp, finish the rows, release the slot.
+// Wait until `slot` holds tile k and its bytes have landed. The two warp groups
+// consume alternate tiles, so a group can be two phases of a slot's barrier ahead
+// of the slot's last completed phase; the parity wait is meaningful only once the
+// slot's current phase is tile k's, which sm.slot_tile tells.
+__device__ __forceinline__ bool slot_wait(const Params &p, const Ring &rg, const Smem &sm, int slot, int k,
+                                          unsigned phase) {
+  if (*(volatile const int *)&sm.slot_tile[slot] != k) {
+    const long long t0 = clock64();
+    for (unsigned it = 0; *(volatile const int *)&sm.slot_tile[slot] != k; it++)
+      if ((it & 63u) == 63u && poll_expired(p, t0)) return false;
+  }
+  return mbar_wait(&rg.full[slot], phase, p.err);
+}
+
+__device__ __forceinline__ void group_sync(int grp) {
+  asm volatile("bar.sync %0, %1;" ::"r"(2 + grp), "n"(NG * 32) : "memory");
+}
+
+// One matvec stage of this CTA. The CTA's tiles alternate between two groups of NG
+// warps (tile k goes to group k & 1), so one group's reductions, epilogues and
+// slot refills overlap the other group's dot products. Within a tile a warp takes
+// two rows at a time (a row pair, or two rows of its input segment when the rows
+// are split into segments) and reduces them together.
 template <int T, int KIND>
 __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int l,
-                             const ActRegs<T> &x, int &slot, unsigned &phase, int &tile_ctr, int pos,
+                             const ActRegs<T> &x, float osc, int &slot, unsigned &phase, int &tile_ctr, int pos,
                              const StageRegs &sr, unsigned tag) {
   constexpr int NW = nwords<T>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / NG, wig = warp % NG;
   const int nseg = stage_nseg(p, KIND), rb = stage_rb(p, KIND), Tr = p.tile_rows[KIND];
   const int in_dim = KIND == ST_O ? p.Q : (KIND == ST_DOWN ? p.F : p.E);
-  const int seg = warp % nseg, rpw = NC / nseg, rs = warp / nseg;
+  const int seg = wig % nseg, rpw = NG / nseg, rs = wig / nseg;
   const bool active = lane_active<T>(seg, lane, in_dim);
   const uint32_t slots = smem_u32(rg.slots);
+  const bool lead = wig == 0 && lane == 0;  // stamps of the group that has the tile
   int r0, r1;
   stage_rows(p, KIND, l, blockIdx.x, r0, r1);
   const int stage_id = KIND == ST_LM ? 5 * p.L : 5 * l + (KIND == ST_QKV ? 0 : KIND + 1);
   for (int r = r0; r < r1; r += Tr) {
-    const int n = min(Tr, r1 - r);
-    const int rows = KIND == ST_GU ? 2 * n : n;
-    const uint32_t tile = slots + (uint32_t)slot * SLOT;
-    float *red = sm.red[tile_ctr & 1];
-    const bool ok = mbar_wait(&rg.full[slot], phase, p.err);
-    if (r == r0) stamp(p, 8 * stage_id + 4);
-    if (r + Tr >= r1) stamp(p, 8 * stage_id + 5);
-    if (ok) {
-      if (nseg == 1) {
-        // warp-owned row pairs: (2i, 2i+1), or (gate i, up i)
-        const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
-        for (int i = warp; i < npairs; i += NC) {
-          const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
-          const bool hasb = b < rows;
-          float va = 0.f, vb = 0.f;
-          if (active) {
-            uint32_t wa[NW], wb[NW];
-            lane_load<T>(tile + (uint32_t)a * rb, 0, lane, wa);
-            if (hasb) lane_load<T>(tile + (uint32_t)b * rb, 0, lane, wb);
-            va = lane_dot<T>(wa, x);
-            if (hasb) vb = lane_dot<T>(wb, x);
+    if ((tile_ctr & 1) == grp) {
+      const int n = min(Tr, r1 - r);
+      const int rows = KIND == ST_GU ? 2 * n : n;
+      const uint32_t tile = slots + (uint32_t)slot * SLOT;
+      float *red = sm.red[2 * grp + ((tile_ctr >> 1) & 1)];
+      const bool ok = slot_wait(p, rg, sm, slot, tile_ctr, phase);
+      if (p.tile_tl && lead) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + tile_ctr) * 3 + 1] = (unsigned long long)clock64();
+      if (lead && r == r0) stamp_now(p, 8 * stage_id + 4);
+      if (lead && r + Tr >= r1) stamp_now(p, 8 * stage_id + 5);
+      if (ok) {
+        if (nseg == 1) {
+          // warp-owned row pairs (2i, 2i+1), or (gate i, up i)
+          const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
+          for (int i = wig; i < npairs; i += NG) {
+            const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
+            const bool hasb = b < rows;
+            float va = 0.f, vb = 0.f;
+            if (active) {
+              uint32_t wa[NW], wb[NW];
+              lane_load<T>(tile + (uint32_t)a * rb, 0, lane, wa);
+              if (hasb) lane_load<T>(tile + (uint32_t)b * rb, 0, lane, wb);
+              va = lane_dot<T>(wa, x);
+              if (hasb) vb = lane_dot<T>(wb, x);
+            }
+            const float2 v = warp_sum2(va, vb);
+            const float fa = v.x * osc, fb = v.y * osc;
+            if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, fa, r + i, fb, true, sr, tag);
+            else finish_rows<KIND>(p, sm, l, pos, r0, r + a, fa, r + b, fb, hasb, sr, tag);
           }
-          const float2 v = warp_sum2(va, vb);
-          if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, v.x, r + i, v.y, true, sr, tag);
-          else finish_rows<KIND>(p, sm, l, pos, r0, r + a, v.x, r + b, v.y, hasb, sr, tag);
+        } else {
+          // segment-split rows: this warp's segment of rows rs, rs + rpw, ...; the
+          // partial sums meet in shared memory
+          for (int i = rs; i < rows; i += 2 * rpw) {
+            const int a = i, b = i + rpw;
+            const bool hasb = b < rows;
+            float va = 0.f, vb = 0.f;
+            if (active) {
+              uint32_t wa[NW], wb[NW];
+              lane_load<T>(tile + (uint32_t)a * rb, seg, lane, wa);
+              if (hasb) lane_load<T>(tile + (uint32_t)b * rb, seg, lane, wb);
+              va = lane_dot<T>(wa, x);
+              if (hasb) vb = lane_dot<T>(wb, x);
+            }
+            const float2 v = warp_sum2(va, vb);
+            if (lane == 0) {
+              red[a * nseg + seg] = v.x;
+              if (hasb) red[b * nseg + seg] = v.y;
+            }
+          }
         }
-      } else {
-        // segment-split rows: partial sums per (row, segment) meet in shared memory
-        for (int i = rs; i < rows; i += 2 * rpw) {
-          const int a = i, b = i + rpw;
-          const bool hasb = b < rows;
-          float va = 0.f, vb = 0.f;
-          if (active) {
-            uint32_t wa[NW], wb[NW];
-            lane_load<T>(tile + (uint32_t)a * rb, seg, lane, wa);
-            if (hasb) lane_load<T>(tile + (uint32_t)b * rb, seg, lane, wb);
-            va = lane_dot<T>(wa, x);
-            if (hasb) vb = lane_dot<T>(wb, x);
-          }
-          const float2 v = warp_sum2(va, vb);
-          if (lane == 0) {
-            red[a * nseg + seg] = v.x;
-            if (hasb) red[b * nseg + seg] = v.y;
+      }
+      release_slot(p, rg, sm, tbl, slot, tile_ctr, NG);
+      if (p.tile_tl && lead) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + tile_ctr) * 3 + 2] = (unsigned long long)clock64();
+      if (nseg > 1) {
+        group_sync(grp);
+        // finish the tile's rows: warp wig takes row pairs wig, wig + NG, ...
+        if (ok) {
+          const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
+          for (int i = wig; i < npairs; i += NG) {
+            const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
+            const bool hasb = b < rows;
+            float va = 0.f, vb = 0.f;
+            for (int s = 0; s < nseg; s++) {
+              va += red[a * nseg + s];
+              if (hasb) vb += red[b * nseg + s];
+            }
+            va *= osc;
+            vb *= osc;
+            if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
+            else finish_rows<KIND>(p, sm, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
           }
         }
       }
     }
-    release_slot(p, rg, sm, tbl, slot, tile_ctr);
     if (++slot == NSLOT) {
       slot = 0;
       phase ^= 1u;
     }
     tile_ctr++;
-    if (nseg > 1) {
-      cta_sync();
-      // finish the tile's rows: warp w takes row pairs w, w+NC, ... (the same pairing as above)
-      if (ok) {
-        const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
-        for (int i = warp; i < npairs; i += NC) {
-          const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
-          const bool hasb = b < rows;
-          float va = 0.f, vb = 0.f;
-          for (int s = 0; s < nseg; s++) {
-            va += red[a * nseg + s];
-            if (hasb) vb += red[b * nseg + s];
-          }
-          if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
-          else finish_rows<KIND>(p, sm, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
-        }
-      }
-    }
   }
   stamp(p, 8 * stage_id + 6);
 }
@@ -1507,6 +1552,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&rg.full[s], 1);
       sm.rel[s] = 0;
       sm.issued[s] = 0;
+      sm.slot_tile[s] = -1;
     }
     mbar_init(tbl_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1534,13 +1580,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
     // ---- RMSNorm + QKV + RoPE + KV append
     load_stage_regs(p, ST_QKV, l, pos, sr, 0u);
+    float osc;
     if (l == 0)
-      stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1,
+      osc = stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1,
                             p.embd + (size_t)tok * p.rb_E, blockIdx.x == 0, hid_in);
     else
-      stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1);
+      osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1);
     stamp(p, 8 * (5 * l) + 2);
-    matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_QKV));
+    matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_QKV));
     // ---- attention (waits on q / K / V words, not on a barrier)
     cta_sync();  // shared scratch of the staging buffer is reused below
     if (DPL <= 2 && pos < SHORT_CTX) attention_heads<DPL <= 2 ? DPL : 2>(p, sm, l, pos, mk_tag(launch, l, TG_QKV), mk_tag(launch, l, TG_ATTN));
@@ -1548,27 +1595,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     stamp(p, 8 * (5 * l + 1) + 6);
     // ---- O projection + residual
     load_stage_regs(p, ST_O, l, pos, sr, hid_in);
-    stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q, 8 * (5 * l + 2) + 1);
+    osc = stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q, 8 * (5 * l + 2) + 1);
     stamp(p, 8 * (5 * l + 2) + 2);
-    matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_O));
+    matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_O));
     // ---- RMSNorm + gate/up + SiLU*up
     cta_sync();
-    stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, p.nseg_E, 8 * (5 * l + 3) + 1);
+    osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, p.nseg_E, 8 * (5 * l + 3) + 1);
     stamp(p, 8 * (5 * l + 3) + 2);
-    matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_ACT));
+    matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_ACT));
     // ---- down + residual
     load_stage_regs(p, ST_DOWN, l, pos, sr, mk_tag(launch, l, TG_POST_O));
     cta_sync();
-    stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F, 8 * (5 * l + 4) + 1);
+    osc = stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F, 8 * (5 * l + 4) + 1);
     stamp(p, 8 * (5 * l + 4) + 2);
-    matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_DOWN));
+    matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_DOWN));
     cta_sync();
   }
   // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
-  stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E, p.nseg_E,
+  const float osc_lm = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E, p.nseg_E,
                        8 * (5 * p.L) + 1);
   stamp(p, 8 * (5 * p.L) + 2);
-  matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, slot, phase, tile_ctr, pos, sr, 0u);
+  matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, osc_lm, slot, phase, tile_ctr, pos, sr, 0u);
   cta_sync();
   stamp(p, p.tl_stride - 2);
   // ---- greedy argmax: this CTA's rows (kept in shared memory) in order, then the
@@ -1668,7 +1715,10 @@ struct DecodeState {
   unsigned *d_err = nullptr, *d_bar = nullptr, *d_ticket = nullptr, *d_attn_cnt = nullptr;
   int *d_pos = nullptr;
   int n_kv_heads = 0, n_layers = 0;
-  unsigned long long *d_timeline = nullptr;  // SQ_DECODE_TIMELINE=<file>: stage stamps of the last launch
+  unsigned long long *d_timeline = nullptr;
+  unsigned long long *d_tile_tl = nullptr;  // per-tile stamps of the last launch (with the timeline)
+  const int2 *d_tiles = nullptr;
+  int max_tiles = 0;  // SQ_DECODE_TIMELINE=<file>: stage stamps of the last launch
   int tl_stride = 0;
   std::string tl_path;
   std::vector<void *> allocs;
@@ -1813,6 +1863,12 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(cudaMemcpy(counts.data(), h.ntiles, nsm * sizeof(int), cudaMemcpyDeviceToHost));
   h.max_tiles = (*std::max_element(counts.begin(), counts.end()) + 1) & ~1;
   SQ_CUDA(alloc((void **)&h.tiles, (size_t)nsm * h.max_tiles * sizeof(int2)));
+  if (h.timeline) {
+    SQ_CUDA(alloc((void **)&h.tile_tl, (size_t)nsm * h.max_tiles * 3 * 8));
+    st->d_tile_tl = h.tile_tl;
+    st->d_tiles = h.tiles;
+    st->max_tiles = h.max_tiles;
+  }
   SQ_CUDA(cudaMemcpy(st->d_params, &h, sizeof(dk::Params), cudaMemcpyHostToDevice));
   dk::k_build_tiles<<<nsm, 32>>>(st->d_params, h.tiles, h.ntiles, h.max_tiles);
   SQ_CHECK_LAUNCH("build tiles");
@@ -1882,6 +1938,14 @@ int decode_check(sq_ctx *c) {
       const int hdr[2] = {st->grid, st->tl_stride};
       fwrite(hdr, sizeof hdr, 1, f);
       fwrite(tl.data(), 8, tl.size(), f);
+      std::vector<unsigned long long> tt((size_t)st->grid * st->max_tiles * 3);
+      if (st->d_tile_tl && cudaMemcpy(tt.data(), st->d_tile_tl, tt.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
+        fwrite(&st->max_tiles, 4, 1, f);
+        fwrite(tt.data(), 8, tt.size(), f);
+        std::vector<int2> tb((size_t)st->grid * st->max_tiles);
+        if (cudaMemcpy(tb.data(), st->d_tiles, tb.size() * sizeof(int2), cudaMemcpyDeviceToHost) == cudaSuccess)
+          fwrite(tb.data(), sizeof(int2), tb.size(), f);
+      }
       fclose(f);
     }
   }
