@@ -58,7 +58,7 @@ struct LayerW {
   const float *attn_norm, *ffn_norm;
 };
 
-struct Params {
+struct Params {  // passed by value to the decode kernel: at most the 32 KB of kernel parameters
   int L, E, Q, KVd, F, V, H, KVH, hd, max_ctx, G;
   int nseg_E, nseg_Q, nseg_F;
   int rb_E, rb_Q, rb_F;        // bytes per weight row with in_dim = E / Q / F
@@ -83,6 +83,7 @@ struct Params {
   int pf;                        // L2 prefetch distance in tiles beyond the ring (0 = off)
   LayerW layers[MAX_LAYERS];
 };
+static_assert(sizeof(Params) + 64 <= 32764, "Params fits the kernel parameter space");
 
 // ---------------------------------------------------------------------------------
 // PTX helpers: mbarrier, bulk copy, shared loads, grid barrier
@@ -177,8 +178,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 // Timeline slot k of this CTA: 0 = start; for stage s (5 per layer, the LM head is
-// stage 5L) 8s+1 = input words arrived, 8s+3 = input digits written, 8s+2 = input
-// staged in registers, 8s+4 / 8s+5 = first / last tile landed, 8s+6 = stage done;
+// stage 5L) 8s+1 = input words arrived, 8s+3 = input staged in shared memory, 8s+2 =
+// input in registers, 8s+4 / 8s+5 = first / last tile landed, 8s+6 = stage done;
 // stride-2 = LM head done, stride-1 = end. Stamps are SM clock counts; each CTA
 // also records one (global ns, clock) pair at a tick of the global timer at start
 // and at end (slots stride-6..stride-3), which maps its clocks onto global time
@@ -399,8 +400,7 @@ struct AttScratch {
 struct Smem {
   float red[4][MAX_TILE_ITEMS];  // segment partial sums: two buffers per warp group
   union {
-    float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index): BF16 stages
-    uint32_t xd[MAX_X];  // the stage input as digits (see stage_digits): Q8_0 / Q4_0 stages
+    float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index)
     AttScratch at;    // attention-stage partials (a different phase of the layer)
   };
   float ssp[NC];      // per-warp partial squared sums of the RMS norm
@@ -529,7 +529,7 @@ __device__ __forceinline__ int xs_index(int e) {
 // every CTA computes the same rms.
 template <int T, int MODE>
 __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
-                         const uint8_t *emb_row, bool write_hidden, unsigned emb_tag) {
+                         const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int stamp_at) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float ss = 0.f;
   if constexpr (MODE == XS_EMBED) {
@@ -599,6 +599,7 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
       }
       if ((it & 15u) == 15u && poll_expired(p, t0)) break;
     }
+    if (stamp_at >= 0) stamp(p, stamp_at);
 #pragma unroll
     for (int k = 0; k < MAXC; k++) {
       const int ci = k * NC * 32 + tid;
@@ -619,6 +620,7 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
     if (lane == 0) sm.ssp[warp] = ss;
   }
   cta_sync();
+  if (stamp_at >= 0) stamp(p, stamp_at + 2);
   if (MODE == XS_PLAIN) return 1.0f;
   float tot = 0.f;
 #pragma unroll
@@ -642,355 +644,28 @@ __device__ __forceinline__ void x_from_smem(float (&x)[64], const Smem &sm, int 
   }
 }
 
-// ---------------------------------------------------------------------------------
-// Q8_0 / Q4_0 stage inputs as int8 digits (integer dot products against the blocks)
-// ---------------------------------------------------------------------------------
-// Each 32-element block of the f32 input x is written as x = sx * (d0 + d1/254 +
-// d2/254^2) with int8 digits d0, d1, d2 in [-127, 127] and sx = amax/127: about 23
-// significant bits of the block's largest element, the precision of an f32 value.
-// A weight block then needs three integer dot products (dp4a, exact int32), one
-// per digit, and one float combination per block:
-//   sum_i w_i x_i = sw * (sx * I0 + (sx/254^2) * (254*I1 + I2))
-// instead of a byte-to-float conversion and an FMA per element. The reference
-// sums q_i * x_i in f32 per block, then scales (dot_prod.rs:86-96, 255-270); the
-// result here differs from that only by f32-level rounding.
-//
-// Shared-memory layout: for each lane of each 2048-element segment, XDW words:
-// the lane's digit words laid out byte for byte against the lane's weight words
-// (a Q8_0 block pair is 17 words: the first block's 32 quants start at byte 2,
-// the second's at byte 36; zero digits sit under the scale bytes), then per-block
-// constants. XDW = 60 words keeps the 16-byte loads of 8 lanes on distinct banks.
-constexpr int XDW = 60;
-constexpr float DIGIT_BASE = 254.0f;
-constexpr float INV_BASE2 = 1.0f / (254.0f * 254.0f);
+// This warp's activation registers: the 64 f32 inputs its lane meets in every row.
 template <int T>
-constexpr int ndigw() {  // digit words per lane
-  return T == SQ_Q8_0 ? 51 : 54;
-}
-// Q8_0: digit d word k (k = 0..16) at d*17 + k; sx of block a / b at 51 / 52.
-// Q4_0: digit d low-nibble word k (k = 0..8) at d*18 + k, high-nibble word at
-// d*18 + 9 + k; sx at 54 / 55; K0 = 8*S0 at 56 / 58 and KJ = 8*(254*S1 + S2) at
-// 57 / 59, where S_d is the block's sum of digit d (Q4_0 values are q - 8, the
-// integer dots use q: sum (q-8)*d = sum q*d - 8*S_d).
-static_assert(XDW * 32 * (MAX_X / 2048) <= MAX_X, "digit staging fits the input buffer");
-
-template <int T>
-struct ActRegs;
-template <>
-struct ActRegs<SQ_BF16> {
+struct ActRegs {
   float x[64];
 };
-template <>
-struct ActRegs<SQ_Q8_0> {
-  uint32_t d[51];
-  float c0a, c0b, c2a, c2b;
-};
-template <>
-struct ActRegs<SQ_Q4_0> {
-  uint32_t d[54];
-  float c0a, c0b, c2a, c2b;
-  int k0a, kja, k0b, kjb;
-};
 
-// The low bytes of four words, in order.
-__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
-}
-
-// Stage the n-element input of a Q8_0 / Q4_0 stage as digits in sm.xd (modes as
-// stage_x: XS_PLAIN the tagged vector v; XS_NORM / XS_EMBED stage h*w of the RMS
-// norm, rms_norm.rs:40-56, and return 1/rms, which the stage applies to each dot
-// product: W.((h*w)/rms) = (W.(h*w)) * (1/rms)). Thread t takes 8 consecutive
-// elements per pass (four threads a block); the squared sum is combined in a fixed
-// order, so every CTA computes the same rms. One barrier follows the data's
-// arrival; the one that guards the buffer against the previous stage's readers
-// runs while the loads are still in flight.
-template <int T, int MODE>
-__device__ float stage_digits(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
-                             const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int nseg, int stamp_at) {
-  constexpr int NT = NC * 32, MAXP = MAX_X / (NT * 8);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ng = n / 8;
-  float h[MAXP][8];
-  float ss = 0.f;
-  if constexpr (MODE == XS_EMBED) {
-    cta_sync();  // every warp is done with the previous input
-#pragma unroll
-    for (int k = 0; k < MAXP; k++) {
-      const int g = k * NT + tid;
-#pragma unroll
-      for (int i = 0; i < 8; i++) h[k][i] = 0.f;
-      if (g < ng) {
-        const int e = g * 8, b = e >> 5, j0 = e & 31;
-        if constexpr (T == SQ_Q8_0) {
-          const uint8_t *blk = emb_row + (size_t)b * Q8_BYTES;
-          const float sc = h2f(ld_u16(blk));
-#pragma unroll
-          for (int i = 0; i < 8; i++) h[k][i] = sc * (float)(int8_t)__ldg(blk + 2 + j0 + i);
-        } else {
-          const uint8_t *blk = emb_row + (size_t)b * Q4_BYTES;
-          const float sc = h2f(ld_u16(blk));
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const uint8_t byte = __ldg(blk + 2 + ((j0 + i) & 15));
-            h[k][i] = sc * (float)((j0 < 16 ? (byte & 0x0F) : (byte >> 4)) - 8);
-          }
-        }
-        if (write_hidden) {
-#pragma unroll
-          for (int i = 0; i < 8; i++) st_ll(p.hid_ll + e + i, h[k][i], emb_tag);
-        }
-      }
-    }
-  } else {
-    ulonglong2 c[MAXP][4];  // every load of this thread in flight before any use
-#pragma unroll
-    for (int k = 0; k < MAXP; k++) {
-      const int g = k * NT + tid;
-#pragma unroll
-      for (int i = 0; i < 4; i++) c[k][i] = g < ng ? ld_ll2(v + 8 * g + 2 * i) : make_ulonglong2(0ull, 0ull);
-    }
-    cta_sync();  // every warp is done with the previous input (while these loads fly)
-    // until every word carries the tag: re-read all stale pairs together (one L2
-    // round trip per retry, not one per word)
-    const long long t0 = clock64();
-    for (unsigned it = 0;; it++) {
-      bool all = true;
-#pragma unroll
-      for (int k = 0; k < MAXP; k++)
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-          if (k * NT + tid < ng && !(ll_ok(c[k][i].x, tag) && ll_ok(c[k][i].y, tag))) all = false;
-      if (all) break;
-#pragma unroll
-      for (int k = 0; k < MAXP; k++) {
-        const int g = k * NT + tid;
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-          if (g < ng && !(ll_ok(c[k][i].x, tag) && ll_ok(c[k][i].y, tag))) c[k][i] = ld_ll2(v + 8 * g + 2 * i);
-      }
-      if ((it & 15u) == 15u && poll_expired(p, t0)) break;
-    }
-#pragma unroll
-    for (int k = 0; k < MAXP; k++) {
-      const int g = k * NT + tid;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        h[k][2 * i] = g < ng ? ll_val(c[k][i].x) : 0.f;
-        h[k][2 * i + 1] = g < ng ? ll_val(c[k][i].y) : 0.f;
-      }
-    }
-  }
-  if constexpr (MODE != XS_PLAIN) {
-#pragma unroll
-    for (int k = 0; k < MAXP; k++) {
-      const int g = k * NT + tid;
-      if (g < ng) {
-        const float4 w0 = ldnc4(w + 8 * g), w1 = ldnc4(w + 8 * g + 4);
-        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          ss = fmaf(h[k][i], h[k][i], ss);
-          h[k][i] = __fmul_rn(h[k][i], wv[i]);
-        }
-      }
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) sm.ssp[warp] = ss;
-  }
-  if (stamp_at >= 0) stamp(p, stamp_at);
-  const int ngs = nseg * 256;  // groups of the staged segments (the tail is zero-filled)
-  const int q = tid & 3;       // quarter of the block
-#pragma unroll
-  for (int k = 0; k < MAXP; k++) {
-    const int g = k * NT + tid;
-    if (k * NT >= ngs) break;  // warp-uniform: whole passes
-    float x[8], amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      x[i] = h[k][i];
-      amax = fmaxf(amax, fabsf(x[i]));
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 2));
-    // t = x/sx in [-127, 127]; each digit is rounded to nearest by adding 1.5*2^23
-    // (the sum's low mantissa bits are the integer, its low byte the int8 digit)
-    const float sx = amax * (1.0f / 127.0f);
-    const float inv = amax > 0.f ? 127.0f * __frcp_rn(amax) : 0.f;
-    constexpr float MAGIC = 12582912.0f;
-    uint32_t mg[3][8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const float t = x[i] * inv;
-      const float m0 = t + MAGIC, r0 = m0 - MAGIC;
-      const float t1 = fmaf(t, DIGIT_BASE, r0 * -DIGIT_BASE);  // (t - r0) * 254, one rounding
-      const float m1 = t1 + MAGIC, r1 = m1 - MAGIC;
-      const float m2 = fmaf(t1 - r1, DIGIT_BASE, MAGIC);
-      mg[0][i] = __float_as_uint(m0);
-      mg[1][i] = __float_as_uint(m1);
-      mg[2][i] = __float_as_uint(m2);
-    }
-    uint32_t D[3][2], prev[3];
-#pragma unroll
-    for (int d = 0; d < 3; d++) {
-      D[d][0] = pack4(mg[d][0], mg[d][1], mg[d][2], mg[d][3]);
-      D[d][1] = pack4(mg[d][4], mg[d][5], mg[d][6], mg[d][7]);
-      prev[d] = __shfl_up_sync(FULL, D[d][1], 1);
-    }
-    int S[3] = {0, 0, 0};
-    if constexpr (T == SQ_Q4_0) {
-#pragma unroll
-      for (int d = 0; d < 3; d++) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) S[d] += (int)(mg[d][i] - 0x4B400000u);
-        S[d] += __shfl_xor_sync(FULL, S[d], 1);
-        S[d] += __shfl_xor_sync(FULL, S[d], 2);
-      }
-    }
-    if (g < ngs) {
-      const int b = g >> 2, seg = b >> 6, ln = (b & 63) >> 1, par = b & 1;
-      uint32_t *reg = sm.xd + (seg * 32 + ln) * XDW;
-      if constexpr (T == SQ_Q8_0) {
-#pragma unroll
-        for (int d = 0; d < 3; d++) {
-          uint32_t *r = reg + d * 17;
-          if (par) {
-            r[9 + 2 * q] = D[d][0];
-            r[10 + 2 * q] = D[d][1];
-          } else {
-            r[2 * q] = __byte_perm(q ? prev[d] : 0u, D[d][0], 0x5432);
-            r[2 * q + 1] = __byte_perm(D[d][0], D[d][1], 0x5432);
-            if (q == 3) r[8] = __byte_perm(D[d][1], 0u, 0x5432);
-          }
-        }
-        if (q == 0) reg[51 + par] = __float_as_uint(sx);
-      } else {
-        const int half = q & 1;  // which 8 of the 16 bytes; q >= 2: the high nibbles
-#pragma unroll
-        for (int d = 0; d < 3; d++) {
-          uint32_t *r = reg + d * 18 + (q >= 2 ? 9 : 0);
-          if (par) {
-            r[5 + 2 * half] = D[d][0];
-            r[6 + 2 * half] = D[d][1];
-          } else {
-            r[2 * half] = __byte_perm(half ? prev[d] : 0u, D[d][0], 0x5432);
-            r[2 * half + 1] = __byte_perm(D[d][0], D[d][1], 0x5432);
-            if (half) r[4] = __byte_perm(D[d][1], 0u, 0x5432);
-          }
-        }
-        if (q == 0) {
-          reg[54 + par] = __float_as_uint(sx);
-          reg[56 + 2 * par] = (uint32_t)(8 * S[0]);
-          reg[57 + 2 * par] = (uint32_t)(8 * (254 * S[1] + S[2]));
-        }
-      }
-    }
-  }
-  cta_sync();
-  if (stamp_at >= 0) stamp(p, stamp_at + 2);
-  if constexpr (MODE == XS_PLAIN) return 1.0f;
-  float tot = 0.f;
-#pragma unroll
-  for (int k = 0; k < NC; k++) tot += sm.ssp[k];
-  return 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
-}
-
-// This warp's activation registers from the staged input.
-template <int T>
-__device__ __forceinline__ void act_from_smem(ActRegs<T> &a, const Smem &sm, int seg, int lane, int n, float scale) {
-  if constexpr (T == SQ_BF16) {
-    x_from_smem<T>(a.x, sm, seg, lane, n, scale);
-  } else {
-    const uint4 *src = reinterpret_cast<const uint4 *>(sm.xd + (seg * 32 + lane) * XDW);
-    uint32_t wv[XDW];
-#pragma unroll
-    for (int k = 0; k < XDW / 4; k++) {
-      const uint4 u = src[k];
-      wv[4 * k] = u.x;
-      wv[4 * k + 1] = u.y;
-      wv[4 * k + 2] = u.z;
-      wv[4 * k + 3] = u.w;
-    }
-    constexpr int ND = ndigw<T>();
-#pragma unroll
-    for (int k = 0; k < ND; k++) a.d[k] = wv[k];
-    a.c0a = __uint_as_float(wv[ND]);
-    a.c0b = __uint_as_float(wv[ND + 1]);
-    a.c2a = a.c0a * INV_BASE2;
-    a.c2b = a.c0b * INV_BASE2;
-    if constexpr (T == SQ_Q4_0) {
-      a.k0a = (int)wv[56];
-      a.kja = (int)wv[57];
-      a.k0b = (int)wv[58];
-      a.kjb = (int)wv[59];
-    }
-  }
-}
-
-// Stage a stage's input and load this warp's activation registers: f32 values for
-// BF16 weights, digits for Q8_0 / Q4_0. Returns the factor the stage's dot
-// products take (1/rms of a norm staged as digits, else 1).
+// Stage a stage's input and load this warp's activation registers (the norm's 1/rms
+// already applied). Returns the factor the stage's dot products take (1 here).
 template <int T, int MODE>
 __device__ __forceinline__ float stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
                                          unsigned tag, const float *w, int n, int nseg, int stamp_at,
                                          const uint8_t *emb_row = nullptr, bool write_hidden = false,
                                          unsigned emb_tag = 0u) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if constexpr (T == SQ_BF16) {
-    const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag);
-    x_from_smem<T>(x.x, sm, (warp % NG) % nseg, lane, n, sc);
-    return 1.0f;
-  } else {
-    const float sc = stage_digits<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, nseg, stamp_at);
-    act_from_smem<T>(x, sm, (warp % NG) % nseg, lane, n, 1.0f);
-    return sc;
-  }
+  const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, stamp_at);
+  x_from_smem<T>(x.x, sm, (warp % NG) % nseg, lane, n, sc);
+  return 1.0f;
 }
 
-// Dot of the lane's block pair of one weight row with the digit registers.
-__device__ __forceinline__ float lane_dot_digits(const uint32_t (&w)[17], const ActRegs<SQ_Q8_0> &a) {
-  int i0 = 0, i1 = 0, i2 = 0, j0 = 0, j1 = 0, j2 = 0;
-#pragma unroll
-  for (int k = 0; k < 9; k++) {  // block a: words 0..8 (scale bytes meet zero digits)
-    i0 = __dp4a((int)w[k], (int)a.d[k], i0);
-    i1 = __dp4a((int)w[k], (int)a.d[17 + k], i1);
-    i2 = __dp4a((int)w[k], (int)a.d[34 + k], i2);
-  }
-#pragma unroll
-  for (int k = 9; k < 17; k++) {  // block b: words 9..16
-    j0 = __dp4a((int)w[k], (int)a.d[k], j0);
-    j1 = __dp4a((int)w[k], (int)a.d[17 + k], j1);
-    j2 = __dp4a((int)w[k], (int)a.d[34 + k], j2);
-  }
-  const float sa = h2f((uint16_t)(w[0] & 0xFFFF)), sb = h2f((uint16_t)(w[8] >> 16));
-  const float ba = fmaf((float)(254 * i1 + i2), a.c2a, (float)i0 * a.c0a);
-  const float bb = fmaf((float)(254 * j1 + j2), a.c2b, (float)j0 * a.c0b);
-  return fmaf(ba, sa, bb * sb);
-}
-__device__ __forceinline__ float lane_dot_digits(const uint32_t (&w)[9], const ActRegs<SQ_Q4_0> &a) {
-  int i0 = 0, i1 = 0, i2 = 0, j0 = 0, j1 = 0, j2 = 0;
-#pragma unroll
-  for (int k = 0; k < 9; k++) {
-    const int lo = (int)(w[k] & 0x0F0F0F0Fu), hi = (int)((w[k] >> 4) & 0x0F0F0F0Fu);
-    if (k < 5) {  // block a: words 0..4
-      i0 = __dp4a(lo, (int)a.d[k], __dp4a(hi, (int)a.d[9 + k], i0));
-      i1 = __dp4a(lo, (int)a.d[18 + k], __dp4a(hi, (int)a.d[27 + k], i1));
-      i2 = __dp4a(lo, (int)a.d[36 + k], __dp4a(hi, (int)a.d[45 + k], i2));
-    } else {      // block b: words 5..8
-      j0 = __dp4a(lo, (int)a.d[k], __dp4a(hi, (int)a.d[9 + k], j0));
-      j1 = __dp4a(lo, (int)a.d[18 + k], __dp4a(hi, (int)a.d[27 + k], j1));
-      j2 = __dp4a(lo, (int)a.d[36 + k], __dp4a(hi, (int)a.d[45 + k], j2));
-    }
-  }
-  const float sa = h2f((uint16_t)(w[0] & 0xFFFF)), sb = h2f((uint16_t)(w[4] >> 16));
-  const float ba = fmaf((float)(254 * i1 + i2 - a.kja), a.c2a, (float)(i0 - a.k0a) * a.c0a);
-  const float bb = fmaf((float)(254 * j1 + j2 - a.kjb), a.c2b, (float)(j0 - a.k0b) * a.c0b);
-  return fmaf(ba, sa, bb * sb);
-}
 template <int T>
 __device__ __forceinline__ float lane_dot(const uint32_t (&w)[nwords<T>()], const ActRegs<T> &a) {
-  if constexpr (T == SQ_BF16) return lane_dot<T>(w, a.x);
-  else return lane_dot_digits(w, a);
+  return lane_dot<T>(w, a.x);
 }
 
 // The bulk copies of tile entry d: f(byte offset in the slot, global source, bytes).
@@ -1077,11 +752,10 @@ struct StageRegs {
 // rows a / b are absolute rows of the stage's row space; vb is ignored when !hasb.
 // Outputs other CTAs read go out as tagged words (`tag`); the K/V row also lands
 // in the cache for later tokens.
-template <int KIND>
-__device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, int pos, int r0, int a, float va, int b,
-                                            float vb, bool hasb, const StageRegs &sr, unsigned tag) {
+__device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int kind, int l, int pos, int r0, int a,
+                                            float va, int b, float vb, bool hasb, const StageRegs &sr, unsigned tag) {
   const int lane = threadIdx.x & 31;
-  if constexpr (KIND == ST_QKV) {  // a even, b = a + 1: RoPE pair (rope.rs:25-31), then q / K / V
+  if (kind == ST_QKV) {  // a even, b = a + 1: RoPE pair (rope.rs:25-31), then q / K / V
     const int j = (a % p.hd) >> 1;
     const float c = __shfl_sync(FULL, j < 32 ? sr.c0 : sr.c1, j & 31);
     const float s = __shfl_sync(FULL, j < 32 ? sr.s0 : sr.s1, j & 31);
@@ -1109,14 +783,14 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int l, in
         st_ll(p.kv_ll + p.KVd + vr + 1, vb, tag);
       }
     }
-  } else if constexpr (KIND == ST_O || KIND == ST_DOWN) {  // residual (elementwise_add.rs:47-61)
+  } else if (kind == ST_O || kind == ST_DOWN) {  // residual (elementwise_add.rs:47-61)
     const float ha = __shfl_sync(FULL, sr.hres, (a - r0) & 31);
     const float hb = __shfl_sync(FULL, sr.hres, (b - r0) & 31);
     if (lane == 0) {
       st_ll(p.hid_ll + a, __fadd_rn(ha, va), tag);
       if (hasb) st_ll(p.hid_ll + b, __fadd_rn(hb, vb), tag);
     }
-  } else if constexpr (KIND == ST_GU) {  // a = gate row, vb = up (silu.rs:4-8, elementwise_mul.rs:3-17)
+  } else if (kind == ST_GU) {  // a = gate row, vb = up (silu.rs:4-8, elementwise_mul.rs:3-17)
     if (lane == 0) st_ll(p.act_ll + a, __fmul_rn(__fmul_rn(va, sigmoid_ref(va)), vb), tag);
   } else {  // LM head logits
     if (lane == 0) {
@@ -1153,26 +827,27 @@ __device__ __forceinline__ void group_sync(int grp) {
 // slot refills overlap the other group's dot products. Within a tile a warp takes
 // two rows at a time (a row pair, or two rows of its input segment when the rows
 // are split into segments) and reduces them together.
-template <int T, int KIND>
-__device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int l,
+template <int T>
+__device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int kind, int l,
                              const ActRegs<T> &x, float osc, int &slot, unsigned &phase, int &tile_ctr, int pos,
                              const StageRegs &sr, unsigned tag) {
   constexpr int NW = nwords<T>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = warp / NG, wig = warp % NG;
-  const int nseg = stage_nseg(p, KIND), rb = stage_rb(p, KIND), Tr = p.tile_rows[KIND];
-  const int in_dim = KIND == ST_O ? p.Q : (KIND == ST_DOWN ? p.F : p.E);
+  const int nseg = stage_nseg(p, kind), rb = stage_rb(p, kind), Tr = p.tile_rows[kind];
+  const int in_dim = kind == ST_O ? p.Q : (kind == ST_DOWN ? p.F : p.E);
+  const bool gu = kind == ST_GU;
   const int seg = wig % nseg, rpw = NG / nseg, rs = wig / nseg;
   const bool active = lane_active<T>(seg, lane, in_dim);
   const uint32_t slots = smem_u32(rg.slots);
   const bool lead = wig == 0 && lane == 0;  // stamps of the group that has the tile
   int r0, r1;
-  stage_rows(p, KIND, l, blockIdx.x, r0, r1);
-  const int stage_id = KIND == ST_LM ? 5 * p.L : 5 * l + (KIND == ST_QKV ? 0 : KIND + 1);
+  stage_rows(p, kind, l, blockIdx.x, r0, r1);
+  const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : kind + 1);
   for (int r = r0; r < r1; r += Tr) {
     if ((tile_ctr & 1) == grp) {
       const int n = min(Tr, r1 - r);
-      const int rows = KIND == ST_GU ? 2 * n : n;
+      const int rows = gu ? 2 * n : n;
       const uint32_t tile = slots + (uint32_t)slot * SLOT;
       float *red = sm.red[2 * grp + ((tile_ctr >> 1) & 1)];
       const bool ok = slot_wait(p, rg, sm, slot, tile_ctr, phase);
@@ -1182,9 +857,9 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
       if (ok) {
         if (nseg == 1) {
           // warp-owned row pairs (2i, 2i+1), or (gate i, up i)
-          const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
+          const int npairs = gu ? n : (n + 1) >> 1;
           for (int i = wig; i < npairs; i += NG) {
-            const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
+            const int a = gu ? i : 2 * i, b = gu ? n + i : 2 * i + 1;
             const bool hasb = b < rows;
             float va = 0.f, vb = 0.f;
             if (active) {
@@ -1196,8 +871,8 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
             }
             const float2 v = warp_sum2(va, vb);
             const float fa = v.x * osc, fb = v.y * osc;
-            if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, fa, r + i, fb, true, sr, tag);
-            else finish_rows<KIND>(p, sm, l, pos, r0, r + a, fa, r + b, fb, hasb, sr, tag);
+            if (gu) finish_rows(p, sm, kind, l, pos, r0, r + i, fa, r + i, fb, true, sr, tag);
+            else finish_rows(p, sm, kind, l, pos, r0, r + a, fa, r + b, fb, hasb, sr, tag);
           }
         } else {
           // segment-split rows: this warp's segment of rows rs, rs + rpw, ...; the
@@ -1227,9 +902,9 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
         group_sync(grp);
         // finish the tile's rows: warp wig takes row pairs wig, wig + NG, ...
         if (ok) {
-          const int npairs = KIND == ST_GU ? n : (n + 1) >> 1;
+          const int npairs = gu ? n : (n + 1) >> 1;
           for (int i = wig; i < npairs; i += NG) {
-            const int a = KIND == ST_GU ? i : 2 * i, b = KIND == ST_GU ? n + i : 2 * i + 1;
+            const int a = gu ? i : 2 * i, b = gu ? n + i : 2 * i + 1;
             const bool hasb = b < rows;
             float va = 0.f, vb = 0.f;
             for (int s = 0; s < nseg; s++) {
@@ -1238,8 +913,8 @@ __device__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const in
             }
             va *= osc;
             vb *= osc;
-            if (KIND == ST_GU) finish_rows<KIND>(p, sm, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
-            else finish_rows<KIND>(p, sm, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
+            if (gu) finish_rows(p, sm, kind, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
+            else finish_rows(p, sm, kind, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
           }
         }
       }
@@ -1534,10 +1209,9 @@ __device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l
 
 template <int T, int DPL>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    k_decode(const Params *__restrict__ pp, const uint32_t *tok_in, uint32_t *tok_out, uint32_t *out_ids,
+    k_decode(const __grid_constant__ Params p, const uint32_t *tok_in, uint32_t *tok_out, uint32_t *out_ids,
              int step) {
   extern __shared__ __align__(128) uint8_t dsm[];
-  const Params &p = *pp;
   Ring rg;
   rg.slots = dsm;
   rg.full = reinterpret_cast<uint64_t *>(dsm + (size_t)NSLOT * SLOT);
@@ -1575,47 +1249,50 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   unsigned phase = 0;
   ActRegs<T> x;
   StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int l = 0; l < p.L; l++) {
-    const LayerW &W = p.layers[l];
+  // One pass per projection stage: QKV, O, gate/up, down of every layer, then the
+  // LM head; a single matvec call site keeps one copy of the tile loop in the
+  // instruction cache for all of them.
+  for (int si = 0; si <= 4 * p.L; si++) {
+    const int l = si >> 2;
+    const int kind = l == p.L ? ST_LM : (si & 3);  // ST_QKV, ST_O, ST_GU, ST_DOWN are 0..3
+    const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : kind + 1);
+    const LayerW &W = p.layers[l < p.L ? l : 0];
     const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
-    // ---- RMSNorm + QKV + RoPE + KV append
-    load_stage_regs(p, ST_QKV, l, pos, sr, 0u);
+    load_stage_regs(p, kind, l, pos, sr, kind == ST_DOWN ? mk_tag(launch, l, TG_POST_O) : hid_in);
+    if (si > 0) cta_sync();  // every warp is done with the previous input: the staging buffer is rewritten
     float osc;
-    if (l == 0)
-      osc = stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1,
-                            p.embd + (size_t)tok * p.rb_E, blockIdx.x == 0, hid_in);
-    else
-      osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E, 8 * (5 * l) + 1);
-    stamp(p, 8 * (5 * l) + 2);
-    matvec_stage<T, ST_QKV>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_QKV));
-    // ---- attention (waits on q / K / V words, not on a barrier)
-    cta_sync();  // shared scratch of the staging buffer is reused below
-    if (DPL <= 2 && pos < SHORT_CTX) attention_heads<DPL <= 2 ? DPL : 2>(p, sm, l, pos, mk_tag(launch, l, TG_QKV), mk_tag(launch, l, TG_ATTN));
-    else attention_chunks<DPL>(p, sm, l, pos, mk_tag(launch, l, TG_QKV), mk_tag(launch, l, TG_ATTN));
-    stamp(p, 8 * (5 * l + 1) + 6);
-    // ---- O projection + residual
-    load_stage_regs(p, ST_O, l, pos, sr, hid_in);
-    osc = stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q, 8 * (5 * l + 2) + 1);
-    stamp(p, 8 * (5 * l + 2) + 2);
-    matvec_stage<T, ST_O>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_O));
-    // ---- RMSNorm + gate/up + SiLU*up
-    cta_sync();
-    osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, l, TG_POST_O), W.ffn_norm, p.E, p.nseg_E, 8 * (5 * l + 3) + 1);
-    stamp(p, 8 * (5 * l + 3) + 2);
-    matvec_stage<T, ST_GU>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_ACT));
-    // ---- down + residual
-    load_stage_regs(p, ST_DOWN, l, pos, sr, mk_tag(launch, l, TG_POST_O));
-    cta_sync();
-    osc = stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F, 8 * (5 * l + 4) + 1);
-    stamp(p, 8 * (5 * l + 4) + 2);
-    matvec_stage<T, ST_DOWN>(p, rg, sm, tbl, l, x, osc, slot, phase, tile_ctr, pos, sr, mk_tag(launch, l, TG_POST_DOWN));
-    cta_sync();
+    unsigned tag_out;
+    if (kind == ST_QKV) {
+      if (l == 0)
+        osc = stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, 8 * stage_id + 1,
+                                    p.embd + (size_t)tok * p.rb_E, blockIdx.x == 0, hid_in);
+      else
+        osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E, 8 * stage_id + 1);
+      tag_out = mk_tag(launch, l, TG_QKV);
+    } else if (kind == ST_O) {
+      osc = stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q,
+                                  8 * stage_id + 1);
+      tag_out = mk_tag(launch, l, TG_POST_O);
+    } else if (kind == ST_DOWN) {
+      osc = stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F,
+                                  8 * stage_id + 1);
+      tag_out = mk_tag(launch, l, TG_POST_DOWN);
+    } else {  // gate/up after the FFN norm, or the LM head after the final norm (model.rs:72-95)
+      const bool lm = kind == ST_LM;
+      osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, lm ? mk_tag(launch, p.L - 1, TG_POST_DOWN) : mk_tag(launch, l, TG_POST_O),
+                                 lm ? p.out_norm : W.ffn_norm, p.E, p.nseg_E, 8 * stage_id + 1);
+      tag_out = lm ? 0u : mk_tag(launch, l, TG_ACT);
+    }
+    stamp(p, 8 * stage_id + 2);
+    matvec_stage<T>(p, rg, sm, tbl, kind, l, x, osc, slot, phase, tile_ctr, pos, sr, tag_out);
+    if (kind == ST_QKV) {
+      // ---- attention (waits on q / K / V words, not on a barrier)
+      cta_sync();  // shared scratch of the staging buffer is reused below
+      if (DPL <= 2 && pos < SHORT_CTX) attention_heads<DPL <= 2 ? DPL : 2>(p, sm, l, pos, tag_out, mk_tag(launch, l, TG_ATTN));
+      else attention_chunks<DPL>(p, sm, l, pos, tag_out, mk_tag(launch, l, TG_ATTN));
+      stamp(p, 8 * (5 * l + 1) + 6);
+    }
   }
-  // ---- final RMSNorm + LM head (last row only, model.rs:72-95)
-  const float osc_lm = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, mk_tag(launch, p.L - 1, TG_POST_DOWN), p.out_norm, p.E, p.nseg_E,
-                       8 * (5 * p.L) + 1);
-  stamp(p, 8 * (5 * p.L) + 2);
-  matvec_stage<T, ST_LM>(p, rg, sm, tbl, p.L, x, osc_lm, slot, phase, tile_ctr, pos, sr, 0u);
   cta_sync();
   stamp(p, p.tl_stride - 2);
   // ---- greedy argmax: this CTA's rows (kept in shared memory) in order, then the
@@ -1708,7 +1385,8 @@ __global__ void k_build_tiles(const Params *__restrict__ pp, int2 *tiles, int *n
 struct DecodeState {
   bool available = false;
   int dev_pos = 0;  // position the device counter holds once queued launches finish
-  dk::Params *d_params = nullptr;
+  dk::Params *d_params = nullptr;  // for the tile-table builder
+  dk::Params hp{};                 // the decode kernel's by-value parameter (constant bank)
   void *kernel = nullptr;
   size_t smem = 0;
   int grid = 0;
@@ -1889,6 +1567,7 @@ int decode_prepare(sq_ctx *c) {
   st->n_kv_heads = cf.n_kv_heads;
   st->n_layers = cf.n_blocks;
   st->d_pos = h.pos;
+  st->hp = h;
   st->kernel = kern;
   st->smem = smem;
   st->grid = nsm;
@@ -1919,7 +1598,7 @@ int decode_launch(sq_ctx *c, uint32_t *d_tok, uint32_t *out_ids, int step) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void *args[] = {&st->d_params, &d_tok, &d_tok, &out_ids, &step};
+  void *args[] = {&st->hp, &d_tok, &d_tok, &out_ids, &step};
   SQ_CUDA(cudaLaunchKernelExC(&cfg, st->kernel, args));
   c->seq_len += 1;
   st->dev_pos += 1;
