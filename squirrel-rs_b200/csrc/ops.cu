@@ -393,7 +393,7 @@ static void linear_q8_t(cudaStream_t s, const uint8_t *xq, int m, int in_dim, co
 }
 
 cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, const void *w, int wtype,
-                          int out_dim, float *y, int acts_q8, void *xq) {
+                          int out_dim, float *y, int acts_q8, void *xq, float *ws, size_t ws_floats) {
   const uint8_t *wb = (const uint8_t *)w;
   if (acts_q8 && wtype != SQ_BF16) {
     if (x) {
@@ -402,6 +402,8 @@ cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, con
     }
     if (wtype == SQ_Q8_0) linear_q8_t<SQ_Q8_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
     else linear_q8_t<SQ_Q4_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
+  } else if (m >= 2) {  // several rows (prefill): tiled GEMM
+    return launch_gemm_f32w(s, x, m, in_dim, w, wtype, out_dim, y, ws, ws_floats);
   } else {
     if (wtype == SQ_Q8_0) linear_f32_t<SQ_Q8_0>(s, x, m, in_dim, wb, out_dim, y);
     else if (wtype == SQ_Q4_0) linear_f32_t<SQ_Q4_0>(s, x, m, in_dim, wb, out_dim, y);

@@ -9,8 +9,13 @@
 namespace sq {
 
 // out[m][out_dim] = x[m][in_dim] @ w; acts_q8 uses `xq` (m*in/32 Q8_0 blocks) when non-null.
+// f32 activations with m >= 2 run the tiled GEMM; `ws` (ws_floats floats, may be null)
+// lets it split K when the output tiles alone would not cover the SMs.
 cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, const void *w, int wtype,
-                          int out_dim, float *y, int acts_q8, void *xq);
+                          int out_dim, float *y, int acts_q8, void *xq, float *ws = nullptr, size_t ws_floats = 0);
+// The tiled GEMM itself (gemm.cu): y[m][N] = x[m][K] @ w^T, native weight rows.
+cudaError_t launch_gemm_f32w(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
+                             float *ws, size_t ws_floats);
 cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out);
 cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype,
                          int embed_dim, int vocab, float *out);

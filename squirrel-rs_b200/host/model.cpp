@@ -458,6 +458,8 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
   SQ_CUDA(ctx_alloc(x.get(), &x->logits, (size_t)c.vocab_size));
   const int widest = std::max(std::max(E, F), Q);
   SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->xq, (size_t)R * (widest / QK) * Q8_BYTES));
+  x->gemm_ws_floats = (size_t)4 * R * widest;
+  SQ_CUDA(ctx_alloc(x.get(), &x->gemm_ws, x->gemm_ws_floats));
   x->sdpa_part_floats = sdpa_max_partials_floats(c.head_dim);
   SQ_CUDA(ctx_alloc(x.get(), &x->sdpa_part, x->sdpa_part_floats));
   SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->argmax_part, (size_t)argmax_partials(c.vocab_size) * 32));
@@ -537,23 +539,23 @@ static cudaError_t forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool la
     float *kc = c->kc + l * layer_kv, *vc = c->vc + l * layer_kv;
     TRY(launch_rms_norm(s, c->hidden, L.attn_norm, c->normed, n, E, cf.rms_eps));
     if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));  // shared quantization
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.q, wt, Q, c->q, aq, c->xq));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.k, wt, KVd, c->k, aq, c->xq));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.v, wt, KVd, c->v, aq, c->xq));
+    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.q, wt, Q, c->q, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.k, wt, KVd, c->k, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.v, wt, KVd, c->v, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_rope_rows_table(s, c->q, n, Q, pos, c->d_cos, c->d_sin, half));
     TRY(launch_rope_rows_table(s, c->k, n, KVd, pos, c->d_cos, c->d_sin, half));
     TRY(launch_kv_append(s, c->k, c->v, kc, vc, n, cf.n_kv_heads, cf.head_dim, pos, c->max_ctx));
     const int ns = sdpa_num_splits(n, pos + n, cf.n_heads);
     TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim,
                     (long long)c->max_ctx * cf.head_dim, ns, c->sdpa_part));
-    TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq));
+    TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
     TRY(launch_rms_norm(s, c->hidden, L.ffn_norm, c->normed, n, E, cf.rms_eps));
     if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.gate, wt, F, c->gate, aq, c->xq));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.up, wt, F, c->up, aq, c->xq));
+    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.gate, wt, F, c->gate, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.up, wt, F, c->up, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_silu_mul(s, c->gate, c->up, c->act, (size_t)n * F));
-    TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq));
+    TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
   }
   c->seq_len += n;
@@ -561,7 +563,7 @@ static cudaError_t forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool la
     // final norm of the last row only: rows are normalized independently (model.rs:72-87)
     TRY(launch_rms_norm(s, c->hidden + (size_t)(n - 1) * E, m->out_norm, c->normed, 1, E, cf.rms_eps));
     TRY(launch_linear(s, c->normed, 1, E, m->out_w, m->out_type, cf.vocab_size, c->logits,
-                      m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16, c->xq));
+                      m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_argmax(s, c->logits, cf.vocab_size, c->argmax_part, c->d_argmax));
   }
 #undef TRY
