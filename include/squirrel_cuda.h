@@ -178,6 +178,30 @@ int sq_generate(sq_ctx *c, const uint32_t *prompt, size_t n_prompt, int max_toke
  * next), no host round trip between steps; the ids land in out_ids (host). The
  * context must hold at least one position (a prior sq_forward). */
 int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids);
+/* ---- tensor parallelism (several GPUs, one process per GPU) -----------------------
+ * No counterpart in the reference (a CPU engine): the multi-GPU form of the model
+ * level above, Megatron column/row sharding with an NCCL all-reduce after the O and
+ * down projections and a greedy argmax across the vocabulary shards. Every rank
+ * makes the same calls in the same order (sq_forward, sq_decode_steps,
+ * sq_generate, sq_ctx_logits are collective); each rank's result is the whole
+ * model's. Rank 0 makes the id with sq_nccl_unique_id and shares its bytes with
+ * the other ranks (e.g. over torch.distributed). NCCL is loaded at first use. */
+/* ncclGetUniqueId into out (n >= 128 bytes). */
+int sq_nccl_unique_id(void *out, size_t n);
+/* sq_model_create / sq_model_load_gguf as rank tp_rank of tp_size GPUs. n_heads,
+ * n_kv_heads, vocab_size and ffn_dim/32 must divide by tp_size. */
+int sq_model_create_tp(const sq_llama_config *cfg, int device, int acts, int tp_rank, int tp_size,
+                       const void *nccl_id, sq_model **out);
+int sq_model_load_gguf_tp(const char *path, int device, int acts, int tp_rank, int tp_size, const void *nccl_id,
+                          sq_model **out);
+/* The shard of one GGUF tensor that rank tp_rank holds (host memory, no GPU):
+ * attn_q/k/v, ffn_gate/up and output keep their rank's rows; attn_output and
+ * ffn_down keep their rank's whole blocks of every row; everything else is copied.
+ * dst == NULL only reports out_dims / out_bytes. */
+int sq_tp_shard_tensor(const char *name, int ggml_type, const uint64_t *dims, int n_dims, int tp_rank, int tp_size,
+                       const void *src, size_t src_bytes, void *dst, size_t dst_cap, uint64_t *out_dims,
+                       size_t *out_bytes);
+
 /* Device stream of the context (cudaStream_t), for timing with events. */
 void *sq_ctx_stream(sq_ctx *c);
 /* Kernel launches one decode step of this context issues: 1 when the persistent

@@ -26,6 +26,18 @@ def sources():
     return cu, cpp
 
 
+def nccl_include():
+    """Directory of nccl.h (types only: libnccl is opened at run time, not linked)."""
+    for d in ("/usr/include", os.path.join(CUDA, "include")):
+        if os.path.exists(os.path.join(d, "nccl.h")):
+            return d
+    try:
+        import nvidia.nccl
+        return os.path.join(os.path.dirname(nvidia.nccl.__file__), "include")
+    except Exception:
+        return "/usr/include"
+
+
 def headers():
     out = [os.path.join(ROOT, "include", "squirrel_cuda.h")]
     for d in ("csrc", "host"):
@@ -43,6 +55,7 @@ def _compile(src):
                                "--expt-relaxed-constexpr", "-c", src, "-o", obj]
     else:
         cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-I" + os.path.join(CUDA, "include"),
+               "-I" + nccl_include(),
                "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
@@ -62,7 +75,7 @@ def build(force: bool = False) -> str:
         objs = list(ex.map(_compile, cu + cpp))
     if not force and os.path.exists(LIB) and all(os.path.getmtime(LIB) >= os.path.getmtime(o) for o in objs):
         return LIB
-    cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lpthread", "-ldl", "-lrt"]
+    cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lpthread", "-ldl", "-lrt"]  # no -lnccl
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

@@ -1471,6 +1471,7 @@ int decode_prepare(sq_ctx *c) {
   auto *st = new DecodeState();
   c->dec = st;
   if (getenv("SQ_DISABLE_DECODE_KERNEL")) return SQ_OK;
+  if (m->tp_size > 1) return SQ_OK;  // tensor-parallel contexts run the op-level sequence with NCCL
   const int E = cf.embed_dim, Q = cf.n_heads * cf.head_dim, KVd = cf.n_kv_heads * cf.head_dim, F = cf.ffn_dim;
   const int wt = cf.weight_type, bb = block_bytes(wt);
   // supported shapes: same type everywhere, rows multiple of 16 bytes, <= 8 segments, GQA group 4

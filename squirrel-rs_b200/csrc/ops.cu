@@ -341,6 +341,26 @@ __global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax_final(const ArgState 
   if (threadIdx.x == 0) *out = arg_result(s);
 }
 
+// The greedy argmax state of one vocabulary shard, indices shifted to the whole
+// vocabulary; and the fold of the shards' states in shard (= index) order.
+__global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax_state(const ArgState *part, int np, long long offset,
+                                                                 ArgState *out) {
+  const int per = (np + ARGMAX_THREADS - 1) / ARGMAX_THREADS;
+  ArgState s = arg_empty();
+  for (int i = threadIdx.x * per; i < (threadIdx.x + 1) * per && i < np; i++) s = arg_combine(s, part[i]);
+  s = block_arg_reduce(s);
+  if (threadIdx.x == 0) {
+    if (s.best >= 0) s.best += offset;
+    if (s.nan >= 0) s.nan += offset;
+    *out = s;
+  }
+}
+__global__ void k_argmax_fold(const ArgState *states, int n, long long *out) {
+  ArgState s = arg_empty();
+  for (int i = 0; i < n; i++) s = arg_combine(s, states[i]);
+  *out = arg_result(s);
+}
+
 // ------------------------------------------------------------------------------------
 // launchers
 // ------------------------------------------------------------------------------------
@@ -469,6 +489,19 @@ cudaError_t launch_silu_mul(cudaStream_t s, const float *g, const float *u, floa
 }
 
 int argmax_partials(size_t n) { return (int)((n + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK); }
+
+cudaError_t launch_argmax_state(cudaStream_t s, const float *x, size_t n, long long offset, void *partials,
+                                void *state) {
+  const int np = argmax_partials(n);
+  k_argmax_partial<<<np, ARGMAX_THREADS, 0, s>>>(x, n, (ArgState *)partials);
+  k_argmax_state<<<1, ARGMAX_THREADS, 0, s>>>((const ArgState *)partials, np, offset, (ArgState *)state);
+  return cudaGetLastError();
+}
+cudaError_t launch_argmax_fold(cudaStream_t s, const void *states, int n, long long *out) {
+  k_argmax_fold<<<1, 1, 0, s>>>((const ArgState *)states, n, out);
+  return cudaGetLastError();
+}
+size_t argmax_state_bytes() { return sizeof(ArgState); }
 
 cudaError_t launch_argmax(cudaStream_t s, const float *x, size_t n, void *partials, long long *out) {
   const int np = argmax_partials(n);

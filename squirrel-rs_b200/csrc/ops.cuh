@@ -35,6 +35,12 @@ cudaError_t launch_dequantize(cudaStream_t s, const void *blocks, int wtype, siz
 // Two-stage greedy argmax; `partials` holds at least argmax_partials(n) states (16 bytes each).
 int argmax_partials(size_t n);
 cudaError_t launch_argmax(cudaStream_t s, const float *x, size_t n, void *partials, long long *out);
+// Tensor parallel: the argmax state of a vocabulary shard starting at `offset`
+// (argmax_state_bytes() bytes), and the fold of n shard states in shard order.
+cudaError_t launch_argmax_state(cudaStream_t s, const float *x, size_t n, long long offset, void *partials,
+                                void *state);
+cudaError_t launch_argmax_fold(cudaStream_t s, const void *states, int n, long long *out);
+size_t argmax_state_bytes();
 
 // Causal GQA attention. q/out rows: [seq_q][n_heads*hd]; key s of kv head g lives at
 // k + s*k_pos_stride + g*k_head_stride (same for v). `part` is scratch for split-KV

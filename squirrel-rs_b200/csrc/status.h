@@ -25,6 +25,13 @@ inline int block_bytes(int t) {
   }
 }
 inline bool is_weight_type(int t) { return t == SQ_Q8_0 || t == SQ_Q4_0 || t == SQ_BF16; }
+// Bytes of a tensor of numel elements (0 for an unsupported type or a partial block).
+inline size_t tensor_nbytes(int type, uint64_t numel) {
+  if (type == SQ_F32) return numel * 4;
+  const int bb = block_bytes(type);
+  if (!bb || numel % QK) return 0;
+  return numel / QK * bb;
+}
 
 // ---- error plumbing -------------------------------------------------------------
 void set_error(const std::string &msg);

@@ -157,13 +157,6 @@ struct GgufFile {
   }
 };
 
-size_t tensor_nbytes(int type, uint64_t numel) {
-  if (type == SQ_F32) return numel * 4;
-  int bb = block_bytes(type);
-  if (!bb || numel % QK) return 0;
-  return numel / QK * bb;
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------------------------
@@ -202,6 +195,7 @@ sq_model::~sq_model() {
   cudaSetDevice(device);
   for (auto &kv : tensors) cudaFree(kv.second.ptr);
   cudaFree(d_inv_freq);
+  nccl_comm_destroy(nccl);
   cudaSetDevice(prev);
 }
 
@@ -217,20 +211,51 @@ static int validate_config(const sq_llama_config &c) {
   return SQ_OK;
 }
 
-extern "C" int sq_model_create(const sq_llama_config *cfg, int device, int acts, sq_model **out) {
+// Model creation, alone (tp_size 1) or as rank tp_rank of a tensor-parallel group
+// whose members share the NCCL unique id `nccl_id`.
+static int model_create(const sq_llama_config *cfg, int device, int acts, int tp_rank, int tp_size,
+                        const void *nccl_id, sq_model **out) {
   if (!cfg || !out) return fail(SQ_ERR_ARG, "model_create: null pointer");
   *out = nullptr;
   int st = validate_config(*cfg);
   if (st) return st;
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return fail(SQ_ERR_ARG, "model_create: bad tp rank / size");
+  if (tp_size > 1) {
+    if (!nccl_id) return fail(SQ_ERR_ARG, "model_create: tensor parallel needs an NCCL unique id");
+    if (cfg->n_heads % tp_size || cfg->n_kv_heads % tp_size || cfg->ffn_dim % (32 * tp_size) ||
+        cfg->vocab_size % tp_size)
+      return fail(SQ_ERR_CONFIG, "model_create: heads, kv heads, FFN blocks and vocabulary must divide by tp_size");
+  }
   int ndev = 0;
   SQ_CUDA(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) return fail(SQ_ERR_ARG, "model_create: no such device");
   auto m = std::make_unique<sq_model>();
   m->cfg = *cfg;
+  m->lc = *cfg;
+  m->lc.n_heads = cfg->n_heads / tp_size;
+  m->lc.n_kv_heads = cfg->n_kv_heads / tp_size;
+  m->lc.ffn_dim = cfg->ffn_dim / tp_size;
+  m->lc.vocab_size = cfg->vocab_size / tp_size;
+  m->vocab0 = tp_rank * m->lc.vocab_size;
   m->device = device;
   m->acts = acts == SQ_ACTS_Q8 ? SQ_ACTS_Q8 : SQ_ACTS_F32;
+  m->tp_rank = tp_rank;
+  m->tp_size = tp_size;
+  if (tp_size > 1) {
+    SQ_CUDA(cudaSetDevice(device));
+    if ((st = nccl_comm_init(nccl_id, tp_rank, tp_size, &m->nccl))) return st;
+  }
   *out = m.release();
   return SQ_OK;
+}
+
+extern "C" int sq_model_create(const sq_llama_config *cfg, int device, int acts, sq_model **out) {
+  return model_create(cfg, device, acts, 0, 1, nullptr, out);
+}
+
+extern "C" int sq_model_create_tp(const sq_llama_config *cfg, int device, int acts, int tp_rank, int tp_size,
+                                  const void *nccl_id, sq_model **out) {
+  return model_create(cfg, device, acts, tp_rank, tp_size, nccl_id, out);
 }
 
 extern "C" int sq_model_upload_tensor(sq_model *m, const char *name, int ggml_type, const uint64_t *dims,
@@ -248,8 +273,23 @@ extern "C" int sq_model_upload_tensor(sq_model *m, const char *name, int ggml_ty
   t.type = ggml_type;
   t.dims.assign(dims, dims + n_dims);
   t.nbytes = nbytes;
-  SQ_CUDA(cudaMalloc(&t.ptr, (nbytes + 255) / 256 * 256));  // native block layout, 256-byte aligned
-  SQ_CUDA(cudaMemcpy(t.ptr, host_data, nbytes, cudaMemcpyHostToDevice));
+  std::vector<uint8_t> shard;
+  if (m->tp_size > 1) {  // this rank's shard, still in the native block layout
+    uint64_t sd[4];
+    size_t sb = 0;
+    int st = sq_tp_shard_tensor(name, ggml_type, dims, n_dims, m->tp_rank, m->tp_size, host_data, nbytes, nullptr, 0,
+                                sd, &sb);
+    if (st) return st;
+    shard.resize(sb);
+    if ((st = sq_tp_shard_tensor(name, ggml_type, dims, n_dims, m->tp_rank, m->tp_size, host_data, nbytes,
+                                 shard.data(), sb, sd, &sb)))
+      return st;
+    t.dims.assign(sd, sd + n_dims);
+    t.nbytes = sb;
+    host_data = shard.data();
+  }
+  SQ_CUDA(cudaMalloc(&t.ptr, (t.nbytes + 255) / 256 * 256));  // native block layout, 256-byte aligned
+  SQ_CUDA(cudaMemcpy(t.ptr, host_data, t.nbytes, cudaMemcpyHostToDevice));
   auto it = m->tensors.find(name);
   if (it != m->tensors.end()) cudaFree(it->second.ptr);
   m->tensors[name] = t;
@@ -269,9 +309,9 @@ static int need_tensor(sq_model *m, const std::string &name, int type, std::vect
 extern "C" int sq_model_finalize(sq_model *m) {
   if (!m) return fail(SQ_ERR_ARG, "finalize: null model");
   if (m->finalized) return SQ_OK;
-  const sq_llama_config &c = m->cfg;
+  const sq_llama_config &c = m->lc;  // this rank's shard of the projections
   const uint64_t E = c.embed_dim, Q = (uint64_t)c.n_heads * c.head_dim, KVd = (uint64_t)c.n_kv_heads * c.head_dim,
-                 F = c.ffn_dim, V = c.vocab_size;
+                 F = c.ffn_dim, V = c.vocab_size, Vall = m->cfg.vocab_size;
   const int wt = c.weight_type;
   m->layers.resize(c.n_blocks);
   const DevTensor *t;
@@ -298,7 +338,7 @@ extern "C" int sq_model_finalize(sq_model *m) {
     if ((st = need_tensor(m, nm("ffn_down.weight"), wt, {F, E}, &t))) return st;
     L.down = t->ptr;
   }
-  if ((st = need_tensor(m, "token_embd.weight", -1, {E, V}, &t))) return st;
+  if ((st = need_tensor(m, "token_embd.weight", -1, {E, Vall}, &t))) return st;  // replicated
   if (!is_weight_type(t->type)) return fail(SQ_ERR_INVALID_TYPE, "token_embd.weight: unsupported type");
   m->embd = t->ptr;
   m->embd_type = t->type;
@@ -309,8 +349,8 @@ extern "C" int sq_model_finalize(sq_model *m) {
     if (!is_weight_type(t->type)) return fail(SQ_ERR_INVALID_TYPE, "output.weight: unsupported type");
     m->out_w = t->ptr;
     m->out_type = t->type;
-  } else {  // tied LM head, weights.rs:87-89
-    m->out_w = m->embd;
+  } else {  // tied LM head, weights.rs:87-89 (this rank's vocabulary rows of token_embd)
+    m->out_w = (const uint8_t *)m->embd + tensor_nbytes(m->embd_type, (uint64_t)m->vocab0 * E);
     m->out_type = m->embd_type;
   }
   rope_inv_freq(c, m->inv_freq);
@@ -321,7 +361,8 @@ extern "C" int sq_model_finalize(sq_model *m) {
   return SQ_OK;
 }
 
-extern "C" int sq_model_load_gguf(const char *path, int device, int acts, sq_model **out) {
+static int load_gguf(const char *path, int device, int acts, int tp_rank, int tp_size, const void *nccl_id,
+                     sq_model **out) {
   if (!path || !out) return fail(SQ_ERR_ARG, "load_gguf: null pointer");
   *out = nullptr;
   GgufFile g;
@@ -365,7 +406,7 @@ extern "C" int sq_model_load_gguf(const char *path, int device, int acts, sq_mod
   c.weight_type = q->second.type;
 
   sq_model *m = nullptr;
-  if ((st = sq_model_create(&c, device, acts, &m))) return st;
+  if ((st = model_create(&c, device, acts, tp_rank, tp_size, nccl_id, &m))) return st;
   for (auto &kv : g.tensors) {
     const std::string &name = kv.first;
     const TInfo &t = kv.second;
@@ -396,6 +437,15 @@ extern "C" int sq_model_load_gguf(const char *path, int device, int acts, sq_mod
   }
   *out = m;
   return SQ_OK;
+}
+
+extern "C" int sq_model_load_gguf(const char *path, int device, int acts, sq_model **out) {
+  return load_gguf(path, device, acts, 0, 1, nullptr, out);
+}
+
+extern "C" int sq_model_load_gguf_tp(const char *path, int device, int acts, int tp_rank, int tp_size,
+                                     const void *nccl_id, sq_model **out) {
+  return load_gguf(path, device, acts, tp_rank, tp_size, nccl_id, out);
 }
 
 extern "C" int sq_model_config(const sq_model *m, sq_llama_config *out) {
@@ -432,7 +482,7 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
   if (!m || !out) return fail(SQ_ERR_ARG, "ctx_create: null pointer");
   if (!m->finalized) return fail(SQ_ERR_ARG, "ctx_create: model not finalized");
   *out = nullptr;
-  const sq_llama_config &c = m->cfg;
+  const sq_llama_config &c = m->lc;  // this rank's heads, KV heads, FFN rows and vocabulary rows
   if (max_ctx <= 0) max_ctx = c.context_length > 0 && c.context_length < 8192 ? c.context_length : 8192;
   SQ_CUDA(cudaSetDevice(m->device));
   auto x = std::make_unique<sq_ctx>();
@@ -464,6 +514,11 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
   SQ_CUDA(ctx_alloc(x.get(), &x->sdpa_part, x->sdpa_part_floats));
   SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->argmax_part, (size_t)argmax_partials(c.vocab_size) * 32));
   SQ_CUDA(ctx_alloc(x.get(), &x->d_argmax, 1));
+  if (m->tp_size > 1) {
+    SQ_CUDA(ctx_alloc(x.get(), &x->logits_full, (size_t)m->cfg.vocab_size));
+    SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->arg_local, argmax_state_bytes()));
+    SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->arg_all, argmax_state_bytes() * m->tp_size));
+  }
   SQ_CUDA(ctx_alloc(x.get(), &x->d_tokens, (size_t)R));
   // RoPE table from the C library's sinf/cosf of pos * inv_freq[j] (rope.rs:25-26)
   const int half = c.head_dim / 2;
@@ -508,7 +563,7 @@ extern "C" int sq_ctx_launches_per_token(const sq_ctx *c, int *out) {
     return SQ_OK;
   }
   // the op-level sequence of forward_rows for one row, plus the token feedback kernel
-  const sq_llama_config &cf = c->m->cfg;
+  const sq_llama_config &cf = c->m->lc;
   const int aq = c->m->acts == SQ_ACTS_Q8 && cf.weight_type != SQ_BF16;
   const int split = sdpa_num_splits(1, c->seq_len + 1, cf.n_heads) > 1;
   *out = 1 + cf.n_blocks * (16 + 2 * aq + split) + 4 + 1;
@@ -519,21 +574,27 @@ namespace sq {
 
 // One prefill chunk of n rows at position c->seq_len through every layer
 // (layers.rs:81-109), then the LM head on the last row when `last`.
-static cudaError_t forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last) {
+static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last) {
   const sq_model *m = c->m;
-  const sq_llama_config &cf = m->cfg;
+  const sq_llama_config &cf = m->lc;  // this rank's shard (the whole model when tp_size == 1)
   cudaStream_t s = c->stream;
   const int E = cf.embed_dim, Q = cf.n_heads * cf.head_dim, KVd = cf.n_kv_heads * cf.head_dim, F = cf.ffn_dim;
   const int wt = cf.weight_type, half = cf.head_dim / 2;
   const int aq = m->acts == SQ_ACTS_Q8 && wt != SQ_BF16;
   const int pos = c->seq_len;
   const size_t layer_kv = (size_t)cf.n_kv_heads * c->max_ctx * cf.head_dim;
-  cudaError_t e;
-#define TRY(x)                        \
-  do {                                \
-    if ((e = (x)) != cudaSuccess) return e; \
+  const bool tp = m->tp_size > 1;
+#define TRY(x)                                                  \
+  do {                                                          \
+    const cudaError_t e_ = (x);                                 \
+    if (e_ != cudaSuccess) return cuda_fail(e_, "forward");     \
   } while (0)
-  TRY(launch_embed(s, d_ids, n, m->embd, m->embd_type, E, cf.vocab_size, c->hidden));
+#define TRY_ST(x)              \
+  do {                         \
+    const int st_ = (x);       \
+    if (st_) return st_;       \
+  } while (0)
+  TRY(launch_embed(s, d_ids, n, m->embd, m->embd_type, E, m->cfg.vocab_size, c->hidden));  // replicated table
   for (int l = 0; l < cf.n_blocks; l++) {
     const auto &L = m->layers[l];
     float *kc = c->kc + l * layer_kv, *vc = c->vc + l * layer_kv;
@@ -549,6 +610,7 @@ static cudaError_t forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool la
     TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim,
                     (long long)c->max_ctx * cf.head_dim, ns, c->sdpa_part));
     TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
     TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
     TRY(launch_rms_norm(s, c->hidden, L.ffn_norm, c->normed, n, E, cf.rms_eps));
     if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));
@@ -556,6 +618,7 @@ static cudaError_t forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool la
     TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.up, wt, F, c->up, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_silu_mul(s, c->gate, c->up, c->act, (size_t)n * F));
     TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));  // row-parallel down
     TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
   }
   c->seq_len += n;
@@ -564,10 +627,17 @@ static cudaError_t forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool la
     TRY(launch_rms_norm(s, c->hidden + (size_t)(n - 1) * E, m->out_norm, c->normed, 1, E, cf.rms_eps));
     TRY(launch_linear(s, c->normed, 1, E, m->out_w, m->out_type, cf.vocab_size, c->logits,
                       m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16, c->xq, c->gemm_ws, c->gemm_ws_floats));
-    TRY(launch_argmax(s, c->logits, cf.vocab_size, c->argmax_part, c->d_argmax));
+    if (!tp) {
+      TRY(launch_argmax(s, c->logits, cf.vocab_size, c->argmax_part, c->d_argmax));
+    } else {  // greedy over the vocabulary shards: per-rank states, folded in rank (= index) order
+      TRY(launch_argmax_state(s, c->logits, cf.vocab_size, m->vocab0, c->argmax_part, c->arg_local));
+      TRY_ST(nccl_all_gather_bytes(m->nccl, c->arg_local, c->arg_all, argmax_state_bytes(), s));
+      TRY(launch_argmax_fold(s, c->arg_all, m->tp_size, c->d_argmax));
+    }
   }
 #undef TRY
-  return cudaSuccess;
+#undef TRY_ST
+  return SQ_OK;
 }
 
 // Model::forward for ids already on the device (prefill in chunks; decode of one
@@ -576,8 +646,8 @@ int forward_device(sq_ctx *c, const uint32_t *d_ids, int n) {
   if (n == 1 && decode_available(c)) return decode_launch(c, const_cast<uint32_t *>(d_ids), nullptr, 0);
   for (int r0 = 0; r0 < n; r0 += c->ws_rows) {
     const int rows = std::min(c->ws_rows, n - r0);
-    cudaError_t e = forward_rows(c, d_ids + r0, rows, r0 + rows == n);
-    if (e != cudaSuccess) return cuda_fail(e, "forward");
+    const int st = forward_rows(c, d_ids + r0, rows, r0 + rows == n);
+    if (st) return st;
   }
   return SQ_OK;
 }
@@ -604,8 +674,7 @@ extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *ou
     if (rows == 1 && r0 == 0 && decode_available(c)) {
       st = decode_launch(c, c->d_tokens, nullptr, 0);
     } else {
-      cudaError_t e = forward_rows(c, c->d_tokens, rows, r0 + rows == n);
-      st = e == cudaSuccess ? SQ_OK : cuda_fail(e, "forward");
+      st = forward_rows(c, c->d_tokens, rows, r0 + rows == n);
     }
     if (st) return st;
   }
@@ -624,7 +693,14 @@ extern "C" int sq_ctx_logits(sq_ctx *c, float *out, size_t n) {
   if (n != (size_t)c->m->cfg.vocab_size) return fail(SQ_ERR_SHAPE, "ctx_logits: buffer must hold vocab_size floats");
   if (!c->have_logits) return fail(SQ_ERR_EMPTY, "ctx_logits: no forward pass yet");
   SQ_CUDA(cudaSetDevice(c->m->device));
-  SQ_CUDA(cudaMemcpyAsync(out, c->logits, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+  const float *src = c->logits;
+  if (c->m->tp_size > 1) {  // vocabulary shards gathered in rank order: every rank of the group calls this
+    const int st = nccl_all_gather_bytes(c->m->nccl, c->logits, c->logits_full,
+                                         (size_t)c->m->lc.vocab_size * sizeof(float), c->stream);
+    if (st) return st;
+    src = c->logits_full;
+  }
+  SQ_CUDA(cudaMemcpyAsync(out, src, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
   SQ_CUDA(cudaStreamSynchronize(c->stream));
   return SQ_OK;
 }
@@ -670,9 +746,11 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
     if (decode_available(c)) {
       st = decode_launch(c, c->d_tokens, d_out, i);
     } else {
-      e = forward_rows(c, c->d_tokens, 1, true);
-      if (e == cudaSuccess) e = launch_feedback(c->stream, c->d_argmax, c->d_tokens, d_out, i);
-      st = e == cudaSuccess ? SQ_OK : cuda_fail(e, "decode_steps");
+      st = forward_rows(c, c->d_tokens, 1, true);
+      if (!st) {
+        e = launch_feedback(c->stream, c->d_argmax, c->d_tokens, d_out, i);
+        st = e == cudaSuccess ? SQ_OK : cuda_fail(e, "decode_steps");
+      }
     }
   }
   if (!st) {

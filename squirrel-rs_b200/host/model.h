@@ -18,14 +18,23 @@ struct DevTensor {
 struct DecodeState;  // persistent decode kernel resources (decode.cu)
 void rope_inv_freq(const sq_llama_config &c, std::vector<float> &out);
 int forward_device(sq_ctx *c, const uint32_t *d_ids, int n);
+// NCCL (tp.cpp): loaded on first use
+int nccl_comm_init(const void *id, int rank, int size, void **comm);
+void nccl_comm_destroy(void *comm);
+int nccl_all_reduce_sum(void *comm, float *buf, size_t n, cudaStream_t s);
+int nccl_all_gather_bytes(void *comm, const void *src, void *dst, size_t bytes_per_rank, cudaStream_t s);
 }  // namespace sq
 
 // LlamaWeights (models/llama/weights.rs:18-47) resolved to device pointers.
 struct sq_model {
-  sq_llama_config cfg{};
+  sq_llama_config cfg{};  // the whole model's configuration
+  sq_llama_config lc{};   // this rank's shard of it (q / kv heads, FFN rows, vocabulary rows)
   int device = 0;
   int acts = SQ_ACTS_F32;
   bool finalized = false;
+  int tp_rank = 0, tp_size = 1;  // tensor-parallel group (tp.cpp)
+  void *nccl = nullptr;          // ncclComm_t when tp_size > 1
+  int vocab0 = 0;                // first vocabulary row of this rank's LM-head shard
   std::unordered_map<std::string, sq::DevTensor> tensors;
   struct Layer {
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
@@ -63,6 +72,8 @@ struct sq_ctx {
   uint32_t *d_tokens = nullptr;
   float *d_cos = nullptr, *d_sin = nullptr;  // RoPE table [max_ctx][head_dim/2]
   sq::DecodeState *dec = nullptr;
+  float *logits_full = nullptr;  // tensor parallel: the gathered vocabulary
+  void *arg_local = nullptr, *arg_all = nullptr;  // tensor parallel: per-rank argmax states
   uint32_t *d_out_ids = nullptr;  // ids of sq_decode_steps
   int out_cap = 0;
   std::vector<void *> allocs;

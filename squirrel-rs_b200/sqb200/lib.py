@@ -80,6 +80,11 @@ SIGNATURES = {
     "sq_decode_steps": (_i, [_vp, _i, C.POINTER(C.c_uint32)]),
     "sq_ctx_stream": (_vp, [_vp]),
     "sq_ctx_launches_per_token": (_i, [_vp, C.POINTER(_i)]),
+    "sq_nccl_unique_id": (_i, [_vp, _sz]),
+    "sq_model_create_tp": (_i, [C.POINTER(LlamaConfig), _i, _i, _i, _i, _vp, C.POINTER(_vp)]),
+    "sq_model_load_gguf_tp": (_i, [C.c_char_p, _i, _i, _i, _i, _vp, C.POINTER(_vp)]),
+    "sq_tp_shard_tensor": (_i, [C.c_char_p, _i, C.POINTER(C.c_uint64), _i, _i, _i, _vp, _sz, _vp, _sz,
+                                C.POINTER(C.c_uint64), C.POINTER(_sz)]),
 }
 
 
@@ -232,14 +237,46 @@ def argmax_noalloc(logits, out=None):
 
 # ---- model level --------------------------------------------------------------------
 
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """ncclGetUniqueId (rank 0 makes it; every rank of the group uses the same bytes)."""
+    buf = C.create_string_buffer(NCCL_ID_BYTES)
+    _check(load().sq_nccl_unique_id(buf, NCCL_ID_BYTES))
+    return buf.raw
+
+
+def tp_shard_tensor(name, ggml_type, dims, data, tp_rank, tp_size):
+    """The shard of one GGUF tensor that rank tp_rank holds (host bytes, no GPU):
+    returns (dims, bytes)."""
+    L = load()
+    data = np.ascontiguousarray(data)
+    d = (C.c_uint64 * len(dims))(*dims)
+    od = (C.c_uint64 * len(dims))()
+    nb = C.c_size_t()
+    _check(L.sq_tp_shard_tensor(name.encode(), ggml_type, d, len(dims), tp_rank, tp_size, None, 0, None, 0, od,
+                                C.byref(nb)))
+    out = np.empty(nb.value, np.uint8)
+    _check(L.sq_tp_shard_tensor(name.encode(), ggml_type, d, len(dims), tp_rank, tp_size,
+                                data.ctypes.data_as(C.c_void_p), data.nbytes, out.ctypes.data_as(C.c_void_p),
+                                out.nbytes, od, C.byref(nb)))
+    return [int(v) for v in od], out
+
+
 class Model:
     """Llama3_2 on one GPU (models/llama/model.rs), loaded from a GGUF file."""
 
-    def __init__(self, path=None, device=0, acts=ACTS_F32, _handle=None):
+    def __init__(self, path=None, device=0, acts=ACTS_F32, _handle=None, tp_rank=0, tp_size=1, nccl_id=None):
+        """tp_size > 1: this process is rank tp_rank of a tensor-parallel group; every
+        rank passes the same nccl_id (bytes from nccl_unique_id() on rank 0)."""
         L = load()
         h = C.c_void_p()
         if _handle is not None:
             h = _handle
+        elif tp_size > 1:
+            buf = C.create_string_buffer(bytes(nccl_id), NCCL_ID_BYTES)
+            _check(L.sq_model_load_gguf_tp(path.encode(), device, acts, tp_rank, tp_size, buf, C.byref(h)))
         else:
             _check(L.sq_model_load_gguf(path.encode(), device, acts, C.byref(h)))
         self._h = h
