@@ -39,7 +39,10 @@ WORKLOADS = {
     "1b-q4_0": ("1b", "q4_0", 32),
     "1b-bf16": ("1b", "bf16", 32),
     "1b-q4_0-long": ("1b", "q4_0", 2048),
+    # Llama-3-8B shape, Q8_0, 128-token prompt: tensor parallel over every rank (config 5)
+    "8b-q8_0": ("8b", "q8_0", 128),
 }
+TP_WORKLOADS = {"8b-q8_0"}
 METRIC = "decode tok/s (Llama-3.2-1B Q8_0, bs1)"
 
 
@@ -204,10 +207,20 @@ def run_ours(args):
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     spec, wt, plen = WORKLOADS[args.workload]
+    tp = args.workload in TP_WORKLOADS and world > 1
+    if rank == 0 or not dist:
+        path = G.ensure_gguf(spec, wt)  # one writer per box; the other ranks wait
+    if dist:
+        dist.barrier()
     path = G.ensure_gguf(spec, wt)
     prompt = G.prompt_ids(plen, seed=1234)
     acts = lib.ACTS_Q8 if args.acts == "q8" else lib.ACTS_F32
-    model = lib.Model(path, device=local, acts=acts)
+    if tp:  # one model sharded over all ranks; rank 0's NCCL id goes to every rank
+        box = [lib.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        model = lib.Model(path, device=local, acts=acts, tp_rank=rank, tp_size=world, nccl_id=box[0])
+    else:
+        model = lib.Model(path, device=local, acts=acts)
     cfg = model.config
     max_ctx = plen + 2 * (args.warmup + args.steps) + 8
     ctx = model.new_context(max_ctx)
@@ -236,7 +249,8 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    value = world * args.steps / (ms / 1e3)
+    tokens_per_step = 1 if tp else world  # tensor parallel: the group makes one token a step
+    value = tokens_per_step * args.steps / (ms / 1e3)
     step_ms = ms / args.steps
 
     # e2e through the host-facing ABI: one sq_forward per token from host memory
@@ -256,30 +270,34 @@ def run_ours(args):
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * args.steps / e2e_s
+    e2e = tokens_per_step * args.steps / e2e_s
 
     # roofline of the decode step (one persistent-kernel launch per token when available)
     mean_kv = kv0 + (args.steps - 1) / 2
-    algo = bytes_per_step(cfg, cfg.weight_type, mean_kv)
+    algo = bytes_per_step(cfg, cfg.weight_type, mean_kv)  # the whole model's bytes (all ranks together)
     achieved = algo / (step_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
+    if tp:
+        peak *= world  # every rank streams its shard from its own HBM
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         th = cpu_threads()
-        tps, cpu_ids = cpu_sample(path, prompt, args.cpu_decode_steps, th)
+        cplen = plen if spec != "8b" else 8  # 8B on the CPU: a short prompt keeps the sample bounded
+        tps, cpu_ids = cpu_sample(path, prompt[:cplen], args.cpu_decode_steps, th)
         cpu = {"value": tps, "unit": "tok/s", "cores": th, "kind": "port",
-               "sample": f"{plen}-token prompt prefill untimed, then {args.cpu_decode_steps} timed decode tokens "
+               "sample": f"{cplen}-token prompt prefill untimed, then {args.cpu_decode_steps} timed decode tokens "
                          f"({spec} {wt}, W8A32 scalar x86 path, C restatement, {th} threads)"}
     if rank == 0:
         line = {
             "metric": METRIC if args.workload == "1b-q8_0" else f"decode tok/s ({args.workload}, bs1)",
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None,
             "dtype": "f32" if args.acts == "f32" else "int8",
             "data": "synthetic (seeded random-init GGUF N(0,0.02) quantized; uniform random prompt ids)",
             "config": {"workload": args.workload, "model": f"llama-3.2-{spec}-arch {wt}", "prompt": plen,
                        "batch": 1, "decode_steps": args.steps, "acts": args.acts,
-                       "parallelism": "replicas" if world > 1 else "single",
+                       "parallelism": f"tp{world}" if tp else ("replicas" if world > 1 else "single"),
                        "l2": "weights %.2f GB > 126 MB L2 per step; no flush needed" % (algo / 1e9),
                        "prefill_tok_s": plen / prefill_s, "kv_len_start": kv0},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},

@@ -176,21 +176,43 @@ def write_gguf(path: str, spec_name: str, wtype: int, seed: int = 0, rope_scalin
     with open(tmp, "wb") as f:
         f.write(header + b"\0" * pad)
         base = f.tell()
-        for ti, ((name, dims, ttype), off) in enumerate(zip(tensors, offsets)):
-            f.seek(base + off)
-            if ttype == F32:
-                f.write(np.ones(int(np.prod(dims)), np.float32).tobytes())
-                continue
-            rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, ti])))
-            rows, in_dim = dims[1], dims[0]
-            chunk = max(1, (1 << 20) // in_dim)  # small chunks: cache-resident temporaries
-            for r0 in range(0, rows, chunk):
-                n = min(chunk, rows - r0)
-                x = rng.standard_normal(n * in_dim, dtype=np.float32) * np.float32(0.02)
-                f.write(quantize(x, ttype).tobytes())
         f.truncate(base + offset)
+    jobs = [(tmp, base + off, ti, dims, ttype, seed) for ti, ((name, dims, ttype), off) in enumerate(zip(tensors, offsets))]
+    big = sum(int(np.prod(d)) for _, d, t in tensors if t != F32) > (1 << 28)
+    workers = min(16, os.cpu_count() or 1) if big else 1
+    workers = int(os.environ.get("SQB200_GEN_WORKERS", workers))
+    if workers > 1:  # every tensor has its own RNG stream and byte range: same bytes in any order
+        import concurrent.futures as cf
+        import multiprocessing as mp
+        with cf.ProcessPoolExecutor(workers, mp_context=mp.get_context("spawn")) as ex:
+            for _ in ex.map(_fill_tensor, jobs, chunksize=1):
+                pass
+    else:
+        for j in jobs:
+            _fill_tensor(j)
     os.replace(tmp, path)
     return path
+
+
+def _fill_tensor(job):
+    """Write one tensor's bytes at its file offset (its own PCG64 stream [seed, index])."""
+    tmp, at, ti, dims, ttype, seed = job
+    fd = os.open(tmp, os.O_WRONLY)
+    try:
+        if ttype == F32:
+            os.pwrite(fd, np.ones(int(np.prod(dims)), np.float32).tobytes(), at)
+            return
+        rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, ti])))
+        rows, in_dim = dims[1], dims[0]
+        chunk = max(1, (1 << 20) // in_dim)  # small chunks: cache-resident temporaries
+        for r0 in range(0, rows, chunk):
+            n = min(chunk, rows - r0)
+            x = rng.standard_normal(n * in_dim, dtype=np.float32) * np.float32(0.02)
+            b = quantize(x, ttype).tobytes()
+            os.pwrite(fd, b, at)
+            at += len(b)
+    finally:
+        os.close(fd)
 
 
 def default_cache_dir() -> str:
