@@ -320,110 +320,6 @@ __device__ __forceinline__ void lane_load(uint32_t row, int seg, int lane, uint3
   }
 }
 
-// Packed f32x2 arithmetic (sm_100): one instruction does two lanes' worth of the
-// float work, element pairs (2j, 2j+1) sharing a 64-bit register.
-typedef unsigned long long f2x;
-__device__ __forceinline__ f2x pk2(float a, float b) {
-  f2x r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ f2x pk2u(uint32_t a, uint32_t b) {
-  f2x r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ float2 up2(f2x v) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ f2x ffma2(f2x a, f2x b, f2x c) {
-  f2x d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ f2x fadd2(f2x a, f2x b) {
-  f2x d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ f2x fmul2(f2x a, f2x b) {
-  f2x d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ float hsum2(f2x a, f2x b) {  // (a.x + a.y) + (b.x + b.y)
-  const float2 u = up2(a), v = up2(b);
-  return (u.x + u.y) + (v.x + v.y);
-}
-
-// Bytes b0, b1 of one word -> two exact floats (as q8f / nibf).
-__device__ __forceinline__ f2x q8f2(uint32_t wx, int b0, int b1) {
-  const f2x bias = pk2(-8388736.0f, -8388736.0f);
-  return fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7540u | (unsigned)b0), __byte_perm(wx, 0x4B000000u, 0x7540u | (unsigned)b1)),
-               bias);
-}
-__device__ __forceinline__ f2x nibf2(uint32_t nib4, int b0, int b1) {
-  const f2x bias = pk2(-8388616.0f, -8388616.0f);
-  return fadd2(pk2u(__byte_perm(nib4, 0x4B000000u, 0x7540u | (unsigned)b0), __byte_perm(nib4, 0x4B000000u, 0x7540u | (unsigned)b1)),
-               bias);
-}
-
-// Dot of the lane's 64 activations (x2[j] = elements 2j, 2j+1) with its 64 weights
-// (f32 activations: W8A32 / W4A32 / BF16 — dot_prod.rs:86-96, 255-270, 464-472; per
-// block the products are summed first and scaled once).
-template <int T>
-__device__ __forceinline__ float lane_dot(const uint32_t (&w)[nwords<T>()], const f2x (&x2)[32]) {
-  if constexpr (T == SQ_Q8_0) {
-    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
-    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
-    f2x a[2] = {0ull, 0ull}, b[2] = {0ull, 0ull};
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) {  // block 0: bytes 2..33 (a pair's bytes share a word)
-      const int c0 = 2 + i;
-      const uint32_t wx = w[c0 >> 2] ^ 0x80808080u;
-      a[(i >> 1) & 1] = ffma2(x2[i >> 1], q8f2(wx, c0 & 3, (c0 & 3) + 1), a[(i >> 1) & 1]);
-    }
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) {  // block 1: bytes 36..67
-      const int c0 = 36 + i;
-      const uint32_t wx = w[c0 >> 2] ^ 0x80808080u;
-      b[(i >> 1) & 1] = ffma2(x2[16 + (i >> 1)], q8f2(wx, c0 & 3, (c0 & 3) + 1), b[(i >> 1) & 1]);
-    }
-    return fmaf(hsum2(a[0], a[1]), s0, hsum2(b[0], b[1]) * s1);
-  } else if constexpr (T == SQ_Q4_0) {
-    const float s0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFF)));
-    const float s1 = __half2float(__ushort_as_half((unsigned short)(w[4] >> 16)));
-    f2x a[2] = {0ull, 0ull}, b[2] = {0ull, 0ull};
-#pragma unroll
-    for (int j = 0; j < 16; j += 2) {  // block 0: quant bytes 2..17 (element j low nibble, j+16 high)
-      const int c0 = 2 + j;               // even: the pair's two bytes share a word
-      const uint32_t w0 = w[c0 >> 2];
-      a[0] = ffma2(x2[j >> 1], nibf2(w0 & 0x0F0F0F0Fu, c0 & 3, (c0 & 3) + 1), a[0]);
-      a[1] = ffma2(x2[8 + (j >> 1)], nibf2((w0 >> 4) & 0x0F0F0F0Fu, c0 & 3, (c0 & 3) + 1), a[1]);
-    }
-#pragma unroll
-    for (int j = 0; j < 16; j += 2) {  // block 1: quant bytes 20..35
-      const int c0 = 20 + j;
-      const uint32_t w0 = w[c0 >> 2];
-      b[0] = ffma2(x2[16 + (j >> 1)], nibf2(w0 & 0x0F0F0F0Fu, c0 & 3, (c0 & 3) + 1), b[0]);
-      b[1] = ffma2(x2[24 + (j >> 1)], nibf2((w0 >> 4) & 0x0F0F0F0Fu, c0 & 3, (c0 & 3) + 1), b[1]);
-    }
-    return fmaf(hsum2(a[0], a[1]), s0, hsum2(b[0], b[1]) * s1);
-  } else {
-    f2x a[2] = {0ull, 0ull};
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint32_t u = w[4 * k + j];
-        a[j & 1] = ffma2(x2[4 * k + j], pk2u(u << 16, u & 0xFFFF0000u), a[j & 1]);
-      }
-    }
-    return hsum2(a[0], a[1]);
-  }
-}
 
 // Sum two values over the warp with one butterfly: afterwards every lane holds
 // both totals (x = a's, y = b's).
@@ -716,7 +612,7 @@ __device__ __forceinline__ float stage_in(const Params &p, Smem &sm, ActRegs<T> 
 
 template <int T>
 __device__ __forceinline__ float lane_dot(const uint32_t (&w)[nwords<T>()], const ActRegs<T> &a) {
-  return lane_dot<T>(w, a.x);
+  return pair_dot<T>(w, a.x);
 }
 
 // The bulk copies of tile entry d: f(byte offset in the slot, global source, bytes).

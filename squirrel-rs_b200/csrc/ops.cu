@@ -113,6 +113,102 @@ __global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x,
   }
 }
 
+// m = 1 (decode through the op level): a matvec streamed through shared memory.
+// A warp walks a stream of row chunks - 32 block pairs (Q8_0 2176, Q4_0 1152, BF16
+// 4096 bytes: whole multiples of 16) of one row - copying each with coalesced
+// 16-byte cp.async into its own ring of MV_STAGES chunk buffers, MV_STAGES - 1
+// chunks ahead of the one it computes; lane j reads pair j of the chunk from shared
+// memory (odd word stride: conflict-free) and meets the input in registers, read
+// from a per-CTA copy of x in the lane-interleaved layout (xs[seg*2048 +
+// (i/4)*128 + lane*4 + i%4] for element i of lane's 64). Rows must be whole
+// multiples of 256 elements (16-byte row starts; the caller checks).
+constexpr int MV_STAGES = 5;
+constexpr int MV_WARPS = 8;
+
+template <int T>
+constexpr int mv_chunk_bytes() {
+  return 32 * pair_words<T>() * 4;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int T>
+__global__ void __launch_bounds__(MV_WARPS * 32, 1) k_matvec(const float *__restrict__ x, int in_dim,
+                                                             const uint8_t *__restrict__ w, int out_dim,
+                                                             float *__restrict__ y) {
+  constexpr int PW = pair_words<T>(), CB = mv_chunk_bytes<T>();
+  extern __shared__ __align__(16) uint8_t mv_smem[];
+  float *xs = reinterpret_cast<float *>(mv_smem);
+  const int nseg = (in_dim + 2047) / 2048;
+  uint8_t *ring = mv_smem + (size_t)nseg * 2048 * 4 + (size_t)(threadIdx.x >> 5) * MV_STAGES * CB;
+  const int lane = threadIdx.x & 31;
+  // x into the lane-interleaved layout (zeros past in_dim)
+  for (int e = threadIdx.x * 4; e < nseg * 2048; e += blockDim.x * 4) {
+    const float4 v = e < in_dim ? __ldg(reinterpret_cast<const float4 *>(x + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int sg = e >> 11, r = e & 2047, ln = r >> 6, i = r & 63;
+    *reinterpret_cast<float4 *>(&xs[(sg << 11) + ((i >> 2) << 7) + (ln << 2)]) = v;
+  }
+  __syncthreads();
+  const int np = in_dim / 64;                       // pairs per row
+  const size_t rb = (size_t)np * PW * 4;            // row bytes
+  const int gw = blockIdx.x * MV_WARPS + (threadIdx.x >> 5), nw = gridDim.x * MV_WARPS;
+  const int rows_mine = gw < out_dim ? (out_dim - 1 - gw) / nw + 1 : 0;
+  const int total = rows_mine * nseg;               // chunks this warp streams
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+  auto issue = [&](int c) {                         // chunk c = (row c / nseg, segment c % nseg)
+    if (c < total) {
+      const int row = gw + (c / nseg) * nw, sg = c % nseg;
+      const int pairs = min(32, np - sg * 32);
+      const uint8_t *src = w + (size_t)row * rb + (size_t)sg * CB;
+      const uint32_t dst = ring_s + (uint32_t)(c % MV_STAGES) * CB;
+      for (int o = lane * 16; o < pairs * PW * 4; o += 32 * 16) cp_async16(dst + o, src + o);
+    }
+    cp_async_commit();  // one group per chunk slot, empty past the end
+  };
+#pragma unroll
+  for (int c = 0; c < MV_STAGES - 1; c++) issue(c);
+  float acc = 0.f;
+  for (int c = 0; c < total; c++) {
+    issue(c + MV_STAGES - 1);
+    cp_async_wait<MV_STAGES - 1>();  // chunk c has landed (this lane's copies)
+    __syncwarp();                    // ... and every lane's
+    const int sg = c % nseg;
+    if (sg * 32 + lane < np) {
+      const uint32_t a = ring_s + (uint32_t)(c % MV_STAGES) * CB + (uint32_t)lane * PW * 4;
+      uint32_t wv[PW];
+#pragma unroll
+      for (int i = 0; i < PW; i++) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wv[i]) : "r"(a + 4 * i));
+      f2x x2[32];
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        const float4 f = *reinterpret_cast<const float4 *>(&xs[(sg << 11) + (k << 7) + (lane << 2)]);
+        x2[2 * k] = pk2(f.x, f.y);
+        x2[2 * k + 1] = pk2(f.z, f.w);
+      }
+      acc += pair_dot<T>(wv, x2);
+    }
+    __syncwarp();  // every lane is done with the slot before it is refilled
+    if (sg == nseg - 1) {
+      acc = warp_sum(acc);
+      if (lane == 0) y[gw + (c / nseg) * nw] = acc;
+      acc = 0.f;
+    }
+  }
+  cp_async_wait<0>();
+}
+
+template <int T>
+size_t mv_smem_bytes(int in_dim) {
+  return (size_t)((in_dim + 2047) / 2048) * 2048 * 4 + (size_t)MV_WARPS * MV_STAGES * mv_chunk_bytes<T>();
+}
+
 // ------------------------------------------------------------------------------------
 // linear, Q8_0 activations (W8A8 / W4A8): dot_prod.rs:378-403 (scalar twins). The
 // integer block sums are exact (dp4a); each block adds (isum * sa) * sb.
@@ -392,7 +488,17 @@ template <int T>
 static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, const uint8_t *w, int out_dim,
                          float *y) {
   const int grid = grid_for((size_t)out_dim, 8, num_sms() * 8);
-  if (m <= 1)
+  const size_t mv_smem = mv_smem_bytes<T>(in_dim);
+  if (m == 1 && in_dim % 256 == 0 && ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0 &&
+      mv_smem <= 200 * 1024) {  // 16-byte row starts; x and the ring fit in shared memory
+    static bool attr_set[3] = {false, false, false};
+    const int ti = T == SQ_Q8_0 ? 0 : (T == SQ_Q4_0 ? 1 : 2);
+    if (!attr_set[ti]) {
+      cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr_set[ti] = true;
+    }
+    k_matvec<T><<<num_sms(), MV_WARPS * 32, mv_smem, s>>>(x, in_dim, w, out_dim, y);
+  } else if (m <= 1)
     k_linear_f32<T, 1><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
   else if (m <= 4)
     k_linear_f32<T, 4><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
