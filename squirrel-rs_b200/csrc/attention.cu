@@ -22,8 +22,12 @@ template <int DPL>  // dims per lane = head_dim / 32
 __global__ void __launch_bounds__(SDPA_WARPS * 32)
     k_sdpa(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
            float *__restrict__ out, float *__restrict__ part, int seq_q, int seq_k, int n_heads,
-           int group, long long kps, long long khs, int split_len, float scale) {
+           int group, long long kps, long long khs, int split_len, float scale, const int *__restrict__ pos_dev) {
   const int hd = DPL * 32;
+  if (pos_dev) {  // the keys end at the position the device holds (graph replay: no host values)
+    seq_k = *pos_dev + seq_q;
+    split_len = (seq_k + (int)gridDim.y - 1) / (int)gridDim.y;
+  }
   const int row = blockIdx.x;  // t * n_heads + h
   const int split = blockIdx.y, n_split = gridDim.y;
   const int t = row / n_heads, h = row % n_heads, g = h / group;
@@ -138,20 +142,20 @@ size_t sdpa_max_partials_floats(int head_dim) { return (size_t)SDPA_MAX_ROW_SPLI
 
 cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
                         int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
-                        int n_split, float *part) {
+                        int n_split, float *part, const int *pos_dev) {
   const int group = n_heads / n_kv_heads;
   const float scale = 1.0f / sqrtf((float)head_dim);  // attention.rs:37
   const int split_len = (seq_k + n_split - 1) / n_split;
   dim3 grid(seq_q * n_heads, n_split);
   switch (head_dim / 32) {
-    case 1: k_sdpa<1><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    case 2: k_sdpa<2><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    case 3: k_sdpa<3><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    case 4: k_sdpa<4><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    case 5: k_sdpa<5><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    case 6: k_sdpa<6><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    case 7: k_sdpa<7><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
-    default: k_sdpa<8><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale); break;
+    case 1: k_sdpa<1><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 2: k_sdpa<2><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 3: k_sdpa<3><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 4: k_sdpa<4><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 5: k_sdpa<5><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 6: k_sdpa<6><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 7: k_sdpa<7><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    default: k_sdpa<8><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
   }
   if (n_split > 1) k_sdpa_combine<<<seq_q * n_heads, 64, 0, s>>>(part, out, n_split, head_dim);
   return cudaGetLastError();

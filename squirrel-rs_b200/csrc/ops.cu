@@ -116,18 +116,21 @@ __global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x,
 // m = 1 (decode through the op level): a matvec streamed through shared memory.
 // A warp walks a stream of row chunks - 32 block pairs (Q8_0 2176, Q4_0 1152, BF16
 // 4096 bytes: whole multiples of 16) of one row - copying each with coalesced
-// 16-byte cp.async into its own ring of MV_STAGES chunk buffers, MV_STAGES - 1
-// chunks ahead of the one it computes; lane j reads pair j of the chunk from shared
+// 16-byte cp.async into its own ring of mv_stages<T>() chunk buffers, all but one
+// of them ahead of the one it computes; lane j reads pair j of the chunk from shared
 // memory (odd word stride: conflict-free) and meets the input in registers, read
 // from a per-CTA copy of x in the lane-interleaved layout (xs[seg*2048 +
 // (i/4)*128 + lane*4 + i%4] for element i of lane's 64). Rows must be whole
 // multiples of 256 elements (16-byte row starts; the caller checks).
-constexpr int MV_STAGES = 5;
 constexpr int MV_WARPS = 8;
 
 template <int T>
 constexpr int mv_chunk_bytes() {
   return 32 * pair_words<T>() * 4;
+}
+template <int T>
+constexpr int mv_stages() {  // chunks in each warp's ring (about 14-15 KB of copies in flight a warp)
+  return T == SQ_BF16 ? 3 : 7;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
@@ -143,19 +146,12 @@ template <int T>
 __global__ void __launch_bounds__(MV_WARPS * 32, 1) k_matvec(const float *__restrict__ x, int in_dim,
                                                              const uint8_t *__restrict__ w, int out_dim,
                                                              float *__restrict__ y) {
-  constexpr int PW = pair_words<T>(), CB = mv_chunk_bytes<T>();
+  constexpr int PW = pair_words<T>(), CB = mv_chunk_bytes<T>(), MV_STAGES = mv_stages<T>();
   extern __shared__ __align__(16) uint8_t mv_smem[];
   float *xs = reinterpret_cast<float *>(mv_smem);
   const int nseg = (in_dim + 2047) / 2048;
   uint8_t *ring = mv_smem + (size_t)nseg * 2048 * 4 + (size_t)(threadIdx.x >> 5) * MV_STAGES * CB;
   const int lane = threadIdx.x & 31;
-  // x into the lane-interleaved layout (zeros past in_dim)
-  for (int e = threadIdx.x * 4; e < nseg * 2048; e += blockDim.x * 4) {
-    const float4 v = e < in_dim ? __ldg(reinterpret_cast<const float4 *>(x + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const int sg = e >> 11, r = e & 2047, ln = r >> 6, i = r & 63;
-    *reinterpret_cast<float4 *>(&xs[(sg << 11) + ((i >> 2) << 7) + (ln << 2)]) = v;
-  }
-  __syncthreads();
   const int np = in_dim / 64;                       // pairs per row
   const size_t rb = (size_t)np * PW * 4;            // row bytes
   const int gw = blockIdx.x * MV_WARPS + (threadIdx.x >> 5), nw = gridDim.x * MV_WARPS;
@@ -173,7 +169,14 @@ __global__ void __launch_bounds__(MV_WARPS * 32, 1) k_matvec(const float *__rest
     cp_async_commit();  // one group per chunk slot, empty past the end
   };
 #pragma unroll
-  for (int c = 0; c < MV_STAGES - 1; c++) issue(c);
+  for (int c = 0; c < MV_STAGES - 1; c++) issue(c);  // the weights stream while x is staged
+  // x into the lane-interleaved layout (zeros past in_dim)
+  for (int e = threadIdx.x * 4; e < nseg * 2048; e += blockDim.x * 4) {
+    const float4 v = e < in_dim ? __ldg(reinterpret_cast<const float4 *>(x + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int sg = e >> 11, r = e & 2047, ln = r >> 6, i = r & 63;
+    *reinterpret_cast<float4 *>(&xs[(sg << 11) + ((i >> 2) << 7) + (ln << 2)]) = v;
+  }
+  __syncthreads();
   float acc = 0.f;
   for (int c = 0; c < total; c++) {
     issue(c + MV_STAGES - 1);
@@ -206,7 +209,7 @@ __global__ void __launch_bounds__(MV_WARPS * 32, 1) k_matvec(const float *__rest
 
 template <int T>
 size_t mv_smem_bytes(int in_dim) {
-  return (size_t)((in_dim + 2047) / 2048) * 2048 * 4 + (size_t)MV_WARPS * MV_STAGES * mv_chunk_bytes<T>();
+  return (size_t)((in_dim + 2047) / 2048) * 2048 * 4 + (size_t)MV_WARPS * mv_stages<T>() * mv_chunk_bytes<T>();
 }
 
 // ------------------------------------------------------------------------------------
@@ -312,6 +315,50 @@ __global__ void k_dequant(const uint8_t *__restrict__ blocks, size_t n, float *_
 }
 
 // rms_norm_f32_into (kernels/rms_norm.rs:40-56): y = (x*w) / sqrt(mean(x^2) + eps), one CTA per row.
+// Rows of dim <= 8 * 4 * 256 with 16-byte row starts: every float4 of a thread loaded
+// at once and kept in registers for the output (one pass over global memory).
+constexpr int RMS_V = 8;
+__global__ void __launch_bounds__(256) k_rms_norm_v(const float *__restrict__ x, const float *__restrict__ w,
+                                                    float *y, int dim, float eps) {
+  __shared__ float red[8];
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * dim);
+  const float4 *wr = reinterpret_cast<const float4 *>(w);
+  float4 *yr = reinterpret_cast<float4 *>(y + (size_t)blockIdx.x * dim);
+  const int nv = dim / 4;
+  float4 v[RMS_V], g[RMS_V];
+#pragma unroll
+  for (int k = 0; k < RMS_V; k++) {
+    const int i = threadIdx.x + k * 256;
+    v[k] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    g[k] = i < nv ? __ldg(wr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < RMS_V; k++) {
+    ss = fmaf(v[k].x, v[k].x, ss);
+    ss = fmaf(v[k].y, v[k].y, ss);
+    ss = fmaf(v[k].z, v[k].z, ss);
+    ss = fmaf(v[k].w, v[k].w, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)dim), eps));
+#pragma unroll
+  for (int k = 0; k < RMS_V; k++) {
+    const int i = threadIdx.x + k * 256;
+    if (i < nv)
+      yr[i] = make_float4(__fdiv_rn(__fmul_rn(v[k].x, g[k].x), rms), __fdiv_rn(__fmul_rn(v[k].y, g[k].y), rms),
+                          __fdiv_rn(__fmul_rn(v[k].z, g[k].z), rms), __fdiv_rn(__fmul_rn(v[k].w, g[k].w), rms));
+  }
+}
+
 __global__ void __launch_bounds__(256) k_rms_norm(const float *__restrict__ x, const float *__restrict__ w,
                                                   float *y, int dim, float eps) {
   __shared__ float red[8];
@@ -352,7 +399,8 @@ __global__ void k_rope(float *x, int seq, int row_dim, int base_pos, const float
 }
 
 __global__ void k_rope_table(float *x, int seq, int row_dim, int base_pos, const float *__restrict__ cos_t,
-                             const float *__restrict__ sin_t, int half) {
+                             const float *__restrict__ sin_t, int half, const int *__restrict__ pos_dev) {
+  if (pos_dev) base_pos = *pos_dev;
   const int pairs = row_dim / 2;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < (long long)seq * pairs;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -559,7 +607,11 @@ cudaError_t launch_dequantize(cudaStream_t s, const void *blocks, int wtype, siz
 
 cudaError_t launch_rms_norm(cudaStream_t s, const float *x, const float *w, float *y, int rows, int dim,
                             float eps) {
-  k_rms_norm<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
+  if (dim % 4 == 0 && dim <= RMS_V * 4 * 256 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
+      ((uintptr_t)y & 15) == 0)
+    k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
+  else
+    k_rms_norm<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
   return cudaGetLastError();
 }
 
@@ -571,9 +623,9 @@ cudaError_t launch_rope_rows(cudaStream_t s, float *x, int seq, int row_dim, int
 }
 
 cudaError_t launch_rope_rows_table(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
-                                   const float *cos_t, const float *sin_t, int half) {
+                                   const float *cos_t, const float *sin_t, int half, const int *pos_dev) {
   k_rope_table<<<grid_for((size_t)seq * row_dim / 2, 256, num_sms() * 8), 256, 0, s>>>(
-      x, seq, row_dim, base_pos, cos_t, sin_t, half);
+      x, seq, row_dim, base_pos, cos_t, sin_t, half, pos_dev);
   return cudaGetLastError();
 }
 
@@ -804,7 +856,8 @@ extern "C" int sq_sdpa_cached(void *stream, const float *q, const float *k, cons
 
 namespace sq {
 __global__ void k_kv_append(const float *__restrict__ k, const float *__restrict__ v, float *kc, float *vc, int n,
-                            int n_kv, int hd, int pos, int max_ctx) {
+                            int n_kv, int hd, int pos, int max_ctx, const int *__restrict__ pos_dev) {
+  if (pos_dev) pos = *pos_dev;
   const long long total = (long long)n * n_kv * hd;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -818,9 +871,19 @@ __global__ void k_kv_append(const float *__restrict__ k, const float *__restrict
 }
 
 cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, float *kc, float *vc, int n,
-                             int n_kv, int hd, int pos, int max_ctx) {
+                             int n_kv, int hd, int pos, int max_ctx, const int *pos_dev) {
   k_kv_append<<<grid_for((size_t)n * n_kv * hd, 256, num_sms() * 8), 256, 0, s>>>(k, v, kc, vc, n, n_kv, hd,
-                                                                                  pos, max_ctx);
+                                                                                  pos, max_ctx, pos_dev);
+  return cudaGetLastError();
+}
+__global__ void k_add_int(int *p, int v) { *p += v; }
+__global__ void k_store_int(int *p, int v) { *p = v; }
+cudaError_t launch_set_int(cudaStream_t s, int *p, int v) {
+  k_store_int<<<1, 1, 0, s>>>(p, v);
+  return cudaGetLastError();
+}
+cudaError_t launch_add_int(cudaStream_t s, int *p, int v) {
+  k_add_int<<<1, 1, 0, s>>>(p, v);
   return cudaGetLastError();
 }
 

@@ -25,8 +25,9 @@ cudaError_t launch_rms_norm(cudaStream_t s, const float *x, const float *w, floa
 cudaError_t launch_rope_rows(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
                              const float *inv_freq, int half);
 // RoPE from a host-computed (C library sinf/cosf) table [n_pos][half].
+// pos_dev (optional): base_pos is read from the device instead (CUDA-graph replay).
 cudaError_t launch_rope_rows_table(cudaStream_t s, float *x, int seq, int row_dim, int base_pos,
-                                   const float *cos_t, const float *sin_t, int half);
+                                   const float *cos_t, const float *sin_t, int half, const int *pos_dev = nullptr);
 cudaError_t launch_silu(cudaStream_t s, float *x, size_t n);
 cudaError_t launch_mul(cudaStream_t s, const float *a, const float *b, float *out, size_t n);
 cudaError_t launch_add(cudaStream_t s, float *a, const float *b, size_t n);
@@ -49,9 +50,11 @@ constexpr long long SDPA_MAX_ROW_SPLITS = 1024;
 int sdpa_num_splits(int seq_q, int seq_k, int n_heads);
 size_t sdpa_partials_floats(int seq_q, int n_heads, int head_dim, int n_split);
 size_t sdpa_max_partials_floats(int head_dim);
+// pos_dev (optional): seq_k is *pos_dev + seq_q, read on the device (CUDA-graph replay).
 cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out,
                         int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim,
-                        long long k_pos_stride, long long k_head_stride, int n_split, float *part);
+                        long long k_pos_stride, long long k_head_stride, int n_split, float *part,
+                        const int *pos_dev = nullptr);
 
 }  // namespace sq
 
@@ -59,7 +62,10 @@ namespace sq {
 // KV append into the head-major cache [n_kv][max_ctx][hd] of one layer:
 // cache[g][pos + r][d] = src[r][g*hd + d] for r < n (kv_cache.rs:38-53 semantics).
 cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, float *kc, float *vc, int n,
-                             int n_kv, int hd, int pos, int max_ctx);
+                             int n_kv, int hd, int pos, int max_ctx, const int *pos_dev = nullptr);
+// *p += v / *p = v (the device position counter of a replayed decode step)
+cudaError_t launch_add_int(cudaStream_t s, int *p, int v);
+cudaError_t launch_set_int(cudaStream_t s, int *p, int v);
 // dst_tok[0] = (uint32)argmax[0]; out_ids[step] = dst_tok[0]  (device-side token feedback)
 cudaError_t launch_feedback(cudaStream_t s, const long long *argmax, uint32_t *tok, uint32_t *out_ids, int step);
 }  // namespace sq

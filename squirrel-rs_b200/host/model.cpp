@@ -464,6 +464,7 @@ sq_ctx::~sq_ctx() {
   cudaGetDevice(&prev);
   cudaSetDevice(m->device);
   if (stream) cudaStreamSynchronize(stream);
+  if (step_graph) cudaGraphExecDestroy(step_graph);  // before the buffers (and any NCCL communicator) it uses
   decode_release(this);
   cudaFree(d_out_ids);
   for (void *p : allocs) cudaFree(p);
@@ -514,6 +515,7 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
   SQ_CUDA(ctx_alloc(x.get(), &x->sdpa_part, x->sdpa_part_floats));
   SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->argmax_part, (size_t)argmax_partials(c.vocab_size) * 32));
   SQ_CUDA(ctx_alloc(x.get(), &x->d_argmax, 1));
+  SQ_CUDA(ctx_alloc(x.get(), &x->d_gpos, 1));
   if (m->tp_size > 1) {
     SQ_CUDA(ctx_alloc(x.get(), &x->logits_full, (size_t)m->cfg.vocab_size));
     SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->arg_local, argmax_state_bytes()));
@@ -574,7 +576,7 @@ namespace sq {
 
 // One prefill chunk of n rows at position c->seq_len through every layer
 // (layers.rs:81-109), then the LM head on the last row when `last`.
-static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last) {
+static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, const int *pos_dev = nullptr) {
   const sq_model *m = c->m;
   const sq_llama_config &cf = m->lc;  // this rank's shard (the whole model when tp_size == 1)
   cudaStream_t s = c->stream;
@@ -603,12 +605,14 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last) {
     TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.q, wt, Q, c->q, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.k, wt, KVd, c->k, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.v, wt, KVd, c->v, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
-    TRY(launch_rope_rows_table(s, c->q, n, Q, pos, c->d_cos, c->d_sin, half));
-    TRY(launch_rope_rows_table(s, c->k, n, KVd, pos, c->d_cos, c->d_sin, half));
-    TRY(launch_kv_append(s, c->k, c->v, kc, vc, n, cf.n_kv_heads, cf.head_dim, pos, c->max_ctx));
-    const int ns = sdpa_num_splits(n, pos + n, cf.n_heads);
+    // pos_dev: positions come from the device counter (a captured decode step); the
+    // attention then keeps the split count of the longest context
+    TRY(launch_rope_rows_table(s, c->q, n, Q, pos, c->d_cos, c->d_sin, half, pos_dev));
+    TRY(launch_rope_rows_table(s, c->k, n, KVd, pos, c->d_cos, c->d_sin, half, pos_dev));
+    TRY(launch_kv_append(s, c->k, c->v, kc, vc, n, cf.n_kv_heads, cf.head_dim, pos, c->max_ctx, pos_dev));
+    const int ns = pos_dev ? sdpa_num_splits(n, c->max_ctx, cf.n_heads) : sdpa_num_splits(n, pos + n, cf.n_heads);
     TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim,
-                    (long long)c->max_ctx * cf.head_dim, ns, c->sdpa_part));
+                    (long long)c->max_ctx * cf.head_dim, ns, c->sdpa_part, pos_dev));
     TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
     TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
@@ -638,6 +642,52 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last) {
 #undef TRY
 #undef TRY_ST
   return SQ_OK;
+}
+
+// One decode step of the op-level sequence (no persistent kernel: tensor-parallel
+// contexts, shapes it does not take) from the token id in c->d_tokens. The first
+// step runs eagerly; the second is captured into a CUDA graph - every kernel, and
+// the NCCL calls of a tensor-parallel context, with positions read from the device
+// counter c->d_gpos and a final kernel advancing it - and every later step is one
+// graph launch. A capture that fails leaves the context on eager launches.
+static int step_one(sq_ctx *c) {
+  cudaStream_t s = c->stream;
+  if (c->gpos != c->seq_len) {  // prefill or reset moved the host's count
+    const cudaError_t e = launch_set_int(s, c->d_gpos, c->seq_len);
+    if (e != cudaSuccess) return cuda_fail(e, "decode position");
+    c->gpos = c->seq_len;
+  }
+  if (!c->step_graph && !c->graph_failed && c->eager_steps >= 1) {
+    cudaGraph_t g = nullptr;
+    int st = SQ_OK;
+    cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      const int saved = c->seq_len;
+      st = forward_rows(c, c->d_tokens, 1, true, c->d_gpos);
+      c->seq_len = saved;  // nothing ran during the capture
+      if (!st) e = launch_add_int(s, c->d_gpos, 1);
+      const cudaError_t e2 = cudaStreamEndCapture(s, &g);
+      if (e == cudaSuccess) e = e2;
+    }
+    if (!st && e == cudaSuccess && g) e = cudaGraphInstantiate(&c->step_graph, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (st || e != cudaSuccess || !c->step_graph) {
+      c->graph_failed = true;
+      c->step_graph = nullptr;
+      cudaGetLastError();  // clear the capture's error; eager launches from here on
+    }
+  }
+  if (c->step_graph) {
+    const cudaError_t e = cudaGraphLaunch(c->step_graph, s);
+    if (e != cudaSuccess) return cuda_fail(e, "decode step graph");
+    c->seq_len += 1;
+    c->gpos = c->seq_len;
+    return SQ_OK;
+  }
+  c->eager_steps++;
+  const int st = forward_rows(c, c->d_tokens, 1, true);
+  c->gpos = -1;  // the device counter did not advance
+  return st;
 }
 
 // Model::forward for ids already on the device (prefill in chunks; decode of one
@@ -673,6 +723,8 @@ extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *ou
     SQ_CUDA(cudaMemcpyAsync(c->d_tokens, ids + r0, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, c->stream));
     if (rows == 1 && r0 == 0 && decode_available(c)) {
       st = decode_launch(c, c->d_tokens, nullptr, 0);
+    } else if (n == 1) {
+      st = step_one(c);
     } else {
       st = forward_rows(c, c->d_tokens, rows, r0 + rows == n);
     }
@@ -746,7 +798,7 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
     if (decode_available(c)) {
       st = decode_launch(c, c->d_tokens, d_out, i);
     } else {
-      st = forward_rows(c, c->d_tokens, 1, true);
+      st = step_one(c);
       if (!st) {
         e = launch_feedback(c->stream, c->d_argmax, c->d_tokens, d_out, i);
         st = e == cudaSuccess ? SQ_OK : cuda_fail(e, "decode_steps");

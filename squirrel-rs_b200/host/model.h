@@ -72,6 +72,11 @@ struct sq_ctx {
   uint32_t *d_tokens = nullptr;
   float *d_cos = nullptr, *d_sin = nullptr;  // RoPE table [max_ctx][head_dim/2]
   sq::DecodeState *dec = nullptr;
+  cudaGraphExec_t step_graph = nullptr;  // the op-level decode step, captured once
+  int *d_gpos = nullptr;  // its device position counter
+  int gpos = -1;          // the value d_gpos holds once queued work finishes (-1: unknown)
+  int eager_steps = 0;
+  bool graph_failed = false;
   float *logits_full = nullptr;  // tensor parallel: the gathered vocabulary
   void *arg_local = nullptr, *arg_all = nullptr;  // tensor parallel: per-rank argmax states
   uint32_t *d_out_ids = nullptr;  // ids of sq_decode_steps
