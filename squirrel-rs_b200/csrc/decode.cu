@@ -978,100 +978,134 @@ __device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsig
   }
 }
 
-// Long contexts: split-KV over (kv head, chunk) items covering the group's GROUP
-// q heads; partial (max, sum, accumulator) per chunk, and the last CTA to finish a
-// kv head merges its chunks.
+// Long contexts: split-KV over (q head, chunk) items. Inside an item a lane owns a
+// position (its K row loaded with the warp's other 31 at once; q.k without
+// shuffles), the warp's softmax over its 32 positions, then lane = dimension for
+// p.V with the warp's V rows loaded up front; the 8 warps merge in shared memory
+// into the chunk's partial (max, sum, accumulator). The chunk that holds the token's
+// own position adds it from the tagged words of the QKV stage, and the last CTA to
+// finish a head merges the head's chunks and publishes the head's output.
 template <int DPL>
 __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsigned tag_in, unsigned tag_out) {
+  constexpr int HD = DPL * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Lk = pos + 1;
-  int n_chunks = (Lk + 31) / 32;
-  const int cap = max(1, (2 * p.G) / p.KVH);
+  int n_chunks = (Lk + NC * 32 - 1) / (NC * 32);
+  const int cap = max(1, (2 * p.G + p.H - 1) / p.H);
   if (n_chunks > cap) n_chunks = cap;
   if (n_chunks > p.max_chunks) n_chunks = p.max_chunks;
   const int CH = (Lk + n_chunks - 1) / n_chunks;
-  const int items = p.KVH * n_chunks;
-  const int hd = p.hd;
+  const int items = p.H * n_chunks;
   for (int item = blockIdx.x; item < items; item += p.G) {
-    const int g = item / n_chunks, c = item % n_chunks;
+    const int h = item / n_chunks, c = item % n_chunks, g = h / GROUP;
     const int s0 = c * CH, s1 = min(Lk, s0 + CH);
-    float qv[GROUP][DPL], m[GROUP], lsum[GROUP], acc[GROUP][DPL];
-    {
-      const unsigned long long *qa[GROUP * DPL];
-      float qf[GROUP * DPL];
+    const int cached_end = min(s1, pos);  // positions below pos come from the cache
+    const float *kb = p.kc + ((size_t)l * p.KVH + g) * p.max_ctx * HD;
+    const float *vb = p.vc + ((size_t)l * p.KVH + g) * p.max_ctx * HD;
+    // this warp's first 32 keys load while q is being fetched
+    float4 kr[HD / 4];
+    auto load_k = [&](int base) {
+      const int s = base + lane;
+      const bool valid = s < cached_end;
 #pragma unroll
-      for (int h = 0; h < GROUP; h++)
+      for (int k = 0; k < HD / 4; k++)
+        kr[k] = valid ? ldcg4(kb + (size_t)s * HD + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    if (s0 + warp * 32 < cached_end) load_k(s0 + warp * 32);
+    if (warp == 0) {
+      const unsigned long long *qa[DPL];
+      float qv[DPL];
 #pragma unroll
-        for (int i = 0; i < DPL; i++) qa[h * DPL + i] = p.q_ll + (size_t)(g * GROUP + h) * hd + lane + 32 * i;
-      poll_ll_n<GROUP * DPL>(p, qa, tag_in, qf);
+      for (int i = 0; i < DPL; i++) qa[i] = p.q_ll + (size_t)h * HD + lane + 32 * i;
+      poll_ll_n<DPL>(p, qa, tag_in, qv);
 #pragma unroll
-      for (int h = 0; h < GROUP; h++) {
-        m[h] = -INFINITY;
-        lsum[h] = 0.f;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) {
-          qv[h][i] = qf[h * DPL + i];
-          acc[h][i] = 0.f;
-        }
-      }
-    }
-    const float *kb = p.kc + ((size_t)l * p.KVH + g) * p.max_ctx * hd;
-    const float *vb = p.vc + ((size_t)l * p.KVH + g) * p.max_ctx * hd;
-    for (int s = s0 + warp; s < s1; s += NC) {
-      float kr[DPL], vr[DPL];
-#pragma unroll
-      for (int i = 0; i < DPL; i++) {
-        if (s == pos) {  // the row this token's QKV stage just produced
-          const unsigned long long *kva[2] = {p.kv_ll + (size_t)g * hd + lane + 32 * i,
-                                              p.kv_ll + p.KVd + (size_t)g * hd + lane + 32 * i};
-          float kv2[2];
-          poll_ll_n<2>(p, kva, tag_in, kv2);
-          kr[i] = kv2[0];
-          vr[i] = kv2[1];
-        } else {
-          kr[i] = __ldcg(kb + (size_t)s * hd + lane + 32 * i);
-          vr[i] = __ldcg(vb + (size_t)s * hd + lane + 32 * i);
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < GROUP; h++) {
-        float d = 0.f;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) d = fmaf(qv[h][i], kr[i], d);
-        const float sc = warp_sum(d) * p.attn_scale;
-        const float mn = fmaxf(m[h], sc);
-        const float corr = expf(m[h] - mn);
-        const float pr = expf(sc - mn);
-        lsum[h] = fmaf(lsum[h], corr, pr);
-#pragma unroll
-        for (int i = 0; i < DPL; i++) acc[h][i] = fmaf(pr, vr[i], acc[h][i] * corr);
-        m[h] = mn;
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < GROUP; h++) {
-      if (lane == 0) {
-        sm.at.m[warp][h] = m[h];
-        sm.at.l[warp][h] = lsum[h];
-      }
-#pragma unroll
-      for (int i = 0; i < DPL; i++) sm.at.a[warp][h][lane + 32 * i] = acc[h][i];
+      for (int i = 0; i < DPL; i++) sm.qh[lane + 32 * i] = qv[i];
     }
     cta_sync();
-    if (warp < GROUP) {  // merge the warps' states of head `warp` into this chunk's partial
-      const int h = warp;
+    float m = -INFINITY, lsum = 0.f, acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) acc[i] = 0.f;
+    constexpr int VJ = DPL >= 4 ? 16 : 32;  // V rows per batch (head_dim 128: two halves, fewer registers)
+    for (int base = s0 + warp * 32; base < cached_end; base += NC * 32) {
+      const int s = base + lane;
+      const bool valid = s < cached_end;
+      float vv[VJ][DPL];
+      auto load_v = [&](int j0) {
+#pragma unroll
+        for (int j = 0; j < VJ; j++)
+#pragma unroll
+          for (int i = 0; i < DPL; i++)
+            vv[j][i] = base + j0 + j < cached_end ? __ldcg(vb + (size_t)(base + j0 + j) * HD + lane + 32 * i) : 0.f;
+      };
+      load_v(0);
+      float d = 0.f;
+#pragma unroll
+      for (int k = 0; k < HD / 4; k++) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(&sm.qh[4 * k]);
+        d = fmaf(q4.x, kr[k].x, d);
+        d = fmaf(q4.y, kr[k].y, d);
+        d = fmaf(q4.z, kr[k].z, d);
+        d = fmaf(q4.w, kr[k].w, d);
+      }
+      const float sc = valid ? d * p.attn_scale : -INFINITY;
+      const float mn = fmaxf(m, warp_max(sc));
+      const float corr = expf(m - mn);
+      const float pj = valid ? expf(sc - mn) : 0.f;
+      lsum = fmaf(lsum, corr, warp_sum(pj));
+#pragma unroll
+      for (int i = 0; i < DPL; i++) acc[i] *= corr;
+#pragma unroll
+      for (int j0 = 0; j0 < 32; j0 += VJ) {
+        if (j0) load_v(j0);
+#pragma unroll
+        for (int j = 0; j < VJ; j++) {
+          const float pjj = __shfl_sync(FULL, pj, j0 + j);
+#pragma unroll
+          for (int i = 0; i < DPL; i++) acc[i] = fmaf(pjj, vv[j][i], acc[i]);
+        }
+      }
+      m = mn;
+      if (base + NC * 32 < cached_end) load_k(base + NC * 32);
+    }
+    if (lane == 0) {
+      sm.at.m[warp][0] = m;
+      sm.at.l[warp][0] = lsum;
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; i++) sm.at.a[warp][0][lane + 32 * i] = acc[i];
+    cta_sync();
+    if (warp == 0) {  // merge the warps, add the token's own position if it is in this chunk
       float M = -INFINITY;
-      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.at.m[w][h]);
+      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.at.m[w][0]);
       float Ls = 0.f, A[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; i++) A[i] = 0.f;
       for (int w = 0; w < NC; w++) {
-        const float f = sm.at.l[w][h] > 0.f ? expf(sm.at.m[w][h] - M) : 0.f;
-        Ls = fmaf(sm.at.l[w][h], f, Ls);
+        const float f = sm.at.l[w][0] > 0.f ? expf(sm.at.m[w][0] - M) : 0.f;
+        Ls = fmaf(sm.at.l[w][0], f, Ls);
 #pragma unroll
-        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.at.a[w][h][lane + 32 * i], f, A[i]);
+        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.at.a[w][0][lane + 32 * i], f, A[i]);
       }
-      float *pp = p.attn_part + (((size_t)g * p.max_chunks + c) * GROUP + h) * (hd + 2);
+      if (s1 == Lk) {
+        const unsigned long long *kva[2 * DPL];
+        float kvq[2 * DPL], d = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) {
+          kva[i] = p.kv_ll + (size_t)g * HD + lane + 32 * i;
+          kva[DPL + i] = p.kv_ll + p.KVd + (size_t)g * HD + lane + 32 * i;
+        }
+        poll_ll_n<2 * DPL>(p, kva, tag_in, kvq);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) d = fmaf(sm.qh[lane + 32 * i], kvq[i], d);
+        const float sc = warp_sum(d) * p.attn_scale;
+        const float mn = fmaxf(M, sc);
+        const float corr = Ls > 0.f ? expf(M - mn) : 0.f, pp = expf(sc - mn);
+        Ls = fmaf(Ls, corr, pp);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) A[i] = fmaf(pp, kvq[DPL + i], A[i] * corr);
+        M = mn;
+      }
+      float *pp = p.attn_part + ((size_t)h * p.max_chunks + c) * (HD + 2);
       if (lane == 0) {
         pp[0] = M;
         pp[1] = Ls;
@@ -1082,38 +1116,34 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
     }
     cta_sync();
     if (threadIdx.x == 0) {
-      const unsigned old = atomicAdd(p.attn_cnt + (size_t)l * p.KVH + g, 1u);
+      const unsigned old = atomicAdd(p.attn_cnt + (size_t)l * p.H + h, 1u);
       sm.flag = old == (unsigned)(n_chunks - 1);
     }
     cta_sync();
-    if (sm.flag) {
+    if (sm.flag && warp == 0) {  // the head's last chunk: combine all of them
       __threadfence();
-      if (warp < GROUP) {  // combine all chunks of head g*GROUP+warp
-        const int h = warp;
-        float M = -INFINITY;
-        for (int cc = 0; cc < n_chunks; cc++) {
-          const float *pp = p.attn_part + (((size_t)g * p.max_chunks + cc) * GROUP + h) * (hd + 2);
-          if (__ldcg(pp + 1) > 0.f) M = fmaxf(M, __ldcg(pp));
-        }
-        float Ls = 0.f, A[DPL];
-#pragma unroll
-        for (int i = 0; i < DPL; i++) A[i] = 0.f;
-        for (int cc = 0; cc < n_chunks; cc++) {
-          const float *pp = p.attn_part + (((size_t)g * p.max_chunks + cc) * GROUP + h) * (hd + 2);
-          const float lc = __ldcg(pp + 1);
-          if (lc > 0.f) {
-            const float f = expf(__ldcg(pp) - M);
-            Ls = fmaf(lc, f, Ls);
-#pragma unroll
-            for (int i = 0; i < DPL; i++) A[i] = fmaf(__ldcg(pp + 2 + lane + 32 * i), f, A[i]);
-          }
-        }
-        const float inv = 1.0f / Ls;
-#pragma unroll
-        for (int i = 0; i < DPL; i++)
-          st_ll(p.attn_ll + (size_t)(g * GROUP + h) * hd + lane + 32 * i, A[i] * inv, tag_out);
+      float M = -INFINITY;
+      for (int cc = 0; cc < n_chunks; cc++) {
+        const float *pp = p.attn_part + ((size_t)h * p.max_chunks + cc) * (HD + 2);
+        if (__ldcg(pp + 1) > 0.f) M = fmaxf(M, __ldcg(pp));
       }
-      if (threadIdx.x == 0) p.attn_cnt[(size_t)l * p.KVH + g] = 0;  // per-layer counter, ready for the next token
+      float Ls = 0.f, A[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) A[i] = 0.f;
+      for (int cc = 0; cc < n_chunks; cc++) {
+        const float *pp = p.attn_part + ((size_t)h * p.max_chunks + cc) * (HD + 2);
+        const float lc = __ldcg(pp + 1);
+        if (lc > 0.f) {
+          const float f = expf(__ldcg(pp) - M);
+          Ls = fmaf(lc, f, Ls);
+#pragma unroll
+          for (int i = 0; i < DPL; i++) A[i] = fmaf(__ldcg(pp + 2 + lane + 32 * i), f, A[i]);
+        }
+      }
+      const float inv = 1.0f / Ls;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) st_ll(p.attn_ll + (size_t)h * HD + lane + 32 * i, A[i] * inv, tag_out);
+      if (lane == 0) p.attn_cnt[(size_t)l * p.H + h] = 0;  // per-layer counter, ready for the next token
     }
     cta_sync();
   }
@@ -1339,7 +1369,7 @@ struct DecodeState {
   int grid = 0;
   unsigned *d_err = nullptr, *d_bar = nullptr, *d_ticket = nullptr, *d_attn_cnt = nullptr;
   int *d_pos = nullptr;
-  int n_kv_heads = 0, n_layers = 0;
+  int n_kv_heads = 0, n_heads = 0, n_layers = 0;
   unsigned long long *d_timeline = nullptr;
   unsigned long long *d_tile_tl = nullptr;  // per-tile stamps of the last launch (with the timeline)
   const int2 *d_tiles = nullptr;
@@ -1423,7 +1453,7 @@ int decode_prepare(sq_ctx *c) {
   h.rb_E = rbE;
   h.rb_Q = rbQ;
   h.rb_F = rbF;
-  h.max_chunks = std::max(1, (2 * nsm) / cf.n_kv_heads);
+  h.max_chunks = std::max(1, (2 * nsm + cf.n_heads - 1) / cf.n_heads);
   h.eps = cf.rms_eps;
   h.attn_scale = 1.0f / sqrtf((float)cf.head_dim);
   h.embd = (const uint8_t *)m->embd;
@@ -1453,8 +1483,8 @@ int decode_prepare(sq_ctx *c) {
     }
     return e;
   };
-  SQ_CUDA(alloc((void **)&h.attn_part, (size_t)cf.n_kv_heads * h.max_chunks * dk::GROUP * (cf.head_dim + 2) * 4));
-  SQ_CUDA(alloc((void **)&h.attn_cnt, (size_t)cf.n_blocks * cf.n_kv_heads * 4));
+  SQ_CUDA(alloc((void **)&h.attn_part, (size_t)cf.n_heads * h.max_chunks * (cf.head_dim + 2) * 4));
+  SQ_CUDA(alloc((void **)&h.attn_cnt, (size_t)cf.n_blocks * cf.n_heads * 4));
   SQ_CUDA(alloc((void **)&h.hid_ll, (size_t)E * 8));
   SQ_CUDA(alloc((void **)&h.q_ll, (size_t)Q * 8));
   SQ_CUDA(alloc((void **)&h.kv_ll, (size_t)2 * KVd * 8));
@@ -1513,6 +1543,7 @@ int decode_prepare(sq_ctx *c) {
   st->d_ticket = h.ticket;
   st->d_attn_cnt = h.attn_cnt;
   st->n_kv_heads = cf.n_kv_heads;
+  st->n_heads = cf.n_heads;
   st->n_layers = cf.n_blocks;
   st->d_pos = h.pos;
   st->hp = h;
@@ -1581,7 +1612,7 @@ int decode_check(sq_ctx *c) {
     cudaMemset(st->d_err, 0, 4);
     cudaMemset(st->d_bar, 0, 4);
     cudaMemset(st->d_ticket, 0, 4);
-    cudaMemset(st->d_attn_cnt, 0, (size_t)st->n_kv_heads * st->n_layers * 4);
+    cudaMemset(st->d_attn_cnt, 0, (size_t)st->n_heads * st->n_layers * 4);
     st->dev_pos = -1;  // force a position resync
     return fail(SQ_ERR_TIMEOUT, "decode kernel: a bounded wait expired (code " + std::to_string(err) + ")");
   }

@@ -181,6 +181,10 @@ def write_gguf(path: str, spec_name: str, wtype: int, seed: int = 0, rope_scalin
     big = sum(int(np.prod(d)) for _, d, t in tensors if t != F32) > (1 << 28)
     workers = min(16, os.cpu_count() or 1) if big else 1
     workers = int(os.environ.get("SQB200_GEN_WORKERS", workers))
+    import sys
+    main_file = getattr(sys.modules.get("__main__"), "__file__", None)
+    if workers > 1 and not (main_file and os.path.exists(main_file)):
+        workers = 1  # spawned workers re-import __main__: impossible for stdin or interactive programs
     if workers > 1:  # every tensor has its own RNG stream and byte range: same bytes in any order
         import concurrent.futures as cf
         import multiprocessing as mp

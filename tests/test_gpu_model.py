@@ -106,6 +106,26 @@ def test_chunked_prefill_and_decode_steps(gpu_lib, models):
     ctx.close()
 
 
+@pytest.mark.parametrize("wt", ["q8_0", "q4_0"])
+def test_long_context_decode_kernel(gpu_lib, models, wt):
+    """Past 512 positions the persistent decode kernel splits attention into
+    (kv head, chunk) items combined by the last CTA of each kv head."""
+    spec = "small"
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(600, seed=9, high=G.SPECS[spec]["vocab"])
+    ref = O.Model(path)
+    ids_ref, _, logits_ref = ref.generate(prompt, 9, want_logits=True)
+    m = gpu_model(models, spec, wt, 0)
+    ctx = m.new_context(700)
+    assert ctx.launches_per_token == 1  # the persistent kernel serves this model
+    first = ctx.forward(prompt)
+    assert first == ids_ref[0]
+    rest = ctx.decode_steps(8)
+    assert np.array_equal(rest, ids_ref[1:9])
+    assert_logits_close(ctx.logits(), logits_ref[8])
+    ctx.close()
+
+
 def test_upload_path_equals_gguf_path(gpu_lib, models):
     """sq_model_create + sq_model_upload_tensor + finalize (the reference-side parser
     path) gives the same model as sq_model_load_gguf."""
