@@ -576,7 +576,9 @@ cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, con
     }
     if (wtype == SQ_Q8_0) linear_q8_t<SQ_Q8_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
     else linear_q8_t<SQ_Q4_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
-  } else if (m >= 2) {  // several rows (prefill): tiled GEMM
+  } else if (m >= 2) {  // several rows (prefill): tensor cores for bf16 weights, else the tiled GEMM
+    if (wtype == SQ_BF16 && gemm_tc_enabled() && gemm_tc_supported(m, in_dim, x, w, wtype, ws, ws_floats))
+      return launch_gemm_tc_bf16(s, x, m, in_dim, w, out_dim, y, ws, ws_floats);
     return launch_gemm_f32w(s, x, m, in_dim, w, wtype, out_dim, y, ws, ws_floats);
   } else {
     if (wtype == SQ_Q8_0) linear_f32_t<SQ_Q8_0>(s, x, m, in_dim, wb, out_dim, y);
@@ -699,6 +701,13 @@ static cudaError_t scratch_alloc(void **p, size_t bytes, cudaStream_t s) {
 extern "C" const char *sq_last_error(void) { return g_last_error.c_str(); }
 extern "C" const char *sq_version(void) { return "squirrel-b200 0.1 (sm_100a)"; }
 
+// Workspace of the tensor-core GEMM for an op-level call (bf16 weights, m >= 2,
+// f32 activations): the three bf16 activation terms plus up to 8 split-K partials.
+static size_t tc_workspace_floats(int m, int in_dim, int out_dim, int wtype, bool q8) {
+  if (q8 || wtype != SQ_BF16 || m < 2) return 0;
+  return (size_t)3 * m * in_dim / 2 + 64 + (size_t)8 * m * out_dim;
+}
+
 static int check_linear(const float *input, int m, int in_dim, const void *weight, int wtype, int out_dim,
                         float *output) {
   if (!input || !weight || !output) return fail(SQ_ERR_ARG, "linear: null pointer");
@@ -718,8 +727,12 @@ extern "C" int sq_linear(void *stream, const float *input, int m, int in_dim, co
   void *xq = nullptr;
   const bool q8 = acts == SQ_ACTS_Q8 && wtype != SQ_BF16;
   if (q8) SQ_CUDA(scratch_alloc(&xq, (size_t)m * (in_dim / QK) * Q8_BYTES, s));
-  cudaError_t e = launch_linear(s, input, m, in_dim, weight, wtype, out_dim, output, q8, xq);
+  void *ws = nullptr;
+  const size_t ws_floats = tc_workspace_floats(m, in_dim, out_dim, wtype, q8);
+  if (ws_floats) SQ_CUDA(scratch_alloc(&ws, ws_floats * sizeof(float), s));
+  cudaError_t e = launch_linear(s, input, m, in_dim, weight, wtype, out_dim, output, q8, xq, (float *)ws, ws_floats);
   if (xq) cudaFreeAsync(xq, s);
+  if (ws) cudaFreeAsync(ws, s);
   if (e != cudaSuccess) return cuda_fail(e, "sq_linear");
   return SQ_OK;
 }
@@ -739,11 +752,20 @@ extern "C" int sq_linear_shared(void *stream, const float *input, int m, int in_
     cudaError_t e = launch_quantize_q8_0(s, input, (size_t)m * in_dim, act_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "linear_shared quantize");
   }
+  int widest = 0;
+  for (int i = 0; i < n; i++) widest = std::max(widest, out_dims[i]);
+  void *ws = nullptr;
+  const size_t ws_floats = tc_workspace_floats(m, in_dim, widest, wtype, q8);
+  if (ws_floats) SQ_CUDA(scratch_alloc(&ws, ws_floats * sizeof(float), s));
   for (int i = 0; i < n; i++) {
     cudaError_t e = launch_linear(s, q8 ? nullptr : input, m, in_dim, weights[i], wtype, out_dims[i],
-                                  outputs[i], q8, act_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "sq_linear_shared");
+                                  outputs[i], q8, act_scratch, (float *)ws, ws_floats);
+    if (e != cudaSuccess) {
+      if (ws) cudaFreeAsync(ws, s);
+      return cuda_fail(e, "sq_linear_shared");
+    }
   }
+  if (ws) cudaFreeAsync(ws, s);
   return SQ_OK;
 }
 

@@ -16,6 +16,16 @@ cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, con
 // The tiled GEMM itself (gemm.cu): y[m][N] = x[m][K] @ w^T, native weight rows.
 cudaError_t launch_gemm_f32w(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
                              float *ws, size_t ws_floats);
+// Tensor-core GEMM for bf16 weights (gemm_tc.cu): the f32 activations are split into
+// three bf16 terms in `ws` (3*m*K/2 floats, then split-K partials). Supported when
+// m >= 2, K % 16 == 0, x and w 16-byte aligned, ws 256-byte aligned and large enough.
+bool gemm_tc_supported(int m, int K, const float *x, const void *w, int wtype, const float *ws, size_t ws_floats);
+cudaError_t launch_gemm_tc_bf16(cudaStream_t s, const float *x, int m, int K, const void *w, int N, float *y,
+                                float *ws, size_t ws_floats);
+// Non-zero when a bounded wait of the tensor-core GEMM gave up (read after a sync).
+unsigned gemm_tc_status(bool clear);
+// False when SQB200_GEMM=simt selects the CUDA-core GEMM for bf16 weights too.
+bool gemm_tc_enabled();
 cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out);
 cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype,
                          int embed_dim, int vocab, float *out);

@@ -736,6 +736,7 @@ extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *ou
   SQ_CUDA(cudaStreamSynchronize(c->stream));
   st = decode_check(c);
   if (st) return st;
+  if (gemm_tc_status(true)) return fail(SQ_ERR_TIMEOUT, "forward: a bounded wait of the tensor-core GEMM expired");
   if (out_argmax) *out_argmax = (uint32_t)id;
   return SQ_OK;
 }

@@ -105,6 +105,29 @@ def test_linear_f32_acts(gpu_lib, wtype, shape):
     assert np.all(np.abs(got - want) <= 1e-5 * mag + 1e-6)
 
 
+# Tensor-core GEMM (bf16 weights, m >= 2): ragged rows and outputs, K not a multiple
+# of the 64-element stage, and shapes small enough in tiles that K is split.
+TC_SHAPES = [(2, 64, 128), (3, 96, 9), (129, 160, 130), (100, 2048, 512), (256, 2048, 2048),
+             (16, 8192, 512), (300, 1024, 384), (64, 4096, 1000)]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES)
+def test_linear_bf16_tensor_cores(gpu_lib, shape):
+    """Activations split into three bf16 terms (exact), bf16 x bf16 products (exact),
+    f32 accumulation on the tensor cores. Same tolerance as the CUDA-core path:
+    |gpu - oracle| <= 1e-5 * sum|a_i w_i| + 1e-6."""
+    from sqb200 import lib
+    m, k, n = shape
+    rng = np.random.default_rng(m * 7 + k * 3 + n)
+    x = (rng.standard_normal((m, k)) * rng.choice([1e-3, 1.0, 40.0], (m, 1))).astype(np.float32)
+    w = quant_weights(O.BF16, n, k, rng)
+    got = host(lib.linear(dev(x), dev(w), O.BF16, n))
+    want = O.linear(x, w, O.BF16, n)
+    mag = term_magnitude(x, w, O.BF16, n)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-5 * mag + 1e-6), float((err / (mag + 1e-6)).max())
+
+
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("shape", SHAPES)
 def test_linear_q8_acts(gpu_lib, wtype, shape):
