@@ -1,0 +1,421 @@
+// attention_tc.cu — tensor-core causal GQA attention for prefill, head_dim 64
+// (kernels/attention.rs:11-70 semantics: scores = (q.k) * 1/sqrt(hd) over keys
+// 0..=offset+t, max-subtracted softmax, probability-weighted sum of V; f32 inputs).
+//
+// Accuracy: q, k, v and the probabilities p are each split into three bf16 terms
+// that sum to the f32 value exactly (x = h + d + l). A product of two split values
+// is formed from the six term products whose weight is at least 2^-16 of the leading
+// one (hh, hd, dh, hl, dd, lh); each bf16 x bf16 product is exact and the tensor core
+// accumulates in f32, so scores and outputs keep f32-level accuracy.
+//
+// Pre-pass (k_split_rows, k_split_vt): the chunk's queries as [3][H][n][64], the
+// keys 0..seq_k-1 as [3][G][seq_k][64] and the values transposed as
+// [3][G][64][seq_k padded to 8] (bf16), in a caller-provided workspace.
+//
+// Kernel: one CTA per (128-query block, q head); the heaviest (last) query blocks
+// start first. 6 warps:
+//   warp 4   TMA: the query block's three term tiles once, then per 64-key block the
+//            key and transposed-value term tiles into a double buffer;
+//   warp 5   one thread issues the MMAs: S_j = Q K_j^T (M = 128 queries, N = 64 keys)
+//            into one of two tensor-memory score buffers, and, once the softmax warps
+//            have written P_j, O_j = P_j V_j (N = 64 dims) into one of two output
+//            buffers; S_{j+1} is issued before O_j so it overlaps the softmax of j;
+//   warps 0-3  one thread per query row: the scores of block j from tensor memory,
+//            causal mask, online softmax (running max and sum, expf), P_j split into
+//            terms and stored 128-byte swizzled for the MMA, then the f32 running
+//            output o = o * exp(m_old - m_new) + O_j in registers (one block behind).
+// Every wait is bounded; on expiry the CTA records the error, stops, drains its
+// copies and MMAs, frees its tensor memory and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "ops.cuh"
+#include "tc.cuh"
+
+namespace sq {
+namespace {
+
+using namespace tc;
+
+constexpr int FA_M = 128;   // query rows per CTA
+constexpr int FA_BK = 64;   // keys per block
+constexpr int FA_HD = 64;   // head dim
+constexpr int FA_THREADS = 192;
+
+constexpr int Q_TERM = FA_M * FA_HD * 2;   // 16 KB
+constexpr int K_TERM = FA_BK * FA_HD * 2;  // 8 KB
+constexpr int V_TERM = FA_HD * FA_BK * 2;  // 8 KB (transposed: 64 dims x 64 keys)
+constexpr int P_TERM = FA_M * FA_BK * 2;   // 16 KB
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + 3 * Q_TERM;      // two buffers of three key terms
+constexpr int OFF_V = OFF_K + 2 * 3 * K_TERM;  // two buffers of three value terms
+constexpr int OFF_P = OFF_V + 2 * 3 * V_TERM;  // three probability terms
+constexpr int OFF_BAR = OFF_P + 3 * P_TERM;
+constexpr int FA_SMEM = 1024 + OFF_BAR + 256;
+static_assert(FA_SMEM <= 232448, "shared memory per CTA");
+static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && OFF_BAR % 8 == 0, "alignment");
+
+// barrier slots (8 bytes each)
+enum : int {
+  B_QFULL = 0,
+  B_KVFULL = 1,   // [2]
+  B_KVEMPTY = 3,  // [2]
+  B_SFULL = 5,    // [2]
+  B_SFREE = 7,    // [2]
+  B_PFULL = 9,
+  B_PEMPTY = 10,
+  B_OFULL = 11,   // [2]
+  B_OFREE = 13,   // [2]
+  B_FIN = 15,
+  N_BARS = 16
+};
+constexpr uint32_t TM_S = 0, TM_O = 128, TM_COLS = 256;  // S[2] at columns 0/64, O[2] at 128/192
+constexpr uint32_t IDESC = idesc_bf16(FA_M, 64);
+
+// term pairs (a, b) with a + b <= 2: the products kept
+__device__ __constant__ int8_t kPairs[6][2] = {{0, 0}, {0, 1}, {1, 0}, {0, 2}, {1, 1}, {2, 0}};
+
+__device__ __forceinline__ void split3(float x, __nv_bfloat16 &h, __nv_bfloat16 &d, __nv_bfloat16 &l) {
+  h = __float2bfloat16_rn(x);
+  const float r1 = x - __bfloat162float(h);
+  d = __float2bfloat16_rn(r1);
+  l = __float2bfloat16_rn(r1 - __bfloat162float(d));
+}
+__device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {
+  return (uint32_t)__bfloat16_as_ushort(a) | ((uint32_t)__bfloat16_as_ushort(b) << 16);
+}
+
+// grid: n_heads * nqb CTAs. offset = seq_k - n (keys before the chunk's first query).
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    k_attn_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+              const __grid_constant__ CUtensorMap tv, float *__restrict__ out, int n, int offset, int n_heads,
+              int group, int nqb, float scale, unsigned *err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = su32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + OFF_BAR;
+  auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+  uint8_t *gen = smem_raw + (base - raw);
+  volatile uint32_t *tmem_slot = (volatile uint32_t *)(gen + OFF_BAR + 8 * N_BARS);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = nqb - 1 - (int)blockIdx.x / n_heads;  // heaviest blocks first
+  const int h = (int)blockIdx.x % n_heads, g = h / group;
+  const int G = n_heads / group;
+  const int q0 = qb * FA_M;
+  const int q_last = min(q0 + FA_M, n) - 1;
+  const int nkb = (offset + q_last) / FA_BK + 1;  // key blocks this query block sees
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < N_BARS; i++) {  // the softmax threads all arrive on S-free, P-full and O-free
+      const bool rows = i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_OFREE || i == B_OFREE + 1;
+      bar_init(bar(i), rows ? FA_M : 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&tq);
+    prefetch_map(&tk);
+    prefetch_map(&tv);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(su32((const void *)tmem_slot), TM_COLS);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    int issued = 0;
+    if (lane == 0) {
+      bar_expect_tx(bar(B_QFULL), 3 * Q_TERM);
+      for (int t = 0; t < 3; t++) tma_load_3d(base + OFF_Q + t * Q_TERM, &tq, 0, q0, t * n_heads + h, bar(B_QFULL));
+      for (int j = 0; j < nkb; j++) {
+        const int b = j & 1;
+        if (j >= 2 && !bar_wait(bar(B_KVEMPTY + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
+        bar_expect_tx(bar(B_KVFULL + b), 3 * K_TERM + 3 * V_TERM);
+        for (int t = 0; t < 3; t++)
+          tma_load_3d(base + OFF_K + (b * 3 + t) * K_TERM, &tk, 0, j * FA_BK, t * G + g, bar(B_KVFULL + b));
+        for (int t = 0; t < 3; t++)
+          tma_load_3d(base + OFF_V + (b * 3 + t) * V_TERM, &tv, j * FA_BK, 0, t * G + g, bar(B_KVFULL + b));
+        issued = j + 1;
+      }
+      // drain: every started copy lands before the CTA exits
+      bar_drain(bar(B_QFULL), 0u);
+      for (int j = std::max(0, issued - 2); j < issued; j++) bar_drain(bar(B_KVFULL + (j & 1)), (unsigned)(j >> 1) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      auto issue_s = [&](int i) -> bool {
+        const int b = i & 1;
+        if (!bar_wait(bar(B_KVFULL + b), (unsigned)(i >> 1) & 1u, err, abort_flag)) return false;
+        if (i >= 2 && !bar_wait(bar(B_SFREE + b), (unsigned)((i >> 1) - 1) & 1u, err, abort_flag)) return false;
+        fence_after();
+        const uint32_t d = tmem + TM_S + 64u * b;
+        const uint32_t qa = base + OFF_Q, ka = base + OFF_K + b * 3 * K_TERM;
+#pragma unroll
+        for (int pr = 0; pr < 6; pr++) {
+          const uint32_t a0 = qa + kPairs[pr][0] * Q_TERM, b0 = ka + kPairs[pr][1] * K_TERM;
+#pragma unroll
+          for (int kk = 0; kk < FA_HD / 16; kk++)
+            mma_bf16(d, sw128_desc(a0 + 32u * kk), sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
+        }
+        mma_commit(bar(B_SFULL + b));
+        return true;
+      };
+      bool ok = bar_wait(bar(B_QFULL), 0u, err, abort_flag) && issue_s(0);
+      for (int j = 0; ok && j < nkb; j++) {
+        const int b = j & 1;
+        if (j + 1 < nkb && !issue_s(j + 1)) break;
+        if (!bar_wait(bar(B_PFULL), (unsigned)j & 1u, err, abort_flag)) break;
+        if (j >= 2 && !bar_wait(bar(B_OFREE + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
+        fence_after();
+        const uint32_t d = tmem + TM_O + 64u * b;
+        const uint32_t pa = base + OFF_P, va = base + OFF_V + b * 3 * V_TERM;
+#pragma unroll
+        for (int pr = 0; pr < 6; pr++) {
+          const uint32_t a0 = pa + kPairs[pr][0] * P_TERM, b0 = va + kPairs[pr][1] * V_TERM;
+#pragma unroll
+          for (int kk = 0; kk < FA_BK / 16; kk++)
+            mma_bf16(d, sw128_desc(a0 + 32u * kk), sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
+        }
+        mma_commit(bar(B_OFULL + b));
+        mma_commit(bar(B_KVEMPTY + b));
+        mma_commit(bar(B_PEMPTY));
+      }
+      mma_commit(bar(B_FIN));
+      bar_drain(bar(B_FIN), 0u);  // every MMA done before the columns are freed
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax / output: thread = query row ----------------
+    const int r = threadIdx.x;  // 0..127 = tensor-memory lane
+    const int qpos = offset + q0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    float o[FA_HD];
+#pragma unroll
+    for (int d = 0; d < FA_HD; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    bool ok = true;
+    auto wait_all = [&](uint32_t b, unsigned par) -> bool {  // lane 0 waits, the warp follows
+      int v = 1;
+      if (lane == 0) v = bar_wait(b, par, err, abort_flag);
+      return __shfl_sync(0xffffffffu, v, 0) != 0;
+    };
+    auto add_block = [&](int j) -> bool {  // o = o * alpha_prev + O_j
+      const int b = j & 1;
+      if (!wait_all(bar(B_OFULL + b), (unsigned)(j >> 1) & 1u)) return false;
+      fence_after();
+#pragma unroll
+      for (int c = 0; c < FA_HD / 16; c++) {
+        uint32_t v[16];
+        tmem_ld16(lane_base + TM_O + 64u * b + 16u * c, v);
+        tmem_wait_ld(v);
+#pragma unroll
+        for (int i = 0; i < 16; i++) o[16 * c + i] = fmaf(o[16 * c + i], alpha_prev, __uint_as_float(v[i]));
+      }
+      fence_before();
+      bar_arrive(bar(B_OFREE + b));
+      return true;
+    };
+    for (int j = 0; j < nkb; j++) {
+      const int b = j & 1;
+      if (!(ok = wait_all(bar(B_SFULL + b), (unsigned)(j >> 1) & 1u))) break;
+      fence_after();
+      uint32_t s[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld16(lane_base + TM_S + 64u * b + 16u * c, s[c]);
+      tmem_wait_ld(s[0]);
+      tmem_tie(s[1]);
+      tmem_tie(s[2]);
+      tmem_tie(s[3]);
+      fence_before();
+      bar_arrive(bar(B_SFREE + b));
+      // scores, causal mask, online softmax
+      const int k0 = j * FA_BK;
+      float sc[FA_BK];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < FA_BK; c++) {
+        const float v = (k0 + c <= qpos) ? __uint_as_float(s[c >> 4][c & 15]) * scale : -INFINITY;
+        sc[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = expf(m - m_new);  // 0 on the first block (m = -inf)
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < FA_BK; c++) {
+        sc[c] = expf(sc[c] - m_new);  // 0 for masked keys
+        sum += sc[c];
+      }
+      l = fmaf(l, alpha, sum);
+      m = m_new;
+      // P_j: three bf16 terms, 128-byte swizzled rows (chunk c of row r at c ^ (r % 8))
+      if (j >= 1 && !(ok = wait_all(bar(B_PEMPTY), (unsigned)(j - 1) & 1u))) break;
+      const uint32_t prow = base + OFF_P + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+#pragma unroll
+      for (int c8 = 0; c8 < FA_BK / 8; c8++) {
+        uint32_t w[3][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          __nv_bfloat16 h0, d0, l0, h1, d1, l1;
+          split3(sc[8 * c8 + 2 * i], h0, d0, l0);
+          split3(sc[8 * c8 + 2 * i + 1], h1, d1, l1);
+          w[0][i] = pack2(h0, h1);
+          w[1][i] = pack2(d0, d1);
+          w[2][i] = pack2(l0, l1);
+        }
+        const uint32_t off = (uint32_t)((c8 ^ (r & 7)) << 4);
+#pragma unroll
+        for (int t = 0; t < 3; t++)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + t * P_TERM + off), "r"(w[t][0]),
+                       "r"(w[t][1]), "r"(w[t][2]), "r"(w[t][3])
+                       : "memory");
+      }
+      fence_proxy_async();
+      bar_arrive(bar(B_PFULL));
+      if (j >= 1 && !(ok = add_block(j - 1))) break;
+      alpha_prev = alpha;
+    }
+    if (ok) ok = add_block(nkb - 1);
+    if (ok && !*abort_flag && q0 + r < n) {
+      const float inv = 1.0f / l;
+      float4 *dst = reinterpret_cast<float4 *>(out + ((size_t)(q0 + r) * n_heads + h) * FA_HD);
+#pragma unroll
+      for (int d = 0; d < FA_HD; d += 4)
+        dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+// dst[t][a][b][0..63] = term t of src[a*sa + b*sb + 0..63] for a < A, b < B.
+__global__ void k_split_rows(const float *__restrict__ src, long long sa, long long sb, int A, int B,
+                             __nv_bfloat16 *__restrict__ dst) {
+  const size_t plane = (size_t)A * B * FA_HD;
+  const size_t total = plane / 4;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = 4 * i;
+    const int d = (int)(e % FA_HD);
+    const size_t ab = e / FA_HD;
+    const int bb = (int)(ab % B), a = (int)(ab / B);
+    const float4 v = *reinterpret_cast<const float4 *>(src + a * sa + bb * sb + d);
+    const float in[4] = {v.x, v.y, v.z, v.w};
+    __nv_bfloat16 th[4], td[4], tl[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) split3(in[k], th[k], td[k], tl[k]);
+    *reinterpret_cast<uint2 *>(dst + e) = make_uint2(pack2(th[0], th[1]), pack2(th[2], th[3]));
+    *reinterpret_cast<uint2 *>(dst + plane + e) = make_uint2(pack2(td[0], td[1]), pack2(td[2], td[3]));
+    *reinterpret_cast<uint2 *>(dst + 2 * plane + e) = make_uint2(pack2(tl[0], tl[1]), pack2(tl[2], tl[3]));
+  }
+}
+
+// dst[t][g][d][s] = term t of v[g*ga + s*sp + d], s < seq_k (rows padded to skp).
+// grid (ceil(seq_k/64), G), 256 threads: a 64-key x 64-dim tile through shared memory.
+__global__ void k_split_vt(const float *__restrict__ v, long long ga, long long sp, int seq_k, int skp,
+                           __nv_bfloat16 *__restrict__ dst) {
+  __shared__ float tile[64][65];
+  const int s0 = blockIdx.x * 64, g = blockIdx.y, G = gridDim.y;
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+    const int s = i / 64, d = i % 64;
+    tile[s][d] = (s0 + s < seq_k) ? v[g * ga + (long long)(s0 + s) * sp + d] : 0.f;
+  }
+  __syncthreads();
+  const size_t plane = (size_t)G * FA_HD * skp;
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+    const int d = i / 64, s = i % 64;
+    if (s0 + s >= skp) continue;
+    __nv_bfloat16 th, td, tl;
+    split3(tile[s][d], th, td, tl);
+    const size_t at = ((size_t)g * FA_HD + d) * skp + s0 + s;
+    dst[at] = th;
+    dst[plane + at] = td;
+    dst[2 * plane + at] = tl;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
+
+bool encode3(CUtensorMap *map, const void *ptr, cuuint64_t d0, cuuint64_t d1, cuuint64_t d2, cuuint64_t stride1,
+             cuuint64_t stride2, cuuint32_t b0, cuuint32_t b1) {
+  const cuuint64_t dims[3] = {d0, d1, d2}, strides[2] = {stride1, stride2};
+  const cuuint32_t box[3] = {b0, b1, 1}, es[3] = {1, 1, 1};
+  return g_enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+}  // namespace
+
+size_t attn_tc_workspace_bytes(int seq_q, int seq_k, int n_heads, int n_kv_heads) {
+  const size_t skp = ((size_t)seq_k + 7) & ~(size_t)7;
+  return align256((size_t)6 * n_heads * seq_q * FA_HD) + align256((size_t)6 * n_kv_heads * seq_k * FA_HD) +
+         align256((size_t)6 * n_kv_heads * FA_HD * skp);
+}
+
+bool attn_tc_supported(int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
+                       const void *q, const void *k, const void *v, size_t ws_bytes) {
+  if (!g_enc) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      g_enc = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  return g_enc && head_dim == FA_HD && seq_q >= 64 && seq_k >= seq_q && n_kv_heads > 0 &&
+         n_heads % n_kv_heads == 0 && kps % 4 == 0 && khs % 4 == 0 && ((uintptr_t)q & 15) == 0 &&
+         ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
+         ws_bytes >= attn_tc_workspace_bytes(seq_q, seq_k, n_heads, n_kv_heads);
+}
+
+cudaError_t launch_attn_tc(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
+                           int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
+                           void *ws, size_t ws_bytes) {
+  if (!attn_tc_supported(seq_q, seq_k, n_heads, n_kv_heads, head_dim, kps, khs, q, k, v, ws_bytes))
+    return cudaErrorNotSupported;
+  const int H = n_heads, G = n_kv_heads, n = seq_q;
+  const int skp = (seq_k + 7) & ~7;
+  uint8_t *w = (uint8_t *)ws;
+  __nv_bfloat16 *qs = (__nv_bfloat16 *)w;
+  __nv_bfloat16 *ks = (__nv_bfloat16 *)(w + align256((size_t)6 * H * n * FA_HD));
+  __nv_bfloat16 *vt = (__nv_bfloat16 *)((uint8_t *)ks + align256((size_t)6 * G * seq_k * FA_HD));
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  auto grid_for = [&](size_t work) { return (unsigned)std::max<size_t>(1, std::min<size_t>((work + 255) / 256, 8 * (size_t)sms)); };
+  k_split_rows<<<grid_for((size_t)H * n * 16), 256, 0, s>>>(q, FA_HD, (long long)H * FA_HD, H, n, qs);
+  k_split_rows<<<grid_for((size_t)G * seq_k * 16), 256, 0, s>>>(k, khs, kps, G, seq_k, ks);
+  k_split_vt<<<dim3((skp + 63) / 64, G), 256, 0, s>>>(v, khs, kps, seq_k, skp, vt);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  CUtensorMap tq, tk, tv;
+  if (!encode3(&tq, qs, FA_HD, n, 3 * H, FA_HD * 2, (cuuint64_t)n * FA_HD * 2, 64, FA_M) ||
+      !encode3(&tk, ks, FA_HD, seq_k, 3 * G, FA_HD * 2, (cuuint64_t)seq_k * FA_HD * 2, 64, FA_BK) ||
+      !encode3(&tv, vt, seq_k, FA_HD, 3 * G, (cuuint64_t)skp * 2, (cuuint64_t)FA_HD * skp * 2, FA_BK, FA_HD))
+    return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+  if (e != cudaSuccess) return e;
+  const int nqb = (n + FA_M - 1) / FA_M;
+  const float scale = 1.0f / sqrtf((float)head_dim);  // attention.rs:37
+  k_attn_tc<<<H * nqb, FA_THREADS, FA_SMEM, s>>>(tq, tk, tv, out, n, seq_k - n, H, H / G, nqb, scale, tc_err_ptr());
+  return cudaGetLastError();
+}
+
+}  // namespace sq

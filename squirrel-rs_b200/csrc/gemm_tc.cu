@@ -36,17 +36,19 @@
 
 #include "ops.cuh"
 #include "status.h"
+#include "tc.cuh"
 
 namespace sq {
 namespace {
+
+using namespace tc;
 
 constexpr int TC_M = 128;       // weight rows per tile (MMA M)
 constexpr int TC_KB = 64;       // K elements per stage: one 128-byte swizzle row of bf16
 constexpr int TC_TERMS = 3;     // bf16 terms per f32 activation
 constexpr int TC_THREADS = 128;
-constexpr long long TC_WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
 
-__device__ unsigned g_tc_err;
+__device__ unsigned g_tc_err;  // set when a bounded wait of a tensor-core kernel gave up
 
 template <int BN>
 struct TcCfg {
@@ -57,104 +59,17 @@ struct TcCfg {
   static constexpr int BAR_OFF = STAGES * STAGE;       // mbarriers after the stages
   static constexpr int SMEM = 1024 + BAR_OFF + 128;    // + alignment slack
   static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;  // f32 accumulator: one column per activation row
-  static constexpr uint32_t IDESC = (1u << 4)          // D format f32
-                                    | (1u << 7)        // A bf16
-                                    | (1u << 10)       // B bf16
-                                    | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+  static constexpr uint32_t IDESC = idesc_bf16(TC_M, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N for M = 128");
   static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "tiles keep 1024-byte swizzle alignment");
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void bar_init(uint32_t b, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(count) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint32_t b, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool bar_try_wait(uint32_t b, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(b), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for the completion of the phase with this parity.
-__device__ __forceinline__ bool bar_wait(uint32_t b, unsigned parity) {
-  if (bar_try_wait(b, parity)) return true;
-  const long long t0 = clock64();
-  while (!bar_try_wait(b, parity)) {
-    if (clock64() - t0 > TC_WAIT_LIMIT) {
-      atomicExch(&g_tc_err, 1u);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          dst),
-      "l"(map), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
-          dst),
-      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major operand tile written by TMA with
-// 128-byte swizzling: rows of 128 bytes, 8-row groups 1024 bytes apart (stride
-// byte offset), leading byte offset 16 (unused by swizzled K-major layouts),
-// descriptor version 1, layout code 2 = 128-byte swizzle. Advancing K by 16 bf16
-// elements inside the 128-byte row adds 32 bytes to the start address.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-// Arrive on the mbarrier once every tcgen05 operation this thread issued has completed.
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // grid: (ceil(N/128), ceil(m/BN), splits). kb_per: K blocks of 64 per split.
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int m, int N,
-              int nkb, int kb_per, float *__restrict__ y, float *__restrict__ part) {
+              int nkb, int kb_per, float *__restrict__ y, float *__restrict__ part, unsigned *err) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = su32(smem_raw);
@@ -180,19 +95,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bar_init(done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tw) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tx) : "memory");
+    prefetch_map(&tw);
+    prefetch_map(&tx);
   }
   __syncwarp();
-  if (warp == 0) {  // the whole warp allocates the accumulator columns
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32((const void *)tmem_slot)),
-                 "r"((uint32_t)C::TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
+  if (warp == 0) tmem_alloc(su32((const void *)tmem_slot), C::TMEM_COLS);  // the whole warp
+  fence_before();
   __syncthreads();
-  tc_fence_after();
+  fence_after();
   const uint32_t tmem = *tmem_slot;
 
   int issued = 0;  // producer: K blocks whose copies were started
@@ -201,8 +111,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int s = i % C::STAGES;
       int ok = 1;
       if (lane == 0) {
-        if (i >= C::STAGES) ok = bar_wait(empty(s), (unsigned)((i / C::STAGES) - 1) & 1u);
-        if (ok && *abort_flag) ok = 0;
+        if (i >= C::STAGES) ok = bar_wait(empty(s), (unsigned)((i / C::STAGES) - 1) & 1u, err, abort_flag);
         if (ok) {
           const uint32_t a = base + (uint32_t)s * C::STAGE;
           const int k = (kb0 + i) * TC_KB;
@@ -211,8 +120,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int t = 0; t < TC_TERMS; t++)
             tma_load_3d(a + C::A_BYTES + (uint32_t)t * C::B_BYTES, &tx, k, t0, t, full(s));
-        } else {
-          *abort_flag = 1;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -220,15 +127,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       issued = i + 1;
     }
   } else if (warp == 1) {
-    int consumed = 0;
     for (int i = 0; i < nk; i++) {
       const int s = i % C::STAGES;
       int ok = 1;
       if (lane == 0) {
-        ok = bar_wait(full(s), (unsigned)(i / C::STAGES) & 1u);
-        if (ok && *abort_flag) ok = 0;
+        ok = bar_wait(full(s), (unsigned)(i / C::STAGES) & 1u, err, abort_flag);
         if (ok) {
-          tc_fence_after();
+          fence_after();
           const uint32_t a = base + (uint32_t)s * C::STAGE;
 #pragma unroll
           for (int t = 0; t < TC_TERMS; t++) {
@@ -239,23 +144,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                        (i | t | kk) != 0 ? 1u : 0u);
           }
           mma_commit(empty(s));  // the stage is free once these MMAs have read it
-        } else {
-          *abort_flag = 1;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
-      consumed = i + 1;
     }
-    (void)consumed;
     if (lane == 0) mma_commit(done);  // arrives when every MMA above has completed
     __syncwarp();
   }
 
   // Epilogue: every warp reads its 32 accumulator lanes (weight rows f0+32*warp ..).
-  int ok = bar_wait(done, 0u);
+  int ok = 1;
+  if (lane == 0) ok = bar_wait(done, 0u, err, abort_flag);
   ok = __shfl_sync(0xffffffffu, ok, 0);
-  tc_fence_after();
+  fence_after();
   if (ok && !*abort_flag) {
     float *out = part ? part + (size_t)blockIdx.z * m * N : y;
     const int f = f0 + 32 * warp + lane;
@@ -264,6 +166,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (t0 + c >= m) break;  // warp-uniform
       uint32_t r[16];
       tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, r);
+      tmem_wait_ld(r);
       if (f < N) {
 #pragma unroll
         for (int j = 0; j < 16; j++) {
@@ -273,18 +176,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   }
-  // Drain: copies started but never consumed (only after an abort) must land before
-  // the CTA's shared memory goes away.
+  // Drain (only after an abort): copies started but not consumed land before the
+  // CTA's shared memory goes away, and the MMAs finish before the columns are freed.
   if (warp == 0 && lane == 0) {
-    for (int i = std::max(0, issued - C::STAGES); i < issued; i++)
-      bar_wait(full(i % C::STAGES), (unsigned)(i / C::STAGES) & 1u);
+    for (int i = std::max(0, issued - C::STAGES); i < issued; i++) bar_drain(full(i % C::STAGES), (unsigned)(i / C::STAGES) & 1u);
   }
-  tc_fence_before();
+  if (warp == 1 && lane == 0) bar_drain(done, 0u);
+  fence_before();
   __syncthreads();
   if (warp == 0) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
-                 : "memory");
+    fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
@@ -323,6 +225,24 @@ __global__ void k_split_sum_tc(const float *__restrict__ part, int splits, size_
     y[i] = s;
   }
 }
+
+}  // namespace
+
+// Device address of the error word of the tensor-core kernels on the current device.
+unsigned *tc_err_ptr() {
+  static unsigned *ptrs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tc_err) != cudaSuccess) return nullptr;
+    ptrs[dev] = (unsigned *)p;
+  }
+  return ptrs[dev];
+}
+
+namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 int g_sms_tc = 0;
@@ -369,7 +289,8 @@ cudaError_t run_tc(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const 
   const int kb_per = (nkb + splits - 1) / splits;
   splits = (nkb + kb_per - 1) / kb_per;  // every split gets at least one block
   const dim3 grid((N + TC_M - 1) / TC_M, (m + BN - 1) / BN, splits);
-  k_gemm_tc<BN><<<grid, TC_THREADS, C::SMEM, s>>>(tw, tx, m, N, nkb, kb_per, y, splits > 1 ? part : nullptr);
+  k_gemm_tc<BN><<<grid, TC_THREADS, C::SMEM, s>>>(tw, tx, m, N, nkb, kb_per, y, splits > 1 ? part : nullptr,
+                                                  tc_err_ptr());
   e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
   const size_t n = (size_t)m * N;

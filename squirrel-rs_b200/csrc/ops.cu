@@ -867,6 +867,15 @@ extern "C" int sq_sdpa_cached(void *stream, const float *q, const float *k, cons
   if (seq_q <= 0 || seq_k < seq_q) return fail(SQ_ERR_SHAPE, "sdpa_cached: need 0 < seq_q <= seq_k");
   if (head_dim > 256 || head_dim % 32) return fail(SQ_ERR_SHAPE, "sdpa_cached: head_dim must be a multiple of 32, <= 256");
   cudaStream_t s = (cudaStream_t)stream;
+  const long long kps = (long long)n_kv_heads * head_dim, khs = head_dim;
+  const size_t tc_bytes = attn_tc_workspace_bytes(seq_q, seq_k, n_heads, n_kv_heads);
+  if (attn_tc_supported(seq_q, seq_k, n_heads, n_kv_heads, head_dim, kps, khs, q, k, v, tc_bytes)) {
+    void *ws = nullptr;  // tensor cores: workspace for the bf16 terms of q, k and v
+    SQ_CUDA(scratch_alloc(&ws, tc_bytes, s));
+    cudaError_t e = launch_attn_tc(s, q, k, v, out, seq_q, seq_k, n_heads, n_kv_heads, head_dim, kps, khs, ws, tc_bytes);
+    cudaFreeAsync(ws, s);
+    return e == cudaSuccess ? SQ_OK : cuda_fail(e, "sq_sdpa_cached");
+  }
   const int ns = sdpa_num_splits(seq_q, seq_k, n_heads);
   float *part = nullptr;
   if (ns > 1) SQ_CUDA(scratch_alloc((void **)&part, sdpa_partials_floats(seq_q, n_heads, head_dim, ns) * 4, s));

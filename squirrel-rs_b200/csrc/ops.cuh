@@ -22,10 +22,20 @@ cudaError_t launch_gemm_f32w(cudaStream_t s, const float *x, int m, int K, const
 bool gemm_tc_supported(int m, int K, const float *x, const void *w, int wtype, const float *ws, size_t ws_floats);
 cudaError_t launch_gemm_tc_bf16(cudaStream_t s, const float *x, int m, int K, const void *w, int N, float *y,
                                 float *ws, size_t ws_floats);
-// Non-zero when a bounded wait of the tensor-core GEMM gave up (read after a sync).
+// Non-zero when a bounded wait of a tensor-core kernel gave up (read after a sync).
 unsigned gemm_tc_status(bool clear);
+unsigned *tc_err_ptr();  // device address of that error word (current device)
 // False when SQB200_GEMM=simt selects the CUDA-core GEMM for bf16 weights too.
 bool gemm_tc_enabled();
+// Tensor-core causal attention (attention_tc.cu), head_dim 64, seq_q >= 64: the same
+// arguments as launch_sdpa plus a workspace of attn_tc_workspace_bytes() bytes for the
+// bf16 terms of q, k and v.
+size_t attn_tc_workspace_bytes(int seq_q, int seq_k, int n_heads, int n_kv_heads);
+bool attn_tc_supported(int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
+                       const void *q, const void *k, const void *v, size_t ws_bytes);
+cudaError_t launch_attn_tc(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
+                           int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
+                           void *ws, size_t ws_bytes);
 cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out);
 cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype,
                          int embed_dim, int vocab, float *out);

@@ -494,7 +494,11 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
   const size_t kv_elems = (size_t)c.n_blocks * c.n_kv_heads * max_ctx * c.head_dim;
   SQ_CUDA(ctx_alloc(x.get(), &x->kc, kv_elems));
   SQ_CUDA(ctx_alloc(x.get(), &x->vc, kv_elems));
-  const int R = x->ws_rows = 256;  // prefill is processed in chunks of this many rows
+  // Prefill is processed in chunks of this many rows (SQB200_PREFILL_ROWS overrides
+  // the default of 2048): the larger the chunk, the more output tiles per GEMM.
+  int rows_cap = 2048;
+  if (const char *v = getenv("SQB200_PREFILL_ROWS")) rows_cap = std::max(1, atoi(v));
+  const int R = x->ws_rows = std::max(1, std::min(rows_cap, max_ctx));
   SQ_CUDA(ctx_alloc(x.get(), &x->hidden, (size_t)R * E));
   SQ_CUDA(ctx_alloc(x.get(), &x->normed, (size_t)R * E));
   SQ_CUDA(ctx_alloc(x.get(), &x->q, (size_t)R * Q));
@@ -610,9 +614,17 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     TRY(launch_rope_rows_table(s, c->q, n, Q, pos, c->d_cos, c->d_sin, half, pos_dev));
     TRY(launch_rope_rows_table(s, c->k, n, KVd, pos, c->d_cos, c->d_sin, half, pos_dev));
     TRY(launch_kv_append(s, c->k, c->v, kc, vc, n, cf.n_kv_heads, cf.head_dim, pos, c->max_ctx, pos_dev));
-    const int ns = pos_dev ? sdpa_num_splits(n, c->max_ctx, cf.n_heads) : sdpa_num_splits(n, pos + n, cf.n_heads);
-    TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim,
-                    (long long)c->max_ctx * cf.head_dim, ns, c->sdpa_part, pos_dev));
+    const long long khs = (long long)c->max_ctx * cf.head_dim;
+    if (!pos_dev && attn_tc_supported(n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs, c->q, kc,
+                                      vc, c->gemm_ws_floats * sizeof(float))) {
+      // tensor cores; the GEMM workspace is free between the projections
+      TRY(launch_attn_tc(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim,
+                         khs, c->gemm_ws, c->gemm_ws_floats * sizeof(float)));
+    } else {
+      const int ns = pos_dev ? sdpa_num_splits(n, c->max_ctx, cf.n_heads) : sdpa_num_splits(n, pos + n, cf.n_heads);
+      TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs,
+                      ns, c->sdpa_part, pos_dev));
+    }
     TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
     TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));

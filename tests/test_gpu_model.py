@@ -126,6 +126,25 @@ def test_long_context_decode_kernel(gpu_lib, models, wt):
     ctx.close()
 
 
+@pytest.mark.parametrize("wt", ["bf16", "q8_0"])
+@pytest.mark.parametrize("rows", ["100", "2048"])
+def test_prefill_chunks(gpu_lib, models, wt, rows, monkeypatch):
+    """A 600-token prompt prefilled in chunks of 100 rows (KV appended between chunks,
+    later chunks attending to earlier ones) or in one chunk matches the oracle."""
+    monkeypatch.setenv("SQB200_PREFILL_ROWS", rows)  # read when the context is created
+    spec = "small"
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(600, seed=21, high=G.SPECS[spec]["vocab"])
+    ref = O.Model(path)
+    ids_ref, _, logits_ref = ref.generate(prompt, 3, want_logits=True)
+    m = gpu_model(models, spec, wt, 0)
+    ctx = m.new_context(700)
+    assert ctx.forward(prompt) == ids_ref[0]
+    assert_logits_close(ctx.logits(), logits_ref[0])
+    assert np.array_equal(ctx.decode_steps(2), ids_ref[1:3])
+    ctx.close()
+
+
 def test_upload_path_equals_gguf_path(gpu_lib, models):
     """sq_model_create + sq_model_upload_tensor + finalize (the reference-side parser
     path) gives the same model as sq_model_load_gguf."""

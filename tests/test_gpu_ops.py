@@ -213,7 +213,11 @@ def test_rope_rows(gpu_lib):
 
 @pytest.mark.parametrize("cfg", [(1, 1, 1, 1, 4), (2, 2, 1, 1, 2), (1, 1, 4, 2, 32), (1, 2049, 32, 8, 64),
                                  (1, 2304, 32, 8, 64), (37, 37, 8, 2, 64), (16, 80, 32, 8, 128),
-                                 (1, 130, 32, 8, 128)])
+                                 (1, 130, 32, 8, 128),
+                                 # seq_q >= 64, head_dim 64: the tensor-core kernel (ragged query
+                                 # blocks, keys before the chunk, GQA groups 1..8)
+                                 (64, 64, 8, 2, 64), (200, 333, 32, 8, 64), (300, 300, 4, 4, 64),
+                                 (129, 1000, 8, 1, 64)])
 def test_sdpa_cached(gpu_lib, cfg):
     """Tolerance |gpu - oracle| <= 2e-5 * max|v| (softmax-weighted average of V rows)."""
     from sqb200 import lib
