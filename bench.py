@@ -56,6 +56,10 @@ def parse():
     ap.add_argument("--acts", default="f32", choices=["f32", "q8"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-decode-steps", type=int, default=4)
+    ap.add_argument("--prefill", default="512,2048,8192",
+                    help="BF16 1B prefill prompt lengths reported beside the decode metric (empty: skip)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the BF16 prefill measurement (one GPU; for profiling the prefill kernels)")
     return ap.parse_args()
 
 
@@ -191,6 +195,67 @@ def run_reference(args):
     return 0
 
 
+def prefill_flops(cfg, n):
+    """Algorithmic FLOPs of prefilling an n-token prompt from position 0: the
+    projections (2 per weight per row), causal attention (q.k and p.v: 4*hd per
+    attended key per q head) and the LM head of the last row."""
+    E, F, hd = cfg.embed_dim, cfg.ffn_dim, cfg.head_dim
+    Q, KV = cfg.n_heads * hd, cfg.n_kv_heads * hd
+    per_row = 2 * cfg.n_blocks * (E * (Q + 2 * KV) + Q * E + 3 * E * F)
+    attn = cfg.n_blocks * cfg.n_heads * 4 * hd * n * (n + 1) // 2
+    mma = 3 * per_row * n + 6 * attn  # bf16 MMA work issued: 3 activation terms; 6 term products
+    return per_row * n + attn + 2 * E * cfg.vocab_size, mma
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def run_prefill(lib, G, lengths, device):
+    """BF16 prefill throughput (the tensor-core GEMM and attention path): one forward
+    of an n-token prompt per length, device time from CUDA events on the context's
+    stream (the forward copies the ids in and the argmax out itself), best of two."""
+    import torch
+    model = lib.Model(G.ensure_gguf("1b", "bf16"), device=device)
+    cfg = model.config
+    out = {}
+    peak, kind = tensor_peak()
+    for n in lengths:
+        ctx = model.new_context(n + 8)
+        stream = torch.cuda.ExternalStream(ctx.stream)
+        prompt = G.prompt_ids(n, seed=1234)
+        ctx.forward(prompt[:64])
+        best = None
+        for _ in range(2):
+            ctx.reset()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            t0 = time.perf_counter()
+            tok = ctx.forward(prompt)
+            wall = time.perf_counter() - t0
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+            if best is None or ms < best[0]:
+                best = (ms, wall, tok)
+        ms, wall, tok = best
+        flops, mma = prefill_flops(cfg, n)
+        achieved = flops / (ms / 1e3) / 1e12
+        out[str(n)] = {"tok_s": n / (ms / 1e3), "e2e_tok_s": n / wall, "ms": ms, "next_id": int(tok),
+                       "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                                    "frac": achieved / peak, "peak_source": kind,
+                                    "mma_tflops_issued": mma / (ms / 1e3) / 1e12}}
+        ctx.close()
+    model.close()
+    return {"workload": "1b-bf16 prefill (config 3)", "dtype": "f32 activations, bf16 weights; bf16 MMA terms",
+            "lengths": out}
+
+
 def run_ours(args):
     import torch
     rank = int(os.environ.get("RANK", "0"))
@@ -287,6 +352,9 @@ def run_ours(args):
         cpu = {"value": tps, "unit": "tok/s", "cores": th, "kind": "port",
                "sample": f"{cplen}-token prompt prefill untimed, then {args.cpu_decode_steps} timed decode tokens "
                          f"({spec} {wt}, W8A32 scalar x86 path, C restatement, {th} threads)"}
+    prefill = None
+    if rank == 0 and world == 1 and args.prefill and spec == "1b":
+        prefill = run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], local)
     if rank == 0:
         line = {
             "metric": METRIC if args.workload == "1b-q8_0" else f"decode tok/s ({args.workload}, bs1)",
@@ -308,6 +376,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "first_ids": [int(first)] + [int(i) for i in ids[:8]],
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     ctx.close()
@@ -321,6 +390,11 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.prefill_only:
+        from sqb200 import gguf_synth as G
+        from sqb200 import lib
+        print(json.dumps(run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], 0)), flush=True)
+        return 0
     return run_ours(args)
 
 
