@@ -1,7 +1,8 @@
-// gemm_tc.cu — tensor-core prefill projections for BF16 weights:
-// Y[m][N] = X[m][K] @ W^T with f32 activations X and bf16 weight rows W (GGUF BF16),
-// the m-row case of ops/linear.rs:26-37 (kernels/matmul.rs:68-128 runs one f32
-// matvec per row; the bf16 weights are widened to f32 exactly).
+// gemm_tc.cu — tensor-core prefill projections: Y[m][N] = X[m][K] @ W^T with f32
+// activations X and native GGUF weight rows W (BF16, Q8_0, Q4_0), the m-row case of
+// ops/linear.rs:26-37 (kernels/matmul.rs:68-128 runs one f32 matvec per row).
+// k_gemm_tc serves BF16 rows (widened to f32 exactly by the reference); k_gemm_tcq
+// serves Q8_0 / Q4_0 rows with per-block scaling (further below).
 //
 // Accuracy: every f32 activation is split into three bf16 terms x = h + d + l
 // (h = bf16(x), d = bf16(x - h), l = bf16(x - h - d); each difference is exact and
@@ -190,6 +191,290 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Q8_0 / Q4_0 weights (kernels/dot_prod.rs W8A32 / W4A32: each 32-element block's
+// products are summed, then the sum is multiplied by the block's f16 scale and added
+// to the row's f32 accumulator). The quants become exact bf16 values for the MMA;
+// each block's sum over the three activation terms lands in its own tensor-memory
+// buffer (four in rotation); the epilogue threads fold sum * scale into f32
+// registers block by block, in block order.
+//
+// Warps 0-3: thread r owns weight row f0 + r: converts its row of each 64-element
+// step from the raw block bytes into the 128-byte swizzled bf16 A tile, and folds the
+// block sums of tensor-memory lane r. Warp 4: TMA of the raw weight rows (eight
+// blocks = 256 elements per copy, 128 rows). Warp 5: TMA of the activation terms.
+// Warp 6: MMA issue.
+// ---------------------------------------------------------------------------------
+constexpr int Q_CHUNK = 256;  // K elements per raw weight copy (eight blocks)
+constexpr int Q_THREADS = 224;
+
+template <int T, int BN>
+struct QCfg {
+  static constexpr int BB = T == SQ_Q8_0 ? Q8_BYTES : Q4_BYTES;
+  static constexpr int CB = 8 * BB;                   // bytes of one row's chunk: 272 / 144
+  static constexpr int RAW = TC_M * CB;               // 34816 / 18432: multiples of 1024
+  static constexpr int A_TILE = TC_M * TC_KB * 2;     // 16 KB
+  static constexpr int B_TERM = BN * TC_KB * 2;
+  static constexpr int B_STAGE = TC_TERMS * B_TERM;
+  static constexpr int NB = BN >= 128 ? 2 : 3;        // activation-term stages
+  static constexpr int OFF_RAW = 0;
+  static constexpr int OFF_A = 2 * RAW;
+  static constexpr int OFF_B = OFF_A + 2 * A_TILE;
+  static constexpr int OFF_BAR = OFF_B + NB * B_STAGE;
+  static constexpr int SMEM = 1024 + OFF_BAR + 256;
+  static constexpr int NP = 4;                        // tensor-memory block-sum buffers
+  static constexpr uint32_t TMEM_COLS = NP * BN < 32 ? 32 : NP * BN;
+  static constexpr uint32_t IDESC = idesc_bf16(TC_M, BN);
+  static_assert(RAW % 1024 == 0 && B_TERM % 1024 == 0, "1024-byte tile alignment");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(TMEM_COLS <= 512, "tensor memory columns");
+};
+
+// barrier slots
+enum : int {
+  QB_RAWFULL = 0,   // [2]
+  QB_RAWEMPTY = 2,  // [2]
+  QB_AFULL = 4,     // [2]
+  QB_AEMPTY = 6,    // [2]
+  QB_PFULL = 8,     // [4]
+  QB_PEMPTY = 12,   // [4]
+  QB_FIN = 16,
+  QB_BFULL = 17,    // [NB]
+  QB_BEMPTY = 20,   // [NB]
+  QB_N = 23
+};
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+// four unsigned bytes b (value b + bias_off) of u -> two bf16x2 words of (b - bias), exact
+__device__ __forceinline__ void bytes_to_bf16(uint32_t u, float bias, uint32_t &lo, uint32_t &hi) {
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - bias;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - bias;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - bias;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - bias;
+  const __nv_bfloat162 a = __floats2bfloat162_rn(f0, f1), b = __floats2bfloat162_rn(f2, f3);
+  lo = *reinterpret_cast<const uint32_t *>(&a);
+  hi = *reinterpret_cast<const uint32_t *>(&b);
+}
+// Four bytes starting at shared address a (2-byte aligned).
+__device__ __forceinline__ uint32_t lds_4at(uint32_t a) {
+  if (a & 2u) return __byte_perm(lds_u32(a - 2), lds_u32(a + 2), 0x5432);
+  return lds_u32(a);
+}
+
+// Row r's 64 elements of blocks (2*sub, 2*sub + 1) of the raw chunk at `row` into
+// the swizzled A tile row at `dst` (chunk c of 8 elements at c ^ (r % 8)).
+template <int T>
+__device__ __forceinline__ void convert_step(uint32_t row, int sub, uint32_t dst, int r7) {
+  constexpr int BB = T == SQ_Q8_0 ? Q8_BYTES : Q4_BYTES;
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    const int blk = 2 * sub + c / 4;
+    uint32_t w0, w1;
+    float bias;
+    if constexpr (T == SQ_Q8_0) {  // elements 8*(c%4) .. +7 of block blk: int8, stored as value + 128
+      const uint32_t a = row + (uint32_t)(blk * BB + 2 + 8 * (c % 4));
+      w0 = lds_4at(a) ^ 0x80808080u;
+      w1 = lds_4at(a + 4) ^ 0x80808080u;
+      bias = 8388736.0f;  // 2^23 + 128
+    } else {  // low nibbles of bytes 0..15 are elements 0..15, high nibbles 16..31; value = nibble - 8
+      const int hi = (c % 4) / 2, part = c % 2;
+      const uint32_t a = row + (uint32_t)(blk * BB + 2 + 8 * part);
+      const uint32_t b0 = lds_4at(a), b1 = lds_4at(a + 4);
+      w0 = hi ? (b0 >> 4) & 0x0F0F0F0Fu : b0 & 0x0F0F0F0Fu;
+      w1 = hi ? (b1 >> 4) & 0x0F0F0F0Fu : b1 & 0x0F0F0F0Fu;
+      bias = 8388616.0f;  // 2^23 + 8
+    }
+    uint32_t v0, v1, v2, v3;
+    bytes_to_bf16(w0, bias, v0, v1);
+    bytes_to_bf16(w1, bias, v2, v3);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + (uint32_t)((c ^ r7) << 4)), "r"(v0), "r"(v1),
+                 "r"(v2), "r"(v3)
+                 : "memory");
+  }
+}
+
+// grid: (ceil(N/128), ceil(m/BN), splits); ch_per: 256-element chunks per split.
+template <int T, int BN>
+__global__ void __launch_bounds__(Q_THREADS, 1)
+    k_gemm_tcq(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int m, int N,
+               int nch, int ch_per, float *__restrict__ y, float *__restrict__ part, unsigned *err) {
+  using C = QCfg<T, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = su32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  const uint32_t bars = base + C::OFF_BAR;
+  auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+  uint8_t *gen = smem_raw + (base - raw0);
+  volatile uint32_t *tmem_slot = (volatile uint32_t *)(gen + C::OFF_BAR + 8 * QB_N);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f0 = blockIdx.x * TC_M, t0 = blockIdx.y * BN;
+  const int c0 = blockIdx.z * ch_per;
+  const int nc = min(nch, c0 + ch_per) - c0;  // >= 1
+  const int nsub = 4 * nc;                    // 64-element steps
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < QB_N; i++) {
+      const bool rows = (i >= QB_RAWEMPTY && i < QB_RAWEMPTY + 2) || (i >= QB_AFULL && i < QB_AFULL + 2) ||
+                        (i >= QB_PEMPTY && i < QB_PEMPTY + 4);
+      bar_init(bar(i), rows ? TC_M : 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&tw);
+    prefetch_map(&tx);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(su32((const void *)tmem_slot), C::TMEM_COLS);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {  // raw weight rows, one 256-element chunk per copy
+    if (lane == 0) {
+      int issued = 0;
+      for (int c = 0; c < nc; c++) {
+        const int rb = c & 1;
+        if (c >= 2 && !bar_wait(bar(QB_RAWEMPTY + rb), (unsigned)((c >> 1) - 1) & 1u, err, abort_flag)) break;
+        bar_expect_tx(bar(QB_RAWFULL + rb), (unsigned)C::RAW);
+        tma_load_2d(base + C::OFF_RAW + rb * C::RAW, &tw, (c0 + c) * (C::CB / 2), f0, bar(QB_RAWFULL + rb));
+        issued = c + 1;
+      }
+      for (int c = std::max(0, issued - 2); c < issued; c++) bar_drain(bar(QB_RAWFULL + (c & 1)), (unsigned)(c >> 1) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 5) {  // activation terms, one 64-element step per stage
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nsub; i++) {
+        const int bb = i % C::NB;
+        if (i >= C::NB && !bar_wait(bar(QB_BEMPTY + bb), (unsigned)((i / C::NB) - 1) & 1u, err, abort_flag)) break;
+        bar_expect_tx(bar(QB_BFULL + bb), (unsigned)C::B_STAGE);
+        const int k = c0 * Q_CHUNK + i * TC_KB;
+#pragma unroll
+        for (int t = 0; t < TC_TERMS; t++)
+          tma_load_3d(base + C::OFF_B + bb * C::B_STAGE + t * C::B_TERM, &tx, k, t0, t, bar(QB_BFULL + bb));
+        issued = i + 1;
+      }
+      for (int i = std::max(0, issued - C::NB); i < issued; i++)
+        bar_drain(bar(QB_BFULL + i % C::NB), (unsigned)(i / C::NB) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 6) {  // MMA issue: per step two blocks, each 3 terms x 2 K steps into its own buffer
+    if (lane == 0) {
+      for (int i = 0; i < nsub; i++) {
+        const int ab = i & 1, bb = i % C::NB;
+        if (!bar_wait(bar(QB_AFULL + ab), (unsigned)(i >> 1) & 1u, err, abort_flag)) break;
+        if (!bar_wait(bar(QB_BFULL + bb), (unsigned)(i / C::NB) & 1u, err, abort_flag)) break;
+        bool ok = true;
+        for (int blk = 0; blk < 2 && ok; blk++) {
+          const int gb = 2 * i + blk, pb = gb & 3;
+          if (gb >= C::NP && !bar_wait(bar(QB_PEMPTY + pb), (unsigned)((gb >> 2) - 1) & 1u, err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t a = base + C::OFF_A + ab * C::A_TILE, b = base + C::OFF_B + bb * C::B_STAGE;
+#pragma unroll
+          for (int t = 0; t < TC_TERMS; t++)
+#pragma unroll
+            for (int kk = 0; kk < 2; kk++) {
+              const uint32_t ko = 32u * (uint32_t)(2 * blk + kk);
+              mma_bf16(tmem + (uint32_t)(pb * BN), sw128_desc(a + ko), sw128_desc(b + t * C::B_TERM + ko), C::IDESC,
+                       (t | kk) != 0 ? 1u : 0u);
+            }
+          mma_commit(bar(QB_PFULL + pb));
+        }
+        if (!ok) break;
+        mma_commit(bar(QB_AEMPTY + ab));
+        mma_commit(bar(QB_BEMPTY + bb));
+      }
+      mma_commit(bar(QB_FIN));
+      bar_drain(bar(QB_FIN), 0u);
+    }
+    __syncwarp();
+  } else {  // warps 0-3: row r converts and folds
+    const int r = threadIdx.x, r7 = r & 7;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    float acc[BN];
+#pragma unroll
+    for (int j = 0; j < BN; j++) acc[j] = 0.f;
+    float sc[8], scp[8];
+    bool ok = true;
+    auto wait_all = [&](uint32_t b, unsigned par) -> bool {
+      int v = 1;
+      if (lane == 0) v = bar_wait(b, par, err, abort_flag);
+      return __shfl_sync(0xffffffffu, v, 0) != 0;
+    };
+    auto fold = [&](int gb, float s) -> bool {  // acc += s * block sum gb
+      const int pb = gb & 3;
+      if (!wait_all(bar(QB_PFULL + pb), (unsigned)(gb >> 2) & 1u)) return false;
+      fence_after();
+#pragma unroll
+      for (int c = 0; c < BN / 16; c++) {
+        uint32_t v[16];
+        tmem_ld16(lane_base + (uint32_t)(pb * BN + 16 * c), v);
+        tmem_wait_ld(v);
+#pragma unroll
+        for (int j = 0; j < 16; j++) acc[16 * c + j] = fmaf(s, __uint_as_float(v[j]), acc[16 * c + j]);
+      }
+      fence_before();
+      bar_arrive(bar(QB_PEMPTY + pb));
+      return true;
+    };
+    for (int c = 0; c < nc && ok; c++) {
+      const int rb = c & 1;
+      if (!(ok = wait_all(bar(QB_RAWFULL + rb), (unsigned)(c >> 1) & 1u))) break;
+      const uint32_t row = base + C::OFF_RAW + rb * C::RAW + (uint32_t)(r * C::CB);
+#pragma unroll
+      for (int j = 0; j < 8; j++) sc[j] = __half2float(__ushort_as_half((uint16_t)lds_u16(row + j * C::BB)));
+#pragma unroll
+      for (int sub = 0; sub < 4; sub++) {
+        const int i = 4 * c + sub, ab = i & 1;
+        if (i >= 2 && !(ok = wait_all(bar(QB_AEMPTY + ab), (unsigned)((i >> 1) - 1) & 1u))) break;
+        convert_step<T>(row, sub, base + C::OFF_A + ab * C::A_TILE + (uint32_t)((r >> 3) * 1024 + r7 * 128), r7);
+        fence_proxy_async();
+        bar_arrive(bar(QB_AFULL + ab));
+        if (sub == 3) bar_arrive(bar(QB_RAWEMPTY + rb));  // scales are in registers
+        if (i >= 1) {  // fold the previous step's two blocks
+          const float s0 = sub == 0 ? scp[6] : sc[2 * sub - 2];
+          const float s1 = sub == 0 ? scp[7] : sc[2 * sub - 1];
+          if (!(ok = fold(2 * (i - 1), s0)) || !(ok = fold(2 * (i - 1) + 1, s1))) break;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) scp[j] = sc[j];
+    }
+    if (ok) ok = fold(2 * (nsub - 1), scp[6]) && fold(2 * (nsub - 1) + 1, scp[7]);
+    if (ok && !*abort_flag) {
+      float *out = part ? part + (size_t)blockIdx.z * m * N : y;
+      const int f = f0 + r;
+      if (f < N) {
+#pragma unroll
+        for (int j = 0; j < BN; j++)
+          if (t0 + j < m) out[(size_t)(t0 + j) * N + f] = acc[j];
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // xs[t][r][k] (t = 0, 1, 2): the three bf16 terms of x[r][k]; n = m*K elements,
 // plane = n, four elements per thread (n % 4 == 0).
 __global__ void k_split3(const float4 *__restrict__ x, size_t n4, __nv_bfloat16 *__restrict__ xs, size_t plane) {
@@ -298,17 +583,60 @@ cudaError_t run_tc(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const 
   return cudaGetLastError();
 }
 
+template <int T, int BN>
+cudaError_t run_tcq(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const void *w, int N, float *y,
+                    int splits, float *part) {
+  using C = QCfg<T, BN>;
+  CUtensorMap tw, tx;
+  const cuuint64_t rowbytes = (cuuint64_t)(K / QK) * C::BB;
+  const cuuint64_t wd[2] = {rowbytes / 2, (cuuint64_t)N}, wst[1] = {rowbytes};
+  const cuuint32_t wb[2] = {(cuuint32_t)(C::CB / 2), TC_M}, es[2] = {1, 1};
+  if (g_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(w), wd, wst, wb, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  const cuuint64_t xd[3] = {(cuuint64_t)K, (cuuint64_t)m, TC_TERMS},
+                   xst[2] = {(cuuint64_t)K * 2, (cuuint64_t)m * K * 2};
+  const cuuint32_t xb[3] = {TC_KB, BN, 1};
+  if (!encode(&tx, xs, 3, xd, xst, xb)) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k_gemm_tcq<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int nch = K / Q_CHUNK;
+  const int ch_per = (nch + splits - 1) / splits;
+  splits = (nch + ch_per - 1) / ch_per;
+  const dim3 grid((N + TC_M - 1) / TC_M, (m + BN - 1) / BN, splits);
+  k_gemm_tcq<T, BN><<<grid, Q_THREADS, C::SMEM, s>>>(tw, tx, m, N, nch, ch_per, y, splits > 1 ? part : nullptr,
+                                                     tc_err_ptr());
+  e = cudaGetLastError();
+  if (e != cudaSuccess || splits == 1) return e;
+  const size_t n = (size_t)m * N;
+  k_split_sum_tc<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(part, splits, n, y);
+  return cudaGetLastError();
+}
+
+template <int T>
+cudaError_t run_tcq_bn(int bn, cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const void *w, int N, float *y,
+                       int splits, float *part) {
+  if (bn == 32) return run_tcq<T, 32>(s, xs, m, K, w, N, y, splits, part);
+  if (bn == 64) return run_tcq<T, 64>(s, xs, m, K, w, N, y, splits, part);
+  return run_tcq<T, 128>(s, xs, m, K, w, N, y, splits, part);
+}
+
 }  // namespace
 
 bool gemm_tc_supported(int m, int K, const float *x, const void *w, int wtype, const float *ws, size_t ws_floats) {
   init_once();
-  return g_encode && wtype == SQ_BF16 && m >= 2 && K % 16 == 0 && x && ws && ((uintptr_t)x & 15) == 0 &&
-         ((uintptr_t)w & 15) == 0 && ((uintptr_t)ws & 255) == 0 && (size_t)3 * m * K / 2 + 64 <= ws_floats;
+  bool ok = g_encode && m >= 2 && K % 16 == 0 && x && ws && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
+            ((uintptr_t)ws & 255) == 0 && (size_t)3 * m * K / 2 + 64 <= ws_floats;
+  if (wtype == SQ_BF16) return ok;
+  if (wtype != SQ_Q8_0 && wtype != SQ_Q4_0) return false;
+  const size_t rowbytes = (size_t)(K / QK) * (wtype == SQ_Q8_0 ? Q8_BYTES : Q4_BYTES);
+  return ok && K % Q_CHUNK == 0 && rowbytes % 16 == 0;  // whole eight-block chunks on 16-byte boundaries
 }
 
-cudaError_t launch_gemm_tc_bf16(cudaStream_t s, const float *x, int m, int K, const void *w, int N, float *y,
-                                float *ws, size_t ws_floats) {
-  if (!gemm_tc_supported(m, K, x, w, SQ_BF16, ws, ws_floats)) return cudaErrorNotSupported;
+cudaError_t launch_gemm_tc(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
+                           float *ws, size_t ws_floats) {
+  if (!gemm_tc_supported(m, K, x, w, wtype, ws, ws_floats)) return cudaErrorNotSupported;
   // workspace: [3][m][K] bf16 terms, then split-K partials (256-byte aligned)
   __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(ws);
   const size_t xs_floats = ((size_t)3 * m * K / 2 + 63) & ~(size_t)63;
@@ -320,6 +648,19 @@ cudaError_t launch_gemm_tc_bf16(cudaStream_t s, const float *x, int m, int K, co
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int ft = (N + TC_M - 1) / TC_M;
+  if (wtype != SQ_BF16) {  // quantized rows: 256-element chunks, BN by the row count
+    const int bn = m <= 32 ? 32 : (m <= 64 ? 64 : 128);
+    const long long tiles = (long long)ft * ((m + bn - 1) / bn);
+    const int nch = K / Q_CHUNK;
+    int splits = 1;
+    if (tiles < g_sms_tc) {
+      splits = (int)std::min<long long>((g_sms_tc + tiles - 1) / tiles, 16);
+      splits = std::min(splits, nch);
+      while (splits > 1 && (size_t)splits * m * N > part_floats) splits--;
+    }
+    return wtype == SQ_Q8_0 ? run_tcq_bn<SQ_Q8_0>(bn, s, xs, m, K, w, N, y, splits, part)
+                            : run_tcq_bn<SQ_Q4_0>(bn, s, xs, m, K, w, N, y, splits, part);
+  }
   const int nkb = (K + TC_KB - 1) / TC_KB;
   const bool wide = (long long)ft * ((m + 127) / 128) >= g_sms_tc;
   const long long tiles = wide ? (long long)ft * ((m + 127) / 128) : (long long)ft * ((m + 63) / 64);

@@ -576,9 +576,9 @@ cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, con
     }
     if (wtype == SQ_Q8_0) linear_q8_t<SQ_Q8_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
     else linear_q8_t<SQ_Q4_0>(s, (const uint8_t *)xq, m, in_dim, wb, out_dim, y);
-  } else if (m >= 2) {  // several rows (prefill): tensor cores for bf16 weights, else the tiled GEMM
-    if (wtype == SQ_BF16 && gemm_tc_enabled() && gemm_tc_supported(m, in_dim, x, w, wtype, ws, ws_floats))
-      return launch_gemm_tc_bf16(s, x, m, in_dim, w, out_dim, y, ws, ws_floats);
+  } else if (m >= 2) {  // several rows (prefill): tensor cores, else the CUDA-core tiled GEMM
+    if (gemm_tc_enabled() && gemm_tc_supported(m, in_dim, x, w, wtype, ws, ws_floats))
+      return launch_gemm_tc(s, x, m, in_dim, w, wtype, out_dim, y, ws, ws_floats);
     return launch_gemm_f32w(s, x, m, in_dim, w, wtype, out_dim, y, ws, ws_floats);
   } else {
     if (wtype == SQ_Q8_0) linear_f32_t<SQ_Q8_0>(s, x, m, in_dim, wb, out_dim, y);
@@ -701,11 +701,12 @@ static cudaError_t scratch_alloc(void **p, size_t bytes, cudaStream_t s) {
 extern "C" const char *sq_last_error(void) { return g_last_error.c_str(); }
 extern "C" const char *sq_version(void) { return "squirrel-b200 0.1 (sm_100a)"; }
 
-// Workspace of the tensor-core GEMM for an op-level call (bf16 weights, m >= 2,
-// f32 activations): the three bf16 activation terms plus up to 8 split-K partials.
+// Workspace of the tensor-core GEMM for an op-level call (m >= 2, f32 activations):
+// the three bf16 activation terms plus up to 16 split-K partials.
 static size_t tc_workspace_floats(int m, int in_dim, int out_dim, int wtype, bool q8) {
-  if (q8 || wtype != SQ_BF16 || m < 2) return 0;
-  return (size_t)3 * m * in_dim / 2 + 64 + (size_t)8 * m * out_dim;
+  (void)wtype;
+  if (q8 || m < 2) return 0;
+  return (size_t)3 * m * in_dim / 2 + 64 + (size_t)16 * m * out_dim;
 }
 
 static int check_linear(const float *input, int m, int in_dim, const void *weight, int wtype, int out_dim,

@@ -16,16 +16,17 @@ cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, con
 // The tiled GEMM itself (gemm.cu): y[m][N] = x[m][K] @ w^T, native weight rows.
 cudaError_t launch_gemm_f32w(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
                              float *ws, size_t ws_floats);
-// Tensor-core GEMM for bf16 weights (gemm_tc.cu): the f32 activations are split into
-// three bf16 terms in `ws` (3*m*K/2 floats, then split-K partials). Supported when
-// m >= 2, K % 16 == 0, x and w 16-byte aligned, ws 256-byte aligned and large enough.
+// Tensor-core GEMM (gemm_tc.cu) for BF16, Q8_0 and Q4_0 weight rows: the f32
+// activations are split into three bf16 terms in `ws` (3*m*K/2 floats, then split-K
+// partials). Supported when m >= 2, K % 16 == 0 (quantized: K % 256 == 0 and 16-byte
+// rows), x and w 16-byte aligned, ws 256-byte aligned and large enough.
 bool gemm_tc_supported(int m, int K, const float *x, const void *w, int wtype, const float *ws, size_t ws_floats);
-cudaError_t launch_gemm_tc_bf16(cudaStream_t s, const float *x, int m, int K, const void *w, int N, float *y,
-                                float *ws, size_t ws_floats);
+cudaError_t launch_gemm_tc(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
+                           float *ws, size_t ws_floats);
 // Non-zero when a bounded wait of a tensor-core kernel gave up (read after a sync).
 unsigned gemm_tc_status(bool clear);
 unsigned *tc_err_ptr();  // device address of that error word (current device)
-// False when SQB200_GEMM=simt selects the CUDA-core GEMM for bf16 weights too.
+// False when SQB200_GEMM=simt selects the CUDA-core GEMM for every weight type.
 bool gemm_tc_enabled();
 // Tensor-core causal attention (attention_tc.cu), head_dim 64, seq_q >= 64: the same
 // arguments as launch_sdpa plus a workspace of attn_tc_workspace_bytes() bytes for the

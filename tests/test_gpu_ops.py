@@ -128,6 +128,30 @@ def test_linear_bf16_tensor_cores(gpu_lib, shape):
     assert np.all(err <= 1e-5 * mag + 1e-6), float((err / (mag + 1e-6)).max())
 
 
+# Quantized rows on the tensor cores: K a multiple of the 256-element raw chunk;
+# ragged rows and outputs, 1..16 K splits, every BN (32, 64, 128).
+TCQ_SHAPES = [(2, 256, 128), (33, 512, 130), (64, 2048, 512), (129, 1024, 300), (256, 2048, 2048),
+              (16, 8192, 512), (300, 768, 384), (32, 2048, 8192)]
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("shape", TCQ_SHAPES)
+def test_linear_quantized_tensor_cores(gpu_lib, wtype, shape):
+    """Quants as exact bf16, activations as three exact bf16 terms, one f32 block sum
+    per 32-element block scaled by its f16 scale and accumulated in block order (the
+    W8A32 / W4A32 scheme). |gpu - oracle| <= 1e-5 * sum|a_i w_i| + 1e-6."""
+    from sqb200 import lib
+    m, k, n = shape
+    rng = np.random.default_rng(m * 5 + k + n * 3 + wtype)
+    x = (rng.standard_normal((m, k)) * rng.choice([1e-3, 1.0, 40.0], (m, 1))).astype(np.float32)
+    w = rand_blocks(wtype, n * k // 32, rng)  # every int8 / nibble value reachable
+    got = host(lib.linear(dev(x), dev(w), wtype, n))
+    want = O.linear(x, w, wtype, n)
+    mag = term_magnitude(x, w, wtype, n)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-5 * mag + 1e-6), float((err / (mag + 1e-6)).max())
+
+
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("shape", SHAPES)
 def test_linear_q8_acts(gpu_lib, wtype, shape):
