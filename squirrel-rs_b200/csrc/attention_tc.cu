@@ -13,17 +13,24 @@
 // [3][G][64][seq_k padded to 8] (bf16), in a caller-provided workspace.
 //
 // Kernel: one CTA per (128-query block, q head); the heaviest (last) query blocks
-// start first. 6 warps:
-//   warp 4   TMA: the query block's three term tiles once, then per 64-key block the
-//            key and transposed-value term tiles into a double buffer;
-//   warp 5   one thread issues the MMAs: S_j = Q K_j^T (M = 128 queries, N = 64 keys)
-//            into one of two tensor-memory score buffers, and, once the softmax warps
-//            have written P_j, O_j = P_j V_j (N = 64 dims) into one of two output
-//            buffers; S_{j+1} is issued before O_j so it overlaps the softmax of j;
-//   warps 0-3  one thread per query row: the scores of block j from tensor memory,
-//            causal mask, online softmax (running max and sum, expf), P_j split into
-//            terms and stored 128-byte swizzled for the MMA, then the f32 running
-//            output o = o * exp(m_old - m_new) + O_j in registers (one block behind).
+// start first. 20 warps:
+//   warps 16, 18  TMA: the query block's three term tiles once, then per 64-key
+//            block the key (warp 16) and the transposed-value (warp 18) term tiles
+//            into separate double buffers (a key buffer is released when its S is
+//            done, a value buffer when its O is);
+//   warps 17, 19  one thread each issues MMAs: S_j = Q K_j^T (M = 128 queries,
+//            N = 64 keys) into one of two tensor-memory score buffers (warp 17), and,
+//            once the softmax warps have written P_j, O_j = P_j V_j (N = 64 dims,
+//            A = P read from tensor memory) into one of two output buffers (warp 19);
+//            the score MMAs of later blocks overlap the softmax of earlier ones;
+//   warps 0-15  four threads per query row (warps w, w + 4, w + 8, w + 12 share
+//            tensor-memory lanes), each with 16 keys and 16 output dims: scores
+//            of block j from tensor memory, causal mask near the diagonal, online
+//            softmax in base 2 (running max combined through shared memory, ex2),
+//            P_j split into terms and stored into one of two tensor-memory P
+//            buffers (so P_{j+1} is written while O_j is computed), then the
+//            f32 running output o = o * 2^(m_old - m_new) + O_j in registers (one
+//            block behind).
 // Every wait is bounded; on expiry the CTA records the error, stops, drains its
 // copies and MMAs, frees its tensor memory and returns.
 #include <cuda.h>
@@ -46,36 +53,44 @@ using namespace tc;
 constexpr int FA_M = 128;   // query rows per CTA
 constexpr int FA_BK = 64;   // keys per block
 constexpr int FA_HD = 64;   // head dim
-constexpr int FA_THREADS = 192;
+constexpr int FA_PARTS = 4;                 // softmax threads per query row
+constexpr int FA_SOFTMAX = 128 * FA_PARTS;  // softmax threads
+constexpr int FA_WARP_TMA = FA_SOFTMAX / 32, FA_WARP_MMA = FA_WARP_TMA + 1, FA_WARP_V = FA_WARP_TMA + 2,
+              FA_WARP_PV = FA_WARP_TMA + 3;
+constexpr int FA_THREADS = FA_SOFTMAX + 128;
 
 constexpr int Q_TERM = FA_M * FA_HD * 2;   // 16 KB
 constexpr int K_TERM = FA_BK * FA_HD * 2;  // 8 KB
 constexpr int V_TERM = FA_HD * FA_BK * 2;  // 8 KB (transposed: 64 dims x 64 keys)
-constexpr int P_TERM = FA_M * FA_BK * 2;   // 16 KB
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 3 * Q_TERM;      // two buffers of three key terms
 constexpr int OFF_V = OFF_K + 2 * 3 * K_TERM;  // two buffers of three value terms
-constexpr int OFF_P = OFF_V + 2 * 3 * V_TERM;  // three probability terms
-constexpr int OFF_BAR = OFF_P + 3 * P_TERM;
+constexpr int OFF_XCHG = OFF_V + 2 * 3 * V_TERM;  // row maxima / sums exchanged by a row's threads
+constexpr int OFF_BAR = OFF_XCHG + 3 * FA_PARTS * FA_M * 4;
 constexpr int FA_SMEM = 1024 + OFF_BAR + 256;
 static_assert(FA_SMEM <= 232448, "shared memory per CTA");
-static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && OFF_BAR % 8 == 0, "alignment");
+static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_BAR % 8 == 0, "alignment");
 
 // barrier slots (8 bytes each)
 enum : int {
   B_QFULL = 0,
-  B_KVFULL = 1,   // [2]
-  B_KVEMPTY = 3,  // [2]
-  B_SFULL = 5,    // [2]
-  B_SFREE = 7,    // [2]
-  B_PFULL = 9,
-  B_PEMPTY = 10,
-  B_OFULL = 11,   // [2]
-  B_OFREE = 13,   // [2]
-  B_FIN = 15,
-  N_BARS = 16
+  B_KFULL = 1,    // [2] key terms of a block landed
+  B_KEMPTY = 3,   // [2] S of that block done: the key buffer is free
+  B_VFULL = 5,    // [2]
+  B_VEMPTY = 7,   // [2] O of that block done: the value buffer is free
+  B_SFULL = 9,    // [2]
+  B_SFREE = 11,   // [2]
+  B_PFULL = 13,   // [2] P of a block written to tensor memory
+  B_PEMPTY = 15,  // [2] O of that block done: the P buffer is free
+  B_OFULL = 17,   // [2]
+  B_OFREE = 19,   // [2]
+  B_FIN = 21,     // the score issuer's MMAs all done
+  B_FIN2 = 22,    // the output issuer's MMAs all done
+  N_BARS = 23
 };
-constexpr uint32_t TM_S = 0, TM_O = 128, TM_COLS = 256;  // S[2] at columns 0/64, O[2] at 128/192
+// tensor-memory columns: S[2] at 0 / 64, O[2] at 128 / 192 (f32), P[2] at 256 / 352:
+// three bf16 terms of 32 columns each (two keys per 32-bit column, lane = query row)
+constexpr uint32_t TM_S = 0, TM_O = 128, TM_P = 256, P_COLS = 96, TM_COLS = 512;
 constexpr uint32_t IDESC = idesc_bf16(FA_M, 64);
 
 // term pairs (a, b) with a + b <= 2: the products kept
@@ -87,15 +102,23 @@ __device__ __forceinline__ void split3(float x, __nv_bfloat16 &h, __nv_bfloat16 
   d = __float2bfloat16_rn(r1);
   l = __float2bfloat16_rn(r1 - __bfloat162float(d));
 }
+// 2^x (hardware approximation, relative error ~2^-22; results below 2^-126 flush
+// to zero, far below any probability that reaches the output).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {
   return (uint32_t)__bfloat16_as_ushort(a) | ((uint32_t)__bfloat16_as_ushort(b) << 16);
 }
 
 // grid: n_heads * nqb CTAs. offset = seq_k - n (keys before the chunk's first query).
+// scale2 = log2(e) / sqrt(hd): scores in base-2 units, p = 2^(s2 - m2).
 __global__ void __launch_bounds__(FA_THREADS, 1)
     k_attn_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
               const __grid_constant__ CUtensorMap tv, float *__restrict__ out, int n, int offset, int n_heads,
-              int group, int nqb, float scale, unsigned *err) {
+              int group, int nqb, float scale2, unsigned *err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = su32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -104,6 +127,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint8_t *gen = smem_raw + (base - raw);
   volatile uint32_t *tmem_slot = (volatile uint32_t *)(gen + OFF_BAR + 8 * N_BARS);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+  float *xchg = (float *)(gen + OFF_XCHG);  // [2 blocks][parts][128 rows] row maxima, then [parts][128] sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = nqb - 1 - (int)blockIdx.x / n_heads;  // heaviest blocks first
@@ -114,9 +138,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int nkb = (offset + q_last) / FA_BK + 1;  // key blocks this query block sees
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < N_BARS; i++) {  // the softmax threads all arrive on S-free, P-full and O-free
-      const bool rows = i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_OFREE || i == B_OFREE + 1;
-      bar_init(bar(i), rows ? FA_M : 1);
+    for (int i = 0; i < N_BARS; i++) {  // every softmax thread arrives on S-free, P-full and O-free
+      const bool rows = i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1 || i == B_OFREE ||
+                        i == B_OFREE + 1;
+      bar_init(bar(i), rows ? FA_SOFTMAX : 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -131,34 +156,50 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == FA_WARP_TMA) {
     // ---------------- TMA producer ----------------
     int issued = 0;
     if (lane == 0) {
       bar_expect_tx(bar(B_QFULL), 3 * Q_TERM);
       for (int t = 0; t < 3; t++) tma_load_3d(base + OFF_Q + t * Q_TERM, &tq, 0, q0, t * n_heads + h, bar(B_QFULL));
+      // keys of block j+2 load once S_j is done (the value copies run in their own
+      // warp, released by O_j): the key copy overlaps the softmax and P.V between
       for (int j = 0; j < nkb; j++) {
         const int b = j & 1;
-        if (j >= 2 && !bar_wait(bar(B_KVEMPTY + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
-        bar_expect_tx(bar(B_KVFULL + b), 3 * K_TERM + 3 * V_TERM);
+        if (j >= 2 && !bar_wait(bar(B_KEMPTY + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
+        bar_expect_tx(bar(B_KFULL + b), 3 * K_TERM);
         for (int t = 0; t < 3; t++)
-          tma_load_3d(base + OFF_K + (b * 3 + t) * K_TERM, &tk, 0, j * FA_BK, t * G + g, bar(B_KVFULL + b));
-        for (int t = 0; t < 3; t++)
-          tma_load_3d(base + OFF_V + (b * 3 + t) * V_TERM, &tv, j * FA_BK, 0, t * G + g, bar(B_KVFULL + b));
+          tma_load_3d(base + OFF_K + (b * 3 + t) * K_TERM, &tk, 0, j * FA_BK, t * G + g, bar(B_KFULL + b));
         issued = j + 1;
       }
       // drain: every started copy lands before the CTA exits
       bar_drain(bar(B_QFULL), 0u);
-      for (int j = std::max(0, issued - 2); j < issued; j++) bar_drain(bar(B_KVFULL + (j & 1)), (unsigned)(j >> 1) & 1u);
+      for (int j = std::max(0, issued - 2); j < issued; j++) bar_drain(bar(B_KFULL + (j & 1)), (unsigned)(j >> 1) & 1u);
     }
     __syncwarp();
-  } else if (warp == 5) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == FA_WARP_V) {
+    // ---------------- TMA producer: transposed values ----------------
     if (lane == 0) {
-      auto issue_s = [&](int i) -> bool {
+      int issued = 0;
+      for (int j = 0; j < nkb; j++) {
+        const int b = j & 1;
+        if (j >= 2 && !bar_wait(bar(B_VEMPTY + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
+        bar_expect_tx(bar(B_VFULL + b), 3 * V_TERM);
+        for (int t = 0; t < 3; t++)
+          tma_load_3d(base + OFF_V + (b * 3 + t) * V_TERM, &tv, j * FA_BK, 0, t * G + g, bar(B_VFULL + b));
+        issued = j + 1;
+      }
+      for (int j = std::max(0, issued - 2); j < issued; j++) bar_drain(bar(B_VFULL + (j & 1)), (unsigned)(j >> 1) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == FA_WARP_MMA) {
+    // ---------------- MMA issue: scores ----------------
+    if (lane == 0) {
+      bool ok = bar_wait(bar(B_QFULL), 0u, err, abort_flag);
+      for (int i = 0; ok && i < nkb; i++) {
         const int b = i & 1;
-        if (!bar_wait(bar(B_KVFULL + b), (unsigned)(i >> 1) & 1u, err, abort_flag)) return false;
-        if (i >= 2 && !bar_wait(bar(B_SFREE + b), (unsigned)((i >> 1) - 1) & 1u, err, abort_flag)) return false;
+        if (!bar_wait(bar(B_KFULL + b), (unsigned)(i >> 1) & 1u, err, abort_flag)) break;
+        if (i >= 2 && !bar_wait(bar(B_SFREE + b), (unsigned)((i >> 1) - 1) & 1u, err, abort_flag)) break;
         fence_after();
         const uint32_t d = tmem + TM_S + 64u * b;
         const uint32_t qa = base + OFF_Q, ka = base + OFF_K + b * 3 * K_TERM;
@@ -170,129 +211,177 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             mma_bf16(d, sw128_desc(a0 + 32u * kk), sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
         }
         mma_commit(bar(B_SFULL + b));
-        return true;
-      };
-      bool ok = bar_wait(bar(B_QFULL), 0u, err, abort_flag) && issue_s(0);
-      for (int j = 0; ok && j < nkb; j++) {
-        const int b = j & 1;
-        if (j + 1 < nkb && !issue_s(j + 1)) break;
-        if (!bar_wait(bar(B_PFULL), (unsigned)j & 1u, err, abort_flag)) break;
-        if (j >= 2 && !bar_wait(bar(B_OFREE + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
-        fence_after();
-        const uint32_t d = tmem + TM_O + 64u * b;
-        const uint32_t pa = base + OFF_P, va = base + OFF_V + b * 3 * V_TERM;
-#pragma unroll
-        for (int pr = 0; pr < 6; pr++) {
-          const uint32_t a0 = pa + kPairs[pr][0] * P_TERM, b0 = va + kPairs[pr][1] * V_TERM;
-#pragma unroll
-          for (int kk = 0; kk < FA_BK / 16; kk++)
-            mma_bf16(d, sw128_desc(a0 + 32u * kk), sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
-        }
-        mma_commit(bar(B_OFULL + b));
-        mma_commit(bar(B_KVEMPTY + b));
-        mma_commit(bar(B_PEMPTY));
+        mma_commit(bar(B_KEMPTY + b));
       }
       mma_commit(bar(B_FIN));
       bar_drain(bar(B_FIN), 0u);  // every MMA done before the columns are freed
     }
     __syncwarp();
-  } else {
-    // ---------------- softmax / output: thread = query row ----------------
-    const int r = threadIdx.x;  // 0..127 = tensor-memory lane
-    const int qpos = offset + q0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
-    float o[FA_HD];
+  } else if (warp == FA_WARP_PV) {
+    // ---------------- MMA issue: outputs (a second issuing thread) ----------------
+    if (lane == 0) {
+      for (int j = 0; j < nkb; j++) {
+        const int b = j & 1;
+        if (!bar_wait(bar(B_PFULL + b), (unsigned)(j >> 1) & 1u, err, abort_flag)) break;
+        if (j >= 2 && !bar_wait(bar(B_OFREE + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
+        if (!bar_wait(bar(B_VFULL + b), (unsigned)(j >> 1) & 1u, err, abort_flag)) break;
+        fence_after();
+        const uint32_t d = tmem + TM_O + 64u * b;
+        const uint32_t pa = tmem + TM_P + P_COLS * b, va = base + OFF_V + b * 3 * V_TERM;
 #pragma unroll
-    for (int d = 0; d < FA_HD; d++) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+        for (int pr = 0; pr < 6; pr++) {
+          const uint32_t a0 = pa + 32u * kPairs[pr][0], b0 = va + kPairs[pr][1] * V_TERM;
+#pragma unroll
+          for (int kk = 0; kk < FA_BK / 16; kk++)  // A = P from tensor memory: 16 keys = 8 columns
+            mma_bf16_ts(d, a0 + 8u * kk, sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
+        }
+        mma_commit(bar(B_OFULL + b));
+        mma_commit(bar(B_VEMPTY + b));
+        mma_commit(bar(B_PEMPTY + b));
+      }
+      mma_commit(bar(B_FIN2));
+      bar_drain(bar(B_FIN2), 0u);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax / output ----------------
+    // FA_PARTS threads per query row: warps w, w + 4, .. share tensor-memory lanes
+    // 32*(w%4) ..; part pt owns keys [KP*pt, KP*pt + KP) of each block and output
+    // dims [KP*pt, KP*pt + KP). Row maxima and sums are combined through shared
+    // memory at named barrier 1 + quarter.
+    constexpr int KP = FA_BK / FA_PARTS;  // keys (and output dims) per thread
+    const int quarter = warp & 3, pt = warp >> 2;
+    const int r = 32 * quarter + lane;  // query row = tensor-memory lane
+    const int qpos = offset + q0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+    const uint32_t col = (uint32_t)(KP * pt);
+    float o[KP];
+#pragma unroll
+    for (int d = 0; d < KP; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;  // m in base-2 units (scores * scale2)
     bool ok = true;
     auto wait_all = [&](uint32_t b, unsigned par) -> bool {  // lane 0 waits, the warp follows
       int v = 1;
       if (lane == 0) v = bar_wait(b, par, err, abort_flag);
       return __shfl_sync(0xffffffffu, v, 0) != 0;
     };
-    auto add_block = [&](int j) -> bool {  // o = o * alpha_prev + O_j
+    // Every wait is followed by a vote of the row group's warps, so they leave the
+    // loop together and never leave one of them at a barrier alone.
+    auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * FA_PARTS) : "memory"); };
+    auto group_and = [&](bool v) -> bool {
+      unsigned res;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.and.pred q, %2, %3, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(res)
+          : "r"((unsigned)v), "r"(1 + quarter), "r"(32 * FA_PARTS)
+          : "memory");
+      return res != 0;
+    };
+    auto add_block = [&](int j) -> bool {  // o = o * alpha_prev + O_j (this part's dims)
       const int b = j & 1;
-      if (!wait_all(bar(B_OFULL + b), (unsigned)(j >> 1) & 1u)) return false;
+      if (!group_and(wait_all(bar(B_OFULL + b), (unsigned)(j >> 1) & 1u))) return false;
       fence_after();
+      uint32_t v[KP / 16][16];
 #pragma unroll
-      for (int c = 0; c < FA_HD / 16; c++) {
-        uint32_t v[16];
-        tmem_ld16(lane_base + TM_O + 64u * b + 16u * c, v);
-        tmem_wait_ld(v);
+      for (int c = 0; c < KP / 16; c++) tmem_ld16(lane_base + TM_O + 64u * b + col + 16u * c, v[c]);
+      tmem_wait_ld(v[0]);
 #pragma unroll
-        for (int i = 0; i < 16; i++) o[16 * c + i] = fmaf(o[16 * c + i], alpha_prev, __uint_as_float(v[i]));
-      }
+      for (int c = 1; c < KP / 16; c++) tmem_tie(v[c]);
       fence_before();
       bar_arrive(bar(B_OFREE + b));
+#pragma unroll
+      for (int i = 0; i < KP; i++) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i >> 4][i & 15]));
       return true;
     };
+    // keys below the query block's first position need no mask
+    const int unmasked_blocks = (offset + q0 + 1) / FA_BK;
     for (int j = 0; j < nkb; j++) {
       const int b = j & 1;
-      if (!(ok = wait_all(bar(B_SFULL + b), (unsigned)(j >> 1) & 1u))) break;
-      fence_after();
-      uint32_t s[4][16];
-#pragma unroll
-      for (int c = 0; c < 4; c++) tmem_ld16(lane_base + TM_S + 64u * b + 16u * c, s[c]);
-      tmem_wait_ld(s[0]);
-      tmem_tie(s[1]);
-      tmem_tie(s[2]);
-      tmem_tie(s[3]);
-      fence_before();
-      bar_arrive(bar(B_SFREE + b));
-      // scores, causal mask, online softmax
-      const int k0 = j * FA_BK;
-      float sc[FA_BK];
+      const bool got = wait_all(bar(B_SFULL + b), (unsigned)(j >> 1) & 1u);
+      float sc[KP];  // raw scores q.k (masked: -inf)
       float mx = -INFINITY;
+      if (got) {
+        fence_after();
+        uint32_t sv[KP / 16][16];
 #pragma unroll
-      for (int c = 0; c < FA_BK; c++) {
-        const float v = (k0 + c <= qpos) ? __uint_as_float(s[c >> 4][c & 15]) * scale : -INFINITY;
-        sc[c] = v;
-        mx = fmaxf(mx, v);
-      }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = expf(m - m_new);  // 0 on the first block (m = -inf)
-      float sum = 0.f;
+        for (int c = 0; c < KP / 16; c++) tmem_ld16(lane_base + TM_S + 64u * b + col + 16u * c, sv[c]);
+        tmem_wait_ld(sv[0]);
 #pragma unroll
-      for (int c = 0; c < FA_BK; c++) {
-        sc[c] = expf(sc[c] - m_new);  // 0 for masked keys
-        sum += sc[c];
+        for (int c = 1; c < KP / 16; c++) tmem_tie(sv[c]);
+        fence_before();
+        bar_arrive(bar(B_SFREE + b));
+        if (j < unmasked_blocks) {
+#pragma unroll
+          for (int c = 0; c < KP; c++) sc[c] = __uint_as_float(sv[c >> 4][c & 15]);
+        } else {
+          const int k0 = j * FA_BK + KP * pt;
+#pragma unroll
+          for (int c = 0; c < KP; c++) sc[c] = (k0 + c <= qpos) ? __uint_as_float(sv[c >> 4][c & 15]) : -INFINITY;
+        }
+        float m4[4] = {sc[0], sc[1], sc[2], sc[3]};  // four independent chains
+#pragma unroll
+        for (int c = 4; c < KP; c++) m4[c & 3] = fmaxf(m4[c & 3], sc[c]);
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale2;  // scale2 > 0: max commutes
+        xchg[(b * FA_PARTS + pt) * FA_M + r] = mx;
       }
+      // the vote doubles as the exchange barrier of the row maxima
+      if (!(ok = group_and(got))) break;
+#pragma unroll
+      for (int q = 1; q < FA_PARTS; q++) mx = fmaxf(mx, xchg[(b * FA_PARTS + ((pt + q) % FA_PARTS)) * FA_M + r]);
+      const float m_new = fmaxf(m, mx);  // finite: key 0 is visible to every row in block 0
+      const float alpha = ex2(m - m_new);  // 0 on the first block (m = -inf)
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < KP; c++) {
+        sc[c] = ex2(fmaf(sc[c], scale2, -m_new));  // 2^(s*scale2 - m); 0 for masked keys
+        s4[c & 3] += sc[c];
+      }
+      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = fmaf(l, alpha, sum);
       m = m_new;
-      // P_j: three bf16 terms, 128-byte swizzled rows (chunk c of row r at c ^ (r % 8))
-      if (j >= 1 && !(ok = wait_all(bar(B_PEMPTY), (unsigned)(j - 1) & 1u))) break;
-      const uint32_t prow = base + OFF_P + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+      // P_j, this part's 16 keys: three bf16 terms into tensor-memory buffer b
+      if (j >= 2 && !(ok = group_and(wait_all(bar(B_PEMPTY + b), (unsigned)((j >> 1) - 1) & 1u)))) break;
+      {
+        uint32_t w[3][KP / 2];
 #pragma unroll
-      for (int c8 = 0; c8 < FA_BK / 8; c8++) {
-        uint32_t w[3][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          __nv_bfloat16 h0, d0, l0, h1, d1, l1;
-          split3(sc[8 * c8 + 2 * i], h0, d0, l0);
-          split3(sc[8 * c8 + 2 * i + 1], h1, d1, l1);
-          w[0][i] = pack2(h0, h1);
-          w[1][i] = pack2(d0, d1);
-          w[2][i] = pack2(l0, l1);
+        for (int i = 0; i < KP / 2; i++) {
+          const float p0 = sc[2 * i], p1 = sc[2 * i + 1];
+          const __nv_bfloat162 t0 = __floats2bfloat162_rn(p0, p1);
+          const float2 f0 = __bfloat1622float2(t0);
+          const float r0 = p0 - f0.x, r1 = p1 - f0.y;
+          const __nv_bfloat162 t1 = __floats2bfloat162_rn(r0, r1);
+          const float2 f1 = __bfloat1622float2(t1);
+          const __nv_bfloat162 t2 = __floats2bfloat162_rn(r0 - f1.x, r1 - f1.y);
+          w[0][i] = *reinterpret_cast<const uint32_t *>(&t0);
+          w[1][i] = *reinterpret_cast<const uint32_t *>(&t1);
+          w[2][i] = *reinterpret_cast<const uint32_t *>(&t2);
         }
-        const uint32_t off = (uint32_t)((c8 ^ (r & 7)) << 4);
+        const uint32_t pcol = lane_base + TM_P + P_COLS * b + (uint32_t)(KP / 2 * pt);
 #pragma unroll
-        for (int t = 0; t < 3; t++)
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + t * P_TERM + off), "r"(w[t][0]),
-                       "r"(w[t][1]), "r"(w[t][2]), "r"(w[t][3])
-                       : "memory");
+        for (int t = 0; t < 3; t++) tmem_st8(pcol + 32u * t, w[t]);
+        tmem_wait_st();
       }
-      fence_proxy_async();
-      bar_arrive(bar(B_PFULL));
+      fence_before();
+      bar_arrive(bar(B_PFULL + b));
       if (j >= 1 && !(ok = add_block(j - 1))) break;
       alpha_prev = alpha;
     }
     if (ok) ok = add_block(nkb - 1);
+    // row sum = the parts' partial sums (same running maximum)
+    if (ok) {
+      xchg[(2 * FA_PARTS + pt) * FA_M + r] = l;
+      group_sync();
+#pragma unroll
+      for (int q = 1; q < FA_PARTS; q++) l += xchg[(2 * FA_PARTS + ((pt + q) % FA_PARTS)) * FA_M + r];
+    }
     if (ok && !*abort_flag && q0 + r < n) {
       const float inv = 1.0f / l;
-      float4 *dst = reinterpret_cast<float4 *>(out + ((size_t)(q0 + r) * n_heads + h) * FA_HD);
+      float4 *dst = reinterpret_cast<float4 *>(out + ((size_t)(q0 + r) * n_heads + h) * FA_HD + KP * pt);
 #pragma unroll
-      for (int d = 0; d < FA_HD; d += 4)
+      for (int d = 0; d < KP; d += 4)
         dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
     }
   }
@@ -413,8 +502,9 @@ cudaError_t launch_attn_tc(cudaStream_t s, const float *q, const float *k, const
   e = cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
   if (e != cudaSuccess) return e;
   const int nqb = (n + FA_M - 1) / FA_M;
-  const float scale = 1.0f / sqrtf((float)head_dim);  // attention.rs:37
-  k_attn_tc<<<H * nqb, FA_THREADS, FA_SMEM, s>>>(tq, tk, tv, out, n, seq_k - n, H, H / G, nqb, scale, tc_err_ptr());
+  // scores * 1/sqrt(hd) (attention.rs:37), in base-2 units for exp2f
+  const float scale2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
+  k_attn_tc<<<H * nqb, FA_THREADS, FA_SMEM, s>>>(tq, tk, tv, out, n, seq_k - n, H, H / G, nqb, scale2, tc_err_ptr());
   return cudaGetLastError();
 }
 

@@ -34,13 +34,26 @@ __device__ __forceinline__ bool bar_try_wait(uint32_t b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread until the phase completes or about
+// `hint_ns` nanoseconds pass (no spinning on the issue slots meanwhile).
+__device__ __forceinline__ bool bar_try_wait_sleep(uint32_t b, unsigned parity, unsigned hint_ns) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(b), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the completion of the phase with this parity. Gives up (false)
 // after WAIT_LIMIT clocks, recording the failure in *err and in the CTA's abort
 // flag, or as soon as another thread of the CTA has set the abort flag.
 __device__ __forceinline__ bool bar_wait(uint32_t b, unsigned parity, unsigned *err, volatile int *abort_flag) {
   if (bar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
-  while (!bar_try_wait(b, parity)) {
+  while (!bar_try_wait_sleep(b, parity, 20000u)) {
     if (*abort_flag) return false;
     if (clock64() - t0 > WAIT_LIMIT) {
       atomicExch(err, 1u);
@@ -101,6 +114,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (16-bit, K-major) read from tensor memory,
+// row i in lane i, two consecutive K elements per 32-bit column.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
 // Arrive on the mbarrier once every tcgen05 operation this thread issued has completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -128,6 +152,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// 8 consecutive 32-bit columns of this thread's tensor-memory lane; complete after
+// tmem_wait_st().
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Waits for this thread's outstanding tensor-memory loads; r is tied to the wait so
 // no use of the loaded registers moves above it (tmem_tie ties further arrays).
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
