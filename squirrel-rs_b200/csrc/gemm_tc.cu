@@ -15,9 +15,11 @@
 //   warp 0   TMA producer: per 64-element K block, the 128 x 64 weight tile and the
 //            three BN x 64 activation-term tiles, 128-byte swizzled, into a ring of
 //            shared-memory stages completing on an mbarrier;
-//   warp 1   one thread issues tcgen05.mma (kind::f16, bf16 inputs, f32 accumulator
-//            in tensor memory, M = 128 weight rows, N = BN rows of X), three terms x
-//            four K steps of 16 per stage, then tcgen05.commit frees the stage;
+//   warps 1-3  one thread each issues tcgen05.mma (kind::f16, bf16 inputs, f32
+//            accumulator in tensor memory, M = 128 weight rows, N = BN rows of X) for
+//            one activation term, four K steps of 16 per stage, then tcgen05.commit;
+//            the stage is free once all three have committed (the accumulator is
+//            zeroed first, so the three threads' MMAs may run in any order);
 //   all      epilogue: tcgen05.ld of the accumulator (lane = weight row, column =
 //            activation row), coalesced f32 stores of Y (or of a split-K partial).
 // K is split across gridDim.z when the tiles alone do not cover the SMs; partials
@@ -91,9 +93,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
       bar_init(full(s), 1);
-      bar_init(empty(s), 1);
+      bar_init(empty(s), TC_TERMS);  // one commit per issuing thread
     }
-    bar_init(done, 1);
+    bar_init(done, TC_TERMS);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&tw);
@@ -105,6 +107,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
+  {  // zero the accumulator: every MMA then accumulates, so three threads can issue
+    const uint32_t zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < BN; c += 8) tmem_st8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, zero);
+    tmem_wait_st();
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
 
   int issued = 0;  // producer: K blocks whose copies were started
   if (warp == 0) {
@@ -127,7 +138,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!ok) break;
       issued = i + 1;
     }
-  } else if (warp == 1) {
+  } else {
+    // warps 1-3: one issuing thread per activation term (term t = warp - 1), all
+    // accumulating into the zeroed accumulator
+    const int t = warp - 1;
     for (int i = 0; i < nk; i++) {
       const int s = i % C::STAGES;
       int ok = 1;
@@ -136,21 +150,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (ok) {
           fence_after();
           const uint32_t a = base + (uint32_t)s * C::STAGE;
+          const uint32_t b = a + C::A_BYTES + (uint32_t)t * C::B_BYTES;
 #pragma unroll
-          for (int t = 0; t < TC_TERMS; t++) {
-            const uint32_t b = a + C::A_BYTES + (uint32_t)t * C::B_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < TC_KB / 16; kk++)
-              mma_bf16(tmem, sw128_desc(a + 32u * kk), sw128_desc(b + 32u * kk), C::IDESC,
-                       (i | t | kk) != 0 ? 1u : 0u);
-          }
-          mma_commit(empty(s));  // the stage is free once these MMAs have read it
+          for (int kk = 0; kk < TC_KB / 16; kk++)
+            mma_bf16(tmem, sw128_desc(a + 32u * kk), sw128_desc(b + 32u * kk), C::IDESC, 1u);
+          mma_commit(empty(s));  // the stage is free once all three threads' MMAs have read it
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
     }
-    if (lane == 0) mma_commit(done);  // arrives when every MMA above has completed
+    if (lane == 0) mma_commit(done);  // arrives when every MMA of this thread has completed
     __syncwarp();
   }
 
@@ -182,7 +192,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     for (int i = std::max(0, issued - C::STAGES); i < issued; i++) bar_drain(full(i % C::STAGES), (unsigned)(i / C::STAGES) & 1u);
   }
-  if (warp == 1 && lane == 0) bar_drain(done, 0u);
+  if (warp >= 1 && lane == 0) bar_drain(done, 0u);
   fence_before();
   __syncthreads();
   if (warp == 0) {
