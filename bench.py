@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--cpu-decode-steps", type=int, default=4)
     ap.add_argument("--prefill", default="512,2048,8192",
                     help="BF16 1B prefill prompt lengths reported beside the decode metric (empty: skip)")
+    ap.add_argument("--prefill-type", default="bf16", choices=["bf16", "q8_0", "q4_0"],
+                    help="weight type of the prefill measurement (config 3 is bf16)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the BF16 prefill measurement (one GPU; for profiling the prefill kernels)")
     return ap.parse_args()
@@ -216,12 +218,12 @@ def tensor_peak():
     return 1590.0, "fallback"
 
 
-def run_prefill(lib, G, lengths, device):
+def run_prefill(lib, G, lengths, device, wtype="bf16"):
     """BF16 prefill throughput (the tensor-core GEMM and attention path): one forward
     of an n-token prompt per length, device time from CUDA events on the context's
     stream (the forward copies the ids in and the argmax out itself), best of two."""
     import torch
-    model = lib.Model(G.ensure_gguf("1b", "bf16"), device=device)
+    model = lib.Model(G.ensure_gguf("1b", wtype), device=device)
     cfg = model.config
     out = {}
     peak, kind = tensor_peak()
@@ -252,8 +254,8 @@ def run_prefill(lib, G, lengths, device):
                                     "mma_tflops_issued": mma / (ms / 1e3) / 1e12}}
         ctx.close()
     model.close()
-    return {"workload": "1b-bf16 prefill (config 3)", "dtype": "f32 activations, bf16 weights; bf16 MMA terms",
-            "lengths": out}
+    return {"workload": f"1b-{wtype} prefill" + (" (config 3)" if wtype == "bf16" else ""),
+            "dtype": f"f32 activations, {wtype} weights; bf16 MMA terms", "lengths": out}
 
 
 def run_ours(args):
@@ -398,7 +400,8 @@ def main():
     if args.prefill_only:
         from sqb200 import gguf_synth as G
         from sqb200 import lib
-        print(json.dumps(run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], 0)), flush=True)
+        print(json.dumps(run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], 0, args.prefill_type)),
+              flush=True)
         return 0
     return run_ours(args)
 

@@ -13,24 +13,24 @@
 // [3][G][64][seq_k padded to 8] (bf16), in a caller-provided workspace.
 //
 // Kernel: one CTA per (128-query block, q head); the heaviest (last) query blocks
-// start first. 20 warps:
-//   warps 16, 18  TMA: the query block's three term tiles once, then per 64-key
-//            block the key (warp 16) and the transposed-value (warp 18) term tiles
-//            into separate double buffers (a key buffer is released when its S is
-//            done, a value buffer when its O is);
-//   warps 17, 19  one thread each issues MMAs: S_j = Q K_j^T (M = 128 queries,
-//            N = 64 keys) into one of two tensor-memory score buffers (warp 17), and,
-//            once the softmax warps have written P_j, O_j = P_j V_j (N = 64 dims,
-//            A = P read from tensor memory) into one of two output buffers (warp 19);
-//            the score MMAs of later blocks overlap the softmax of earlier ones;
-//   warps 0-15  four threads per query row (warps w, w + 4, w + 8, w + 12 share
-//            tensor-memory lanes), each with 16 keys and 16 output dims: scores
-//            of block j from tensor memory, causal mask near the diagonal, online
-//            softmax in base 2 (running max combined through shared memory, ex2),
-//            P_j split into terms and stored into one of two tensor-memory P
-//            buffers (so P_{j+1} is written while O_j is computed), then the
-//            f32 running output o = o * 2^(m_old - m_new) + O_j in registers (one
-//            block behind).
+// start first. 14 warps:
+//   warps 8, 10  TMA: the query block's three term tiles once, then per 64-key block
+//            the key (warp 8) and transposed-value (warp 10) term tiles into separate
+//            double buffers (a key buffer is released when its S is done, a value
+//            buffer when its O is);
+//   warps 9, 12  MMA issue for S_j = Q K_j^T (M = 128 queries, N = 64 keys), three of
+//            the six term pairs each, into one of two tensor-memory score buffers;
+//   warps 11, 13  MMA issue for O_j = P_j V_j (N = 64 dims, A = P read from tensor
+//            memory), three term pairs each, into one of two output buffers. The
+//            softmax threads zero each score / output buffer after reading it, so
+//            every MMA accumulates and the issuing threads need no mutual order;
+//   warps 0-7  two threads per query row (warps w and w + 4 share tensor-memory
+//            lanes), each with 32 keys and 32 output dims: scores of block j from
+//            tensor memory, causal mask near the diagonal, online softmax in base 2
+//            (running max combined through shared memory, ex2), P_j split into terms
+//            and stored into one of two tensor-memory P buffers (so P_{j+1} is
+//            written while O_j is computed), then the f32 running output
+//            o = o * 2^(m_old - m_new) + O_j in registers (one block behind).
 // Every wait is bounded; on expiry the CTA records the error, stops, drains its
 // copies and MMAs, frees its tensor memory and returns.
 #include <cuda.h>
@@ -53,11 +53,11 @@ using namespace tc;
 constexpr int FA_M = 128;   // query rows per CTA
 constexpr int FA_BK = 64;   // keys per block
 constexpr int FA_HD = 64;   // head dim
-constexpr int FA_PARTS = 4;                 // softmax threads per query row
+constexpr int FA_PARTS = 2;                 // softmax threads per query row
 constexpr int FA_SOFTMAX = 128 * FA_PARTS;  // softmax threads
 constexpr int FA_WARP_TMA = FA_SOFTMAX / 32, FA_WARP_MMA = FA_WARP_TMA + 1, FA_WARP_V = FA_WARP_TMA + 2,
-              FA_WARP_PV = FA_WARP_TMA + 3;
-constexpr int FA_THREADS = FA_SOFTMAX + 128;
+              FA_WARP_PV = FA_WARP_TMA + 3, FA_WARP_S2 = FA_WARP_TMA + 4, FA_WARP_PV2 = FA_WARP_TMA + 5;
+constexpr int FA_THREADS = FA_SOFTMAX + 192;
 
 constexpr int Q_TERM = FA_M * FA_HD * 2;   // 16 KB
 constexpr int K_TERM = FA_BK * FA_HD * 2;  // 8 KB
@@ -78,19 +78,20 @@ enum : int {
   B_KEMPTY = 3,   // [2] S of that block done: the key buffer is free
   B_VFULL = 5,    // [2]
   B_VEMPTY = 7,   // [2] O of that block done: the value buffer is free
-  B_SFULL = 9,    // [2]
-  B_SFREE = 11,   // [2]
+  B_SFULL = 9,    // [2] both score accumulators of a block done
+  B_SPFREE = 11,  // [2] O of the block done: its score / P buffer is free
   B_PFULL = 13,   // [2] P of a block written to tensor memory
-  B_PEMPTY = 15,  // [2] O of that block done: the P buffer is free
-  B_OFULL = 17,   // [2]
-  B_OFREE = 19,   // [2]
-  B_FIN = 21,     // the score issuer's MMAs all done
-  B_FIN2 = 22,    // the output issuer's MMAs all done
-  N_BARS = 23
+  B_OFULL = 15,   // [2] both output accumulators of a block done
+  B_OFREE = 17,   // [2] the softmax threads have read them
+  B_FIN = 19,     // the score issuers' MMAs all done
+  B_FIN2 = 20,    // the output issuers' MMAs all done
+  N_BARS = 21
 };
-// tensor-memory columns: S[2] at 0 / 64, O[2] at 128 / 192 (f32), P[2] at 256 / 352:
-// three bf16 terms of 32 columns each (two keys per 32-bit column, lane = query row)
-constexpr uint32_t TM_S = 0, TM_O = 128, TM_P = 256, P_COLS = 96, TM_COLS = 512;
+// tensor-memory columns. SP[2] at 0 / 128: the two score accumulators (issuer A at
+// +0, issuer B at +64, f32, column = key); once read, the same columns take P as
+// three bf16 terms of 32 columns (two keys per 32-bit column). O[2] at 256 / 384:
+// the two output accumulators (+0, +64; column = head dim). Lane = query row.
+constexpr uint32_t TM_SP = 0, TM_O = 256, TM_COLS = 512;
 constexpr uint32_t IDESC = idesc_bf16(FA_M, 64);
 
 // term pairs (a, b) with a + b <= 2: the products kept
@@ -138,10 +139,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int nkb = (offset + q_last) / FA_BK + 1;  // key blocks this query block sees
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < N_BARS; i++) {  // every softmax thread arrives on S-free, P-full and O-free
-      const bool rows = i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1 || i == B_OFREE ||
-                        i == B_OFREE + 1;
-      bar_init(bar(i), rows ? FA_SOFTMAX : 1);
+    for (int i = 0; i < N_BARS; i++) {  // every softmax thread arrives on P-full and O-free
+      const bool rows = i == B_PFULL || i == B_PFULL + 1 || i == B_OFREE || i == B_OFREE + 1;
+      const bool by_issuers = !rows && i != B_QFULL && !(i >= B_KFULL && i < B_KFULL + 2) &&
+                              !(i >= B_VFULL && i < B_VFULL + 2);  // committed by two issuing threads
+      bar_init(bar(i), rows ? FA_SOFTMAX : (by_issuers ? 2 : 1));
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
+  constexpr int KP = FA_BK / FA_PARTS;  // keys (and output dims) per softmax thread
 
   if (warp == FA_WARP_TMA) {
     // ---------------- TMA producer ----------------
@@ -192,23 +195,25 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       for (int j = std::max(0, issued - 2); j < issued; j++) bar_drain(bar(B_VFULL + (j & 1)), (unsigned)(j >> 1) & 1u);
     }
     __syncwarp();
-  } else if (warp == FA_WARP_MMA) {
-    // ---------------- MMA issue: scores ----------------
+  } else if (warp == FA_WARP_MMA || warp == FA_WARP_S2) {
+    // ---------------- MMA issue: scores (two threads, three term pairs each, own accumulators) ----------------
+    const int p0 = warp == FA_WARP_MMA ? 0 : 3;
     if (lane == 0) {
       bool ok = bar_wait(bar(B_QFULL), 0u, err, abort_flag);
       for (int i = 0; ok && i < nkb; i++) {
         const int b = i & 1;
         if (!bar_wait(bar(B_KFULL + b), (unsigned)(i >> 1) & 1u, err, abort_flag)) break;
-        if (i >= 2 && !bar_wait(bar(B_SFREE + b), (unsigned)((i >> 1) - 1) & 1u, err, abort_flag)) break;
+        if (i >= 2 && !bar_wait(bar(B_SPFREE + b), (unsigned)((i >> 1) - 1) & 1u, err, abort_flag)) break;
         fence_after();
-        const uint32_t d = tmem + TM_S + 64u * b;
+        const uint32_t d = tmem + TM_SP + 128u * b + (p0 ? 64u : 0u);
         const uint32_t qa = base + OFF_Q, ka = base + OFF_K + b * 3 * K_TERM;
 #pragma unroll
-        for (int pr = 0; pr < 6; pr++) {
+        for (int q = 0; q < 3; q++) {
+          const int pr = p0 + q;
           const uint32_t a0 = qa + kPairs[pr][0] * Q_TERM, b0 = ka + kPairs[pr][1] * K_TERM;
 #pragma unroll
           for (int kk = 0; kk < FA_HD / 16; kk++)
-            mma_bf16(d, sw128_desc(a0 + 32u * kk), sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
+            mma_bf16(d, sw128_desc(a0 + 32u * kk), sw128_desc(b0 + 32u * kk), IDESC, (q | kk) != 0 ? 1u : 0u);
         }
         mma_commit(bar(B_SFULL + b));
         mma_commit(bar(B_KEMPTY + b));
@@ -217,8 +222,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       bar_drain(bar(B_FIN), 0u);  // every MMA done before the columns are freed
     }
     __syncwarp();
-  } else if (warp == FA_WARP_PV) {
-    // ---------------- MMA issue: outputs (a second issuing thread) ----------------
+  } else if (warp == FA_WARP_PV || warp == FA_WARP_PV2) {
+    // ---------------- MMA issue: outputs (two threads, three term pairs each, own accumulators) ----------------
+    const int p0 = warp == FA_WARP_PV ? 0 : 3;
     if (lane == 0) {
       for (int j = 0; j < nkb; j++) {
         const int b = j & 1;
@@ -226,18 +232,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (j >= 2 && !bar_wait(bar(B_OFREE + b), (unsigned)((j >> 1) - 1) & 1u, err, abort_flag)) break;
         if (!bar_wait(bar(B_VFULL + b), (unsigned)(j >> 1) & 1u, err, abort_flag)) break;
         fence_after();
-        const uint32_t d = tmem + TM_O + 64u * b;
-        const uint32_t pa = tmem + TM_P + P_COLS * b, va = base + OFF_V + b * 3 * V_TERM;
+        const uint32_t d = tmem + TM_O + 128u * b + (p0 ? 64u : 0u);
+        const uint32_t pa = tmem + TM_SP + 128u * b, va = base + OFF_V + b * 3 * V_TERM;
 #pragma unroll
-        for (int pr = 0; pr < 6; pr++) {
+        for (int q = 0; q < 3; q++) {
+          const int pr = p0 + q;
           const uint32_t a0 = pa + 32u * kPairs[pr][0], b0 = va + kPairs[pr][1] * V_TERM;
 #pragma unroll
           for (int kk = 0; kk < FA_BK / 16; kk++)  // A = P from tensor memory: 16 keys = 8 columns
-            mma_bf16_ts(d, a0 + 8u * kk, sw128_desc(b0 + 32u * kk), IDESC, (pr | kk) != 0 ? 1u : 0u);
+            mma_bf16_ts(d, a0 + 8u * kk, sw128_desc(b0 + 32u * kk), IDESC, (q | kk) != 0 ? 1u : 0u);
         }
         mma_commit(bar(B_OFULL + b));
         mma_commit(bar(B_VEMPTY + b));
-        mma_commit(bar(B_PEMPTY + b));
+        mma_commit(bar(B_SPFREE + b));
       }
       mma_commit(bar(B_FIN2));
       bar_drain(bar(B_FIN2), 0u);
@@ -249,7 +256,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     // 32*(w%4) ..; part pt owns keys [KP*pt, KP*pt + KP) of each block and output
     // dims [KP*pt, KP*pt + KP). Row maxima and sums are combined through shared
     // memory at named barrier 1 + quarter.
-    constexpr int KP = FA_BK / FA_PARTS;  // keys (and output dims) per thread
     const int quarter = warp & 3, pt = warp >> 2;
     const int r = 32 * quarter + lane;  // query row = tensor-memory lane
     const int qpos = offset + q0 + r;
@@ -284,16 +290,24 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const int b = j & 1;
       if (!group_and(wait_all(bar(B_OFULL + b), (unsigned)(j >> 1) & 1u))) return false;
       fence_after();
-      uint32_t v[KP / 16][16];
+      uint32_t va[KP / 16][16], vb[KP / 16][16];
+      const uint32_t oa = lane_base + TM_O + 128u * b + col;
 #pragma unroll
-      for (int c = 0; c < KP / 16; c++) tmem_ld16(lane_base + TM_O + 64u * b + col + 16u * c, v[c]);
-      tmem_wait_ld(v[0]);
+      for (int c = 0; c < KP / 16; c++) {
+        tmem_ld16(oa + 16u * c, va[c]);
+        tmem_ld16(oa + 64u + 16u * c, vb[c]);
+      }
+      tmem_wait_ld(va[0]);
 #pragma unroll
-      for (int c = 1; c < KP / 16; c++) tmem_tie(v[c]);
+      for (int c = 0; c < KP / 16; c++) {
+        if (c) tmem_tie(va[c]);
+        tmem_tie(vb[c]);
+      }
       fence_before();
       bar_arrive(bar(B_OFREE + b));
 #pragma unroll
-      for (int i = 0; i < KP; i++) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i >> 4][i & 15]));
+      for (int i = 0; i < KP; i++)  // the two accumulators in a fixed order: deterministic
+        o[i] = fmaf(o[i], alpha_prev, __uint_as_float(va[i >> 4][i & 15]) + __uint_as_float(vb[i >> 4][i & 15]));
       return true;
     };
     // keys below the query block's first position need no mask
@@ -305,14 +319,23 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       float mx = -INFINITY;
       if (got) {
         fence_after();
-        uint32_t sv[KP / 16][16];
+        uint32_t sv[KP / 16][16], sw[KP / 16][16];
+        const uint32_t sa = lane_base + TM_SP + 128u * b + col;
 #pragma unroll
-        for (int c = 0; c < KP / 16; c++) tmem_ld16(lane_base + TM_S + 64u * b + col + 16u * c, sv[c]);
+        for (int c = 0; c < KP / 16; c++) {
+          tmem_ld16(sa + 16u * c, sv[c]);
+          tmem_ld16(sa + 64u + 16u * c, sw[c]);
+        }
         tmem_wait_ld(sv[0]);
 #pragma unroll
-        for (int c = 1; c < KP / 16; c++) tmem_tie(sv[c]);
-        fence_before();
-        bar_arrive(bar(B_SFREE + b));
+        for (int c = 0; c < KP / 16; c++) {
+          if (c) tmem_tie(sv[c]);
+          tmem_tie(sw[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < KP / 16; c++)  // S = accumulator A + accumulator B, fixed order
+#pragma unroll
+          for (int e = 0; e < 16; e++) sv[c][e] = __float_as_uint(__uint_as_float(sv[c][e]) + __uint_as_float(sw[c][e]));
         if (j < unmasked_blocks) {
 #pragma unroll
           for (int c = 0; c < KP; c++) sc[c] = __uint_as_float(sv[c >> 4][c & 15]);
@@ -327,8 +350,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale2;  // scale2 > 0: max commutes
         xchg[(b * FA_PARTS + pt) * FA_M + r] = mx;
       }
-      // the vote doubles as the exchange barrier of the row maxima
-      if (!(ok = group_and(got))) break;
+      // the vote doubles as the exchange barrier of the row maxima, and orders every
+      // thread's score loads before any thread's P stores into the same columns
+      fence_before();
+      ok = group_and(got);
+      fence_after();
+      if (!ok) break;
 #pragma unroll
       for (int q = 1; q < FA_PARTS; q++) mx = fmaxf(mx, xchg[(b * FA_PARTS + ((pt + q) % FA_PARTS)) * FA_M + r]);
       const float m_new = fmaxf(m, mx);  // finite: key 0 is visible to every row in block 0
@@ -342,8 +369,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = fmaf(l, alpha, sum);
       m = m_new;
-      // P_j, this part's 16 keys: three bf16 terms into tensor-memory buffer b
-      if (j >= 2 && !(ok = group_and(wait_all(bar(B_PEMPTY + b), (unsigned)((j >> 1) - 1) & 1u)))) break;
+      // P_j, this part's keys: three bf16 terms into the columns that held S_j (every
+      // thread of the row has read its scores: the vote above is a barrier)
       {
         uint32_t w[3][KP / 2];
 #pragma unroll
@@ -359,9 +386,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           w[1][i] = *reinterpret_cast<const uint32_t *>(&t1);
           w[2][i] = *reinterpret_cast<const uint32_t *>(&t2);
         }
-        const uint32_t pcol = lane_base + TM_P + P_COLS * b + (uint32_t)(KP / 2 * pt);
+        const uint32_t pcol = lane_base + TM_SP + 128u * b + (uint32_t)(KP / 2 * pt);
 #pragma unroll
-        for (int t = 0; t < 3; t++) tmem_st8(pcol + 32u * t, w[t]);
+        for (int t = 0; t < 3; t++)
+#pragma unroll
+          for (int h8 = 0; h8 < KP / 16; h8++) tmem_st8(pcol + 32u * t + 8u * h8, &w[t][8 * h8]);
         tmem_wait_st();
       }
       fence_before();

@@ -17,11 +17,12 @@
 //            shared-memory stages completing on an mbarrier;
 //   warps 1-3  one thread each issues tcgen05.mma (kind::f16, bf16 inputs, f32
 //            accumulator in tensor memory, M = 128 weight rows, N = BN rows of X) for
-//            one activation term, four K steps of 16 per stage, then tcgen05.commit;
-//            the stage is free once all three have committed (the accumulator is
-//            zeroed first, so the three threads' MMAs may run in any order);
-//   all      epilogue: tcgen05.ld of the accumulator (lane = weight row, column =
-//            activation row), coalesced f32 stores of Y (or of a split-K partial).
+//            one activation term into that term's own accumulator, four K steps of
+//            16 per stage, then tcgen05.commit; the stage is free once all three
+//            have committed;
+//   all      epilogue: tcgen05.ld of the three accumulators (lane = weight row,
+//            column = activation row), summed in a fixed order (deterministic),
+//            coalesced f32 stores of Y (or of a split-K partial).
 // K is split across gridDim.z when the tiles alone do not cover the SMs; partials
 // are summed in split order by k_split_sum (deterministic).
 // Every mbarrier wait is bounded; on expiry the CTA records an error, drains its
@@ -61,7 +62,8 @@ struct TcCfg {
   static constexpr int STAGES = BN >= 256 ? 2 : (BN >= 128 ? 3 : 5);
   static constexpr int BAR_OFF = STAGES * STAGE;       // mbarriers after the stages
   static constexpr int SMEM = 1024 + BAR_OFF + 128;    // + alignment slack
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;  // f32 accumulator: one column per activation row
+  // one f32 accumulator per activation term (one column per activation row each)
+  static constexpr int TMEM_COLS = TC_TERMS * BN <= 32 ? 32 : (TC_TERMS * BN <= 64 ? 64 : (TC_TERMS * BN <= 128 ? 128 : (TC_TERMS * BN <= 256 ? 256 : 512)));
   static constexpr uint32_t IDESC = idesc_bf16(TC_M, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N for M = 128");
   static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "tiles keep 1024-byte swizzle alignment");
@@ -107,15 +109,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-  {  // zero the accumulator: every MMA then accumulates, so three threads can issue
-    const uint32_t zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-    for (int c = 0; c < BN; c += 8) tmem_st8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, zero);
-    tmem_wait_st();
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
 
   int issued = 0;  // producer: K blocks whose copies were started
   if (warp == 0) {
@@ -139,8 +132,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       issued = i + 1;
     }
   } else {
-    // warps 1-3: one issuing thread per activation term (term t = warp - 1), all
-    // accumulating into the zeroed accumulator
+    // warps 1-3: one issuing thread per activation term (term t = warp - 1), each
+    // into its own accumulator (columns t*BN ..)
     const int t = warp - 1;
     for (int i = 0; i < nk; i++) {
       const int s = i % C::STAGES;
@@ -153,7 +146,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t b = a + C::A_BYTES + (uint32_t)t * C::B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < TC_KB / 16; kk++)
-            mma_bf16(tmem, sw128_desc(a + 32u * kk), sw128_desc(b + 32u * kk), C::IDESC, 1u);
+            mma_bf16(tmem + (uint32_t)(t * BN), sw128_desc(a + 32u * kk), sw128_desc(b + 32u * kk), C::IDESC,
+                     (i | kk) != 0 ? 1u : 0u);
           mma_commit(empty(s));  // the stage is free once all three threads' MMAs have read it
         }
       }
@@ -175,14 +169,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll 1
     for (int c = 0; c < BN; c += 16) {
       if (t0 + c >= m) break;  // warp-uniform
-      uint32_t r[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, r);
-      tmem_wait_ld(r);
+      uint32_t r[3][16];
+      const uint32_t lb = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c;
+      tmem_ld16(lb, r[0]);
+      tmem_ld16(lb + BN, r[1]);
+      tmem_ld16(lb + 2 * BN, r[2]);
+      tmem_wait_ld(r[0]);
+      tmem_tie(r[1]);
+      tmem_tie(r[2]);
       if (f < N) {
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-          const int t = t0 + c + j;
-          if (t < m) out[(size_t)t * N + f] = __uint_as_float(r[j]);
+          const int t = t0 + c + j;  // the terms' sums in a fixed order: deterministic
+          const float v = (__uint_as_float(r[0][j]) + __uint_as_float(r[1][j])) + __uint_as_float(r[2][j]);
+          if (t < m) out[(size_t)t * N + f] = v;
         }
       }
     }
@@ -212,11 +212,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // Warps 0-3: thread r owns weight row f0 + r: converts its row of each 64-element
 // step from the raw block bytes into the 128-byte swizzled bf16 A tile, and folds the
 // block sums of tensor-memory lane r. Warp 4: TMA of the raw weight rows (eight
-// blocks = 256 elements per copy, 128 rows). Warp 5: TMA of the activation terms.
-// Warp 6: MMA issue.
+// blocks = 256 elements per copy, 128 rows, one chunk ahead) and of the activation
+// terms. Warp 5: MMA issue (one thread: the block sums keep a fixed order).
 // ---------------------------------------------------------------------------------
 constexpr int Q_CHUNK = 256;  // K elements per raw weight copy (eight blocks)
-constexpr int Q_THREADS = 224;
+constexpr int Q_THREADS = 192;  // 6 warps: at most 2 per SM sub-partition, so 255 registers fit
 
 template <int T, int BN>
 struct QCfg {
@@ -351,23 +351,22 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {  // raw weight rows, one 256-element chunk per copy
+  if (warp == 4) {
+    // TMA: raw weight rows (one 256-element chunk = eight blocks per copy, issued a
+    // chunk ahead) and the activation terms of each 64-element step
     if (lane == 0) {
-      int issued = 0;
-      for (int c = 0; c < nc; c++) {
+      int raw_issued = 0, issued = 0;
+      auto load_raw = [&](int c) -> bool {
         const int rb = c & 1;
-        if (c >= 2 && !bar_wait(bar(QB_RAWEMPTY + rb), (unsigned)((c >> 1) - 1) & 1u, err, abort_flag)) break;
+        if (c >= 2 && !bar_wait(bar(QB_RAWEMPTY + rb), (unsigned)((c >> 1) - 1) & 1u, err, abort_flag)) return false;
         bar_expect_tx(bar(QB_RAWFULL + rb), (unsigned)C::RAW);
         tma_load_2d(base + C::OFF_RAW + rb * C::RAW, &tw, (c0 + c) * (C::CB / 2), f0, bar(QB_RAWFULL + rb));
-        issued = c + 1;
-      }
-      for (int c = std::max(0, issued - 2); c < issued; c++) bar_drain(bar(QB_RAWFULL + (c & 1)), (unsigned)(c >> 1) & 1u);
-    }
-    __syncwarp();
-  } else if (warp == 5) {  // activation terms, one 64-element step per stage
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nsub; i++) {
+        raw_issued = c + 1;
+        return true;
+      };
+      bool ok = load_raw(0);
+      for (int i = 0; ok && i < nsub; i++) {
+        if (i % 4 == 1 && i / 4 + 1 < nc && !(ok = load_raw(i / 4 + 1))) break;
         const int bb = i % C::NB;
         if (i >= C::NB && !bar_wait(bar(QB_BEMPTY + bb), (unsigned)((i / C::NB) - 1) & 1u, err, abort_flag)) break;
         bar_expect_tx(bar(QB_BFULL + bb), (unsigned)C::B_STAGE);
@@ -377,11 +376,13 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
           tma_load_3d(base + C::OFF_B + bb * C::B_STAGE + t * C::B_TERM, &tx, k, t0, t, bar(QB_BFULL + bb));
         issued = i + 1;
       }
+      for (int c = std::max(0, raw_issued - 2); c < raw_issued; c++)
+        bar_drain(bar(QB_RAWFULL + (c & 1)), (unsigned)(c >> 1) & 1u);
       for (int i = std::max(0, issued - C::NB); i < issued; i++)
         bar_drain(bar(QB_BFULL + i % C::NB), (unsigned)(i / C::NB) & 1u);
     }
     __syncwarp();
-  } else if (warp == 6) {  // MMA issue: per step two blocks, each 3 terms x 2 K steps into its own buffer
+  } else if (warp == 5) {  // MMA issue: per step two blocks, each 3 terms x 2 K steps into its own buffer
     if (lane == 0) {
       for (int i = 0; i < nsub; i++) {
         const int ab = i & 1, bb = i % C::NB;

@@ -154,12 +154,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 // 8 consecutive 32-bit columns of this thread's tensor-memory lane; complete after
 // tmem_wait_st().
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
                "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Zero N (a multiple of 8) consecutive columns of this thread's lane (after tmem_wait_st).
+template <int N>
+__device__ __forceinline__ void tmem_zero(uint32_t taddr) {
+  const uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+  for (int c = 0; c < N; c += 8) tmem_st8(taddr + (uint32_t)c, z);
+}
 // Waits for this thread's outstanding tensor-memory loads; r is tied to the wait so
 // no use of the loaded registers moves above it (tmem_tie ties further arrays).
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
