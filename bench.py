@@ -60,6 +60,7 @@ def parse():
                     help="BF16 1B prefill prompt lengths reported beside the decode metric (empty: skip)")
     ap.add_argument("--prefill-type", default="bf16", choices=["bf16", "q8_0", "q4_0"],
                     help="weight type of the prefill measurement (config 3 is bf16)")
+    ap.add_argument("--sweep", action="store_true", help="only the isolated matvec sweep (config 2)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the BF16 prefill measurement (one GPU; for profiling the prefill kernels)")
     return ap.parse_args()
@@ -258,6 +259,73 @@ def run_prefill(lib, G, lengths, device, wtype="bf16"):
             "dtype": f"f32 activations, {wtype} weights; bf16 MMA terms", "lengths": out}
 
 
+SWEEP_SHAPES = [(2048, 2048), (512, 2048), (8192, 2048), (2048, 8192), (128256, 2048)]  # [out x in]
+
+
+def sweep_weights(lib, wtype, out_dim, in_dim, copies, device):
+    """`copies` distinct weight matrices in the native block layout (random quants,
+    finite f16 scales; BF16 from N(0,1)), generated on the device."""
+    import torch
+    n = out_dim * in_dim
+    g = torch.Generator(device=device).manual_seed(1234 + n + wtype)
+    if wtype == lib.BF16:
+        return [torch.randn(n, generator=g, device=device).to(torch.bfloat16).view(torch.uint8) for _ in range(copies)]
+    bb = 34 if wtype == lib.Q8_0 else 18
+    out = []
+    for _ in range(copies):
+        w = torch.randint(0, 256, (n // 32, bb), generator=g, device=device, dtype=torch.uint8)
+        w[:, 0] = 0x00
+        w[:, 1] = 0x14  # f16 scale 2^-10
+        out.append(w.view(-1))
+    return out
+
+
+def run_sweep(lib, device, reps=20):
+    """Isolated matvec sweep (config 2): sq_linear with m = 1 through the C ABI on
+    every [out x in] shape x weight type. Enough distinct weight copies rotate that
+    their bytes exceed 4x the 126 MB L2, so every launch streams from HBM. Launches
+    are captured into a CUDA graph (reps per copy) and replayed; per-launch device
+    time = event time / launches. bytes = weights + activation (in*4) + output (out*4)."""
+    import torch
+    torch.cuda.set_device(device)
+    peak, kind = peaks()
+    l2 = 126 * 2 ** 20
+    res = []
+    for tname, wt in (("q8_0", lib.Q8_0), ("q4_0", lib.Q4_0), ("bf16", lib.BF16)):
+        for out_dim, in_dim in SWEEP_SHAPES:
+            wbytes = out_dim * in_dim // 32 * {lib.Q8_0: 34, lib.Q4_0: 18, lib.BF16: 64}[wt]
+            copies = max(2, -(-4 * l2 // wbytes))
+            ws = sweep_weights(lib, wt, out_dim, in_dim, copies, device)
+            x = torch.randn((1, in_dim), device=device)
+            y = torch.empty((1, out_dim), device=device)
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for w in ws:  # warm up (loads the kernel, sets attributes)
+                    lib.linear(x, w, wt, out_dim, out=y)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            n_launch = max(reps, copies)
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(n_launch):
+                    lib.linear(x, ws[i % copies], wt, out_dim, out=y)
+            with torch.cuda.stream(s):  # replay and events on the same stream
+                graph.replay()
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(s)
+                graph.replay()
+                b.record(s)
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1e3 / n_launch
+            nbytes = wbytes + 4 * in_dim + 4 * out_dim
+            res.append({"type": tname, "shape": [out_dim, in_dim], "us": us, "gb_s": nbytes / us / 1e3,
+                        "frac": nbytes / us / 1e3 / peak, "bytes": nbytes, "copies": copies})
+            del graph, ws
+            torch.cuda.empty_cache()
+    return {"workload": "isolated matvec sweep (config 2), m = 1, f32 activation N(0,1)", "peak_gb_s": peak,
+            "peak_source": kind, "results": res}
+
+
 def run_ours(args):
     import torch
     rank = int(os.environ.get("RANK", "0"))
@@ -397,6 +465,10 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        from sqb200 import lib
+        print(json.dumps(run_sweep(lib, 0)), flush=True)
+        return 0
     if args.prefill_only:
         from sqb200 import gguf_synth as G
         from sqb200 import lib

@@ -645,19 +645,31 @@ bool gemm_tc_supported(int m, int K, const float *x, const void *w, int wtype, c
   return ok && K % Q_CHUNK == 0 && rowbytes % 16 == 0;  // whole eight-block chunks on 16-byte boundaries
 }
 
+cudaError_t launch_split_terms(cudaStream_t s, const float *x, int m, int K, float *ws) {
+  init_once();
+  const size_t n = (size_t)m * K;  // a multiple of 16
+  k_split3<<<(unsigned)std::min<size_t>((n / 4 + 255) / 256, 8 * (size_t)g_sms_tc), 256, 0, s>>>(
+      reinterpret_cast<const float4 *>(x), n / 4, reinterpret_cast<__nv_bfloat16 *>(ws), n);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_gemm_tc(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
                            float *ws, size_t ws_floats) {
   if (!gemm_tc_supported(m, K, x, w, wtype, ws, ws_floats)) return cudaErrorNotSupported;
+  cudaError_t e = launch_split_terms(s, x, m, K, ws);
+  if (e != cudaSuccess) return e;
+  return launch_gemm_tc_terms(s, m, K, w, wtype, N, y, ws, ws_floats);
+}
+
+cudaError_t launch_gemm_tc_terms(cudaStream_t s, int m, int K, const void *w, int wtype, int N, float *y, float *ws,
+                                 size_t ws_floats) {
+  // the terms' source is only checked for alignment: pass the workspace itself
+  if (!gemm_tc_supported(m, K, ws, w, wtype, ws, ws_floats)) return cudaErrorNotSupported;
   // workspace: [3][m][K] bf16 terms, then split-K partials (256-byte aligned)
   __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(ws);
   const size_t xs_floats = ((size_t)3 * m * K / 2 + 63) & ~(size_t)63;
   float *part = ws + xs_floats;
   const size_t part_floats = ws_floats - xs_floats;
-  const size_t n = (size_t)m * K;  // a multiple of 16
-  k_split3<<<(unsigned)std::min<size_t>((n / 4 + 255) / 256, 8 * (size_t)g_sms_tc), 256, 0, s>>>(
-      reinterpret_cast<const float4 *>(x), n / 4, xs, n);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
   const int ft = (N + TC_M - 1) / TC_M;
   if (wtype != SQ_BF16) {  // quantized rows: 256-element chunks, BN by the row count
     const int bn = m <= 32 ? 32 : (m <= 64 ? 64 : 128);

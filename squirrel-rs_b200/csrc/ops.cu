@@ -1,6 +1,7 @@
 // ops.cu — op-level kernels for sm_100a and the C-ABI entry points that replace
 // squirrel-rs's `src/ops` functions. Decode of one token runs in the persistent
 // decode kernel (decode.cu); these kernels serve the op-level ABI and prefill.
+#include <cuda_bf16.h>
 #include <math.h>
 #include <stdio.h>
 
@@ -114,102 +115,199 @@ __global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x,
 }
 
 // m = 1 (decode through the op level): a matvec streamed through shared memory.
-// A warp walks a stream of row chunks - 32 block pairs (Q8_0 2176, Q4_0 1152, BF16
-// 4096 bytes: whole multiples of 16) of one row - copying each with coalesced
-// 16-byte cp.async into its own ring of mv_stages<T>() chunk buffers, all but one
-// of them ahead of the one it computes; lane j reads pair j of the chunk from shared
-// memory (odd word stride: conflict-free) and meets the input in registers, read
-// from a per-CTA copy of x in the lane-interleaved layout (xs[seg*2048 +
-// (i/4)*128 + lane*4 + i%4] for element i of lane's 64). Rows must be whole
-// multiples of 256 elements (16-byte row starts; the caller checks).
-constexpr int MV_WARPS = 8;
+// Each CTA owns a contiguous block of rows. A producer warp streams it as tiles of
+// whole consecutive rows (at most 36 KB, one bulk copy each, L2 evict-first: the
+// weights are read once) into a ring of MV_NS slots completing on mbarriers. A row is
+// split into segments of 2048 inputs (32 block pairs); the 8 consumer warps form
+// groups of nseg warps, warp `seg` of a group keeps its input segment in registers
+// (lane j holds elements 64j .. 64j+63, read once) and takes that segment of rows
+// g, g + G, .. of every tile (two rows at a time: independent dots, one paired
+// reduction); lane j reads pair j of the row from shared memory. With one segment
+// the warp writes the row; otherwise the partial sums meet in shared memory and
+// warp 0 adds them in segment order (deterministic). Rows must be whole multiples of
+// 256 elements (16-byte row starts) and in_dim <= 8 * 2048 (the caller checks).
+// Waits are bounded (~2 s); on expiry the warp records an error and stops.
+constexpr int MV_CONS = 8;                     // consumer warps
+constexpr int MV_THREADS = 32 * (MV_CONS + 1);  // + the producer warp
+constexpr int MV_SLOT = 36864;                 // bytes per ring slot
+constexpr int MV_NS = 5;                       // ring slots
+constexpr int MV_TRMAX = 64;                   // rows per tile at most
+constexpr int MV_HDR = 2 * MV_NS * 8 + 2 * MV_TRMAX * MV_CONS * 4;  // mbarriers + partial sums
+constexpr int MV_RING_OFF = (MV_HDR + 127) & ~127;
 
-template <int T>
-constexpr int mv_chunk_bytes() {
-  return 32 * pair_words<T>() * 4;
-}
-template <int T>
-constexpr int mv_stages() {  // chunks in each warp's ring (about 14-15 KB of copies in flight a warp)
-  return T == SQ_BF16 ? 3 : 7;
-}
+__device__ unsigned g_mv_err;  // set when a bounded wait of k_matvec gave up
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ uint32_t mv_su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool mv_try_wait(uint32_t b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(b), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-template <int T>
-__global__ void __launch_bounds__(MV_WARPS * 32, 1) k_matvec(const float *__restrict__ x, int in_dim,
-                                                             const uint8_t *__restrict__ w, int out_dim,
-                                                             float *__restrict__ y) {
-  constexpr int PW = pair_words<T>(), CB = mv_chunk_bytes<T>(), MV_STAGES = mv_stages<T>();
-  extern __shared__ __align__(16) uint8_t mv_smem[];
-  float *xs = reinterpret_cast<float *>(mv_smem);
-  const int nseg = (in_dim + 2047) / 2048;
-  uint8_t *ring = mv_smem + (size_t)nseg * 2048 * 4 + (size_t)(threadIdx.x >> 5) * MV_STAGES * CB;
-  const int lane = threadIdx.x & 31;
-  const int np = in_dim / 64;                       // pairs per row
-  const size_t rb = (size_t)np * PW * 4;            // row bytes
-  const int gw = blockIdx.x * MV_WARPS + (threadIdx.x >> 5), nw = gridDim.x * MV_WARPS;
-  const int rows_mine = gw < out_dim ? (out_dim - 1 - gw) / nw + 1 : 0;
-  const int total = rows_mine * nseg;               // chunks this warp streams
-  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
-  auto issue = [&](int c) {                         // chunk c = (row c / nseg, segment c % nseg)
-    if (c < total) {
-      const int row = gw + (c / nseg) * nw, sg = c % nseg;
-      const int pairs = min(32, np - sg * 32);
-      const uint8_t *src = w + (size_t)row * rb + (size_t)sg * CB;
-      const uint32_t dst = ring_s + (uint32_t)(c % MV_STAGES) * CB;
-      for (int o = lane * 16; o < pairs * PW * 4; o += 32 * 16) cp_async16(dst + o, src + o);
+__device__ __forceinline__ bool mv_wait(uint32_t b, unsigned parity) {
+  if (mv_try_wait(b, parity)) return true;
+  const long long t0 = clock64();
+  while (!mv_try_wait(b, parity)) {
+    if (clock64() - t0 > 4000000000LL) {
+      atomicExch(&g_mv_err, 1u);
+      return false;
     }
-    cp_async_commit();  // one group per chunk slot, empty past the end
-  };
+  }
+  return true;
+}
+
+template <int T>
+__device__ __forceinline__ void mv_load_pair(uint32_t a, uint32_t (&wv)[pair_words<T>()]) {
+  constexpr int PW = pair_words<T>();
+  if constexpr (PW % 4 == 0) {  // BF16: 128 bytes a lane, 16-byte aligned
 #pragma unroll
-  for (int c = 0; c < MV_STAGES - 1; c++) issue(c);  // the weights stream while x is staged
-  // x into the lane-interleaved layout (zeros past in_dim)
-  for (int e = threadIdx.x * 4; e < nseg * 2048; e += blockDim.x * 4) {
-    const float4 v = e < in_dim ? __ldg(reinterpret_cast<const float4 *>(x + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const int sg = e >> 11, r = e & 2047, ln = r >> 6, i = r & 63;
-    *reinterpret_cast<float4 *>(&xs[(sg << 11) + ((i >> 2) << 7) + (ln << 2)]) = v;
+    for (int i = 0; i < PW; i += 4)
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(wv[i]), "=r"(wv[i + 1]), "=r"(wv[i + 2]), "=r"(wv[i + 3])
+                   : "r"(a + 4 * i));
+  } else {  // odd word stride between lanes: conflict-free 4-byte loads
+#pragma unroll
+    for (int i = 0; i < PW; i++) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wv[i]) : "r"(a + 4 * i));
+  }
+}
+
+template <int T>
+__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restrict__ x, int in_dim,
+                                                          const uint8_t *__restrict__ w, int out_dim,
+                                                          float *__restrict__ y) {
+  constexpr int PW = pair_words<T>(), CB = 32 * PW * 4;
+  extern __shared__ __align__(128) uint8_t mv_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nseg = (in_dim + 2047) / 2048;
+  const int G = MV_CONS / nseg;  // row groups (consumer warps past G * nseg idle)
+  const int ncons = G * nseg;
+  const int np = in_dim / 64;               // pairs per row
+  const int rb = np * PW * 4;               // row bytes (a multiple of 16)
+  const int TR = min(MV_TRMAX, MV_SLOT / rb);  // rows per tile (>= 1: rows fit a slot)
+  const int per_cta = (out_dim + gridDim.x - 1) / gridDim.x;
+  const int cta0 = blockIdx.x * per_cta, cta1 = min(out_dim, cta0 + per_cta);
+  const int ntiles = cta1 > cta0 ? (cta1 - cta0 + TR - 1) / TR : 0;
+  const uint32_t full = mv_su32(mv_smem), empty = full + 8u * MV_NS;
+  float *red = reinterpret_cast<float *>(mv_smem + 2 * MV_NS * 8);  // [2][MV_TRMAX][nseg]
+  const uint32_t ring = mv_su32(mv_smem + MV_RING_OFF);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < MV_NS; i++) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(full + 8u * i) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty + 8u * i), "r"(ncons) : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  float acc = 0.f;
-  for (int c = 0; c < total; c++) {
-    issue(c + MV_STAGES - 1);
-    cp_async_wait<MV_STAGES - 1>();  // chunk c has landed (this lane's copies)
-    __syncwarp();                    // ... and every lane's
-    const int sg = c % nseg;
-    if (sg * 32 + lane < np) {
-      const uint32_t a = ring_s + (uint32_t)(c % MV_STAGES) * CB + (uint32_t)lane * PW * 4;
-      uint32_t wv[PW];
-#pragma unroll
-      for (int i = 0; i < PW; i++) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wv[i]) : "r"(a + 4 * i));
-      f2x x2[32];
-#pragma unroll
-      for (int k = 0; k < 16; k++) {
-        const float4 f = *reinterpret_cast<const float4 *>(&xs[(sg << 11) + (k << 7) + (lane << 2)]);
-        x2[2 * k] = pk2(f.x, f.y);
-        x2[2 * k + 1] = pk2(f.z, f.w);
+  if (warp == MV_CONS) {  // producer
+    if (lane == 0) {
+      uint64_t pol;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+      int issued = 0;
+      for (int t = 0; t < ntiles; t++) {
+        const int slot = t % MV_NS;
+        if (t >= MV_NS && !mv_wait(empty + 8u * slot, (unsigned)((t / MV_NS) - 1) & 1u)) break;
+        const int r0 = cta0 + t * TR, rows = min(TR, cta1 - r0);
+        const unsigned bytes = (unsigned)(rows * rb);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full + 8u * slot), "r"(bytes)
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+                ring + (uint32_t)slot * MV_SLOT),
+            "l"(w + (size_t)r0 * rb), "r"(bytes), "r"(full + 8u * slot), "l"(pol)
+            : "memory");
+        issued = t + 1;
       }
-      acc += pair_dot<T>(wv, x2);
+      for (int t = max(0, issued - MV_NS); t < issued; t++) {  // drain: copies land before exit
+        const long long t0 = clock64();
+        while (!mv_try_wait(full + 8u * (t % MV_NS), (unsigned)(t / MV_NS) & 1u) && clock64() - t0 < 4000000000LL) {
+        }
+      }
     }
-    __syncwarp();  // every lane is done with the slot before it is refilled
-    if (sg == nseg - 1) {
-      acc = warp_sum(acc);
-      if (lane == 0) y[gw + (c / nseg) * nw] = acc;
-      acc = 0.f;
+    return;
+  }
+  if (warp >= ncons) return;
+  const int g = warp / nseg, seg = warp % nseg;
+  const int pairs = min(32, np - seg * 32);  // pairs in this segment (>= 1)
+  const bool active = lane < pairs;
+  f2x x2[32];
+  if (active) {
+    const float4 *xp = reinterpret_cast<const float4 *>(x + seg * 2048 + lane * 64);
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const float4 f = __ldg(xp + k);
+      x2[2 * k] = pk2(f.x, f.y);
+      x2[2 * k + 1] = pk2(f.z, f.w);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; k++) x2[k] = 0ull;
+  }
+  for (int t = 0; t < ntiles; t++) {
+    const int slot = t % MV_NS;
+    int ok = 1;
+    if (lane == 0) ok = mv_wait(full + 8u * slot, (unsigned)(t / MV_NS) & 1u);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok && nseg == 1) break;  // (with segments every warp reaches the vote below first)
+    const int r0 = cta0 + t * TR, rows = ok ? min(TR, cta1 - r0) : 0;
+    const uint32_t tile = ring + (uint32_t)slot * MV_SLOT + (uint32_t)seg * CB + (uint32_t)lane * PW * 4;
+    float *rd = red + (t & 1) * MV_TRMAX * nseg;
+    for (int r = g; r < rows; r += 2 * G) {  // rows r and r + G of the tile
+      const bool two = r + G < rows;
+      float d0 = 0.f, d1 = 0.f;
+      if (active) {
+        uint32_t wa[PW], wb[PW];
+        mv_load_pair<T>(tile + (uint32_t)(r * rb), wa);
+        if (two) mv_load_pair<T>(tile + (uint32_t)((r + G) * rb), wb);
+        d0 = pair_dot<T>(wa, x2);
+        if (two) d1 = pair_dot<T>(wb, x2);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        d0 += __shfl_xor_sync(0xffffffffu, d0, o);
+        d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+      }
+      if (lane == 0) {
+        if (nseg == 1) {
+          y[r0 + r] = d0;
+          if (two) y[r0 + r + G] = d1;
+        } else {
+          rd[r * nseg + seg] = d0;
+          if (two) rd[(r + G) * nseg + seg] = d1;
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with the slot
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty + 8u * slot) : "memory");
+    if (nseg > 1) {  // partial sums of the tile's rows, added in segment order
+      unsigned all_ok;  // the consumers' vote doubles as the barrier: they stop together
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.and.pred q, 1, %2, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(all_ok)
+          : "r"((unsigned)ok), "r"(32 * ncons)
+          : "memory");
+      if (!all_ok) break;
+      if (warp == 0)
+        for (int r = lane; r < rows; r += 32) {
+          float sum = rd[r * nseg];
+          for (int q = 1; q < nseg; q++) sum += rd[r * nseg + q];
+          y[r0 + r] = sum;
+        }
     }
   }
-  cp_async_wait<0>();
 }
 
 template <int T>
 size_t mv_smem_bytes(int in_dim) {
-  return (size_t)((in_dim + 2047) / 2048) * 2048 * 4 + (size_t)MV_WARPS * mv_stages<T>() * mv_chunk_bytes<T>();
+  (void)in_dim;
+  return (size_t)MV_RING_OFF + (size_t)MV_NS * MV_SLOT;
 }
 
 // ------------------------------------------------------------------------------------
@@ -318,8 +416,34 @@ __global__ void k_dequant(const uint8_t *__restrict__ blocks, size_t n, float *_
 // Rows of dim <= 8 * 4 * 256 with 16-byte row starts: every float4 of a thread loaded
 // at once and kept in registers for the output (one pass over global memory).
 constexpr int RMS_V = 8;
+
+// Four f32 values -> their three exact bf16 terms (x = h + d + l), stored at element
+// offset e of the three planes [3][plane] (the tensor-core GEMM's activation input).
+__device__ __forceinline__ void store_terms4(__nv_bfloat16 *terms, size_t plane, size_t e, float4 v) {
+  const float in[4] = {v.x, v.y, v.z, v.w};
+  uint32_t hw[2], dw[2], lw[2];
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(in[2 * k], in[2 * k + 1]);
+    const float2 hf = __bfloat1622float2(h);
+    const float r0 = in[2 * k] - hf.x, r1 = in[2 * k + 1] - hf.y;
+    const __nv_bfloat162 d = __floats2bfloat162_rn(r0, r1);
+    const float2 df = __bfloat1622float2(d);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - df.x, r1 - df.y);
+    hw[k] = *reinterpret_cast<const uint32_t *>(&h);
+    dw[k] = *reinterpret_cast<const uint32_t *>(&d);
+    lw[k] = *reinterpret_cast<const uint32_t *>(&l);
+  }
+  *reinterpret_cast<uint2 *>(terms + e) = make_uint2(hw[0], hw[1]);
+  *reinterpret_cast<uint2 *>(terms + plane + e) = make_uint2(dw[0], dw[1]);
+  *reinterpret_cast<uint2 *>(terms + 2 * plane + e) = make_uint2(lw[0], lw[1]);
+}
+
+// y (may be null) and / or the three bf16 terms of the output (terms may be null;
+// plane = rows * dim).
 __global__ void __launch_bounds__(256) k_rms_norm_v(const float *__restrict__ x, const float *__restrict__ w,
-                                                    float *y, int dim, float eps) {
+                                                    float *y, int dim, float eps, __nv_bfloat16 *terms,
+                                                    size_t plane) {
   __shared__ float red[8];
   const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * dim);
   const float4 *wr = reinterpret_cast<const float4 *>(w);
@@ -353,9 +477,12 @@ __global__ void __launch_bounds__(256) k_rms_norm_v(const float *__restrict__ x,
 #pragma unroll
   for (int k = 0; k < RMS_V; k++) {
     const int i = threadIdx.x + k * 256;
-    if (i < nv)
-      yr[i] = make_float4(__fdiv_rn(__fmul_rn(v[k].x, g[k].x), rms), __fdiv_rn(__fmul_rn(v[k].y, g[k].y), rms),
-                          __fdiv_rn(__fmul_rn(v[k].z, g[k].z), rms), __fdiv_rn(__fmul_rn(v[k].w, g[k].w), rms));
+    if (i < nv) {
+      const float4 o = make_float4(__fdiv_rn(__fmul_rn(v[k].x, g[k].x), rms), __fdiv_rn(__fmul_rn(v[k].y, g[k].y), rms),
+                                   __fdiv_rn(__fmul_rn(v[k].z, g[k].z), rms), __fdiv_rn(__fmul_rn(v[k].w, g[k].w), rms));
+      if (y) yr[i] = o;
+      if (terms) store_terms4(terms, plane, (size_t)blockIdx.x * dim + 4 * i, o);
+    }
   }
 }
 
@@ -437,6 +564,16 @@ __global__ void k_add(float *a, const float *b, size_t n) {
 __global__ void k_silu_mul(const float *g, const float *u, float *out, size_t n) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     out[i] = __fmul_rn(silu_ref(g[i]), u[i]);
+}
+// silu(g) * u written only as its three bf16 terms (n % 4 == 0, 16-byte aligned).
+__global__ void k_silu_mul_terms(const float4 *__restrict__ g, const float4 *__restrict__ u, size_t n4,
+                                 __nv_bfloat16 *__restrict__ terms) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = g[i], b = u[i];
+    const float4 o = make_float4(__fmul_rn(silu_ref(a.x), b.x), __fmul_rn(silu_ref(a.y), b.y),
+                                 __fmul_rn(silu_ref(a.z), b.z), __fmul_rn(silu_ref(a.w), b.w));
+    store_terms4(terms, 4 * n4, 4 * i, o);
+  }
 }
 
 // GreedySampler (greedy.rs:6-15): per-CTA ordered reduction of a contiguous chunk,
@@ -537,15 +674,15 @@ static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, cons
                          float *y) {
   const int grid = grid_for((size_t)out_dim, 8, num_sms() * 8);
   const size_t mv_smem = mv_smem_bytes<T>(in_dim);
-  if (m == 1 && in_dim % 256 == 0 && ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0 &&
-      mv_smem <= 200 * 1024) {  // 16-byte row starts; x and the ring fit in shared memory
+  if (m == 1 && in_dim % 256 == 0 && in_dim <= MV_CONS * 2048 && (size_t)(in_dim / 64) * pair_words<T>() * 4 <= MV_SLOT &&
+      ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0) {  // 16-byte row starts; a row fits a slot
     static bool attr_set[3] = {false, false, false};
     const int ti = T == SQ_Q8_0 ? 0 : (T == SQ_Q4_0 ? 1 : 2);
     if (!attr_set[ti]) {
-      cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
       attr_set[ti] = true;
     }
-    k_matvec<T><<<num_sms(), MV_WARPS * 32, mv_smem, s>>>(x, in_dim, w, out_dim, y);
+    k_matvec<T><<<num_sms(), MV_THREADS, mv_smem, s>>>(x, in_dim, w, out_dim, y);
   } else if (m <= 1)
     k_linear_f32<T, 1><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
   else if (m <= 4)
@@ -611,7 +748,7 @@ cudaError_t launch_rms_norm(cudaStream_t s, const float *x, const float *w, floa
                             float eps) {
   if (dim % 4 == 0 && dim <= RMS_V * 4 * 256 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
       ((uintptr_t)y & 15) == 0)
-    k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
+    k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, y, dim, eps, nullptr, 0);
   else
     k_rms_norm<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
   return cudaGetLastError();
@@ -643,6 +780,22 @@ cudaError_t launch_add(cudaStream_t s, float *a, const float *b, size_t n) {
   k_add<<<grid_for(n, 256, num_sms() * 8), 256, 0, s>>>(a, b, n);
   return cudaGetLastError();
 }
+bool rms_norm_terms_ok(const float *x, const float *w, int dim) {
+  return dim % 4 == 0 && dim <= RMS_V * 4 * 256 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0;
+}
+cudaError_t launch_rms_norm_terms(cudaStream_t s, const float *x, const float *w, void *terms, int rows, int dim,
+                                  float eps) {
+  if (!rms_norm_terms_ok(x, w, dim) || ((uintptr_t)terms & 15)) return cudaErrorNotSupported;
+  k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, nullptr, dim, eps, (__nv_bfloat16 *)terms, (size_t)rows * dim);
+  return cudaGetLastError();
+}
+cudaError_t launch_silu_mul_terms(cudaStream_t s, const float *g, const float *u, void *terms, size_t n) {
+  if (n % 4 || ((uintptr_t)g & 15) || ((uintptr_t)u & 15) || ((uintptr_t)terms & 15)) return cudaErrorNotSupported;
+  k_silu_mul_terms<<<grid_for(n / 4, 256, num_sms() * 8), 256, 0, s>>>(
+      reinterpret_cast<const float4 *>(g), reinterpret_cast<const float4 *>(u), n / 4, (__nv_bfloat16 *)terms);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_silu_mul(cudaStream_t s, const float *g, const float *u, float *out, size_t n) {
   k_silu_mul<<<grid_for(n, 256, num_sms() * 8), 256, 0, s>>>(g, u, out, n);
   return cudaGetLastError();

@@ -37,6 +37,16 @@ bool attn_tc_supported(int seq_q, int seq_k, int n_heads, int n_kv_heads, int he
 cudaError_t launch_attn_tc(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
                            int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
                            void *ws, size_t ws_bytes);
+// The same GEMM on activation terms already in ws ([3][m][K] bf16 at its start), e.g.
+// written by launch_rms_norm_terms / launch_silu_mul_terms / launch_split_terms.
+cudaError_t launch_gemm_tc_terms(cudaStream_t s, int m, int K, const void *w, int wtype, int N, float *y, float *ws,
+                                 size_t ws_floats);
+cudaError_t launch_split_terms(cudaStream_t s, const float *x, int m, int K, float *ws);
+// RMSNorm / SiLU.mul writing only the three bf16 terms of their output ([3][rows][dim]).
+bool rms_norm_terms_ok(const float *x, const float *w, int dim);
+cudaError_t launch_rms_norm_terms(cudaStream_t s, const float *x, const float *w, void *terms, int rows, int dim,
+                                  float eps);
+cudaError_t launch_silu_mul_terms(cudaStream_t s, const float *g, const float *u, void *terms, size_t n);
 cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out);
 cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype,
                          int embed_dim, int vocab, float *out);

@@ -601,14 +601,31 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     if (st_) return st_;       \
   } while (0)
   TRY(launch_embed(s, d_ids, n, m->embd, m->embd_type, E, m->cfg.vocab_size, c->hidden));  // replicated table
+  float *ws = c->gemm_ws;
+  const size_t wsf = c->gemm_ws_floats;
   for (int l = 0; l < cf.n_blocks; l++) {
     const auto &L = m->layers[l];
     float *kc = c->kc + l * layer_kv, *vc = c->vc + l * layer_kv;
-    TRY(launch_rms_norm(s, c->hidden, L.attn_norm, c->normed, n, E, cf.rms_eps));
-    if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));  // shared quantization
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.q, wt, Q, c->q, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.k, wt, KVd, c->k, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.v, wt, KVd, c->v, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    // Tensor-core layer: the normalised inputs and SiLU.mul go straight to the GEMMs'
+    // bf16 terms (written once, shared by q/k/v and by gate/up); only the attention
+    // output is split by a separate pass.
+    const bool tcl = !aq && gemm_tc_enabled() && n >= 2 && rms_norm_terms_ok(c->hidden, L.attn_norm, E) &&
+                     gemm_tc_supported(n, E, ws, L.q, wt, ws, wsf) && gemm_tc_supported(n, E, ws, L.k, wt, ws, wsf) &&
+                     gemm_tc_supported(n, E, ws, L.v, wt, ws, wsf) && gemm_tc_supported(n, Q, ws, L.o, wt, ws, wsf) &&
+                     gemm_tc_supported(n, E, ws, L.gate, wt, ws, wsf) && gemm_tc_supported(n, E, ws, L.up, wt, ws, wsf) &&
+                     gemm_tc_supported(n, F, ws, L.down, wt, ws, wsf);
+    if (tcl) {
+      TRY(launch_rms_norm_terms(s, c->hidden, L.attn_norm, ws, n, E, cf.rms_eps));
+      TRY(launch_gemm_tc_terms(s, n, E, L.q, wt, Q, c->q, ws, wsf));
+      TRY(launch_gemm_tc_terms(s, n, E, L.k, wt, KVd, c->k, ws, wsf));
+      TRY(launch_gemm_tc_terms(s, n, E, L.v, wt, KVd, c->v, ws, wsf));
+    } else {
+      TRY(launch_rms_norm(s, c->hidden, L.attn_norm, c->normed, n, E, cf.rms_eps));
+      if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));  // shared quantization
+      TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.q, wt, Q, c->q, aq, c->xq, ws, wsf));
+      TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.k, wt, KVd, c->k, aq, c->xq, ws, wsf));
+      TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.v, wt, KVd, c->v, aq, c->xq, ws, wsf));
+    }
     // pos_dev: positions come from the device counter (a captured decode step); the
     // attention then keeps the split count of the longest context
     TRY(launch_rope_rows_table(s, c->q, n, Q, pos, c->d_cos, c->d_sin, half, pos_dev));
@@ -625,15 +642,28 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs,
                       ns, c->sdpa_part, pos_dev));
     }
-    TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    if (tcl) {
+      TRY(launch_split_terms(s, c->attn, n, Q, ws));
+      TRY(launch_gemm_tc_terms(s, n, Q, L.o, wt, E, c->attn_out, ws, wsf));
+    } else {
+      TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, ws, wsf));
+    }
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
     TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
-    TRY(launch_rms_norm(s, c->hidden, L.ffn_norm, c->normed, n, E, cf.rms_eps));
-    if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.gate, wt, F, c->gate, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
-    TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.up, wt, F, c->up, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
-    TRY(launch_silu_mul(s, c->gate, c->up, c->act, (size_t)n * F));
-    TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    if (tcl) {
+      TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
+      TRY(launch_gemm_tc_terms(s, n, E, L.gate, wt, F, c->gate, ws, wsf));
+      TRY(launch_gemm_tc_terms(s, n, E, L.up, wt, F, c->up, ws, wsf));
+      TRY(launch_silu_mul_terms(s, c->gate, c->up, ws, (size_t)n * F));
+      TRY(launch_gemm_tc_terms(s, n, F, L.down, wt, E, c->ffn_out, ws, wsf));
+    } else {
+      TRY(launch_rms_norm(s, c->hidden, L.ffn_norm, c->normed, n, E, cf.rms_eps));
+      if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));
+      TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.gate, wt, F, c->gate, aq, c->xq, ws, wsf));
+      TRY(launch_linear(s, aq ? nullptr : c->normed, n, E, L.up, wt, F, c->up, aq, c->xq, ws, wsf));
+      TRY(launch_silu_mul(s, c->gate, c->up, c->act, (size_t)n * F));
+      TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, ws, wsf));
+    }
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));  // row-parallel down
     TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
   }

@@ -105,6 +105,30 @@ def test_linear_f32_acts(gpu_lib, wtype, shape):
     assert np.all(np.abs(got - want) <= 1e-5 * mag + 1e-6)
 
 
+# The m = 1 streaming matvec: 7 input segments (8B ffn_down width), a partial segment,
+# short rows (64-row tiles), two segments; output counts not a multiple of anything.
+MV_SHAPES = [(1, 14336, 300), (1, 1536, 1000), (1, 256, 5000), (1, 4096, 4097)]
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0, O.BF16])
+@pytest.mark.parametrize("shape", MV_SHAPES)
+def test_matvec_shapes(gpu_lib, wtype, shape):
+    """Same tolerance as test_linear_f32_acts; the segment partial sums are added in
+    segment order, so two calls give identical bits."""
+    from sqb200 import lib
+    m, k, n = shape
+    rng = np.random.default_rng(k + n + wtype)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = quant_weights(wtype, n, k, rng)
+    xd, wd = dev(x), dev(w)
+    got = host(lib.linear(xd, wd, wtype, n))
+    again = host(lib.linear(xd, wd, wtype, n))
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+    want = O.linear(x, w, wtype, n)
+    mag = term_magnitude(x, w, wtype, n)
+    assert np.all(np.abs(got - want) <= 1e-5 * mag + 1e-6)
+
+
 # Tensor-core GEMM (bf16 weights, m >= 2): ragged rows and outputs, K not a multiple
 # of the 64-element stage, and shapes small enough in tiles that K is split.
 TC_SHAPES = [(2, 64, 128), (3, 96, 9), (129, 160, 130), (100, 2048, 512), (256, 2048, 2048),
