@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--prefill-type", default="bf16", choices=["bf16", "q8_0", "q4_0"],
                     help="weight type of the prefill measurement (config 3 is bf16)")
     ap.add_argument("--sweep", action="store_true", help="only the isolated matvec sweep (config 2)")
+    ap.add_argument("--sweep-filter", default="", help="e.g. bf16:128256x2048 - one case of the sweep")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the BF16 prefill measurement (one GPU; for profiling the prefill kernels)")
     return ap.parse_args()
@@ -280,7 +281,7 @@ def sweep_weights(lib, wtype, out_dim, in_dim, copies, device):
     return out
 
 
-def run_sweep(lib, device, reps=20):
+def run_sweep(lib, device, reps=20, only=""):
     """Isolated matvec sweep (config 2): sq_linear with m = 1 through the C ABI on
     every [out x in] shape x weight type. Enough distinct weight copies rotate that
     their bytes exceed 4x the 126 MB L2, so every launch streams from HBM. Launches
@@ -293,6 +294,8 @@ def run_sweep(lib, device, reps=20):
     res = []
     for tname, wt in (("q8_0", lib.Q8_0), ("q4_0", lib.Q4_0), ("bf16", lib.BF16)):
         for out_dim, in_dim in SWEEP_SHAPES:
+            if only and only != f"{tname}:{out_dim}x{in_dim}":
+                continue
             wbytes = out_dim * in_dim // 32 * {lib.Q8_0: 34, lib.Q4_0: 18, lib.BF16: 64}[wt]
             copies = max(2, -(-4 * l2 // wbytes))
             ws = sweep_weights(lib, wt, out_dim, in_dim, copies, device)
@@ -467,7 +470,7 @@ def main():
         return run_reference(args)
     if args.sweep:
         from sqb200 import lib
-        print(json.dumps(run_sweep(lib, 0)), flush=True)
+        print(json.dumps(run_sweep(lib, 0, only=args.sweep_filter)), flush=True)
         return 0
     if args.prefill_only:
         from sqb200 import gguf_synth as G
