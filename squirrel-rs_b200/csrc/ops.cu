@@ -121,8 +121,8 @@ __global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x,
 // split into segments of 2048 inputs (32 block pairs); the 8 consumer warps form
 // groups of nseg warps, warp `seg` of a group keeps its input segment in registers
 // (lane j holds elements 64j .. 64j+63, read once) and takes that segment of rows
-// g, g + G, .. of every tile (two rows at a time: independent dots, one paired
-// reduction); lane j reads pair j of the row from shared memory. With one segment
+// g, g + G, .. of every tile (two rows at a time, four for Q4_0: independent dots,
+// one joint reduction); lane j reads pair j of the row from shared memory. With one segment
 // the warp writes the row; otherwise the partial sums meet in shared memory and
 // warp 0 adds them in segment order (deterministic). Rows must be whole multiples of
 // 256 elements (16-byte row starts) and in_dim <= 8 * 2048 (the caller checks).
@@ -162,14 +162,16 @@ __device__ __forceinline__ bool mv_wait(uint32_t b, unsigned parity) {
 }
 
 template <int T>
-__device__ __forceinline__ void mv_load_pair(uint32_t a, uint32_t (&wv)[pair_words<T>()]) {
+__device__ __forceinline__ void mv_load_pair(uint32_t a, int lane, uint32_t (&wv)[pair_words<T>()]) {
   constexpr int PW = pair_words<T>();
-  if constexpr (PW % 4 == 0) {  // BF16: 128 bytes a lane, 16-byte aligned
+  if constexpr (PW % 4 == 0) {  // BF16: 128 bytes a lane, 16-byte aligned. Step i reads the
+    // lane's 16-byte chunk i ^ (lane % 8): the 8 lanes of a quarter-warp hit 8 different
+    // bank groups (the input registers are permuted the same way)
 #pragma unroll
-    for (int i = 0; i < PW; i += 4)
+    for (int i = 0; i < PW / 4; i++)
       asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(wv[i]), "=r"(wv[i + 1]), "=r"(wv[i + 2]), "=r"(wv[i + 3])
-                   : "r"(a + 4 * i));
+                   : "=r"(wv[4 * i]), "=r"(wv[4 * i + 1]), "=r"(wv[4 * i + 2]), "=r"(wv[4 * i + 3])
+                   : "r"(a + 16u * (uint32_t)(i ^ (lane & 7))));
   } else {  // odd word stride between lanes: conflict-free 4-byte loads
 #pragma unroll
     for (int i = 0; i < PW; i++) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wv[i]) : "r"(a + 4 * i));
@@ -188,7 +190,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
   const int ncons = G * nseg;
   const int np = in_dim / 64;               // pairs per row
   const int rb = np * PW * 4;               // row bytes (a multiple of 16)
-  const int TR = min(MV_TRMAX, MV_SLOT / rb);  // rows per tile (>= 1: rows fit a slot)
+  int TR = min(MV_TRMAX, MV_SLOT / rb);  // rows per tile (>= 1: rows fit a slot) ...
+  if (TR >= G) TR -= TR % G;             // ... a multiple of the row groups: even work per warp
   const int per_cta = (out_dim + gridDim.x - 1) / gridDim.x;
   const int cta0 = blockIdx.x * per_cta, cta1 = min(out_dim, cta0 + per_cta);
   const int ntiles = cta1 > cta0 ? (cta1 - cta0 + TR - 1) / TR : 0;
@@ -238,8 +241,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
   if (active) {
     const float4 *xp = reinterpret_cast<const float4 *>(x + seg * 2048 + lane * 64);
 #pragma unroll
-    for (int k = 0; k < 16; k++) {
-      const float4 f = __ldg(xp + k);
+    for (int k = 0; k < 16; k++) {  // BF16: 8-element chunk i holds chunk i ^ (lane % 8), as the weights
+      const int src = T == SQ_BF16 ? ((((k >> 1) ^ (lane & 7)) << 1) | (k & 1)) : k;
+      const float4 f = __ldg(xp + src);
       x2[2 * k] = pk2(f.x, f.y);
       x2[2 * k + 1] = pk2(f.z, f.w);
     }
@@ -256,28 +260,32 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
     const int r0 = cta0 + t * TR, rows = ok ? min(TR, cta1 - r0) : 0;
     const uint32_t tile = ring + (uint32_t)slot * MV_SLOT + (uint32_t)seg * CB + (uint32_t)lane * PW * 4;
     float *rd = red + (t & 1) * MV_TRMAX * nseg;
-    for (int r = g; r < rows; r += 2 * G) {  // rows r and r + G of the tile
-      const bool two = r + G < rows;
-      float d0 = 0.f, d1 = 0.f;
+    constexpr int RI = T == SQ_Q4_0 ? 4 : 2;  // rows an iteration: independent dot chains
+    for (int r = g; r < rows; r += RI * G) {  // rows r, r + G, .. of the tile
+      float d[RI];
+#pragma unroll
+      for (int q = 0; q < RI; q++) d[q] = 0.f;
       if (active) {
-        uint32_t wa[PW], wb[PW];
-        mv_load_pair<T>(tile + (uint32_t)(r * rb), wa);
-        if (two) mv_load_pair<T>(tile + (uint32_t)((r + G) * rb), wb);
-        d0 = pair_dot<T>(wa, x2);
-        if (two) d1 = pair_dot<T>(wb, x2);
+        uint32_t wv[RI][PW];
+#pragma unroll
+        for (int q = 0; q < RI; q++)
+          if (r + q * G < rows) mv_load_pair<T>(tile + (uint32_t)((r + q * G) * rb), lane, wv[q]);
+#pragma unroll
+        for (int q = 0; q < RI; q++)
+          if (r + q * G < rows) d[q] = pair_dot<T>(wv[q], x2);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        d0 += __shfl_xor_sync(0xffffffffu, d0, o);
-        d1 += __shfl_xor_sync(0xffffffffu, d1, o);
-      }
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int q = 0; q < RI; q++) d[q] += __shfl_xor_sync(0xffffffffu, d[q], o);
       if (lane == 0) {
-        if (nseg == 1) {
-          y[r0 + r] = d0;
-          if (two) y[r0 + r + G] = d1;
-        } else {
-          rd[r * nseg + seg] = d0;
-          if (two) rd[(r + G) * nseg + seg] = d1;
+#pragma unroll
+        for (int q = 0; q < RI; q++) {
+          const int rr = r + q * G;
+          if (rr < rows) {
+            if (nseg == 1) y[r0 + rr] = d[q];
+            else rd[rr * nseg + seg] = d[q];
+          }
         }
       }
     }
