@@ -132,7 +132,7 @@ constexpr int MV_THREADS = 32 * (MV_CONS + 1);  // + the producer warp
 constexpr int MV_SLOT = 36864;                 // bytes per ring slot
 constexpr int MV_NS = 5;                       // ring slots
 constexpr int MV_TRMAX = 64;                   // rows per tile at most
-constexpr int MV_HDR = 2 * MV_NS * 8 + 2 * MV_TRMAX * MV_CONS * 4;  // mbarriers + partial sums
+constexpr int MV_HDR = 2 * MV_NS * 8 + (2 * MV_TRMAX + 1) * MV_CONS * 4;  // mbarriers + partial sums
 constexpr int MV_RING_OFF = (MV_HDR + 127) & ~127;
 
 __device__ unsigned g_mv_err;  // set when a bounded wait of k_matvec gave up
@@ -178,13 +178,14 @@ __device__ __forceinline__ void mv_load_pair(uint32_t a, int lane, uint32_t (&wv
   }
 }
 
+__device__ __forceinline__ float silu_ref(float x);
+
 template <int T>
-__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restrict__ x, int in_dim,
-                                                          const uint8_t *__restrict__ w, int out_dim,
-                                                          float *__restrict__ y) {
+__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant__ MvArgs a) {
   constexpr int PW = pair_words<T>(), CB = 32 * PW * 4;
   extern __shared__ __align__(128) uint8_t mv_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int in_dim = a.in_dim;
   const int nseg = (in_dim + 2047) / 2048;
   const int G = MV_CONS / nseg;  // row groups (consumer warps past G * nseg idle)
   const int ncons = G * nseg;
@@ -192,11 +193,41 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
   const int rb = np * PW * 4;               // row bytes (a multiple of 16)
   int TR = min(MV_TRMAX, MV_SLOT / rb);  // rows per tile (>= 1: rows fit a slot) ...
   if (TR >= G) TR -= TR % G;             // ... a multiple of the row groups: even work per warp
-  const int per_cta = (out_dim + gridDim.x - 1) / gridDim.x;
-  const int cta0 = blockIdx.x * per_cta, cta1 = min(out_dim, cta0 + per_cta);
-  const int ntiles = cta1 > cta0 ? (cta1 - cta0 + TR - 1) / TR : 0;
+  // each CTA owns a contiguous block of rows of every matrix: [b0, b1) of matrix i
+  auto block_of = [&](int i, int &b0, int &b1) {
+    const int od = i < a.n ? a.out_dim[i] : 0;
+    const int per = (od + gridDim.x - 1) / gridDim.x;
+    b0 = blockIdx.x * per;
+    b1 = min(od, b0 + per);
+  };
+  int s00, s01, s10, s11, s20, s21;
+  block_of(0, s00, s01);
+  block_of(1, s10, s11);
+  block_of(2, s20, s21);
+  auto ntile = [&](int b0, int b1) { return b1 > b0 ? (b1 - b0 + TR - 1) / TR : 0; };
+  const int nt0 = ntile(s00, s01), nt1 = ntile(s10, s11), nt2 = ntile(s20, s21);
+  const int ntiles = nt0 + nt1 + nt2;
+  // tile t -> (matrix, first row, rows)
+  auto tile_of = [&](int t, int &mi, int &r0, int &rows) {
+    int b0 = s00, b1 = s01;
+    mi = 0;
+    if (t >= nt0) {
+      t -= nt0;
+      mi = 1;
+      b0 = s10;
+      b1 = s11;
+      if (t >= nt1) {
+        t -= nt1;
+        mi = 2;
+        b0 = s20;
+        b1 = s21;
+      }
+    }
+    r0 = b0 + t * TR;
+    rows = min(TR, b1 - r0);
+  };
   const uint32_t full = mv_su32(mv_smem), empty = full + 8u * MV_NS;
-  float *red = reinterpret_cast<float *>(mv_smem + 2 * MV_NS * 8);  // [2][MV_TRMAX][nseg]
+  float *red = reinterpret_cast<float *>(mv_smem + 2 * MV_NS * 8);  // [2][MV_TRMAX][nseg], then [MV_CONS]
   const uint32_t ring = mv_su32(mv_smem + MV_RING_OFF);
   if (threadIdx.x == 0) {
     for (int i = 0; i < MV_NS; i++) {
@@ -214,14 +245,15 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
       for (int t = 0; t < ntiles; t++) {
         const int slot = t % MV_NS;
         if (t >= MV_NS && !mv_wait(empty + 8u * slot, (unsigned)((t / MV_NS) - 1) & 1u)) break;
-        const int r0 = cta0 + t * TR, rows = min(TR, cta1 - r0);
+        int mi, r0, rows;
+        tile_of(t, mi, r0, rows);
         const unsigned bytes = (unsigned)(rows * rb);
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full + 8u * slot), "r"(bytes)
                      : "memory");
         asm volatile(
             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
                 ring + (uint32_t)slot * MV_SLOT),
-            "l"(w + (size_t)r0 * rb), "r"(bytes), "r"(full + 8u * slot), "l"(pol)
+            "l"(a.w[mi] + (size_t)r0 * rb), "r"(bytes), "r"(full + 8u * slot), "l"(pol)
             : "memory");
         issued = t + 1;
       }
@@ -237,13 +269,41 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
   const int g = warp / nseg, seg = warp % nseg;
   const int pairs = min(32, np - seg * 32);  // pairs in this segment (>= 1)
   const bool active = lane < pairs;
+  float rms = 1.f;
+  if (a.norm_w) {  // the consumers' sum of squares over the whole row, in a fixed order
+    float ss = 0.f;
+    for (int e = 4 * (warp * 32 + lane); e < in_dim; e += 4 * 32 * ncons) {
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(a.x + e));
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    float *part = red + 2 * MV_TRMAX * MV_CONS;  // [MV_CONS]
+    if (lane == 0) part[warp] = ss;
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * ncons) : "memory");
+    float tot = part[0];
+    for (int q = 1; q < ncons; q++) tot += part[q];
+    rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)in_dim), a.eps));
+  }
   f2x x2[32];
   if (active) {
-    const float4 *xp = reinterpret_cast<const float4 *>(x + seg * 2048 + lane * 64);
+    const int base = seg * 2048 + lane * 64;
 #pragma unroll
     for (int k = 0; k < 16; k++) {  // BF16: 8-element chunk i holds chunk i ^ (lane % 8), as the weights
       const int src = T == SQ_BF16 ? ((((k >> 1) ^ (lane & 7)) << 1) | (k & 1)) : k;
-      const float4 f = __ldg(xp + src);
+      float4 f = __ldg(reinterpret_cast<const float4 *>(a.x + base) + src);
+      if (a.xu) {  // SiLU(gate) * up (silu.rs, elementwise_mul.rs)
+        const float4 u = __ldg(reinterpret_cast<const float4 *>(a.xu + base) + src);
+        f = make_float4(__fmul_rn(silu_ref(f.x), u.x), __fmul_rn(silu_ref(f.y), u.y), __fmul_rn(silu_ref(f.z), u.z),
+                        __fmul_rn(silu_ref(f.w), u.w));
+      }
+      if (a.norm_w) {  // (x * w) / rms, as k_rms_norm_v rounds it
+        const float4 gw = __ldg(reinterpret_cast<const float4 *>(a.norm_w + base) + src);
+        f = make_float4(__fdiv_rn(__fmul_rn(f.x, gw.x), rms), __fdiv_rn(__fmul_rn(f.y, gw.y), rms),
+                        __fdiv_rn(__fmul_rn(f.z, gw.z), rms), __fdiv_rn(__fmul_rn(f.w, gw.w), rms));
+      }
       x2[2 * k] = pk2(f.x, f.y);
       x2[2 * k + 1] = pk2(f.z, f.w);
     }
@@ -251,13 +311,18 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
 #pragma unroll
     for (int k = 0; k < 32; k++) x2[k] = 0ull;
   }
+  auto out_row = [&](int mi, int row, float v) {
+    a.y[mi][row] = a.res[mi] ? __fadd_rn(a.res[mi][row], v) : v;
+  };
   for (int t = 0; t < ntiles; t++) {
     const int slot = t % MV_NS;
     int ok = 1;
     if (lane == 0) ok = mv_wait(full + 8u * slot, (unsigned)(t / MV_NS) & 1u);
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (!ok && nseg == 1) break;  // (with segments every warp reaches the vote below first)
-    const int r0 = cta0 + t * TR, rows = ok ? min(TR, cta1 - r0) : 0;
+    int mi, r0, rows;
+    tile_of(t, mi, r0, rows);
+    if (!ok) rows = 0;
     const uint32_t tile = ring + (uint32_t)slot * MV_SLOT + (uint32_t)seg * CB + (uint32_t)lane * PW * 4;
     float *rd = red + (t & 1) * MV_TRMAX * nseg;
     constexpr int RI = T == SQ_Q4_0 ? 4 : 2;  // rows an iteration: independent dot chains
@@ -283,7 +348,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
         for (int q = 0; q < RI; q++) {
           const int rr = r + q * G;
           if (rr < rows) {
-            if (nseg == 1) y[r0 + rr] = d[q];
+            if (nseg == 1) out_row(mi, r0 + rr, d[q]);
             else rd[rr * nseg + seg] = d[q];
           }
         }
@@ -306,7 +371,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const float *__restric
         for (int r = lane; r < rows; r += 32) {
           float sum = rd[r * nseg];
           for (int q = 1; q < nseg; q++) sum += rd[r * nseg + q];
-          y[r0 + r] = sum;
+          out_row(mi, r0 + r, sum);
         }
     }
   }
@@ -677,6 +742,39 @@ cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void 
   return cudaGetLastError();
 }
 
+// The fused single-row matvec (k_matvec with MvArgs): every matrix must take the
+// streaming path (whole 256-element multiples, 16-byte rows and pointers).
+bool matvec_fused_ok(const MvArgs &a, int wtype) {
+  if (a.n < 1 || a.n > 3 || !a.x || a.in_dim <= 0 || a.in_dim % 256 || a.in_dim > MV_CONS * 2048) return false;
+  if (wtype != SQ_Q8_0 && wtype != SQ_Q4_0 && wtype != SQ_BF16) return false;
+  const int pw = wtype == SQ_Q8_0 ? pair_words<SQ_Q8_0>() : (wtype == SQ_Q4_0 ? pair_words<SQ_Q4_0>() : pair_words<SQ_BF16>());
+  if ((size_t)(a.in_dim / 64) * pw * 4 > MV_SLOT) return false;
+  auto al = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+  if (!al(a.x) || (a.xu && !al(a.xu)) || (a.norm_w && !al(a.norm_w))) return false;
+  for (int i = 0; i < a.n; i++)
+    if (!a.w[i] || !al(a.w[i]) || !a.y[i] || a.out_dim[i] <= 0) return false;
+  return true;
+}
+
+template <int T>
+static cudaError_t matvec_fused_t(cudaStream_t s, const MvArgs &a) {
+  const size_t mv_smem = mv_smem_bytes<T>(a.in_dim);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
+    attr_set = true;
+  }
+  k_matvec<T><<<num_sms(), MV_THREADS, mv_smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype) {
+  if (!matvec_fused_ok(a, wtype)) return cudaErrorNotSupported;
+  if (wtype == SQ_Q8_0) return matvec_fused_t<SQ_Q8_0>(s, a);
+  if (wtype == SQ_Q4_0) return matvec_fused_t<SQ_Q4_0>(s, a);
+  return matvec_fused_t<SQ_BF16>(s, a);
+}
+
 template <int T>
 static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, const uint8_t *w, int out_dim,
                          float *y) {
@@ -690,7 +788,14 @@ static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, cons
       cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
       attr_set[ti] = true;
     }
-    k_matvec<T><<<num_sms(), MV_THREADS, mv_smem, s>>>(x, in_dim, w, out_dim, y);
+    MvArgs a{};
+    a.x = x;
+    a.in_dim = in_dim;
+    a.n = 1;
+    a.w[0] = w;
+    a.out_dim[0] = out_dim;
+    a.y[0] = y;
+    k_matvec<T><<<num_sms(), MV_THREADS, mv_smem, s>>>(a);
   } else if (m <= 1)
     k_linear_f32<T, 1><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
   else if (m <= 4)

@@ -16,6 +16,25 @@ cudaError_t launch_linear(cudaStream_t s, const float *x, int m, int in_dim, con
 // The tiled GEMM itself (gemm.cu): y[m][N] = x[m][K] @ w^T, native weight rows.
 cudaError_t launch_gemm_f32w(cudaStream_t s, const float *x, int m, int K, const void *w, int wtype, int N, float *y,
                              float *ws, size_t ws_floats);
+// A fused single-row matvec (one launch of the streaming matvec): up to three
+// matrices of one type and input width over one input row; the input optionally
+// RMS-normalised (rms_norm_f32_into arithmetic, weight norm_w) or formed as
+// silu(x) * xu; each output optionally added to a residual row (may be the output).
+struct MvArgs {
+  const float *x;       // input row [in_dim]
+  const float *xu;      // optional: input = silu(x) * xu
+  const float *norm_w;  // optional: input = (x * norm_w) / sqrt(mean(x^2) + eps)
+  float eps;
+  int in_dim;
+  int n;  // matrices (1..3)
+  const uint8_t *w[3];
+  int out_dim[3];
+  float *y[3];
+  const float *res[3];  // optional residual rows: y[r] = res[r] + dot
+};
+bool matvec_fused_ok(const MvArgs &a, int wtype);
+cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype);
+
 // Tensor-core GEMM (gemm_tc.cu) for BF16, Q8_0 and Q4_0 weight rows: the f32
 // activations are split into three bf16 terms in `ws` (3*m*K/2 floats, then split-K
 // partials). Supported when m >= 2, K % 16 == 0 (quantized: K % 256 == 0 and 16-byte

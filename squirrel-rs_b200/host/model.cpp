@@ -614,7 +614,25 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
                      gemm_tc_supported(n, E, ws, L.v, wt, ws, wsf) && gemm_tc_supported(n, Q, ws, L.o, wt, ws, wsf) &&
                      gemm_tc_supported(n, E, ws, L.gate, wt, ws, wsf) && gemm_tc_supported(n, E, ws, L.up, wt, ws, wsf) &&
                      gemm_tc_supported(n, F, ws, L.down, wt, ws, wsf);
-    if (tcl) {
+    // One-row layer (decode through the op level): the streaming matvec with the norm,
+    // SiLU.mul and residual add folded in, q/k/v and gate/up as one launch each.
+    MvArgs qkv{}, o{}, gu{}, dn{};
+    qkv.x = c->hidden, qkv.norm_w = L.attn_norm, qkv.eps = cf.rms_eps, qkv.in_dim = E, qkv.n = 3;
+    qkv.w[0] = (const uint8_t *)L.q, qkv.w[1] = (const uint8_t *)L.k, qkv.w[2] = (const uint8_t *)L.v;
+    qkv.out_dim[0] = Q, qkv.out_dim[1] = KVd, qkv.out_dim[2] = KVd;
+    qkv.y[0] = c->q, qkv.y[1] = c->k, qkv.y[2] = c->v;
+    o.x = c->attn, o.in_dim = Q, o.n = 1, o.w[0] = (const uint8_t *)L.o, o.out_dim[0] = E;
+    o.y[0] = tp ? c->attn_out : c->hidden, o.res[0] = tp ? nullptr : c->hidden;
+    gu.x = c->hidden, gu.norm_w = L.ffn_norm, gu.eps = cf.rms_eps, gu.in_dim = E, gu.n = 2;
+    gu.w[0] = (const uint8_t *)L.gate, gu.w[1] = (const uint8_t *)L.up, gu.out_dim[0] = F, gu.out_dim[1] = F;
+    gu.y[0] = c->gate, gu.y[1] = c->up;
+    dn.x = c->gate, dn.xu = c->up, dn.in_dim = F, dn.n = 1, dn.w[0] = (const uint8_t *)L.down, dn.out_dim[0] = E;
+    dn.y[0] = tp ? c->ffn_out : c->hidden, dn.res[0] = tp ? nullptr : c->hidden;
+    const bool fused = n == 1 && !aq && matvec_fused_ok(qkv, wt) && matvec_fused_ok(o, wt) &&
+                       matvec_fused_ok(gu, wt) && matvec_fused_ok(dn, wt);
+    if (fused) {
+      TRY(launch_matvec_fused(s, qkv, wt));
+    } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.attn_norm, ws, n, E, cf.rms_eps));
       TRY(launch_gemm_tc_terms(s, n, E, L.q, wt, Q, c->q, ws, wsf));
       TRY(launch_gemm_tc_terms(s, n, E, L.k, wt, KVd, c->k, ws, wsf));
@@ -642,15 +660,20 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs,
                       ns, c->sdpa_part, pos_dev));
     }
-    if (tcl) {
+    if (fused) {
+      TRY(launch_matvec_fused(s, o, wt));  // single GPU: hidden += O.attn in the epilogue
+    } else if (tcl) {
       TRY(launch_split_terms(s, c->attn, n, Q, ws));
       TRY(launch_gemm_tc_terms(s, n, Q, L.o, wt, E, c->attn_out, ws, wsf));
     } else {
       TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, ws, wsf));
     }
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
-    TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
-    if (tcl) {
+    if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
+    if (fused) {
+      TRY(launch_matvec_fused(s, gu, wt));
+      TRY(launch_matvec_fused(s, dn, wt));  // SiLU(gate) * up formed as it is read
+    } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
       TRY(launch_gemm_tc_terms(s, n, E, L.gate, wt, F, c->gate, ws, wsf));
       TRY(launch_gemm_tc_terms(s, n, E, L.up, wt, F, c->up, ws, wsf));
@@ -665,14 +688,22 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, ws, wsf));
     }
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));  // row-parallel down
-    TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
+    if (!fused || tp) TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
   }
   c->seq_len += n;
   if (last) {
     // final norm of the last row only: rows are normalized independently (model.rs:72-87)
-    TRY(launch_rms_norm(s, c->hidden + (size_t)(n - 1) * E, m->out_norm, c->normed, 1, E, cf.rms_eps));
-    TRY(launch_linear(s, c->normed, 1, E, m->out_w, m->out_type, cf.vocab_size, c->logits,
-                      m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16, c->xq, c->gemm_ws, c->gemm_ws_floats));
+    MvArgs lm{};
+    lm.x = c->hidden + (size_t)(n - 1) * E, lm.norm_w = m->out_norm, lm.eps = cf.rms_eps, lm.in_dim = E, lm.n = 1;
+    lm.w[0] = (const uint8_t *)m->out_w, lm.out_dim[0] = cf.vocab_size, lm.y[0] = c->logits;
+    const bool lm_q8 = m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16;
+    if (!lm_q8 && matvec_fused_ok(lm, m->out_type)) {
+      TRY(launch_matvec_fused(s, lm, m->out_type));  // the norm folded into the LM head
+    } else {
+      TRY(launch_rms_norm(s, c->hidden + (size_t)(n - 1) * E, m->out_norm, c->normed, 1, E, cf.rms_eps));
+      TRY(launch_linear(s, c->normed, 1, E, m->out_w, m->out_type, cf.vocab_size, c->logits, lm_q8, c->xq,
+                        c->gemm_ws, c->gemm_ws_floats));
+    }
     if (!tp) {
       TRY(launch_argmax(s, c->logits, cf.vocab_size, c->argmax_part, c->d_argmax));
     } else {  // greedy over the vocabulary shards: per-rank states, folded in rank (= index) order

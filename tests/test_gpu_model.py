@@ -57,6 +57,29 @@ def test_generate_matches_oracle(gpu_lib, models, spec, wt):
     ctx.close()
 
 
+@pytest.mark.parametrize("wt", ["q8_0", "q4_0", "bf16"])
+def test_op_level_decode(gpu_lib, models, wt, monkeypatch):
+    """Decode without the persistent kernel (the path of tensor-parallel and
+    unsupported shapes): one fused matvec launch for q/k/v and for gate/up, RMSNorm,
+    SiLU.mul and the residual adds folded into the matvecs; steps replayed from a
+    CUDA graph. Identical ids and logits within tolerance."""
+    monkeypatch.setenv("SQ_DISABLE_DECODE_KERNEL", "1")  # read when the context is created
+    spec = "small"
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(8, seed=13, high=G.SPECS[spec]["vocab"])
+    ref = O.Model(path)
+    ids_ref, _, logits_ref = ref.generate(prompt, 12, want_logits=True)
+    m = gpu_model(models, spec, wt, 0)
+    ctx = m.new_context(128)
+    assert ctx.launches_per_token > 1
+    assert ctx.forward(prompt) == ids_ref[0]
+    assert_logits_close(ctx.logits(), logits_ref[0])
+    rest = ctx.decode_steps(11)  # eager step, then graph capture and replays
+    assert np.array_equal(rest, ids_ref[1:12])
+    assert_logits_close(ctx.logits(), logits_ref[11])
+    ctx.close()
+
+
 Q8_ACTS_ABS_TOL = 5e-2
 
 
