@@ -3,8 +3,9 @@
 // 0..=offset+t, max-subtracted softmax, probability-weighted sum of V).
 //
 // One CTA per (query row t, head h, key split). Each of the 4 warps walks a
-// strided subset of the split's keys with an online softmax (running max m,
-// running sum l, accumulator a[d]); lanes own head_dim/32 dimensions each, so K
+// strided subset of the split's keys, four consecutive keys at a time, with an
+// online softmax (running max m, running sum l, accumulator a[d]); lanes own
+// head_dim/32 dimensions each, so K
 // and V rows are read coalesced. Warp states are merged in shared memory; with
 // one split the CTA writes out = a * (1/l), otherwise it writes (m, l, a) and
 // k_sdpa_combine merges the splits.
@@ -16,6 +17,7 @@
 namespace sq {
 
 constexpr int SDPA_WARPS = 4;
+constexpr int SDPA_KPI = 4;  // keys a warp iteration
 constexpr int SDPA_MAX_HD = 256;
 
 template <int DPL>  // dims per lane = head_dim / 32
@@ -45,19 +47,50 @@ __global__ void __launch_bounds__(SDPA_WARPS * 32)
   for (int i = 0; i < DPL; i++) acc[i] = 0.f;
 
   const float *kb = k + g * khs, *vb = v + g * khs;
-  for (int s = k0 + wid; s < k1; s += SDPA_WARPS) {
-    const float *kr = kb + (size_t)s * kps;
-    float d = 0.f;
+  // four consecutive keys a warp iteration: their loads, dots and reductions are
+  // independent, so one key's latency hides behind the others'
+  for (int s = k0 + SDPA_KPI * wid; s < k1; s += SDPA_KPI * SDPA_WARPS) {
+    float d[SDPA_KPI], vv[SDPA_KPI][DPL];
 #pragma unroll
-    for (int i = 0; i < DPL; i++) d = fmaf(qv[i], kr[lane + 32 * i], d);
-    const float sc = warp_sum(d) * scale;
-    const float mn = fmaxf(m, sc);
-    const float corr = expf(m - mn);  // 0 on the first key (m = -inf)
-    const float p = expf(sc - mn);
-    l = l * corr + p;
-    const float *vr = vb + (size_t)s * kps;
+    for (int j = 0; j < SDPA_KPI; j++) {
+      d[j] = 0.f;
+      if (s + j < k1) {
+        const float *kr = kb + (size_t)(s + j) * kps, *vr = vb + (size_t)(s + j) * kps;
 #pragma unroll
-    for (int i = 0; i < DPL; i++) acc[i] = fmaf(p, vr[lane + 32 * i], acc[i] * corr);
+        for (int i = 0; i < DPL; i++) {
+          d[j] = fmaf(qv[i], kr[lane + 32 * i], d[j]);
+          vv[j][i] = vr[lane + 32 * i];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; i++) vv[j][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < SDPA_KPI; j++) d[j] += __shfl_xor_sync(0xffffffffu, d[j], o);
+    float sc[SDPA_KPI], mn = m;
+#pragma unroll
+    for (int j = 0; j < SDPA_KPI; j++) {
+      sc[j] = s + j < k1 ? d[j] * scale : -INFINITY;
+      mn = fmaxf(mn, sc[j]);
+    }
+    const float corr = expf(m - mn);  // 0 on the first keys (m = -inf); key s is always live
+    float p[SDPA_KPI], ps = 0.f;
+#pragma unroll
+    for (int j = 0; j < SDPA_KPI; j++) {
+      p[j] = expf(sc[j] - mn);  // 0 past the live keys
+      ps += p[j];
+    }
+    l = l * corr + ps;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) {
+      float a = acc[i] * corr;
+#pragma unroll
+      for (int j = 0; j < SDPA_KPI; j++) a = fmaf(p[j], vv[j][i], a);
+      acc[i] = a;
+    }
     m = mn;
   }
 
@@ -126,7 +159,7 @@ __global__ void k_sdpa_combine(const float *__restrict__ part, float *__restrict
 int sdpa_num_splits(int seq_q, int seq_k, int n_heads) {
   const long long rows = (long long)seq_q * n_heads;
   if (rows >= 2 * 148) return 1;
-  int ns = (seq_k + 255) / 256;
+  int ns = (seq_k + 31) / 32;  // at least 32 keys a split (two iterations of the CTA's warps)
   const int want = (int)((4 * 148 + rows - 1) / rows);
   if (ns > want) ns = want;
   if (ns > 64) ns = 64;
