@@ -122,17 +122,22 @@ __global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x,
 // groups of nseg warps, warp `seg` of a group keeps its input segment in registers
 // (lane j holds elements 64j .. 64j+63, read once) and takes that segment of rows
 // g, g + G, .. of every tile (two rows at a time, four for Q4_0: independent dots,
-// one joint reduction); lane j reads pair j of the row from shared memory. With one segment
-// the warp writes the row; otherwise the partial sums meet in shared memory and
-// warp 0 adds them in segment order (deterministic). Rows must be whole multiples of
-// 256 elements (16-byte row starts) and in_dim <= 8 * 2048 (the caller checks).
+// one joint reduction); lane j reads pair j of the row from shared memory. With one
+// segment the warp writes the row; otherwise the partial sums go to the slot's
+// buffer in shared memory and the producer warp adds them in segment order
+// (deterministic) once every consumer has released the slot, so consumers never
+// wait on each other. The input may be RMS-normalised or formed as silu(x) * up as
+// it is read, and outputs may be added to a residual row (MvArgs). Rows must be
+// whole multiples of 256 elements (16-byte row starts) and in_dim <= 8 * 2048 (the
+// caller checks).
 // Waits are bounded (~2 s); on expiry the warp records an error and stops.
 constexpr int MV_CONS = 8;                     // consumer warps
 constexpr int MV_THREADS = 32 * (MV_CONS + 1);  // + the producer warp
 constexpr int MV_SLOT = 36864;                 // bytes per ring slot
 constexpr int MV_NS = 5;                       // ring slots
 constexpr int MV_TRMAX = 64;                   // rows per tile at most
-constexpr int MV_HDR = 2 * MV_NS * 8 + (2 * MV_TRMAX + 1) * MV_CONS * 4;  // mbarriers + partial sums
+constexpr int MV_REDROWS = 32;                 // rows per tile when rows are split into segments
+constexpr int MV_HDR = 2 * MV_NS * 8 + (MV_NS * MV_REDROWS + 1) * MV_CONS * 4;  // mbarriers + partial sums
 constexpr int MV_RING_OFF = (MV_HDR + 127) & ~127;
 
 __device__ unsigned g_mv_err;  // set when a bounded wait of k_matvec gave up
@@ -180,7 +185,11 @@ __device__ __forceinline__ void mv_load_pair(uint32_t a, int lane, uint32_t (&wv
 
 __device__ __forceinline__ float silu_ref(float x);
 
-template <int T>
+// MODE: what is folded into the input read (MV_PLAIN, MV_NORM, MV_SILU): a separate
+// instantiation each, so the plain matvec carries none of that code.
+constexpr int MV_PLAIN = 0, MV_NORM = 1, MV_SILU = 2, MV_GENERAL = 3;  // GENERAL: several matrices or residuals
+
+template <int T, int MODE>
 __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant__ MvArgs a) {
   constexpr int PW = pair_words<T>(), CB = 32 * PW * 4;
   extern __shared__ __align__(128) uint8_t mv_smem[];
@@ -191,19 +200,20 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
   const int ncons = G * nseg;
   const int np = in_dim / 64;               // pairs per row
   const int rb = np * PW * 4;               // row bytes (a multiple of 16)
-  int TR = min(MV_TRMAX, MV_SLOT / rb);  // rows per tile (>= 1: rows fit a slot) ...
+  int TR = min(nseg > 1 ? MV_REDROWS : MV_TRMAX, MV_SLOT / rb);  // rows per tile (>= 1: rows fit a slot) ...
   if (TR >= G) TR -= TR % G;             // ... a multiple of the row groups: even work per warp
-  // each CTA owns a contiguous block of rows of every matrix: [b0, b1) of matrix i
-  auto block_of = [&](int i, int &b0, int &b1) {
-    const int od = i < a.n ? a.out_dim[i] : 0;
-    const int per = (od + gridDim.x - 1) / gridDim.x;
-    b0 = blockIdx.x * per;
-    b1 = min(od, b0 + per);
-  };
-  int s00, s01, s10, s11, s20, s21;
-  block_of(0, s00, s01);
-  block_of(1, s10, s11);
-  block_of(2, s20, s21);
+  // Fields of `a` are read by name only (never through its address, e.g. by a
+  // lambda's reference capture), so they stay operands from the parameter bank.
+#define MV_SEL(f, mi) ((mi) == 0 ? a.f[0] : ((mi) == 1 ? a.f[1] : a.f[2]))
+  // each CTA owns a contiguous block of rows of every matrix: [sX0, sX1) of matrix X
+  // the plain mode has one matrix and no residual (known at compile time)
+  const int od0 = a.out_dim[0], od1 = MODE != MV_PLAIN && a.n > 1 ? a.out_dim[1] : 0,
+            od2 = MODE != MV_PLAIN && a.n > 2 ? a.out_dim[2] : 0;
+  const int pe0 = (od0 + gridDim.x - 1) / gridDim.x, pe1 = (od1 + gridDim.x - 1) / gridDim.x,
+            pe2 = (od2 + gridDim.x - 1) / gridDim.x;
+  const int s00 = blockIdx.x * pe0, s01 = min(od0, s00 + pe0);
+  const int s10 = blockIdx.x * pe1, s11 = min(od1, s10 + pe1);
+  const int s20 = blockIdx.x * pe2, s21 = min(od2, s20 + pe2);
   auto ntile = [&](int b0, int b1) { return b1 > b0 ? (b1 - b0 + TR - 1) / TR : 0; };
   const int nt0 = ntile(s00, s01), nt1 = ntile(s10, s11), nt2 = ntile(s20, s21);
   const int ntiles = nt0 + nt1 + nt2;
@@ -227,8 +237,17 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     rows = min(TR, b1 - r0);
   };
   const uint32_t full = mv_su32(mv_smem), empty = full + 8u * MV_NS;
-  float *red = reinterpret_cast<float *>(mv_smem + 2 * MV_NS * 8);  // [2][MV_TRMAX][nseg], then [MV_CONS]
+  float *red = reinterpret_cast<float *>(mv_smem + 2 * MV_NS * 8);  // [MV_NS][MV_REDROWS][nseg], then [MV_CONS]
   const uint32_t ring = mv_su32(mv_smem + MV_RING_OFF);
+#define MV_OUT_ROW(mi, row, v)                                    \
+  do {                                                            \
+    if constexpr (MODE == MV_PLAIN) {                             \
+      a.y[0][row] = (v);                                          \
+    } else {                                                      \
+      const float *rs_ = MV_SEL(res, mi);                          \
+      MV_SEL(y, mi)[row] = rs_ ? __fadd_rn(rs_[row], (v)) : (v);  \
+    }                                                             \
+  } while (0)
   if (threadIdx.x == 0) {
     for (int i = 0; i < MV_NS; i++) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(full + 8u * i) : "memory");
@@ -237,14 +256,43 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (warp == MV_CONS) {  // producer
-    if (lane == 0) {
-      uint64_t pol;
-      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-      int issued = 0;
-      for (int t = 0; t < ntiles; t++) {
-        const int slot = t % MV_NS;
-        if (t >= MV_NS && !mv_wait(empty + 8u * slot, (unsigned)((t / MV_NS) - 1) & 1u)) break;
+  if (warp == MV_CONS) {
+    // producer: streams the tiles; with segments it also adds each tile's partial
+    // sums (in segment order) once every consumer has released the tile's slot
+    uint64_t pol = 0;
+    if (lane == 0) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    // the outputs as locals (the lambda below must not capture `a`)
+    float *const py0 = a.y[0], *const py1 = a.y[1], *const py2 = a.y[2];
+    const float *const pr0 = a.res[0], *const pr1 = a.res[1], *const pr2 = a.res[2];
+    auto finish = [&](int t) {
+      int mi, r0, rows;
+      tile_of(t, mi, r0, rows);
+      float *yp = mi == 0 ? py0 : (mi == 1 ? py1 : py2);
+      const float *rp = mi == 0 ? pr0 : (mi == 1 ? pr1 : pr2);
+      const float *rd = red + (t % MV_NS) * MV_REDROWS * nseg;
+      for (int r = lane; r < rows; r += 32) {
+        float sum = rd[r * nseg];
+        for (int q = 1; q < nseg; q++) sum += rd[r * nseg + q];
+        yp[r0 + r] = rp ? __fadd_rn(rp[r0 + r], sum) : sum;
+      }
+    };
+    const bool solo = nseg == 1;  // nothing to finish: lane 0 alone streams the tiles
+    if (solo && lane != 0) return;
+    auto wait_empty = [&](int t) -> bool {  // the consumers are done with tile t
+      if (solo) return mv_wait(empty + 8u * (t % MV_NS), (unsigned)(t / MV_NS) & 1u);
+      int ok = 1;
+      if (lane == 0) ok = mv_wait(empty + 8u * (t % MV_NS), (unsigned)(t / MV_NS) & 1u);
+      return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+    int issued = 0, finished = 0;
+    for (int t = 0; t < ntiles; t++) {
+      const int slot = t % MV_NS;
+      if (t >= MV_NS) {
+        if (!wait_empty(t - MV_NS)) break;
+        if (nseg > 1) finish(t - MV_NS);
+        finished = t - MV_NS + 1;
+      }
+      if (lane == 0) {
         int mi, r0, rows;
         tile_of(t, mi, r0, rows);
         const unsigned bytes = (unsigned)(rows * rb);
@@ -253,16 +301,22 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
         asm volatile(
             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
                 ring + (uint32_t)slot * MV_SLOT),
-            "l"(a.w[mi] + (size_t)r0 * rb), "r"(bytes), "r"(full + 8u * slot), "l"(pol)
+            "l"(MV_SEL(w, mi) + (size_t)r0 * rb), "r"(bytes), "r"(full + 8u * slot), "l"(pol)
             : "memory");
-        issued = t + 1;
       }
+      issued = t + 1;
+    }
+    if (nseg > 1 && issued == ntiles)  // the last tiles' partial sums
+      for (int t = finished; t < ntiles; t++) {
+        if (!wait_empty(t)) break;
+        finish(t);
+      }
+    if (lane == 0)
       for (int t = max(0, issued - MV_NS); t < issued; t++) {  // drain: copies land before exit
         const long long t0 = clock64();
         while (!mv_try_wait(full + 8u * (t % MV_NS), (unsigned)(t / MV_NS) & 1u) && clock64() - t0 < 4000000000LL) {
         }
       }
-    }
     return;
   }
   if (warp >= ncons) return;
@@ -270,7 +324,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
   const int pairs = min(32, np - seg * 32);  // pairs in this segment (>= 1)
   const bool active = lane < pairs;
   float rms = 1.f;
-  if (a.norm_w) {  // the consumers' sum of squares over the whole row, in a fixed order
+  if constexpr (MODE == MV_NORM) {  // the consumers' sum of squares over the whole row, in a fixed order
     float ss = 0.f;
     for (int e = 4 * (warp * 32 + lane); e < in_dim; e += 4 * 32 * ncons) {
       const float4 v = __ldg(reinterpret_cast<const float4 *>(a.x + e));
@@ -280,7 +334,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
       ss = fmaf(v.w, v.w, ss);
     }
     ss = warp_sum(ss);
-    float *part = red + 2 * MV_TRMAX * MV_CONS;  // [MV_CONS]
+    float *part = red + MV_NS * MV_REDROWS * MV_CONS;  // [MV_CONS]
     if (lane == 0) part[warp] = ss;
     asm volatile("bar.sync 1, %0;" ::"r"(32 * ncons) : "memory");
     float tot = part[0];
@@ -294,12 +348,12 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     for (int k = 0; k < 16; k++) {  // BF16: 8-element chunk i holds chunk i ^ (lane % 8), as the weights
       const int src = T == SQ_BF16 ? ((((k >> 1) ^ (lane & 7)) << 1) | (k & 1)) : k;
       float4 f = __ldg(reinterpret_cast<const float4 *>(a.x + base) + src);
-      if (a.xu) {  // SiLU(gate) * up (silu.rs, elementwise_mul.rs)
+      if constexpr (MODE == MV_SILU) {  // SiLU(gate) * up (silu.rs, elementwise_mul.rs)
         const float4 u = __ldg(reinterpret_cast<const float4 *>(a.xu + base) + src);
         f = make_float4(__fmul_rn(silu_ref(f.x), u.x), __fmul_rn(silu_ref(f.y), u.y), __fmul_rn(silu_ref(f.z), u.z),
                         __fmul_rn(silu_ref(f.w), u.w));
       }
-      if (a.norm_w) {  // (x * w) / rms, as k_rms_norm_v rounds it
+      if constexpr (MODE == MV_NORM) {  // (x * w) / rms, as k_rms_norm_v rounds it
         const float4 gw = __ldg(reinterpret_cast<const float4 *>(a.norm_w + base) + src);
         f = make_float4(__fdiv_rn(__fmul_rn(f.x, gw.x), rms), __fdiv_rn(__fmul_rn(f.y, gw.y), rms),
                         __fdiv_rn(__fmul_rn(f.z, gw.z), rms), __fdiv_rn(__fmul_rn(f.w, gw.w), rms));
@@ -311,20 +365,15 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
 #pragma unroll
     for (int k = 0; k < 32; k++) x2[k] = 0ull;
   }
-  auto out_row = [&](int mi, int row, float v) {
-    a.y[mi][row] = a.res[mi] ? __fadd_rn(a.res[mi][row], v) : v;
-  };
   for (int t = 0; t < ntiles; t++) {
     const int slot = t % MV_NS;
     int ok = 1;
     if (lane == 0) ok = mv_wait(full + 8u * slot, (unsigned)(t / MV_NS) & 1u);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (!ok && nseg == 1) break;  // (with segments every warp reaches the vote below first)
+    if (!__shfl_sync(0xffffffffu, ok, 0)) break;
     int mi, r0, rows;
     tile_of(t, mi, r0, rows);
-    if (!ok) rows = 0;
     const uint32_t tile = ring + (uint32_t)slot * MV_SLOT + (uint32_t)seg * CB + (uint32_t)lane * PW * 4;
-    float *rd = red + (t & 1) * MV_TRMAX * nseg;
+    float *rd = red + slot * MV_REDROWS * nseg;  // partial sums, added by the producer
     constexpr int RI = T == SQ_Q4_0 ? 4 : 2;  // rows an iteration: independent dot chains
     for (int r = g; r < rows; r += RI * G) {  // rows r, r + G, .. of the tile
       float d[RI];
@@ -348,33 +397,17 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
         for (int q = 0; q < RI; q++) {
           const int rr = r + q * G;
           if (rr < rows) {
-            if (nseg == 1) out_row(mi, r0 + rr, d[q]);
+            if (nseg == 1) MV_OUT_ROW(mi, r0 + rr, d[q]);
             else rd[rr * nseg + seg] = d[q];
           }
         }
       }
     }
-    __syncwarp();  // every lane is done with the slot
+    __syncwarp();  // every lane is done with the slot (and lane 0's partial sums are written)
     if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty + 8u * slot) : "memory");
-    if (nseg > 1) {  // partial sums of the tile's rows, added in segment order
-      unsigned all_ok;  // the consumers' vote doubles as the barrier: they stop together
-      asm volatile(
-          "{\n\t.reg .pred p, q;\n\t"
-          "setp.ne.u32 p, %1, 0;\n\t"
-          "bar.red.and.pred q, 1, %2, p;\n\t"
-          "selp.u32 %0, 1, 0, q;\n\t}"
-          : "=r"(all_ok)
-          : "r"((unsigned)ok), "r"(32 * ncons)
-          : "memory");
-      if (!all_ok) break;
-      if (warp == 0)
-        for (int r = lane; r < rows; r += 32) {
-          float sum = rd[r * nseg];
-          for (int q = 1; q < nseg; q++) sum += rd[r * nseg + q];
-          out_row(mi, r0 + r, sum);
-        }
-    }
   }
+#undef MV_OUT_ROW
+#undef MV_SEL
 }
 
 template <int T>
@@ -750,22 +783,29 @@ bool matvec_fused_ok(const MvArgs &a, int wtype) {
   const int pw = wtype == SQ_Q8_0 ? pair_words<SQ_Q8_0>() : (wtype == SQ_Q4_0 ? pair_words<SQ_Q4_0>() : pair_words<SQ_BF16>());
   if ((size_t)(a.in_dim / 64) * pw * 4 > MV_SLOT) return false;
   auto al = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
-  if (!al(a.x) || (a.xu && !al(a.xu)) || (a.norm_w && !al(a.norm_w))) return false;
+  if (!al(a.x) || (a.xu && !al(a.xu)) || (a.norm_w && !al(a.norm_w)) || (a.xu && a.norm_w)) return false;
   for (int i = 0; i < a.n; i++)
     if (!a.w[i] || !al(a.w[i]) || !a.y[i] || a.out_dim[i] <= 0) return false;
   return true;
 }
 
-template <int T>
-static cudaError_t matvec_fused_t(cudaStream_t s, const MvArgs &a) {
+template <int T, int MODE>
+static cudaError_t matvec_mode_t(cudaStream_t s, const MvArgs &a) {
   const size_t mv_smem = mv_smem_bytes<T>(a.in_dim);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
+    cudaFuncSetAttribute(k_matvec<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
     attr_set = true;
   }
-  k_matvec<T><<<num_sms(), MV_THREADS, mv_smem, s>>>(a);
+  k_matvec<T, MODE><<<num_sms(), MV_THREADS, mv_smem, s>>>(a);
   return cudaGetLastError();
+}
+template <int T>
+static cudaError_t matvec_fused_t(cudaStream_t s, const MvArgs &a) {
+  if (a.norm_w) return matvec_mode_t<T, MV_NORM>(s, a);
+  if (a.xu) return matvec_mode_t<T, MV_SILU>(s, a);
+  if (a.n > 1 || a.res[0]) return matvec_mode_t<T, MV_GENERAL>(s, a);
+  return matvec_mode_t<T, MV_PLAIN>(s, a);
 }
 
 cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype) {
@@ -782,12 +822,6 @@ static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, cons
   const size_t mv_smem = mv_smem_bytes<T>(in_dim);
   if (m == 1 && in_dim % 256 == 0 && in_dim <= MV_CONS * 2048 && (size_t)(in_dim / 64) * pair_words<T>() * 4 <= MV_SLOT &&
       ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0) {  // 16-byte row starts; a row fits a slot
-    static bool attr_set[3] = {false, false, false};
-    const int ti = T == SQ_Q8_0 ? 0 : (T == SQ_Q4_0 ? 1 : 2);
-    if (!attr_set[ti]) {
-      cudaFuncSetAttribute(k_matvec<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
-      attr_set[ti] = true;
-    }
     MvArgs a{};
     a.x = x;
     a.in_dim = in_dim;
@@ -795,7 +829,7 @@ static void linear_f32_t(cudaStream_t s, const float *x, int m, int in_dim, cons
     a.w[0] = w;
     a.out_dim[0] = out_dim;
     a.y[0] = y;
-    k_matvec<T><<<num_sms(), MV_THREADS, mv_smem, s>>>(a);
+    matvec_mode_t<T, MV_PLAIN>(s, a);
   } else if (m <= 1)
     k_linear_f32<T, 1><<<grid, 256, 0, s>>>(x, m, in_dim, w, out_dim, y);
   else if (m <= 4)
