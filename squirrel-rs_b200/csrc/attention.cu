@@ -7,8 +7,9 @@
 // online softmax (running max m, running sum l, accumulator a[d]); lanes own
 // head_dim/32 dimensions each, so K
 // and V rows are read coalesced. Warp states are merged in shared memory; with
-// one split the CTA writes out = a * (1/l), otherwise it writes (m, l, a) and
-// k_sdpa_combine merges the splits.
+// one split the CTA writes out = a * (1/l), otherwise it writes (m, l, a) and the
+// splits are merged in split order: by k_sdpa_combine, or (with a counter per query
+// row) by the row's last CTA to finish, which saves a launch per call.
 #include <math.h>
 
 #include "common.cuh"
@@ -20,11 +21,39 @@ constexpr int SDPA_WARPS = 4;
 constexpr int SDPA_KPI = 4;  // keys a warp iteration
 constexpr int SDPA_MAX_HD = 256;
 
+// Merge the n_split partials (m, l, a[hd]) of one query row in split order
+// (splits without keys carry l = 0 and are skipped); threads stride the dimensions.
+__device__ __forceinline__ void combine_row(const float *pp, float *out_row, int n_split, int hd) {
+  float M = -INFINITY;
+  for (int i = 0; i < n_split; i++)
+    if (__ldcg(pp + i * (hd + 2) + 1) > 0.f) M = fmaxf(M, __ldcg(pp + i * (hd + 2)));
+  float L = 0.f;
+  for (int i = 0; i < n_split; i++) {
+    const float l = __ldcg(pp + i * (hd + 2) + 1);
+    if (l > 0.f) L = fmaf(l, expf(__ldcg(pp + i * (hd + 2)) - M), L);
+  }
+  const float inv = 1.0f / L;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float a = 0.f;
+    for (int i = 0; i < n_split; i++) {
+      const float l = __ldcg(pp + i * (hd + 2) + 1);
+      if (l > 0.f) a = fmaf(__ldcg(pp + i * (hd + 2) + 2 + d), expf(__ldcg(pp + i * (hd + 2)) - M), a);
+    }
+    out_row[d] = a * inv;
+  }
+}
+
+__global__ void k_sdpa_combine(const float *__restrict__ part, float *__restrict__ out, int n_split, int hd) {
+  const int row = blockIdx.x;
+  combine_row(part + (size_t)row * n_split * (hd + 2), out + (size_t)row * hd, n_split, hd);
+}
+
 template <int DPL>  // dims per lane = head_dim / 32
 __global__ void __launch_bounds__(SDPA_WARPS * 32)
     k_sdpa(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
            float *__restrict__ out, float *__restrict__ part, int seq_q, int seq_k, int n_heads,
-           int group, long long kps, long long khs, int split_len, float scale, const int *__restrict__ pos_dev) {
+           int group, long long kps, long long khs, int split_len, float scale, const int *__restrict__ pos_dev,
+           int *__restrict__ split_cnt) {
   const int hd = DPL * 32;
   if (pos_dev) {  // the keys end at the position the device holds (graph replay: no host values)
     seq_k = *pos_dev + seq_q;
@@ -129,27 +158,16 @@ __global__ void __launch_bounds__(SDPA_WARPS * 32)
       for (int i = 0; i < DPL; i++) pp[2 + lane + 32 * i] = A[i];
     }
   }
-}
-
-__global__ void k_sdpa_combine(const float *__restrict__ part, float *__restrict__ out, int n_split, int hd) {
-  const int row = blockIdx.x;
-  const float *pp = part + (size_t)row * n_split * (hd + 2);
-  float M = -INFINITY;
-  for (int i = 0; i < n_split; i++)
-    if (pp[i * (hd + 2) + 1] > 0.f) M = fmaxf(M, pp[i * (hd + 2)]);
-  float L = 0.f;
-  for (int i = 0; i < n_split; i++) {
-    const float l = pp[i * (hd + 2) + 1];
-    if (l > 0.f) L = fmaf(l, expf(pp[i * (hd + 2)] - M), L);
-  }
-  const float inv = 1.0f / L;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float a = 0.f;
-    for (int i = 0; i < n_split; i++) {
-      const float l = pp[i * (hd + 2) + 1];
-      if (l > 0.f) a = fmaf(pp[i * (hd + 2) + 2 + d], expf(pp[i * (hd + 2)] - M), a);
-    }
-    out[(size_t)row * hd + d] = a * inv;
+  if (n_split > 1 && split_cnt) {  // the row's last CTA to finish merges the splits
+    __shared__ int last;
+    __threadfence();  // this CTA's partials are visible before its arrival is counted
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(split_cnt + row, 1) == n_split - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    combine_row(part + (size_t)row * n_split * (hd + 2), out + (size_t)row * hd, n_split, hd);
+    if (threadIdx.x == 0) split_cnt[row] = 0;  // ready for the next call
   }
 }
 
@@ -175,22 +193,22 @@ size_t sdpa_max_partials_floats(int head_dim) { return (size_t)SDPA_MAX_ROW_SPLI
 
 cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
                         int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
-                        int n_split, float *part, const int *pos_dev) {
+                        int n_split, float *part, const int *pos_dev, int *split_cnt) {
   const int group = n_heads / n_kv_heads;
   const float scale = 1.0f / sqrtf((float)head_dim);  // attention.rs:37
   const int split_len = (seq_k + n_split - 1) / n_split;
   dim3 grid(seq_q * n_heads, n_split);
   switch (head_dim / 32) {
-    case 1: k_sdpa<1><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    case 2: k_sdpa<2><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    case 3: k_sdpa<3><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    case 4: k_sdpa<4><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    case 5: k_sdpa<5><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    case 6: k_sdpa<6><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    case 7: k_sdpa<7><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
-    default: k_sdpa<8><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev); break;
+    case 1: k_sdpa<1><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 2: k_sdpa<2><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 3: k_sdpa<3><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 4: k_sdpa<4><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 5: k_sdpa<5><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 6: k_sdpa<6><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 7: k_sdpa<7><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    default: k_sdpa<8><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
   }
-  if (n_split > 1) k_sdpa_combine<<<seq_q * n_heads, 64, 0, s>>>(part, out, n_split, head_dim);
+  if (n_split > 1 && !split_cnt) k_sdpa_combine<<<seq_q * n_heads, 64, 0, s>>>(part, out, n_split, head_dim);
   return cudaGetLastError();
 }
 

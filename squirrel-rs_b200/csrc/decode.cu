@@ -43,7 +43,7 @@ constexpr int NTHREADS = NC * 32;
 constexpr int NG = NC / 2;               // warps per group (the groups take alternate tiles)
 constexpr int SLOT = 36864;              // bytes per ring slot
 constexpr int NSLOT = 5;
-constexpr int PF_TILES = 12;             // tiles prefetched into L2 beyond the ring
+constexpr int PF_TILES = 0;              // tiles prefetched into L2 beyond the ring (off: measured faster)
 constexpr int MAX_LAYERS = 128;
 constexpr int MAX_TILE_ITEMS = 256;      // rows x segments per tile
 constexpr int MAX_X = 8192;              // longest stage input staged in shared memory (floats)
@@ -651,7 +651,7 @@ __device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) 
 
 // Issue tile j of this CTA's table into `slot`: bulk copies completing on full[slot].
 // The weights are read once per token, so the copies mark their L2 lines
-// evict-first; what the L2 keeps is the prefetched tiles not yet consumed.
+// evict-first; what the L2 keeps is the (optional) prefetched tiles not yet consumed.
 __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
   const int2 d = tbl[j];
   if (p.tile_tl) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + j) * 3] = (unsigned long long)clock64();
@@ -1422,6 +1422,12 @@ int decode_prepare(sq_ctx *c) {
   h.tile_rows[dk::ST_GU] = rows_fit(rbE, 2);
   h.tile_rows[dk::ST_DOWN] = rows_fit(rbF, 1);
   h.tile_rows[dk::ST_LM] = rows_fit(rbE, 1);
+  if (const char *tr = getenv("SQ_DECODE_TILE_ROWS")) {  // tuning: caps "qkv,o,gu,down,lm" (even, >= 2)
+    int v[5];
+    if (sscanf(tr, "%d,%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3], &v[4]) == 5)
+      for (int k = 0; k < 5; k++)
+        if (v[k] >= 2) h.tile_rows[k] = std::min(h.tile_rows[k], v[k] & ~1);
+  }
   for (int k = 0; k < 5; k++) {
     const int nseg = k == dk::ST_O ? nQ : (k == dk::ST_DOWN ? nF : nE);
     ok = ok && h.tile_rows[k] >= 2 && h.tile_rows[k] * (k == dk::ST_GU ? 2 : 1) * nseg <= dk::MAX_TILE_ITEMS;

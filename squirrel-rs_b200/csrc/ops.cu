@@ -1208,6 +1208,57 @@ cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, flo
                                                                                   pos, max_ctx, pos_dev);
   return cudaGetLastError();
 }
+
+// RoPE of the q and k rows (rope.rs:7-36, the cos/sin table of k_rope_table) and the
+// append of the rotated K and the V rows to the cache (kv_cache.rs:8-78), one launch:
+// work item p of a row is q pair p (p < Q/2), k pair p - Q/2, or v pair p - Q/2 - KVd/2.
+// The arithmetic is k_rope_table's and k_kv_append's; q is rotated in place, k only
+// into the cache.
+__global__ void k_rope_append(float *q, const float *__restrict__ k, const float *__restrict__ v, float *kc,
+                              float *vc, int n, int Q, int KVd, int hd, int max_ctx, int pos,
+                              const float *__restrict__ cos_t, const float *__restrict__ sin_t,
+                              const int *__restrict__ pos_dev) {
+  if (pos_dev) pos = *pos_dev;
+  const int half = hd / 2, qp = Q / 2, kp = KVd / 2, per = qp + 2 * kp;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < (long long)n * per;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(idx / per), p = (int)(idx % per);
+    if (p < qp + kp) {
+      const int pr = p < qp ? p : p - qp;  // pair index within the q or k row
+      const size_t t = (size_t)(pos + r) * half + pr % half;
+      const float c = cos_t[t], sn = sin_t[t];
+      const float *src = p < qp ? q + (size_t)r * Q + 2 * pr : k + (size_t)r * KVd + 2 * pr;
+      const float a = src[0], b = src[1];
+      const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+      const float rb = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+      if (p < qp) {
+        float *e = q + (size_t)r * Q + 2 * pr;
+        e[0] = ra;
+        e[1] = rb;
+      } else {
+        const int g = 2 * pr / hd, d = 2 * pr % hd;
+        float *dst = kc + ((size_t)g * max_ctx + pos + r) * hd + d;
+        dst[0] = ra;
+        dst[1] = rb;
+      }
+    } else {
+      const int pv = p - qp - kp, g = 2 * pv / hd, d = 2 * pv % hd;
+      const float *src = v + (size_t)r * KVd + 2 * pv;
+      float *dst = vc + ((size_t)g * max_ctx + pos + r) * hd + d;
+      dst[0] = src[0];
+      dst[1] = src[1];
+    }
+  }
+}
+
+cudaError_t launch_rope_append(cudaStream_t s, float *q, const float *k, const float *v, float *kc, float *vc,
+                               int n, int Q, int KVd, int hd, int pos, int max_ctx, const float *cos_t,
+                               const float *sin_t, const int *pos_dev) {
+  const size_t items = (size_t)n * (Q / 2 + KVd);
+  k_rope_append<<<grid_for(items, 256, num_sms() * 8), 256, 0, s>>>(q, k, v, kc, vc, n, Q, KVd, hd, max_ctx, pos,
+                                                                     cos_t, sin_t, pos_dev);
+  return cudaGetLastError();
+}
 __global__ void k_add_int(int *p, int v) { *p += v; }
 __global__ void k_store_int(int *p, int v) { *p = v; }
 cudaError_t launch_set_int(cudaStream_t s, int *p, int v) {

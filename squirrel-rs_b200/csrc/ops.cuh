@@ -104,7 +104,10 @@ size_t sdpa_max_partials_floats(int head_dim);
 cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out,
                         int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim,
                         long long k_pos_stride, long long k_head_stride, int n_split, float *part,
-                        const int *pos_dev = nullptr);
+                        const int *pos_dev = nullptr, int *split_cnt = nullptr);
+// split_cnt (optional, seq_q * n_heads ints, zero before the first call): the last CTA of
+// a query row to finish merges the splits itself (and re-zeroes its counter) instead
+// of a separate combine launch; same arithmetic, same order.
 
 }  // namespace sq
 
@@ -113,6 +116,11 @@ namespace sq {
 // cache[g][pos + r][d] = src[r][g*hd + d] for r < n (kv_cache.rs:38-53 semantics).
 cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, float *kc, float *vc, int n,
                              int n_kv, int hd, int pos, int max_ctx, const int *pos_dev = nullptr);
+// RoPE of q (in place) and k rows from the cos/sin table, then the rotated K and the V
+// rows appended to the cache, in one launch (q: [n][Q], k / v: [n][KVd]).
+cudaError_t launch_rope_append(cudaStream_t s, float *q, const float *k, const float *v, float *kc, float *vc,
+                               int n, int Q, int KVd, int hd, int pos, int max_ctx, const float *cos_t,
+                               const float *sin_t, const int *pos_dev = nullptr);
 // *p += v / *p = v (the device position counter of a replayed decode step)
 cudaError_t launch_add_int(cudaStream_t s, int *p, int v);
 cudaError_t launch_set_int(cudaStream_t s, int *p, int v);

@@ -517,6 +517,8 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
   SQ_CUDA(ctx_alloc(x.get(), &x->gemm_ws, x->gemm_ws_floats));
   x->sdpa_part_floats = sdpa_max_partials_floats(c.head_dim);
   SQ_CUDA(ctx_alloc(x.get(), &x->sdpa_part, x->sdpa_part_floats));
+  SQ_CUDA(ctx_alloc(x.get(), &x->sdpa_cnt, (size_t)SDPA_MAX_ROW_SPLITS));
+  SQ_CUDA(cudaMemset(x->sdpa_cnt, 0, (size_t)SDPA_MAX_ROW_SPLITS * sizeof(int)));
   SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->argmax_part, (size_t)argmax_partials(c.vocab_size) * 32));
   SQ_CUDA(ctx_alloc(x.get(), &x->d_argmax, 1));
   SQ_CUDA(ctx_alloc(x.get(), &x->d_gpos, 1));
@@ -562,17 +564,75 @@ extern "C" int sq_ctx_seq_len(const sq_ctx *c, int *out) {
 
 extern "C" void *sq_ctx_stream(sq_ctx *c) { return c ? (void *)c->stream : nullptr; }
 
+namespace sq {
+
+// The one-row matvecs of layer l (decode through the op level): q/k/v and gate/up
+// as one launch each, the norms, SiLU.mul and (single GPU) residual adds folded in.
+// Returns whether the streaming matvec takes all four.
+static bool layer_matvecs(const sq_ctx *c, int l, MvArgs &qkv, MvArgs &o, MvArgs &gu, MvArgs &dn) {
+  const sq_model *m = c->m;
+  const sq_llama_config &cf = m->lc;
+  const auto &L = m->layers[l];
+  const int E = cf.embed_dim, Q = cf.n_heads * cf.head_dim, KVd = cf.n_kv_heads * cf.head_dim, F = cf.ffn_dim;
+  const bool tp = m->tp_size > 1;
+  qkv = MvArgs{}, o = MvArgs{}, gu = MvArgs{}, dn = MvArgs{};
+  qkv.x = c->hidden, qkv.norm_w = L.attn_norm, qkv.eps = cf.rms_eps, qkv.in_dim = E, qkv.n = 3;
+  qkv.w[0] = (const uint8_t *)L.q, qkv.w[1] = (const uint8_t *)L.k, qkv.w[2] = (const uint8_t *)L.v;
+  qkv.out_dim[0] = Q, qkv.out_dim[1] = KVd, qkv.out_dim[2] = KVd;
+  qkv.y[0] = c->q, qkv.y[1] = c->k, qkv.y[2] = c->v;
+  o.x = c->attn, o.in_dim = Q, o.n = 1, o.w[0] = (const uint8_t *)L.o, o.out_dim[0] = E;
+  o.y[0] = tp ? c->attn_out : c->hidden, o.res[0] = tp ? nullptr : c->hidden;
+  gu.x = c->hidden, gu.norm_w = L.ffn_norm, gu.eps = cf.rms_eps, gu.in_dim = E, gu.n = 2;
+  gu.w[0] = (const uint8_t *)L.gate, gu.w[1] = (const uint8_t *)L.up, gu.out_dim[0] = F, gu.out_dim[1] = F;
+  gu.y[0] = c->gate, gu.y[1] = c->up;
+  dn.x = c->gate, dn.xu = c->up, dn.in_dim = F, dn.n = 1, dn.w[0] = (const uint8_t *)L.down, dn.out_dim[0] = E;
+  dn.y[0] = tp ? c->ffn_out : c->hidden, dn.res[0] = tp ? nullptr : c->hidden;
+  const int wt = cf.weight_type;
+  const bool aq = m->acts == SQ_ACTS_Q8 && wt != SQ_BF16;
+  return !aq && matvec_fused_ok(qkv, wt) && matvec_fused_ok(o, wt) && matvec_fused_ok(gu, wt) &&
+         matvec_fused_ok(dn, wt);
+}
+
+// The LM head of row `row` with the final norm folded in; whether the streaming
+// matvec takes it.
+static bool lm_matvec(const sq_ctx *c, int row, MvArgs &lm) {
+  const sq_model *m = c->m;
+  const sq_llama_config &cf = m->lc;
+  const int E = cf.embed_dim;
+  lm = MvArgs{};
+  lm.x = c->hidden + (size_t)row * E, lm.norm_w = m->out_norm, lm.eps = cf.rms_eps, lm.in_dim = E, lm.n = 1;
+  lm.w[0] = (const uint8_t *)m->out_w, lm.out_dim[0] = cf.vocab_size, lm.y[0] = c->logits;
+  const bool lm_q8 = m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16;
+  return !lm_q8 && matvec_fused_ok(lm, m->out_type);
+}
+
+}  // namespace sq
+
+// Kernels of ours one decode step launches (NCCL's not counted): the op-level
+// sequence of forward_rows for one row plus the position counter, or the
+// persistent decode kernel.
 extern "C" int sq_ctx_launches_per_token(const sq_ctx *c, int *out) {
   if (!c || !out) return fail(SQ_ERR_ARG, "launches_per_token: null pointer");
   if (decode_available(c)) {
     *out = 1;
     return SQ_OK;
   }
-  // the op-level sequence of forward_rows for one row, plus the token feedback kernel
   const sq_llama_config &cf = c->m->lc;
+  const bool tp = c->m->tp_size > 1;
   const int aq = c->m->acts == SQ_ACTS_Q8 && cf.weight_type != SQ_BF16;
-  const int split = sdpa_num_splits(1, c->seq_len + 1, cf.n_heads) > 1;
-  *out = 1 + cf.n_blocks * (16 + 2 * aq + split) + 4 + 1;
+  int n = 1;  // embedding
+  for (int l = 0; l < cf.n_blocks; l++) {
+    sq::MvArgs a, b, g, d;
+    // fused: qkv, rope+append, attention, o, gate/up, down (+ two residual adds after
+    // the all-reduces); otherwise norm, q, k, v, rope+append, attention, o, add, norm,
+    // gate, up, silu_mul, down, add (+ two activation quantizations)
+    n += sq::layer_matvecs(c, l, a, b, g, d) ? 6 + (tp ? 2 : 0) : 14 + 2 * aq;
+  }
+  sq::MvArgs lm;
+  n += sq::lm_matvec(c, 0, lm) ? 1 : 2;  // LM head (+ the final norm)
+  n += 2;                                // argmax: partials and final (shards: state and fold)
+  n += 1;                                // the device position counter
+  *out = n;
   return SQ_OK;
 }
 
@@ -585,7 +645,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
   const sq_llama_config &cf = m->lc;  // this rank's shard (the whole model when tp_size == 1)
   cudaStream_t s = c->stream;
   const int E = cf.embed_dim, Q = cf.n_heads * cf.head_dim, KVd = cf.n_kv_heads * cf.head_dim, F = cf.ffn_dim;
-  const int wt = cf.weight_type, half = cf.head_dim / 2;
+  const int wt = cf.weight_type;
   const int aq = m->acts == SQ_ACTS_Q8 && wt != SQ_BF16;
   const int pos = c->seq_len;
   const size_t layer_kv = (size_t)cf.n_kv_heads * c->max_ctx * cf.head_dim;
@@ -616,20 +676,8 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
                      gemm_tc_supported(n, F, ws, L.down, wt, ws, wsf);
     // One-row layer (decode through the op level): the streaming matvec with the norm,
     // SiLU.mul and residual add folded in, q/k/v and gate/up as one launch each.
-    MvArgs qkv{}, o{}, gu{}, dn{};
-    qkv.x = c->hidden, qkv.norm_w = L.attn_norm, qkv.eps = cf.rms_eps, qkv.in_dim = E, qkv.n = 3;
-    qkv.w[0] = (const uint8_t *)L.q, qkv.w[1] = (const uint8_t *)L.k, qkv.w[2] = (const uint8_t *)L.v;
-    qkv.out_dim[0] = Q, qkv.out_dim[1] = KVd, qkv.out_dim[2] = KVd;
-    qkv.y[0] = c->q, qkv.y[1] = c->k, qkv.y[2] = c->v;
-    o.x = c->attn, o.in_dim = Q, o.n = 1, o.w[0] = (const uint8_t *)L.o, o.out_dim[0] = E;
-    o.y[0] = tp ? c->attn_out : c->hidden, o.res[0] = tp ? nullptr : c->hidden;
-    gu.x = c->hidden, gu.norm_w = L.ffn_norm, gu.eps = cf.rms_eps, gu.in_dim = E, gu.n = 2;
-    gu.w[0] = (const uint8_t *)L.gate, gu.w[1] = (const uint8_t *)L.up, gu.out_dim[0] = F, gu.out_dim[1] = F;
-    gu.y[0] = c->gate, gu.y[1] = c->up;
-    dn.x = c->gate, dn.xu = c->up, dn.in_dim = F, dn.n = 1, dn.w[0] = (const uint8_t *)L.down, dn.out_dim[0] = E;
-    dn.y[0] = tp ? c->ffn_out : c->hidden, dn.res[0] = tp ? nullptr : c->hidden;
-    const bool fused = n == 1 && !aq && matvec_fused_ok(qkv, wt) && matvec_fused_ok(o, wt) &&
-                       matvec_fused_ok(gu, wt) && matvec_fused_ok(dn, wt);
+    MvArgs qkv, o, gu, dn;
+    const bool fused = layer_matvecs(c, l, qkv, o, gu, dn) && n == 1;
     if (fused) {
       TRY(launch_matvec_fused(s, qkv, wt));
     } else if (tcl) {
@@ -646,9 +694,8 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     }
     // pos_dev: positions come from the device counter (a captured decode step); the
     // attention then keeps the split count of the longest context
-    TRY(launch_rope_rows_table(s, c->q, n, Q, pos, c->d_cos, c->d_sin, half, pos_dev));
-    TRY(launch_rope_rows_table(s, c->k, n, KVd, pos, c->d_cos, c->d_sin, half, pos_dev));
-    TRY(launch_kv_append(s, c->k, c->v, kc, vc, n, cf.n_kv_heads, cf.head_dim, pos, c->max_ctx, pos_dev));
+    TRY(launch_rope_append(s, c->q, c->k, c->v, kc, vc, n, Q, KVd, cf.head_dim, pos, c->max_ctx, c->d_cos, c->d_sin,
+                           pos_dev));
     const long long khs = (long long)c->max_ctx * cf.head_dim;
     if (!pos_dev && attn_tc_supported(n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs, c->q, kc,
                                       vc, c->gemm_ws_floats * sizeof(float))) {
@@ -658,7 +705,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     } else {
       const int ns = pos_dev ? sdpa_num_splits(n, c->max_ctx, cf.n_heads) : sdpa_num_splits(n, pos + n, cf.n_heads);
       TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs,
-                      ns, c->sdpa_part, pos_dev));
+                      ns, c->sdpa_part, pos_dev, c->sdpa_cnt));
     }
     if (fused) {
       TRY(launch_matvec_fused(s, o, wt));  // single GPU: hidden += O.attn in the epilogue
@@ -693,11 +740,9 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
   c->seq_len += n;
   if (last) {
     // final norm of the last row only: rows are normalized independently (model.rs:72-87)
-    MvArgs lm{};
-    lm.x = c->hidden + (size_t)(n - 1) * E, lm.norm_w = m->out_norm, lm.eps = cf.rms_eps, lm.in_dim = E, lm.n = 1;
-    lm.w[0] = (const uint8_t *)m->out_w, lm.out_dim[0] = cf.vocab_size, lm.y[0] = c->logits;
+    MvArgs lm;
     const bool lm_q8 = m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16;
-    if (!lm_q8 && matvec_fused_ok(lm, m->out_type)) {
+    if (lm_matvec(c, n - 1, lm)) {
       TRY(launch_matvec_fused(s, lm, m->out_type));  // the norm folded into the LM head
     } else {
       TRY(launch_rms_norm(s, c->hidden + (size_t)(n - 1) * E, m->out_norm, c->normed, 1, E, cf.rms_eps));

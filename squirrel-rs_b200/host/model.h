@@ -65,6 +65,7 @@ struct sq_ctx {
   void *xq = nullptr;  // Q8_0 activation scratch (the reference's act_q)
   float *sdpa_part = nullptr;
   size_t sdpa_part_floats = 0;
+  int *sdpa_cnt = nullptr;  // per query row: split CTAs finished (the last one merges; self-resetting)
   float *gemm_ws = nullptr;  // split-K partial tiles of the prefill GEMM
   size_t gemm_ws_floats = 0;
   void *argmax_part = nullptr;
