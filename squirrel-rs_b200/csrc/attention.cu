@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(SDPA_WARPS * 32)
            int group, long long kps, long long khs, int split_len, float scale, const int *__restrict__ pos_dev,
            int *__restrict__ split_cnt) {
   const int hd = DPL * 32;
+  pdl_wait();  // q and the cache come from earlier kernels
+  pdl_trigger();
   if (pos_dev) {  // the keys end at the position the device holds (graph replay: no host values)
     seq_k = *pos_dev + seq_q;
     split_len = (seq_k + (int)gridDim.y - 1) / (int)gridDim.y;
@@ -193,21 +195,23 @@ size_t sdpa_max_partials_floats(int head_dim) { return (size_t)SDPA_MAX_ROW_SPLI
 
 cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out, int seq_q,
                         int seq_k, int n_heads, int n_kv_heads, int head_dim, long long kps, long long khs,
-                        int n_split, float *part, const int *pos_dev, int *split_cnt) {
+                        int n_split, float *part, const int *pos_dev, int *split_cnt, bool pdl) {
   const int group = n_heads / n_kv_heads;
   const float scale = 1.0f / sqrtf((float)head_dim);  // attention.rs:37
   const int split_len = (seq_k + n_split - 1) / n_split;
   dim3 grid(seq_q * n_heads, n_split);
+  cudaError_t e = cudaSuccess;
   switch (head_dim / 32) {
-    case 1: k_sdpa<1><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    case 2: k_sdpa<2><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    case 3: k_sdpa<3><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    case 4: k_sdpa<4><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    case 5: k_sdpa<5><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    case 6: k_sdpa<6><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    case 7: k_sdpa<7><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
-    default: k_sdpa<8><<<grid, SDPA_WARPS * 32, 0, s>>>(q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 1: e = launch_ex(k_sdpa<1>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 2: e = launch_ex(k_sdpa<2>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 3: e = launch_ex(k_sdpa<3>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 4: e = launch_ex(k_sdpa<4>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 5: e = launch_ex(k_sdpa<5>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 6: e = launch_ex(k_sdpa<6>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    case 7: e = launch_ex(k_sdpa<7>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
+    default: e = launch_ex(k_sdpa<8>, grid, dim3(SDPA_WARPS * 32), 0, s, pdl, q, k, v, out, part, seq_q, seq_k, n_heads, group, kps, khs, split_len, scale, pos_dev, split_cnt); break;
   }
+  if (e != cudaSuccess) return e;
   if (n_split > 1 && !split_cnt) k_sdpa_combine<<<seq_q * n_heads, 64, 0, s>>>(part, out, n_split, head_dim);
   return cudaGetLastError();
 }

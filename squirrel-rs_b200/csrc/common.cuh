@@ -10,6 +10,14 @@ namespace sq {
 
 // ---- device helpers ---------------------------------------------------------------
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel of the stream is still running;
+// every thread calls pdl_wait() before it reads anything an earlier kernel wrote or
+// writes anything an earlier kernel may still read (it returns at once for a plain
+// launch). pdl_trigger() lets the next such kernel be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // f16 -> f32 is exact (half::f16::to_f32).
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
@@ -184,6 +192,24 @@ __device__ __forceinline__ float pair_dot(const uint32_t (&w)[pair_words<T>()], 
     }
     return hsum2(a[0], a[1]);
   }
+}
+
+// Launch kernel k on stream s, with programmatic stream serialization when pdl (the
+// kernel must then call pdl_wait() as described above).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 }  // namespace sq

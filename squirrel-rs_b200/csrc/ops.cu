@@ -287,6 +287,10 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     int issued = 0, finished = 0;
     for (int t = 0; t < ntiles; t++) {
       const int slot = t % MV_NS;
+      if (t == MV_NS) {  // the first ring fill (weights only) went out before the previous kernel ended
+        pdl_wait();
+        if (lane == 0) pdl_trigger();
+      }
       if (t >= MV_NS) {
         if (!wait_empty(t - MV_NS)) break;
         if (nseg > 1) finish(t - MV_NS);
@@ -306,6 +310,10 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
       }
       issued = t + 1;
     }
+    if (ntiles <= MV_NS) {
+      pdl_wait();
+      if (lane == 0) pdl_trigger();
+    }
     if (nseg > 1 && issued == ntiles)  // the last tiles' partial sums
       for (int t = finished; t < ntiles; t++) {
         if (!wait_empty(t)) break;
@@ -320,6 +328,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     return;
   }
   if (warp >= ncons) return;
+  pdl_wait();  // the input row (and residual rows) come from earlier kernels
   const int g = warp / nseg, seg = warp % nseg;
   const int pairs = min(32, np - seg * 32);  // pairs in this segment (>= 1)
   const bool active = lane < pairs;
@@ -790,29 +799,36 @@ bool matvec_fused_ok(const MvArgs &a, int wtype) {
 }
 
 template <int T, int MODE>
-static cudaError_t matvec_mode_t(cudaStream_t s, const MvArgs &a) {
+static cudaError_t matvec_mode_t(cudaStream_t s, const MvArgs &a, bool pdl = false) {
   const size_t mv_smem = mv_smem_bytes<T>(a.in_dim);
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(k_matvec<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
     attr_set = true;
   }
-  k_matvec<T, MODE><<<num_sms(), MV_THREADS, mv_smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_ex(k_matvec<T, MODE>, dim3(num_sms()), dim3(MV_THREADS), mv_smem, s, pdl, a);
 }
 template <int T>
-static cudaError_t matvec_fused_t(cudaStream_t s, const MvArgs &a) {
-  if (a.norm_w) return matvec_mode_t<T, MV_NORM>(s, a);
-  if (a.xu) return matvec_mode_t<T, MV_SILU>(s, a);
-  if (a.n > 1 || a.res[0]) return matvec_mode_t<T, MV_GENERAL>(s, a);
-  return matvec_mode_t<T, MV_PLAIN>(s, a);
+static cudaError_t matvec_fused_t(cudaStream_t s, const MvArgs &a, bool pdl) {
+  if (a.norm_w) return matvec_mode_t<T, MV_NORM>(s, a, pdl);
+  if (a.xu) return matvec_mode_t<T, MV_SILU>(s, a, pdl);
+  if (a.n > 1 || a.res[0]) return matvec_mode_t<T, MV_GENERAL>(s, a, pdl);
+  return matvec_mode_t<T, MV_PLAIN>(s, a, pdl);
 }
 
-cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype) {
+cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype, bool pdl) {
   if (!matvec_fused_ok(a, wtype)) return cudaErrorNotSupported;
-  if (wtype == SQ_Q8_0) return matvec_fused_t<SQ_Q8_0>(s, a);
-  if (wtype == SQ_Q4_0) return matvec_fused_t<SQ_Q4_0>(s, a);
-  return matvec_fused_t<SQ_BF16>(s, a);
+  if (wtype == SQ_Q8_0) return matvec_fused_t<SQ_Q8_0>(s, a, pdl);
+  if (wtype == SQ_Q4_0) return matvec_fused_t<SQ_Q4_0>(s, a, pdl);
+  return matvec_fused_t<SQ_BF16>(s, a, pdl);
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("SQB200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 template <int T>
@@ -1218,6 +1234,8 @@ __global__ void k_rope_append(float *q, const float *__restrict__ k, const float
                               float *vc, int n, int Q, int KVd, int hd, int max_ctx, int pos,
                               const float *__restrict__ cos_t, const float *__restrict__ sin_t,
                               const int *__restrict__ pos_dev) {
+  pdl_wait();
+  pdl_trigger();
   if (pos_dev) pos = *pos_dev;
   const int half = hd / 2, qp = Q / 2, kp = KVd / 2, per = qp + 2 * kp;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < (long long)n * per;
@@ -1253,11 +1271,10 @@ __global__ void k_rope_append(float *q, const float *__restrict__ k, const float
 
 cudaError_t launch_rope_append(cudaStream_t s, float *q, const float *k, const float *v, float *kc, float *vc,
                                int n, int Q, int KVd, int hd, int pos, int max_ctx, const float *cos_t,
-                               const float *sin_t, const int *pos_dev) {
+                               const float *sin_t, const int *pos_dev, bool pdl) {
   const size_t items = (size_t)n * (Q / 2 + KVd);
-  k_rope_append<<<grid_for(items, 256, num_sms() * 8), 256, 0, s>>>(q, k, v, kc, vc, n, Q, KVd, hd, max_ctx, pos,
-                                                                     cos_t, sin_t, pos_dev);
-  return cudaGetLastError();
+  return launch_ex(k_rope_append, dim3(grid_for(items, 256, num_sms() * 8)), dim3(256), 0, s, pdl, q, k, v, kc, vc,
+                   n, Q, KVd, hd, max_ctx, pos, cos_t, sin_t, pos_dev);
 }
 __global__ void k_add_int(int *p, int v) { *p += v; }
 __global__ void k_store_int(int *p, int v) { *p = v; }

@@ -33,7 +33,11 @@ struct MvArgs {
   const float *res[3];  // optional residual rows: y[r] = res[r] + dot
 };
 bool matvec_fused_ok(const MvArgs &a, int wtype);
-cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype);
+// pdl: launched with programmatic stream serialization (the kernel streams its first
+// weight tiles while the previous kernel finishes; see pdl_enabled()).
+cudaError_t launch_matvec_fused(cudaStream_t s, const MvArgs &a, int wtype, bool pdl = false);
+// Programmatic dependent launches for the one-row decode step (SQB200_PDL=0 turns them off).
+bool pdl_enabled();
 
 // Tensor-core GEMM (gemm_tc.cu) for BF16, Q8_0 and Q4_0 weight rows: the f32
 // activations are split into three bf16 terms in `ws` (3*m*K/2 floats, then split-K
@@ -104,7 +108,7 @@ size_t sdpa_max_partials_floats(int head_dim);
 cudaError_t launch_sdpa(cudaStream_t s, const float *q, const float *k, const float *v, float *out,
                         int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim,
                         long long k_pos_stride, long long k_head_stride, int n_split, float *part,
-                        const int *pos_dev = nullptr, int *split_cnt = nullptr);
+                        const int *pos_dev = nullptr, int *split_cnt = nullptr, bool pdl = false);
 // split_cnt (optional, seq_q * n_heads ints, zero before the first call): the last CTA of
 // a query row to finish merges the splits itself (and re-zeroes its counter) instead
 // of a separate combine launch; same arithmetic, same order.
@@ -120,7 +124,7 @@ cudaError_t launch_kv_append(cudaStream_t s, const float *k, const float *v, flo
 // rows appended to the cache, in one launch (q: [n][Q], k / v: [n][KVd]).
 cudaError_t launch_rope_append(cudaStream_t s, float *q, const float *k, const float *v, float *kc, float *vc,
                                int n, int Q, int KVd, int hd, int pos, int max_ctx, const float *cos_t,
-                               const float *sin_t, const int *pos_dev = nullptr);
+                               const float *sin_t, const int *pos_dev = nullptr, bool pdl = false);
 // *p += v / *p = v (the device position counter of a replayed decode step)
 cudaError_t launch_add_int(cudaStream_t s, int *p, int v);
 cudaError_t launch_set_int(cudaStream_t s, int *p, int v);

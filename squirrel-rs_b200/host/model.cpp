@@ -678,8 +678,11 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     // SiLU.mul and residual add folded in, q/k/v and gate/up as one launch each.
     MvArgs qkv, o, gu, dn;
     const bool fused = layer_matvecs(c, l, qkv, o, gu, dn) && n == 1;
+    // the one-row step's kernels start while their predecessor finishes (each waits
+    // for it before touching activations)
+    const bool pdl = fused && pdl_enabled();
     if (fused) {
-      TRY(launch_matvec_fused(s, qkv, wt));
+      TRY(launch_matvec_fused(s, qkv, wt, pdl));
     } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.attn_norm, ws, n, E, cf.rms_eps));
       TRY(launch_gemm_tc_terms(s, n, E, L.q, wt, Q, c->q, ws, wsf));
@@ -695,7 +698,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     // pos_dev: positions come from the device counter (a captured decode step); the
     // attention then keeps the split count of the longest context
     TRY(launch_rope_append(s, c->q, c->k, c->v, kc, vc, n, Q, KVd, cf.head_dim, pos, c->max_ctx, c->d_cos, c->d_sin,
-                           pos_dev));
+                           pos_dev, pdl));
     const long long khs = (long long)c->max_ctx * cf.head_dim;
     if (!pos_dev && attn_tc_supported(n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs, c->q, kc,
                                       vc, c->gemm_ws_floats * sizeof(float))) {
@@ -705,10 +708,10 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     } else {
       const int ns = pos_dev ? sdpa_num_splits(n, c->max_ctx, cf.n_heads) : sdpa_num_splits(n, pos + n, cf.n_heads);
       TRY(launch_sdpa(s, c->q, kc, vc, c->attn, n, pos + n, cf.n_heads, cf.n_kv_heads, cf.head_dim, cf.head_dim, khs,
-                      ns, c->sdpa_part, pos_dev, c->sdpa_cnt));
+                      ns, c->sdpa_part, pos_dev, c->sdpa_cnt, pdl));
     }
     if (fused) {
-      TRY(launch_matvec_fused(s, o, wt));  // single GPU: hidden += O.attn in the epilogue
+      TRY(launch_matvec_fused(s, o, wt, pdl));  // single GPU: hidden += O.attn in the epilogue
     } else if (tcl) {
       TRY(launch_split_terms(s, c->attn, n, Q, ws));
       TRY(launch_gemm_tc_terms(s, n, Q, L.o, wt, E, c->attn_out, ws, wsf));
@@ -718,8 +721,8 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
     if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
     if (fused) {
-      TRY(launch_matvec_fused(s, gu, wt));
-      TRY(launch_matvec_fused(s, dn, wt));  // SiLU(gate) * up formed as it is read
+      TRY(launch_matvec_fused(s, gu, wt, pdl));
+      TRY(launch_matvec_fused(s, dn, wt, pdl));  // SiLU(gate) * up formed as it is read
     } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
       TRY(launch_gemm_tc_terms(s, n, E, L.gate, wt, F, c->gate, ws, wsf));
@@ -743,7 +746,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     MvArgs lm;
     const bool lm_q8 = m->acts == SQ_ACTS_Q8 && m->out_type != SQ_BF16;
     if (lm_matvec(c, n - 1, lm)) {
-      TRY(launch_matvec_fused(s, lm, m->out_type));  // the norm folded into the LM head
+      TRY(launch_matvec_fused(s, lm, m->out_type, n == 1 && pdl_enabled()));  // the norm folded into the LM head
     } else {
       TRY(launch_rms_norm(s, c->hidden + (size_t)(n - 1) * E, m->out_norm, c->normed, 1, E, cf.rms_eps));
       TRY(launch_linear(s, c->normed, 1, E, m->out_w, m->out_type, cf.vocab_size, c->logits, lm_q8, c->xq,
