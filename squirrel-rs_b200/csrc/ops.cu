@@ -137,7 +137,8 @@ constexpr int MV_SLOT = 36864;                 // bytes per ring slot
 constexpr int MV_NS = 5;                       // ring slots
 constexpr int MV_TRMAX = 64;                   // rows per tile at most
 constexpr int MV_REDROWS = 32;                 // rows per tile when rows are split into segments
-constexpr int MV_HDR = 2 * MV_NS * 8 + (MV_NS * MV_REDROWS + 1) * MV_CONS * 4;  // mbarriers + partial sums
+constexpr int MV_GATE_ROWS = 1024;             // gate rows per CTA kept for SiLU(gate) * up (gate_act)
+constexpr int MV_HDR = 2 * MV_NS * 8 + ((MV_NS * MV_REDROWS + 1) * MV_CONS + MV_GATE_ROWS) * 4;  // mbarriers, sums, gates
 constexpr int MV_RING_OFF = (MV_HDR + 127) & ~127;
 
 __device__ unsigned g_mv_err;  // set when a bounded wait of k_matvec gave up
@@ -238,11 +239,17 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
   };
   const uint32_t full = mv_su32(mv_smem), empty = full + 8u * MV_NS;
   float *red = reinterpret_cast<float *>(mv_smem + 2 * MV_NS * 8);  // [MV_NS][MV_REDROWS][nseg], then [MV_CONS]
+  // gate_act: the gate rows of this CTA, by row within its block; the thread that
+  // writes gate row i is the one that later finishes up row i (same tile slot)
+  float *gsm = red + (MV_NS * MV_REDROWS + 1) * MV_CONS;
   const uint32_t ring = mv_su32(mv_smem + MV_RING_OFF);
 #define MV_OUT_ROW(mi, row, v)                                    \
   do {                                                            \
     if constexpr (MODE == MV_PLAIN) {                             \
       a.y[0][row] = (v);                                          \
+    } else if (a.gate_act) {                                      \
+      if ((mi) == 0) gsm[(row) - s00] = (v);                      \
+      else a.y[1][row] = __fmul_rn(silu_ref(gsm[(row) - s00]), (v)); \
     } else {                                                      \
       const float *rs_ = MV_SEL(res, mi);                          \
       MV_SEL(y, mi)[row] = rs_ ? __fadd_rn(rs_[row], (v)) : (v);  \
@@ -264,6 +271,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     // the outputs as locals (the lambda below must not capture `a`)
     float *const py0 = a.y[0], *const py1 = a.y[1], *const py2 = a.y[2];
     const float *const pr0 = a.res[0], *const pr1 = a.res[1], *const pr2 = a.res[2];
+    const bool gact = MODE != MV_PLAIN && a.gate_act != 0;
     auto finish = [&](int t) {
       int mi, r0, rows;
       tile_of(t, mi, r0, rows);
@@ -273,7 +281,12 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
       for (int r = lane; r < rows; r += 32) {
         float sum = rd[r * nseg];
         for (int q = 1; q < nseg; q++) sum += rd[r * nseg + q];
-        yp[r0 + r] = rp ? __fadd_rn(rp[r0 + r], sum) : sum;
+        if (gact) {
+          if (mi == 0) gsm[r0 + r - s00] = sum;
+          else py1[r0 + r] = __fmul_rn(silu_ref(gsm[r0 + r - s00]), sum);
+        } else {
+          yp[r0 + r] = rp ? __fadd_rn(rp[r0 + r], sum) : sum;
+        }
       }
     };
     const bool solo = nseg == 1;  // nothing to finish: lane 0 alone streams the tiles
@@ -795,6 +808,9 @@ bool matvec_fused_ok(const MvArgs &a, int wtype) {
   if (!al(a.x) || (a.xu && !al(a.xu)) || (a.norm_w && !al(a.norm_w)) || (a.xu && a.norm_w)) return false;
   for (int i = 0; i < a.n; i++)
     if (!a.w[i] || !al(a.w[i]) || !a.y[i] || a.out_dim[i] <= 0) return false;
+  if (a.gate_act && (a.n != 2 || a.out_dim[0] != a.out_dim[1] || a.res[0] || a.res[1] || a.xu ||
+                     (a.out_dim[0] + num_sms() - 1) / num_sms() > MV_GATE_ROWS))
+    return false;
   return true;
 }
 

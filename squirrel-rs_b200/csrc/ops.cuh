@@ -31,6 +31,7 @@ struct MvArgs {
   int out_dim[3];
   float *y[3];
   const float *res[3];  // optional residual rows: y[r] = res[r] + dot
+  int gate_act;         // n == 2 (gate, up; same rows, no residual): y[1] = silu(gate . x) * (up . x); y[0] unused
 };
 bool matvec_fused_ok(const MvArgs &a, int wtype);
 // pdl: launched with programmatic stream serialization (the kernel streams its first

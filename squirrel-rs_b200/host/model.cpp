@@ -567,7 +567,8 @@ extern "C" void *sq_ctx_stream(sq_ctx *c) { return c ? (void *)c->stream : nullp
 namespace sq {
 
 // The one-row matvecs of layer l (decode through the op level): q/k/v and gate/up
-// as one launch each, the norms, SiLU.mul and (single GPU) residual adds folded in.
+// as one launch each, the norms, SiLU.mul (the gate/up epilogue) and (single GPU)
+// residual adds folded in.
 // Returns whether the streaming matvec takes all four.
 static bool layer_matvecs(const sq_ctx *c, int l, MvArgs &qkv, MvArgs &o, MvArgs &gu, MvArgs &dn) {
   const sq_model *m = c->m;
@@ -584,8 +585,8 @@ static bool layer_matvecs(const sq_ctx *c, int l, MvArgs &qkv, MvArgs &o, MvArgs
   o.y[0] = tp ? c->attn_out : c->hidden, o.res[0] = tp ? nullptr : c->hidden;
   gu.x = c->hidden, gu.norm_w = L.ffn_norm, gu.eps = cf.rms_eps, gu.in_dim = E, gu.n = 2;
   gu.w[0] = (const uint8_t *)L.gate, gu.w[1] = (const uint8_t *)L.up, gu.out_dim[0] = F, gu.out_dim[1] = F;
-  gu.y[0] = c->gate, gu.y[1] = c->up;
-  dn.x = c->gate, dn.xu = c->up, dn.in_dim = F, dn.n = 1, dn.w[0] = (const uint8_t *)L.down, dn.out_dim[0] = E;
+  gu.y[0] = c->gate, gu.y[1] = c->act, gu.gate_act = 1;  // SiLU(gate) * up formed in the epilogue
+  dn.x = c->act, dn.in_dim = F, dn.n = 1, dn.w[0] = (const uint8_t *)L.down, dn.out_dim[0] = E;
   dn.y[0] = tp ? c->ffn_out : c->hidden, dn.res[0] = tp ? nullptr : c->hidden;
   const int wt = cf.weight_type;
   const bool aq = m->acts == SQ_ACTS_Q8 && wt != SQ_BF16;
@@ -722,7 +723,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
     if (fused) {
       TRY(launch_matvec_fused(s, gu, wt, pdl));
-      TRY(launch_matvec_fused(s, dn, wt, pdl));  // SiLU(gate) * up formed as it is read
+      TRY(launch_matvec_fused(s, dn, wt, pdl));
     } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
       TRY(launch_gemm_tc_terms(s, n, E, L.gate, wt, F, c->gate, ws, wsf));
