@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
   const int g = warp / nseg, seg = warp % nseg;
   const int pairs = min(32, np - seg * 32);  // pairs in this segment (>= 1)
   const bool active = lane < pairs;
-  float rms = 1.f;
+  float inv_rms = 1.f;
   if constexpr (MODE == MV_NORM) {  // the consumers' sum of squares over the whole row, in a fixed order
     float ss = 0.f;
     for (int e = 4 * (warp * 32 + lane); e < in_dim; e += 4 * 32 * ncons) {
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     asm volatile("bar.sync 1, %0;" ::"r"(32 * ncons) : "memory");
     float tot = part[0];
     for (int q = 1; q < ncons; q++) tot += part[q];
-    rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)in_dim), a.eps));
+    inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)in_dim), a.eps)));
   }
   f2x x2[32];
   if (active) {
@@ -375,10 +375,12 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
         f = make_float4(__fmul_rn(silu_ref(f.x), u.x), __fmul_rn(silu_ref(f.y), u.y), __fmul_rn(silu_ref(f.z), u.z),
                         __fmul_rn(silu_ref(f.w), u.w));
       }
-      if constexpr (MODE == MV_NORM) {  // (x * w) / rms, as k_rms_norm_v rounds it
+      if constexpr (MODE == MV_NORM) {  // (x * w) * (1/rms): one multiply a element (the
+        // reference divides by rms, one rounding apart; a division per element per CTA
+        // cost this launch ~1 us)
         const float4 gw = __ldg(reinterpret_cast<const float4 *>(a.norm_w + base) + src);
-        f = make_float4(__fdiv_rn(__fmul_rn(f.x, gw.x), rms), __fdiv_rn(__fmul_rn(f.y, gw.y), rms),
-                        __fdiv_rn(__fmul_rn(f.z, gw.z), rms), __fdiv_rn(__fmul_rn(f.w, gw.w), rms));
+        f = make_float4(__fmul_rn(__fmul_rn(f.x, gw.x), inv_rms), __fmul_rn(__fmul_rn(f.y, gw.y), inv_rms),
+                        __fmul_rn(__fmul_rn(f.z, gw.z), inv_rms), __fmul_rn(__fmul_rn(f.w, gw.w), inv_rms));
       }
       x2[2 * k] = pk2(f.x, f.y);
       x2[2 * k + 1] = pk2(f.z, f.w);

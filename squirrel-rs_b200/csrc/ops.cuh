@@ -18,7 +18,8 @@ cudaError_t launch_gemm_f32w(cudaStream_t s, const float *x, int m, int K, const
                              float *ws, size_t ws_floats);
 // A fused single-row matvec (one launch of the streaming matvec): up to three
 // matrices of one type and input width over one input row; the input optionally
-// RMS-normalised (rms_norm_f32_into arithmetic, weight norm_w) or formed as
+// RMS-normalised (weight norm_w; (x * w) * (1/rms), one rounding from the reference's
+// (x * w) / rms) or formed as
 // silu(x) * xu; each output optionally added to a residual row (may be the output).
 struct MvArgs {
   const float *x;       // input row [in_dim]
