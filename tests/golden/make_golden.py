@@ -1,0 +1,63 @@
+"""Generate the end-to-end golden fixtures (tests/golden/e2e_*.npz).
+
+The reference pins no end-to-end output (its tests are op-level), so these files
+pin the oracle's: for each small seeded model (the synthetic GGUF writer with seed
+0) and weight type, the prompt, the oracle's greedy ids for 16 steps (EOS ignored,
+text_generator.rs:58-97) and its full logits after the prompt and after the last
+step, plus the GGUF's sha256 so a change of the writer is caught too. The CPU tests
+check that the oracle still reproduces them bit for bit; the GPU tests check the
+CUDA path against them (identical ids, logits within tolerance).
+
+    python tests/golden/make_golden.py
+"""
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+for p in (ROOT, os.path.join(ROOT, "squirrel-rs_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+CASES = [(spec, wt) for spec in ("tiny", "small") for wt in ("q8_0", "q4_0", "bf16")]
+PROMPT_LEN, STEPS, PROMPT_SEED = 8, 16, 21
+
+
+def sha256(path):
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def fixture_path(spec, wt):
+    return os.path.join(HERE, f"e2e_{spec}_{wt}.npz")
+
+
+def compute(spec, wt):
+    from oracle import oracle as O
+    from sqb200 import gguf_synth as G
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(PROMPT_LEN, seed=PROMPT_SEED, high=G.SPECS[spec]["vocab"])
+    m = O.Model(path)
+    ids, _, logits = m.generate(prompt, STEPS, want_logits=True)
+    m.close()
+    return dict(prompt=np.asarray(prompt, np.uint32), ids=np.asarray(ids, np.uint32),
+                logits_first=np.asarray(logits[0], np.float32), logits_last=np.asarray(logits[-1], np.float32),
+                gguf_sha256=np.array(sha256(path)))
+
+
+def main():
+    from oracle import build as oracle_build
+    oracle_build.build()
+    for spec, wt in CASES:
+        np.savez_compressed(fixture_path(spec, wt), **compute(spec, wt))
+        print("wrote", fixture_path(spec, wt))
+
+
+if __name__ == "__main__":
+    main()
