@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--workload", default="1b-q8_0", choices=sorted(WORKLOADS))
     ap.add_argument("--acts", default="f32", choices=["f32", "q8"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-decode-steps", type=int, default=4)
+    ap.add_argument("--cpu-decode-steps", type=int, default=200)  # ~10 s of oracle decode on the host
     ap.add_argument("--prefill", default="512,2048,8192",
                     help="BF16 1B prefill prompt lengths reported beside the decode metric (empty: skip)")
     ap.add_argument("--prefill-type", default="bf16", choices=["bf16", "q8_0", "q4_0"],
