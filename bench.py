@@ -353,10 +353,10 @@ def run_ours(args):
     path = G.ensure_gguf(spec, wt)
     prompt = G.prompt_ids(plen, seed=1234)
     acts = lib.ACTS_Q8 if args.acts == "q8" else lib.ACTS_F32
-    if tp:  # one model sharded over all ranks; rank 0's NCCL id goes to every rank
-        box = [lib.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(box, src=0)
-        model = lib.Model(path, device=local, acts=acts, tp_rank=rank, tp_size=world, nccl_id=box[0])
+    if tp:  # one model sharded over all ranks; every rank checks in, then rank 0's NCCL id goes to all
+        from sqb200 import tp as sqtp
+        nccl_id = sqtp.Group.from_default_store(timeout_s=300).share_id(lib.nccl_unique_id)
+        model = lib.Model(path, device=local, acts=acts, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     else:
         model = lib.Model(path, device=local, acts=acts)
     cfg = model.config
