@@ -25,6 +25,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -87,7 +88,9 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # raw samples (the JSON line carries their summary); SQB200_CLOCKS_DIR keeps them
+        self.path = os.path.join(os.environ.get("SQB200_CLOCKS_DIR", tempfile.gettempdir()),
+                                 f"sqb200_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
         os.makedirs(os.path.dirname(self.path), exist_ok=True)
