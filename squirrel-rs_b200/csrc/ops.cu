@@ -127,9 +127,9 @@ __global__ void __launch_bounds__(256) k_linear_f32(const float *__restrict__ x,
 // buffer in shared memory and the producer warp adds them in segment order
 // (deterministic) once every consumer has released the slot, so consumers never
 // wait on each other. The input may be RMS-normalised or formed as silu(x) * up as
-// it is read, and outputs may be added to a residual row (MvArgs). Rows must be
-// whole multiples of 256 elements (16-byte row starts) and in_dim <= 8 * 2048 (the
-// caller checks).
+// it is read, outputs may be added to a residual row, and a gate/up pair may leave
+// only SiLU(gate) * up (MvArgs::gate_act). Rows must be whole multiples of 256
+// elements (16-byte row starts) and in_dim <= 8 * 2048 (the caller checks).
 // Waits are bounded (~2 s); on expiry the warp records an error and stops.
 constexpr int MV_CONS = 8;                     // consumer warps
 constexpr int MV_THREADS = 32 * (MV_CONS + 1);  // + the producer warp
