@@ -23,6 +23,8 @@ for p in (ROOT, os.path.join(ROOT, "squirrel-rs_b200")):
         sys.path.insert(0, p)
 
 CASES = [(spec, wt) for spec in ("tiny", "small") for wt in ("q8_0", "q4_0", "bf16")]
+# the aarch64 scheme (Q8_0 activations, W8A8 / W4A8 integer block dots): oracle pins only
+CASES_A8 = [(spec, wt) for spec in ("tiny", "small") for wt in ("q8_0", "q4_0")]
 PROMPT_LEN, STEPS, PROMPT_SEED = 8, 16, 21
 
 
@@ -34,16 +36,16 @@ def sha256(path):
     return h.hexdigest()
 
 
-def fixture_path(spec, wt):
-    return os.path.join(HERE, f"e2e_{spec}_{wt}.npz")
+def fixture_path(spec, wt, acts_q8=False):
+    return os.path.join(HERE, f"e2e_{spec}_{wt}{'_a8' if acts_q8 else ''}.npz")
 
 
-def compute(spec, wt):
+def compute(spec, wt, acts_q8=False):
     from oracle import oracle as O
     from sqb200 import gguf_synth as G
     path = G.ensure_gguf(spec, wt)
     prompt = G.prompt_ids(PROMPT_LEN, seed=PROMPT_SEED, high=G.SPECS[spec]["vocab"])
-    m = O.Model(path)
+    m = O.Model(path, acts_q8=acts_q8)
     ids, _, logits = m.generate(prompt, STEPS, want_logits=True)
     m.close()
     return dict(prompt=np.asarray(prompt, np.uint32), ids=np.asarray(ids, np.uint32),
@@ -57,6 +59,9 @@ def main():
     for spec, wt in CASES:
         np.savez_compressed(fixture_path(spec, wt), **compute(spec, wt))
         print("wrote", fixture_path(spec, wt))
+    for spec, wt in CASES_A8:
+        np.savez_compressed(fixture_path(spec, wt, True), **compute(spec, wt, True))
+        print("wrote", fixture_path(spec, wt, True))
 
 
 if __name__ == "__main__":

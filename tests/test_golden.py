@@ -37,6 +37,16 @@ def test_oracle_reproduces_golden(spec, wt):
     assert np.array_equal(got["logits_last"], g["logits_last"])
 
 
+@pytest.mark.parametrize("spec,wt", MG.CASES_A8)
+def test_oracle_reproduces_golden_q8_acts(spec, wt):
+    from oracle import build as oracle_build
+    oracle_build.build()
+    z = np.load(MG.fixture_path(spec, wt, True))
+    got = MG.compute(spec, wt, True)
+    for k in ("prompt", "ids", "logits_first", "logits_last"):
+        assert np.array_equal(got[k], z[k]), k
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("op_level", [False, True])
 @pytest.mark.parametrize("spec,wt", MG.CASES)
