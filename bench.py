@@ -358,7 +358,16 @@ def run_ours(args):
     acts = lib.ACTS_Q8 if args.acts == "q8" else lib.ACTS_F32
     if tp:  # one model sharded over all ranks; every rank checks in, then rank 0's NCCL id goes to all
         from sqb200 import tp as sqtp
-        nccl_id = sqtp.Group.from_default_store(timeout_s=300).share_id(lib.nccl_unique_id)
+        try:
+            grp = sqtp.Group.from_default_store(timeout_s=300)
+        except (AttributeError, ImportError):  # no store accessor in this torch: plain broadcast
+            grp = None
+        if grp is not None:
+            nccl_id = grp.share_id(lib.nccl_unique_id)
+        else:
+            box = [lib.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            nccl_id = box[0]
         model = lib.Model(path, device=local, acts=acts, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     else:
         model = lib.Model(path, device=local, acts=acts)
