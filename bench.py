@@ -14,11 +14,19 @@ LM head, device argmax fed back as the next input).
           HBM copy bandwidth (MEASURED_PEAKS.json)
   cpu_baseline: the CPU oracle (C restatement of the reference's x86 scalar path)
           on the host cores, on a bounded sample of the same workload
+  parity: the GPU's greedy ids against the oracle's on the same prompt (the run
+          exits 1 when they differ)
+  long_context: config 3 (1B Q4_0, 2048-token prompt, decode at KV 2048-2304)
+  sweep : config 2 (isolated matvec, five shapes x three weight types)
+  tp    : config 5 (8B Q8_0) tensor parallel over all ranks (TP1 on one GPU)
+  prefill: config 4 (1B BF16 prefill of 512 / 2048 / 8192 tokens)
 
 `--impl reference` times that CPU restatement alone on this workload (the Rust
 reference cannot be built here: no Rust toolchain).
-Multi-GPU (torchrun): each rank runs an independent replica of the workload (the
-1B model does not shard: "replicas only"); value = all ranks' tokens / max time.
+Multi-GPU (torchrun): each rank runs an independent replica of the headline
+workload (the 1B model does not shard: "replicas only"); value = all ranks' tokens
+/ max time. The `tp` key is the one multi-GPU design measurement: the 8B model
+sharded over all ranks with its all-reduces after the O and down projections.
 """
 import argparse
 import json
@@ -56,6 +64,8 @@ def parse():
     ap.add_argument("--workload", default="1b-q8_0", choices=sorted(WORKLOADS))
     ap.add_argument("--acts", default="f32", choices=["f32", "q8"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the long_context, sweep and tp measurements (profiling runs)")
     ap.add_argument("--cpu-decode-steps", type=int, default=200)  # ~10 s of oracle decode on the host
     ap.add_argument("--prefill", default="512,2048,8192",
                     help="BF16 1B prefill prompt lengths reported beside the decode metric (empty: skip)")
@@ -156,15 +166,35 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def cpu_sample(path, prompt, decode_steps, threads):
+def cpu_sample(path, prompt, decode_steps, threads, acts_q8=False):
     """The oracle on the host cores: prefill the prompt, then `decode_steps` timed
     decode tokens. Returns (tok/s over the decode steps, ids)."""
     from oracle import oracle as O
-    m = O.Model(path)
+    m = O.Model(path, acts_q8=acts_q8)
     ids, ms, _ = m.generate(prompt, decode_steps + 1, nthreads=threads)
     m.close()
     dec = ms[1:]
     return float(len(dec) / (dec.sum() / 1e3)), ids
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def workload_config(args, world):
+    """The `config` of both arms' lines (the same dict, so the two can be compared)."""
+    spec, wt, plen = WORKLOADS[args.workload]
+    tp = args.workload in TP_WORKLOADS and world > 1
+    return {"workload": args.workload, "model": f"llama-3.2-{spec}-arch {wt}", "prompt": plen, "batch": 1,
+            "decode_steps": args.steps, "acts": args.acts,
+            "parallelism": f"tp{world}" if tp else ("replicas" if world > 1 else "single"),
+            "l2": "weights exceed the 126 MB L2 per step; no flush needed"}
 
 
 def run_reference(args):
@@ -177,7 +207,7 @@ def run_reference(args):
     prompt = G.prompt_ids(plen, seed=1234)
     threads = cpu_threads()
     from oracle import oracle as O
-    m = O.Model(path)
+    m = O.Model(path, acts_q8=args.acts == "q8")
     # untimed prefill, warm-up decode steps, then K timed decode steps (one token each)
     logits = m.forward(prompt, nthreads=threads)
     tok = np.array([O.greedy(logits)], np.uint32)
@@ -189,17 +219,26 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     m.close()
     v = args.steps / dt
-    sample = (f"{spec} {wt} W8A32 scalar x86 path (C restatement, -O2 -ffp-contract=off), {plen}-token prompt "
+    scheme = "W8A8 scalar (aarch64 semantics)" if args.acts == "q8" else "W8A32 scalar x86 path"
+    sample = (f"{spec} {wt} {scheme} (C restatement, -O2 -ffp-contract=off), {plen}-token prompt "
               f"untimed, {args.warmup} warm-up + {args.steps} timed decode tokens")
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+    line = {"impl": "reference", "metric": metric_name(args), "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded random-init GGUF, random prompt ids)",
-            "config": {"workload": args.workload, "prompt": plen, "batch": 1},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if args.acts == "f32" else "int8",
+            "data": "synthetic (seeded random-init GGUF N(0,0.02) quantized; uniform random prompt ids)",
+            "config": workload_config(args, int(os.environ.get("WORLD_SIZE", "1"))),
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample,
+                             "cpu_model": cpu_model(), "simd": "scalar fallback (x86), compiler autovectorised"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def metric_name(args):
+    if args.workload == "1b-q8_0" and args.acts == "f32":
+        return METRIC
+    return f"decode tok/s ({args.workload}{', acts q8' if args.acts == 'q8' else ''}, bs1)"
 
 
 def prefill_flops(cfg, n):
@@ -332,6 +371,156 @@ def run_sweep(lib, device, reps=20, only=""):
             "peak_source": kind, "results": res}
 
 
+def golden_ids(name):
+    """Greedy ids the oracle produced for a BASELINE-shape case (tests/golden, made by
+    tests/golden/make_golden.py --configs): same GGUF seed and prompt as the bench."""
+    p = os.path.join(ROOT, "tests", "golden", f"{name}.npz")
+    if not os.path.exists(p):
+        return None
+    return np.load(p)["ids"]
+
+
+def run_long_context(lib, G, device, steps=256):
+    """Config 3: the 1B Q4_0 model after a 2048-token prompt, `steps` greedy decode
+    tokens at KV lengths 2048-2304 (split-KV attention), steps chained on the device
+    and timed by CUDA events on the context stream. The first ids are checked against
+    the oracle's (tests/golden/cfg3_1b_q4_0.npz)."""
+    import torch
+    model = lib.Model(G.ensure_gguf("1b", "q4_0"), device=device)
+    cfg = model.config
+    prompt = G.prompt_ids(2048, seed=1234)
+    ctx = model.new_context(2048 + steps + 8)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    first = ctx.forward(prompt)
+    ctx.decode_steps(3)  # warm-up
+    ctx.reset()
+    first = ctx.forward(prompt)
+    kv0 = ctx.seq_len
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    ids = ctx.decode_steps(steps)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    got = np.concatenate([[first], ids]).astype(np.uint32)
+    want = golden_ids("cfg3_1b_q4_0")
+    parity = None
+    if want is not None:
+        n = min(len(want), len(got))
+        parity = {"ids_equal": bool(np.array_equal(got[:n], want[:n])), "n": int(n),
+                  "against": "oracle ids, tests/golden/cfg3_1b_q4_0.npz"}
+    peak, kind = peaks()
+    mean_kv = kv0 + (steps - 1) / 2
+    algo = bytes_per_step(cfg, cfg.weight_type, mean_kv)
+    achieved = algo / (ms / steps / 1e3) / 1e9
+    ctx.close()
+    model.close()
+    return {"workload": "1b-q4_0, 2048-token prompt, decode at KV %d-%d (config 3)" % (kv0, kv0 + steps),
+            "tok_s": steps / (ms / 1e3), "ms_per_token": ms / steps, "launches_per_token": None,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": kind, "algorithmic_bytes_per_step": algo},
+            "parity": parity}
+
+
+def nccl_allreduce_us(world, n_calls=64, floats=4096, reps=20):
+    """Device time of the TP step's collectives alone: `n_calls` all-reduces (sum) of
+    `floats` f32 (the 8B hidden size: one after O and one after down in each of the
+    32 layers) through torch's NCCL group, CUDA events on one stream; max over ranks."""
+    import torch
+    import torch.distributed as dist
+    buf = torch.zeros(floats, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3 * n_calls):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        for _ in range(reps * n_calls):
+            dist.all_reduce(buf)
+        b.record(s)
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) * 1e3 / reps], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3):
+    """Config 5: the 8B Q8_0 model (128-token prompt) sharded over all ranks (tensor
+    parallel, NCCL all-reduce after the O and down projections; TP1 on one GPU),
+    `steps` greedy decode tokens chained on the device, CUDA events on each rank's
+    context stream, max over ranks. Ids of the group are checked against the
+    oracle's ids of the same model (tests/golden/cfg5_8b_q8_0.npz has a 16-token
+    prompt, so the check decodes that prompt first)."""
+    import torch
+    if rank == 0:
+        G.ensure_gguf("8b", "q8_0")
+    if dist:
+        dist.barrier()
+    path = G.ensure_gguf("8b", "q8_0")
+    nccl_id = None
+    if world > 1:
+        from sqb200 import tp as sqtp
+        try:
+            grp = sqtp.Group.from_default_store(timeout_s=300)
+        except (AttributeError, ImportError):
+            grp = None
+        if grp is not None:
+            nccl_id = grp.share_id(lib.nccl_unique_id)
+        else:
+            box = [lib.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            nccl_id = box[0]
+        model = lib.Model(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    else:
+        model = lib.Model(path, device=local)
+    cfg = model.config
+    # parity: the fixture's prompt and ids
+    parity = None
+    gz = os.path.join(ROOT, "tests", "golden", "cfg5_8b_q8_0.npz")
+    if os.path.exists(gz):
+        z = np.load(gz)
+        ctx = model.new_context(64)
+        got = [ctx.forward(z["prompt"])] + [int(i) for i in ctx.decode_steps(len(z["ids"]) - 1)]
+        ctx.close()
+        parity = {"ids_equal": bool(np.array_equal(np.asarray(got, np.uint32), z["ids"])), "n": len(got),
+                  "against": "oracle ids, tests/golden/cfg5_8b_q8_0.npz"}
+    prompt = G.prompt_ids(128, seed=1234)
+    ctx = model.new_context(128 + warmup + steps + 8)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    ctx.forward(prompt)
+    ctx.decode_steps(warmup)
+    kv0 = ctx.seq_len
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    ctx.decode_steps(steps)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    lpt = ctx.launches_per_token
+    ctx.close()
+    model.close()
+    ar_us = nccl_allreduce_us(world) if dist else 0.0
+    peak, kind = peaks()
+    algo = bytes_per_step(cfg, cfg.weight_type, kv0 + (steps - 1) / 2)  # the whole model's bytes
+    per_rank = algo / world / (ms / steps / 1e3) / 1e9
+    return {"workload": f"8b-q8_0, 128-token prompt, tp{world}", "tp": world, "tok_s": steps / (ms / 1e3),
+            "ms_per_token": ms / steps, "launches_per_token": lpt,
+            "per_rank_gb_s": per_rank, "frac": per_rank / peak, "peak_gb_s": peak, "peak_source": kind,
+            "allreduce_us_per_token": ar_us,
+            "allreduce_note": "64 NCCL all-reduces of 4096 f32 timed alone through torch's NCCL group (the same "
+                              "library, size and count as the step's); 0 on one GPU",
+            "parity": parity}
+
+
 def run_ours(args):
     import torch
     rank = int(os.environ.get("RANK", "0"))
@@ -385,7 +574,7 @@ def run_ours(args):
     t0 = time.perf_counter()
     first = ctx.forward(prompt)
     prefill_s = time.perf_counter() - t0
-    ctx.decode_steps(args.warmup)
+    warm_ids = ctx.decode_steps(args.warmup)
     kv0 = ctx.seq_len
     lpt = ctx.launches_per_token
 
@@ -407,6 +596,7 @@ def run_ours(args):
     tokens_per_step = 1 if tp else world  # tensor parallel: the group makes one token a step
     value = tokens_per_step * args.steps / (ms / 1e3)
     step_ms = ms / args.steps
+    gpu_ids = np.concatenate([[first], warm_ids, ids]).astype(np.uint32)
 
     # e2e through the host-facing ABI: one sq_forward per token from host memory
     ctx.reset()
@@ -417,15 +607,18 @@ def run_ours(args):
         dist.barrier()
     t0 = time.perf_counter()
     host_tok = np.zeros(1, np.uint32)
+    e2e_ids = []
     for _ in range(args.steps):
         host_tok[0] = tok
         tok = ctx.forward(host_tok)
+        e2e_ids.append(tok)
     e2e_s = time.perf_counter() - t0
     if dist:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e = tokens_per_step * args.steps / e2e_s
+    e2e_same = bool(np.array_equal(np.asarray(e2e_ids, np.uint32), gpu_ids[1 + args.warmup:]))
 
     # roofline of the decode step (one persistent-kernel launch per token when available)
     mean_kv = kv0 + (args.steps - 1) / 2
@@ -434,30 +627,52 @@ def run_ours(args):
     peak, peak_kind = peaks()
     if tp:
         peak *= world  # every rank streams its shard from its own HBM
+    ctx.close()
+    model.close()
+
     cpu = None
+    parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         th = cpu_threads()
         cplen = plen if spec != "8b" else 8  # 8B on the CPU: a short prompt keeps the sample bounded
-        tps, cpu_ids = cpu_sample(path, prompt[:cplen], args.cpu_decode_steps, th)
-        cpu = {"value": tps, "unit": "tok/s", "cores": th, "kind": "port",
-               "sample": f"{cplen}-token prompt prefill untimed, then {args.cpu_decode_steps} timed decode tokens "
-                         f"({spec} {wt}, W8A32 scalar x86 path, C restatement, {th} threads)"}
-    prefill = None
-    if rank == 0 and world == 1 and args.prefill and spec == "1b":
+        n_cpu = args.cpu_decode_steps if spec != "8b" else 8
+        tps, cpu_ids = cpu_sample(path, prompt[:cplen], n_cpu, th, acts_q8=args.acts == "q8")
+        cpu = {"value": tps, "unit": "tok/s", "cores": th, "kind": "port", "cpu_model": cpu_model(),
+               "simd": "scalar fallback (x86), compiler autovectorised",
+               "sample": f"{cplen}-token prompt prefill untimed, then {n_cpu} timed decode tokens "
+                         f"({spec} {wt}, {'W8A8' if args.acts == 'q8' else 'W8A32'} scalar path, C restatement, "
+                         f"{th} threads)"}
+        if cplen == plen:
+            n = min(len(cpu_ids), len(gpu_ids))
+            parity = {"ids_equal": bool(np.array_equal(cpu_ids[:n], gpu_ids[:n])), "n": int(n),
+                      "e2e_ids_equal": e2e_same, "against": "oracle ids on the same GGUF and prompt"}
+    if parity is None:
+        want = golden_ids({"1b-q8_0": "cfg1_1b_q8_0"}.get(args.workload, "")) if args.acts == "f32" else None
+        if want is not None and plen == 32:
+            n = min(len(want), len(gpu_ids))
+            parity = {"ids_equal": bool(np.array_equal(want[:n], gpu_ids[:n])), "n": int(n),
+                      "e2e_ids_equal": e2e_same, "against": "oracle ids, tests/golden/cfg1_1b_q8_0.npz"}
+    single = rank == 0 and world == 1
+    prefill = long_ctx = sweep = None
+    if single and args.prefill and spec == "1b":
         prefill = run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], local)
+    if single and not args.no_extra:
+        long_ctx = run_long_context(lib, G, local)
+        sweep = run_sweep(lib, local)
+    tp_line = None
+    if not args.no_extra and not tp:
+        tp_line = run_tp(lib, G, rank, world, local, dist)
     if rank == 0:
+        conf = workload_config(args, world)
         line = {
-            "metric": METRIC if args.workload == "1b-q8_0" else f"decode tok/s ({args.workload}, bs1)",
+            "metric": metric_name(args),
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": "f32" if args.acts == "f32" else "int8",
             "data": "synthetic (seeded random-init GGUF N(0,0.02) quantized; uniform random prompt ids)",
-            "config": {"workload": args.workload, "model": f"llama-3.2-{spec}-arch {wt}", "prompt": plen,
-                       "batch": 1, "decode_steps": args.steps, "acts": args.acts,
-                       "parallelism": f"tp{world}" if tp else ("replicas" if world > 1 else "single"),
-                       "l2": "weights %.2f GB > 126 MB L2 per step; no flush needed" % (algo / 1e9),
-                       "prefill_tok_s": plen / prefill_s, "kv_len_start": kv0},
+            "config": conf,
+            "decode": {"prefill_tok_s": plen / prefill_s, "kv_len_start": kv0, "launches_per_token": lpt},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic_for(args.workload),
@@ -465,14 +680,22 @@ def run_ours(args):
             "gpu_launches": args.steps * lpt,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
-            "first_ids": [int(first)] + [int(i) for i in ids[:8]],
+            "parity": parity,
+            "first_ids": [int(i) for i in gpu_ids[:9]],
             "prefill": prefill,
+            "long_context": long_ctx,
+            "sweep": sweep,
+            "tp": tp_line,
         }
         print(json.dumps(line), flush=True)
-    ctx.close()
-    model.close()
     if dist:
+        dist.barrier()
         dist.destroy_process_group()
+    bad = [k for k, v in (("decode", parity), ("long_context", long_ctx and long_ctx["parity"]),
+                          ("tp", tp_line and tp_line["parity"])) if v is not None and not v["ids_equal"]]
+    if bad:
+        print(f"parity failure: GPU greedy ids differ from the oracle's in {', '.join(bad)}", file=sys.stderr)
+        return 1
     return 0
 
 

@@ -60,6 +60,19 @@ const char *sq_last_error(void);
 /* Library build string (arch, version). */
 const char *sq_version(void);
 
+/* Bounded-wait status of the current device. Every device-side wait in this
+ * library gives up after a time limit instead of hanging. The model-level calls
+ * (sq_forward, sq_decode_steps, sq_generate) check this themselves and return
+ * SQ_ERR_TIMEOUT. Op-level calls are asynchronous and cannot: a wait that expired
+ * inside sq_linear / sq_linear_shared (the streaming matvec, m = 1) or sq_linear /
+ * sq_sdpa_cached (the tensor-core GEMM and attention, m >= 2) is recorded in a word
+ * of the device. After synchronizing the stream, this returns SQ_OK, or
+ * SQ_ERR_TIMEOUT when such a wait expired since the record was last cleared (the
+ * outputs of the calls since then are not valid); `clear` != 0 resets the record.
+ * The record covers every stream and context of the device. No counterpart in the
+ * reference, whose CPU kernels cannot time out (kernels/kernel_error.rs:2-7). */
+int sq_wait_status(int clear);
+
 /* ---- op level (device pointers; async on stream) ---------------------------- */
 
 /* ops/linear.rs:26-37 `linear`: output[m][out_dim] = input[m][in_dim] @ weight,

@@ -20,7 +20,7 @@ def build(force: bool = False) -> str:
     if not force and os.path.exists(LIB) and os.path.getmtime(LIB) >= newest:
         return LIB
     cmd = ["gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-fPIC", "-shared",
-           "-std=c11", "-Wall", "-Wno-unused-function", "-o", LIB] + SRCS + ["-lm"]
+           "-std=c11", "-Wall", "-Wno-unused-function", "-Wno-psabi", "-o", LIB] + SRCS + ["-lm"]
     subprocess.run(cmd, check=True)
     return LIB
 

@@ -197,6 +197,54 @@ float or_dot_f32_f32(const float *a, const float *b, size_t n) {
     return acc;
 }
 
+/* Eight activation rows against one weight row at once, for prefill (m > 1). Lane j
+ * of every vector belongs to row j alone and takes exactly the operations of the
+ * single-row function above in the same order (f32 mul, then add; -ffp-contract=off
+ * keeps them unfused), so each output is bit-identical to or_dot_f32_*; the lanes
+ * only let eight independent sums run side by side. `at` is the row block
+ * transposed: at[i * 8 + j] = row j, element i. */
+#define OR_RB 8
+typedef float or_v8 __attribute__((vector_size(32)));
+
+static inline or_v8 v8_splat(float x) { return (or_v8){x, x, x, x, x, x, x, x}; }
+
+static or_v8 dot8_f32_q8_0(const or_v8 *at, const uint8_t *b, size_t nblocks) {
+    or_v8 acc = v8_splat(0.0f);
+    for (size_t k = 0; k < nblocks; k++) {
+        const uint8_t *blk = b + k * 34;
+        const or_v8 *ch = at + k * 32;
+        or_v8 block_acc = v8_splat(0.0f);
+        for (int i = 0; i < 32; i++) block_acc = block_acc + ch[i] * v8_splat((float)(int8_t)blk[2 + i]);
+        acc = acc + block_acc * v8_splat(or_f16_to_f32(rd16(blk)));
+    }
+    return acc;
+}
+
+static or_v8 dot8_f32_q4_0(const or_v8 *at, const uint8_t *b, size_t nblocks) {
+    or_v8 acc = v8_splat(0.0f);
+    for (size_t k = 0; k < nblocks; k++) {
+        const uint8_t *blk = b + k * 18;
+        const or_v8 *ch = at + k * 32;
+        or_v8 block_acc = v8_splat(0.0f);
+        for (int j = 0; j < 16; j++) {
+            uint8_t byte = blk[2 + j];
+            int lo = (int)(byte & 0x0F) - 8, hi = (int)(byte >> 4) - 8;
+            block_acc = block_acc + (ch[j] * v8_splat((float)lo) + ch[j + 16] * v8_splat((float)hi));
+        }
+        acc = acc + block_acc * v8_splat(or_f16_to_f32(rd16(blk)));
+    }
+    return acc;
+}
+
+static or_v8 dot8_f32_bf16(const or_v8 *at, const uint8_t *b, size_t nblocks) {
+    or_v8 acc = v8_splat(0.0f);
+    for (size_t k = 0; k < nblocks; k++) {
+        const uint8_t *blk = b + k * 64;
+        for (int i = 0; i < 32; i++) acc = acc + at[k * 32 + i] * v8_splat(or_bf16_to_f32(rd16(blk + 2 * i)));
+    }
+    return acc;
+}
+
 /* ------------------------------------------------------------------------- */
 /* linear  (ops/linear.rs:26-168, kernels/matmul.rs:28-171)                    */
 /* ------------------------------------------------------------------------- */
@@ -214,6 +262,25 @@ int or_linear(const float *in, int m, int in_dim, const uint8_t *w, int type, in
         or_quantize_row_q8_0(in, (size_t)m * in_dim, aq);
     }
     if (nthreads <= 0) nthreads = 1;
+    if (!int_acts && m > 1) {
+        /* prefill: blocks of OR_RB rows against each weight row (outputs identical to
+         * the row-outermost loop of matmul.rs:34, which only orders independent sums) */
+        or_v8 *at = (or_v8 *)aligned_alloc(32, sizeof(or_v8) * (size_t)in_dim);
+        for (int r0 = 0; r0 < m; r0 += OR_RB) {
+            int nr = m - r0 < OR_RB ? m - r0 : OR_RB;
+            for (int i = 0; i < in_dim; i++)
+                for (int j = 0; j < OR_RB; j++) at[i][j] = j < nr ? in[(size_t)(r0 + j) * in_dim + i] : 0.0f;
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+            for (int n = 0; n < out_dim; n++) {
+                const uint8_t *wr = w + (size_t)n * bpr * bb;
+                or_v8 v = type == OR_Q8_0 ? dot8_f32_q8_0(at, wr, bpr)
+                                          : (type == OR_Q4_0 ? dot8_f32_q4_0(at, wr, bpr) : dot8_f32_bf16(at, wr, bpr));
+                for (int j = 0; j < nr; j++) out[(size_t)(r0 + j) * out_dim + n] = v[j];
+            }
+        }
+        free(at);
+        return OR_OK;
+    }
     for (int r = 0; r < m; r++) { /* fused_bridge_rows: row loop outermost, matmul.rs:34 */
         const float *a = in + (size_t)r * in_dim;
 #pragma omp parallel for num_threads(nthreads) schedule(static)

@@ -16,6 +16,7 @@ namespace sq {
 // elements need 4096 states (96 KiB). Every state the final pass reads is written
 // by the partial pass of the same call, so nothing needs clearing between calls.
 constexpr int NOALLOC_ARGMAX_STATES = 4096;
+static_assert(sizeof(ArgState) == 24, "the 96 KiB figure counts 24-byte states");
 static __device__ __align__(256) ArgState g_argmax_states[NOALLOC_ARGMAX_STATES];
 
 // Device address of g_argmax_states, looked up once per device with that device

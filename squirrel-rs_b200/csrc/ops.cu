@@ -141,7 +141,7 @@ constexpr int MV_GATE_ROWS = 1024;             // gate rows per CTA kept for SiL
 constexpr int MV_HDR = 2 * MV_NS * 8 + ((MV_NS * MV_REDROWS + 1) * MV_CONS + MV_GATE_ROWS) * 4;  // mbarriers, sums, gates
 constexpr int MV_RING_OFF = (MV_HDR + 127) & ~127;
 
-__device__ unsigned g_mv_err;  // set when a bounded wait of k_matvec gave up
+__device__ unsigned g_mv_err;  // set when a bounded wait of k_matvec gave up (matvec_status)
 
 __device__ __forceinline__ uint32_t mv_su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ bool mv_try_wait(uint32_t b, unsigned parity) {
@@ -997,6 +997,24 @@ cudaError_t launch_argmax_fold(cudaStream_t s, const void *states, int n, long l
 }
 size_t argmax_state_bytes() { return sizeof(ArgState); }
 
+unsigned matvec_status(bool clear) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_mv_err, sizeof(v));
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_mv_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+int device_wait_status(bool clear, const char *what) {
+  const unsigned mv = matvec_status(clear), tc = gemm_tc_status(clear);
+  if (!mv && !tc) return SQ_OK;
+  std::string who = mv ? "the streaming matvec" : "";
+  if (tc) who += std::string(mv ? " and " : "") + "a tensor-core kernel";
+  return fail(SQ_ERR_TIMEOUT, std::string(what) + ": a bounded wait of " + who + " expired");
+}
+
 cudaError_t launch_argmax(cudaStream_t s, const float *x, size_t n, void *partials, long long *out) {
   const int np = argmax_partials(n);
   k_argmax_partial<<<np, ARGMAX_THREADS, 0, s>>>(x, n, (ArgState *)partials);
@@ -1034,6 +1052,7 @@ static cudaError_t scratch_alloc(void **p, size_t bytes, cudaStream_t s) {
 
 extern "C" const char *sq_last_error(void) { return g_last_error.c_str(); }
 extern "C" const char *sq_version(void) { return "squirrel-b200 0.1 (sm_100a)"; }
+extern "C" int sq_wait_status(int clear) { return sq::device_wait_status(clear != 0, "wait_status"); }
 
 // Workspace of the tensor-core GEMM for an op-level call (m >= 2, f32 activations):
 // the three bf16 activation terms plus up to 16 split-K partials.

@@ -50,6 +50,11 @@ cudaError_t launch_gemm_tc(cudaStream_t s, const float *x, int m, int K, const v
                            float *ws, size_t ws_floats);
 // Non-zero when a bounded wait of a tensor-core kernel gave up (read after a sync).
 unsigned gemm_tc_status(bool clear);
+// Non-zero when a bounded wait of the streaming matvec (k_matvec) gave up (read after a sync).
+unsigned matvec_status(bool clear);
+// Both words of the current device, read (and cleared when `clear`) after a sync:
+// SQ_OK, or SQ_ERR_TIMEOUT with a message naming `what` and the kernels that gave up.
+int device_wait_status(bool clear, const char *what);
 unsigned *tc_err_ptr();  // device address of that error word (current device)
 // False when SQB200_GEMM=simt selects the CUDA-core GEMM for every weight type.
 bool gemm_tc_enabled();
@@ -89,7 +94,8 @@ cudaError_t launch_mul(cudaStream_t s, const float *a, const float *b, float *ou
 cudaError_t launch_add(cudaStream_t s, float *a, const float *b, size_t n);
 cudaError_t launch_silu_mul(cudaStream_t s, const float *g, const float *u, float *out, size_t n);
 cudaError_t launch_dequantize(cudaStream_t s, const void *blocks, int wtype, size_t n, float *out);
-// Two-stage greedy argmax; `partials` holds at least argmax_partials(n) states (16 bytes each).
+// Two-stage greedy argmax; `partials` holds at least argmax_partials(n) states
+// (sizeof(ArgState) = 24 bytes each).
 int argmax_partials(size_t n);
 cudaError_t launch_argmax(cudaStream_t s, const float *x, size_t n, void *partials, long long *out);
 // Tensor parallel: the argmax state of a vocabulary shard starting at `offset`

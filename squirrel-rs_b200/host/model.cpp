@@ -858,7 +858,8 @@ extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *ou
   SQ_CUDA(cudaStreamSynchronize(c->stream));
   st = decode_check(c);
   if (st) return st;
-  if (gemm_tc_status(true)) return fail(SQ_ERR_TIMEOUT, "forward: a bounded wait of the tensor-core GEMM expired");
+  st = device_wait_status(true, "forward");
+  if (st) return st;
   if (out_argmax) *out_argmax = (uint32_t)id;
   return SQ_OK;
 }
@@ -935,6 +936,7 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
   cudaError_t e3 = cudaStreamSynchronize(c->stream);
   if (!st && e3 != cudaSuccess) st = cuda_fail(e3, "decode_steps sync");
   if (!st) st = decode_check(c);
+  if (!st) st = device_wait_status(true, "decode_steps");
   c->have_logits = true;
   return st;
 }

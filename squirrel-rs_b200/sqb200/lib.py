@@ -48,6 +48,7 @@ _vp, _i, _sz, _f = C.c_void_p, C.c_int, C.c_size_t, C.c_float
 SIGNATURES = {
     "sq_last_error": (C.c_char_p, []),
     "sq_version": (C.c_char_p, []),
+    "sq_wait_status": (_i, [_i]),
     "sq_linear": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i]),
     "sq_linear_shared": (_i, [_vp, _vp, _i, _i, _i, C.POINTER(_vp), C.POINTER(_i), _i, C.POINTER(_vp), _i, _vp]),
     "sq_embed": (_i, [_vp, _vp, _i, _vp, _i, _i, _i, _vp]),
@@ -120,6 +121,12 @@ def _p(t):
 def _stream():
     import torch
     return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def wait_status(clear=True):
+    """sq_wait_status: raise KernelError (Timeout) if a bounded device-side wait of an
+    op-level call expired on the current device (call after synchronizing)."""
+    _check(load().sq_wait_status(int(clear)))
 
 
 # ---- op level (torch CUDA tensors) ------------------------------------------------

@@ -65,3 +65,18 @@ def test_cuda_matches_golden(gpu_lib, monkeypatch, spec, wt, op_level):
     assert_logits_close(ctx.logits(), g["logits_last"])
     ctx.close()
     m.close()
+
+
+def test_oracle_reproduces_config1_golden():
+    """The 1B Q8_0 fixture of config 1 (tests/golden/cfg1_1b_q8_0.npz: the bench's GGUF
+    seed and 32-token prompt, 33 greedy ids, logits after the prompt and after the last
+    step) is the oracle's output bit for bit; the GPU tests and the bench check their
+    ids against it."""
+    from oracle import build as oracle_build
+    from sqb200 import gguf_synth as G
+    oracle_build.build()
+    z = np.load(MG.config_fixture_path("cfg1_1b_q8_0"))
+    assert MG.sha256(G.ensure_gguf("1b", "q8_0")) == str(z["gguf_sha256"])
+    got = MG.compute_config("cfg1_1b_q8_0")
+    for k in ("prompt", "ids", "logits_first", "logits_last"):
+        assert np.array_equal(got[k], z[k]), k

@@ -28,6 +28,28 @@ def _rank(rank, world, port, scenario, q):
             return
         if scenario == "slow" and rank == 1:
             time.sleep(1.0)
+        if scenario == "reuse":
+            # a second share_id, a second group and a repeated tag must wait for fresh
+            # keys: rank 0 publishes each new id late, and a rank that left after the
+            # first "step" check-in must be missed at the second one
+            ids = [grp.share_id(lambda: b"first" + bytes(123))]
+            if rank == 0:
+                time.sleep(0.5)
+            ids.append(grp.share_id(lambda: b"second" + bytes(122)))
+            grp2 = tp.Group.from_default_store(timeout_s=TIMEOUT_S)
+            if rank == 0:
+                time.sleep(0.5)
+            ids.append(grp2.share_id(lambda: b"third" + bytes(123)))
+            grp.check_in("step")
+            if rank == 1:
+                out = ("left",)
+                return
+            try:
+                grp.check_in("step")
+                out = ("ok", ids, None)
+            except tp.GroupTimeout as e:
+                out = ("ok", ids, sorted(e.missing))
+            return
         t0 = time.monotonic()
         try:
             nid = grp.share_id(lambda: b"id-from-rank-0" + bytes(114))
@@ -99,3 +121,15 @@ def test_rank_leaving_between_steps_is_found_before_the_next_step():
         kind, missing, waited = res[r]
         assert kind == "timeout" and missing == [1], res
         assert waited < TIMEOUT_S + 5.0
+
+
+def test_keys_are_not_reused_across_groups_ids_and_tags():
+    """A second share_id, a second group and a repeated check-in tag wait for keys
+    of their own instead of passing on keys an earlier phase left in the store."""
+    res = run("reuse")
+    assert res[1] == ("left",)
+    for r in (0, 2):
+        kind, ids, missing = res[r]
+        assert kind == "ok", res
+        assert [i[:6].rstrip(b"\0") for i in ids] == [b"first", b"second", b"third"], res
+        assert missing == [1], res
