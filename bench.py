@@ -446,19 +446,25 @@ def nccl_allreduce_us(world, n_calls=64, floats=4096, reps=20):
     return float(t.item())
 
 
-def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3):
+def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3, mode="peer"):
     """Config 5: the 8B Q8_0 model (128-token prompt) sharded over all ranks (tensor
-    parallel, NCCL all-reduce after the O and down projections; TP1 on one GPU),
-    `steps` greedy decode tokens chained on the device, CUDA events on each rank's
-    context stream, max over ranks. Ids of the group are checked against the
-    oracle's ids of the same model (tests/golden/cfg5_8b_q8_0.npz has a 16-token
-    prompt, so the check decodes that prompt first)."""
+    parallel, all-reduce after the O and down projections; TP1 on one GPU), `steps`
+    greedy decode tokens chained on the device, CUDA events on each rank's context
+    stream, max over ranks. mode "peer": the decode row's all-reduces on the one-shot
+    NVLink peer-memory kernel (the default); "nccl": on NCCL (SQB200_TP_ALLREDUCE).
+    Ids of the group are checked against the oracle's ids of the same model
+    (tests/golden/cfg5_8b_q8_0.npz has a 16-token prompt, so the check decodes that
+    prompt first)."""
     import torch
     if rank == 0:
         G.ensure_gguf("8b", "q8_0")
     if dist:
         dist.barrier()
     path = G.ensure_gguf("8b", "q8_0")
+    if mode == "nccl":
+        os.environ["SQB200_TP_ALLREDUCE"] = "nccl"  # read when the model is created
+    else:
+        os.environ.pop("SQB200_TP_ALLREDUCE", None)
     nccl_id = None
     if world > 1:
         from sqb200 import tp as sqtp
@@ -508,16 +514,20 @@ def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3):
     lpt = ctx.launches_per_token
     ctx.close()
     model.close()
-    ar_us = nccl_allreduce_us(world) if dist else 0.0
+    os.environ.pop("SQB200_TP_ALLREDUCE", None)
+    ar_us = nccl_allreduce_us(world) if dist and mode == "nccl" else None
     peak, kind = peaks()
     algo = bytes_per_step(cfg, cfg.weight_type, kv0 + (steps - 1) / 2)  # the whole model's bytes
     per_rank = algo / world / (ms / steps / 1e3) / 1e9
-    return {"workload": f"8b-q8_0, 128-token prompt, tp{world}", "tp": world, "tok_s": steps / (ms / 1e3),
+    return {"workload": f"8b-q8_0, 128-token prompt, tp{world}", "tp": world,
+            "allreduce": ("peer-memory one-shot kernel (NVLink stores, fused residual add)" if mode == "peer"
+                          else "NCCL") if world > 1 else "none (one GPU)",
+            "tok_s": steps / (ms / 1e3),
             "ms_per_token": ms / steps, "launches_per_token": lpt,
             "per_rank_gb_s": per_rank, "frac": per_rank / peak, "peak_gb_s": peak, "peak_source": kind,
-            "allreduce_us_per_token": ar_us,
-            "allreduce_note": "64 NCCL all-reduces of 4096 f32 timed alone through torch's NCCL group (the same "
-                              "library, size and count as the step's); 0 on one GPU",
+            "nccl_allreduce_us_per_token": ar_us,
+            "nccl_allreduce_note": "64 NCCL all-reduces of 4096 f32 timed alone through torch's NCCL group (the same "
+                                   "library, size and count as the step's); null unless mode nccl on several GPUs",
             "parity": parity}
 
 
@@ -662,6 +672,8 @@ def run_ours(args):
     tp_line = None
     if not args.no_extra and not tp:
         tp_line = run_tp(lib, G, rank, world, local, dist)
+        if world > 1:  # the same step with NCCL's all-reduce, for comparison
+            tp_line["nccl"] = run_tp(lib, G, rank, world, local, dist, mode="nccl")
     if rank == 0:
         conf = workload_config(args, world)
         line = {
@@ -692,7 +704,9 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     bad = [k for k, v in (("decode", parity), ("long_context", long_ctx and long_ctx["parity"]),
-                          ("tp", tp_line and tp_line["parity"])) if v is not None and not v["ids_equal"]]
+                          ("tp", tp_line and tp_line["parity"]),
+                          ("tp nccl", tp_line and tp_line.get("nccl") and tp_line["nccl"]["parity"]))
+           if v is not None and not v["ids_equal"]]
     if bad:
         print(f"parity failure: GPU greedy ids differ from the oracle's in {', '.join(bad)}", file=sys.stderr)
         return 1

@@ -193,14 +193,28 @@ int sq_generate(sq_ctx *c, const uint32_t *prompt, size_t n_prompt, int max_toke
 int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids);
 /* ---- tensor parallelism (several GPUs, one process per GPU) -----------------------
  * No counterpart in the reference (a CPU engine): the multi-GPU form of the model
- * level above, Megatron column/row sharding with an NCCL all-reduce after the O and
- * down projections and a greedy argmax across the vocabulary shards. Every rank
- * makes the same calls in the same order (sq_forward, sq_decode_steps,
- * sq_generate, sq_ctx_logits are collective); each rank's result is the whole
+ * level above, Megatron column/row sharding with an all-reduce after the O and down
+ * projections and a greedy argmax across the vocabulary shards. Every rank makes
+ * the same calls in the same order (sq_forward, sq_decode_steps, sq_generate,
+ * sq_ctx_logits, sq_tp_recover are collective); each rank's result is the whole
  * model's. Rank 0 makes the id with sq_nccl_unique_id and shares its bytes with
- * the other ranks (e.g. over torch.distributed). NCCL is loaded at first use. */
+ * the other ranks (e.g. over torch.distributed). NCCL is loaded at first use.
+ * The all-reduces of a decode row run on a one-shot kernel over NVLink peer memory
+ * (each rank stores its partial into every rank's mailbox, then sums them in rank
+ * order with the residual add); prefill rows, and groups whose GPUs cannot map each
+ * other's memory, use NCCL's. SQB200_TP_ALLREDUCE=nccl, set when the model is
+ * created, selects NCCL's for decode rows too. Contexts of one tensor-parallel
+ * model must not run concurrently. */
 /* ncclGetUniqueId into out (n >= 128 bytes). */
 int sq_nccl_unique_id(void *out, size_t n);
+/* After SQ_ERR_TIMEOUT on any rank (a peer's partial sum did not arrive in time,
+ * e.g. because a rank stopped issuing steps), the ranks' all-reduce sequence
+ * numbers may differ. Once every rank has stopped issuing work, every rank calls
+ * this (collective, over NCCL): it clears the peer-memory all-reduce's mailboxes,
+ * sequence numbers and error word. Contexts must then be reset (sq_ctx_reset):
+ * their KV cache past the last good position is undefined. SQ_OK without effect for
+ * a model on one GPU or one on NCCL's all-reduce. */
+int sq_tp_recover(sq_model *m);
 /* sq_model_create / sq_model_load_gguf as rank tp_rank of tp_size GPUs. n_heads,
  * n_kv_heads, vocab_size and ffn_dim/32 must divide by tp_size. */
 int sq_model_create_tp(const sq_llama_config *cfg, int device, int acts, int tp_rank, int tp_size,

@@ -6,7 +6,7 @@
 // attention, O + residual, RMSNorm + gate/up + SiLU*up, down + residual], final
 // RMSNorm, LM head, argmax — and feeds the argmax back as the next token id.
 //
-// Layout: one CTA of NC warps per SM. Every weight row the CTA owns for the whole
+// Layout: one CTA of NC warps (NGRP groups of four) per SM. Every weight row the CTA owns for the whole
 // token streams through a ring of NSLOT shared-memory slots with 1-D bulk async
 // copies (cp.async.bulk ... mbarrier::complete_tx): the last warp to finish with a
 // slot immediately refills it with the tile NSLOT positions ahead in the CTA's tile
@@ -38,14 +38,17 @@
 namespace sq {
 namespace dk {
 
-constexpr int NC = 8;                    // warps per CTA (2 per SM sub-partition: 255 registers each)
+#ifndef SQ_DECODE_GROUPS
+#define SQ_DECODE_GROUPS 2
+#endif
+constexpr int NG = 4;                    // warps per group (one per SM sub-partition)
+constexpr int NGRP = SQ_DECODE_GROUPS;   // groups per CTA: tile k goes to group k % NGRP
+constexpr int NC = NG * NGRP;            // warps per CTA
 constexpr int NTHREADS = NC * 32;
-constexpr int NG = NC / 2;               // warps per group (the groups take alternate tiles)
 constexpr int SLOT = 36864;              // bytes per ring slot
 constexpr int NSLOT = 5;
-constexpr int PF_TILES = 0;              // tiles prefetched into L2 beyond the ring (off: measured faster)
 constexpr int MAX_LAYERS = 128;
-constexpr int MAX_TILE_ITEMS = 256;      // rows x segments per tile
+constexpr int MAX_TILE_ITEMS = 64;       // rows x segments per tile
 constexpr int MAX_X = 8192;              // longest stage input staged in shared memory (floats)
 constexpr int MAX_LM_ROWS = 1024;        // LM-head rows per CTA kept in shared memory
 constexpr int GROUP = 4;                 // q heads per kv head supported here
@@ -74,13 +77,21 @@ struct Params {  // passed by value to the decode kernel: at most the 32 KB of k
   int *pos;
   unsigned long long *hid_ll, *q_ll, *kv_ll, *attn_ll, *act_ll;  // tagged exchange vectors
   unsigned *launch;              // launches so far (the high bits of every tag)
-  unsigned long long *timeline;  // optional per-CTA stage timestamps (SQ_DECODE_TIMELINE)
+#ifdef SQ_DECODE_TIMELINE
+  // profiling builds only (-DSQ_DECODE_TIMELINE): per-CTA stage timestamps, and per
+  // tile {issued, landed, done} clocks [G][max_tiles][3]
+  unsigned long long *timeline;
   int tl_stride;
-  unsigned long long *tile_tl;   // with the timeline: per tile {issued, landed, done} clocks [G][max_tiles][3]
+  unsigned long long *tile_tl;
+#endif
   int2 *tiles;                   // [G][max_tiles] tile table: {row, layer<<16 | kind<<12 | rows}
   int *ntiles;                   // [G]
   int max_tiles;
-  int pf;                        // L2 prefetch distance in tiles beyond the ring (0 = off)
+  // Failure-detection tests only (SQ_TEST_DROP_EXCHANGE=n, read when the context is
+  // created): in the context's n-th launch the producer of residual word 0 after
+  // layer 0's O projection does not write it, so the gate/up stage's bounded poll
+  // expires and the kernel reports a timeout. 0 = off.
+  unsigned drop_tag;
   LayerW layers[MAX_LAYERS];
 };
 static_assert(sizeof(Params) + 64 <= 32764, "Params fits the kernel parameter space");
@@ -147,10 +158,6 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
-// Prefetch [src, src + bytes) into L2 (no completion to wait for).
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ uint32_t lds32(uint32_t a) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
@@ -172,18 +179,19 @@ __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+#ifdef SQ_DECODE_TIMELINE
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Timeline slot k of this CTA: 0 = start; for stage s (5 per layer, the LM head is
-// stage 5L) 8s+1 = input words arrived, 8s+3 = input staged in shared memory, 8s+2 =
-// input in registers, 8s+4 / 8s+5 = first / last tile landed, 8s+6 = stage done;
-// stride-2 = LM head done, stride-1 = end. Stamps are SM clock counts; each CTA
-// also records one (global ns, clock) pair at a tick of the global timer at start
-// and at end (slots stride-6..stride-3), which maps its clocks onto global time
-// more finely than the timer's own resolution.
+// Profiling builds only. Timeline slot k of this CTA: 0 = start; for stage s (5 per
+// layer, the LM head is stage 5L) 8s+1 = input words arrived, 8s+3 = input staged in
+// shared memory, 8s+2 = input in registers, 8s+4 / 8s+5 = first / last tile landed,
+// 8s+6 = stage done; stride-2 = LM head done, stride-1 = end. Stamps are SM clock
+// counts; each CTA also records one (global ns, clock) pair at a tick of the global
+// timer at start and at end (slots stride-6..stride-3), which maps its clocks onto
+// global time more finely than the timer's own resolution.
 __device__ __forceinline__ void stamp(const Params &p, int k) {
   if (p.timeline && threadIdx.x == 0) p.timeline[(size_t)blockIdx.x * p.tl_stride + k] = (unsigned long long)clock64();
 }
@@ -200,6 +208,17 @@ __device__ __forceinline__ void stamp_sync(const Params &p, int k) {
     p.timeline[(size_t)blockIdx.x * p.tl_stride + k + 1] = (unsigned long long)c;
   }
 }
+__device__ __forceinline__ void stamp_tile(const Params &p, int j, int which) {
+  if (p.tile_tl) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + j) * 3 + which] = (unsigned long long)clock64();
+}
+#define TL_STRIDE(p) ((p).tl_stride)
+#else
+__device__ __forceinline__ void stamp(const Params &, int) {}
+__device__ __forceinline__ void stamp_now(const Params &, int) {}
+__device__ __forceinline__ void stamp_sync(const Params &, int) {}
+__device__ __forceinline__ void stamp_tile(const Params &, int, int) {}
+#define TL_STRIDE(p) 6
+#endif
 
 // ---------------------------------------------------------------------------------
 // work split (the same in the tile tables and in the consumers)
@@ -291,46 +310,143 @@ __device__ __forceinline__ float nibf(uint32_t nib4, int byte) {  // nib4 = 4 ni
   return __uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7540u | (unsigned)byte)) - 8388616.0f;
 }
 
+// Four weight rows at a time. The lane's partial dot products of rows at shared
+// addresses ra[0..3] with its 64 activations (x2[j] = elements 2j, 2j+1): Q8_0 /
+// Q4_0 one 68 / 36-byte block pair of segment `seg` (4-byte words at an odd word
+// stride between lanes: conflict-free), BF16 eight 16-byte chunks. The loop runs
+// word by word with the four rows innermost, so each step has four independent
+// load -> convert -> FMA chains and the weights never sit in registers longer than
+// one step. Per block the products are summed first and scaled once, as the
+// reference does (dot_prod.rs:86-96, 255-270; BF16 one running sum, :464-472).
 template <int T>
-constexpr int nwords() {
-  return T == SQ_Q8_0 ? 17 : (T == SQ_Q4_0 ? 9 : 32);
-}
-
-// This lane's weight words of one row: Q8_0 / Q4_0 one 68 / 36-byte block pair
-// (4-byte aligned, conflict-free: odd word stride), BF16 eight 16-byte chunks.
-template <int T>
-__device__ __forceinline__ void lane_load(uint32_t row, int seg, int lane, uint32_t (&w)[nwords<T>()]) {
+__device__ __forceinline__ void quad_dot(const uint32_t (&ra)[4], int seg, int lane, const f2x (&x2)[32],
+                                         float (&out)[4]) {
   if constexpr (T == SQ_Q8_0) {
-    const uint32_t a = row + (uint32_t)(seg * 32 + lane) * 68u;
+    const uint32_t off = (uint32_t)(seg * 32 + lane) * 68u;
+    const f2x bias = pk2(-8388736.0f, -8388736.0f);  // 2^23 + 128: sign-flipped int8 under 2^23
+    f2x A[4], B[4];
+    float s0[4], s1[4];
 #pragma unroll
-    for (int i = 0; i < 17; i++) w[i] = lds32(a + 4 * i);
+    for (int r = 0; r < 4; r++) A[r] = B[r] = 0ull;
+#pragma unroll
+    for (int k = 0; k < 17; k++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t wx = w[r] ^ 0x80808080u;
+        const f2x lo = fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7540u), __byte_perm(wx, 0x4B000000u, 0x7541u)), bias);
+        const f2x hi = fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7542u), __byte_perm(wx, 0x4B000000u, 0x7543u)), bias);
+        if (k == 0) {  // scale of block 0, quants 0, 1
+          s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
+          A[r] = ffma2(x2[0], hi, A[r]);
+        } else if (k < 8) {  // quants 4k-2 .. 4k+1 of block 0
+          A[r] = ffma2(x2[2 * k - 1], lo, A[r]);
+          A[r] = ffma2(x2[2 * k], hi, A[r]);
+        } else if (k == 8) {  // quants 30, 31 of block 0, scale of block 1
+          A[r] = ffma2(x2[15], lo, A[r]);
+          s1[r] = h2f((uint16_t)(w[r] >> 16));
+        } else {  // quants 4k-36 .. 4k-33 of block 1
+          B[r] = ffma2(x2[2 * k - 2], lo, B[r]);
+          B[r] = ffma2(x2[2 * k - 1], hi, B[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const float2 a = up2(A[r]), b = up2(B[r]);
+      out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
+    }
   } else if constexpr (T == SQ_Q4_0) {
-    const uint32_t a = row + (uint32_t)(seg * 32 + lane) * 36u;
+    const uint32_t off = (uint32_t)(seg * 32 + lane) * 36u;
+    const f2x bias = pk2(-8388616.0f, -8388616.0f);  // 2^23 + 8: nibble q under 2^23, value q - 8
+    f2x A[4], B[4];
+    float s0[4], s1[4];
 #pragma unroll
-    for (int i = 0; i < 9; i++) w[i] = lds32(a + 4 * i);
+    for (int r = 0; r < 4; r++) A[r] = B[r] = 0ull;
+#pragma unroll
+    for (int k = 0; k < 9; k++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        // low nibbles are elements j, high nibbles elements j + 16 of their block
+        const uint32_t nl = w[r] & 0x0F0F0F0Fu, nh = (w[r] >> 4) & 0x0F0F0F0Fu;
+        const f2x l01 = fadd2(pk2u(__byte_perm(nl, 0x4B000000u, 0x7540u), __byte_perm(nl, 0x4B000000u, 0x7541u)), bias);
+        const f2x l23 = fadd2(pk2u(__byte_perm(nl, 0x4B000000u, 0x7542u), __byte_perm(nl, 0x4B000000u, 0x7543u)), bias);
+        const f2x h01 = fadd2(pk2u(__byte_perm(nh, 0x4B000000u, 0x7540u), __byte_perm(nh, 0x4B000000u, 0x7541u)), bias);
+        const f2x h23 = fadd2(pk2u(__byte_perm(nh, 0x4B000000u, 0x7542u), __byte_perm(nh, 0x4B000000u, 0x7543u)), bias);
+        if (k == 0) {  // scale of block 0, its bytes 0, 1
+          s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
+          A[r] = ffma2(x2[0], l23, A[r]);
+          A[r] = ffma2(x2[8], h23, A[r]);
+        } else if (k < 4) {  // bytes 4k-2 .. 4k+1 of block 0
+          A[r] = ffma2(x2[2 * k - 1], l01, A[r]);
+          A[r] = ffma2(x2[2 * k], l23, A[r]);
+          A[r] = ffma2(x2[2 * k + 7], h01, A[r]);
+          A[r] = ffma2(x2[2 * k + 8], h23, A[r]);
+        } else if (k == 4) {  // bytes 14, 15 of block 0, scale of block 1
+          A[r] = ffma2(x2[7], l01, A[r]);
+          A[r] = ffma2(x2[15], h01, A[r]);
+          s1[r] = h2f((uint16_t)(w[r] >> 16));
+        } else {  // bytes 4k-20 .. 4k-17 of block 1
+          B[r] = ffma2(x2[2 * k + 6], l01, B[r]);
+          B[r] = ffma2(x2[2 * k + 7], l23, B[r]);
+          B[r] = ffma2(x2[2 * k + 14], h01, B[r]);
+          B[r] = ffma2(x2[2 * k + 15], h23, B[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const float2 a = up2(A[r]), b = up2(B[r]);
+      out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
+    }
   } else {
+    f2x A[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) A[r] = 0ull;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      const uint4 u = lds128(row + (uint32_t)(seg * 2048 + k * 256 + lane * 8) * 2u);
-      w[4 * k] = u.x;
-      w[4 * k + 1] = u.y;
-      w[4 * k + 2] = u.z;
-      w[4 * k + 3] = u.w;
+      uint4 u[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) u[r] = lds128(ra[r] + (uint32_t)(seg * 2048 + k * 256 + lane * 8) * 2u);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        A[r] = ffma2(x2[4 * k], pk2u(u[r].x << 16, u[r].x & 0xFFFF0000u), A[r]);
+        A[r] = ffma2(x2[4 * k + 1], pk2u(u[r].y << 16, u[r].y & 0xFFFF0000u), A[r]);
+        A[r] = ffma2(x2[4 * k + 2], pk2u(u[r].z << 16, u[r].z & 0xFFFF0000u), A[r]);
+        A[r] = ffma2(x2[4 * k + 3], pk2u(u[r].w << 16, u[r].w & 0xFFFF0000u), A[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const float2 a = up2(A[r]);
+      out[r] = a.x + a.y;
     }
   }
 }
 
-
-// Sum two values over the warp with one butterfly: afterwards every lane holds
-// both totals (x = a's, y = b's).
-__device__ __forceinline__ float2 warp_sum2(float a, float b) {
+// Sum four values over the warp: a butterfly that halves the values it carries at
+// each of the first two steps (6 shuffles in all, against 4 x 5 for four separate
+// sums), then every lane gets all four totals.
+__device__ __forceinline__ void warp_sum4(float (&v)[4]) {
   const int lane = threadIdx.x & 31;
-  float keep = (lane & 16) ? b : a;
-  const float send = (lane & 16) ? a : b;
-  keep += __shfl_xor_sync(FULL, send, 16);
+  const bool b4 = lane & 16, b3 = lane & 8;
+  float k0 = b4 ? v[2] : v[0], k1 = b4 ? v[3] : v[1];
+  const float s0 = b4 ? v[0] : v[2], s1 = b4 ? v[1] : v[3];
+  k0 += __shfl_xor_sync(FULL, s0, 16);
+  k1 += __shfl_xor_sync(FULL, s1, 16);
+  float k = b3 ? k1 : k0;
+  k += __shfl_xor_sync(FULL, b3 ? k0 : k1, 8);
+  k += __shfl_xor_sync(FULL, k, 4);
+  k += __shfl_xor_sync(FULL, k, 2);
+  k += __shfl_xor_sync(FULL, k, 1);
+  // lanes 8g .. 8g+7 now hold the total of value g
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(FULL, keep, o);
-  return make_float2(__shfl_sync(FULL, keep, 0), __shfl_sync(FULL, keep, 16));
+  for (int r = 0; r < 4; r++) v[r] = __shfl_sync(FULL, k, 8 * r);
 }
 
 __device__ __forceinline__ uint32_t ldnc32(const uint8_t *p) {
@@ -345,7 +461,7 @@ struct AttScratch {
 };
 
 struct Smem {
-  float red[4][MAX_TILE_ITEMS];  // segment partial sums: two buffers per warp group
+  float red[2 * NGRP][MAX_TILE_ITEMS];  // segment partial sums: two buffers per warp group
   union {
     float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index)
     AttScratch at;    // attention-stage partials (a different phase of the layer)
@@ -372,7 +488,7 @@ enum { XS_PLAIN = 0, XS_NORM = 1, XS_EMBED = 2 };
 // synchronization — no grid barrier, no flag round trip. Tags are
 // launch << 10 | layer << 3 | kind (kind below), so a stale word never matches.
 enum { TG_EMBED = 0, TG_QKV = 1, TG_ATTN = 2, TG_POST_O = 3, TG_ACT = 4, TG_POST_DOWN = 5 };
-__device__ __forceinline__ unsigned mk_tag(unsigned launch, int l, int kind) {
+__host__ __device__ __forceinline__ unsigned mk_tag(unsigned launch, int l, int kind) {
   return (launch << 10) | ((unsigned)l << 3) | (unsigned)kind;
 }
 __device__ __forceinline__ void st_ll(unsigned long long *a, float v, unsigned tag) {
@@ -522,7 +638,7 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
     }
   } else {
     // word pairs (two elements), every load of this thread in flight before any use
-    constexpr int MAXC = MAX_X / 2 / (NC * 32);
+    constexpr int MAXC = (MAX_X / 2 + NC * 32 - 1) / (NC * 32);
     ulonglong2 c[MAXC];
     float2 wv[MAXC];
     const int nc = n / 2;
@@ -610,11 +726,6 @@ __device__ __forceinline__ float stage_in(const Params &p, Smem &sm, ActRegs<T> 
   return 1.0f;
 }
 
-template <int T>
-__device__ __forceinline__ float lane_dot(const uint32_t (&w)[nwords<T>()], const ActRegs<T> &a) {
-  return pair_dot<T>(w, a.x);
-}
-
 // The bulk copies of tile entry d: f(byte offset in the slot, global source, bytes).
 // Rows of a QKV tile may span Wq / Wk / Wv; a gate/up tile carries its gate rows,
 // then the same rows of Wup. Returns the tile's total bytes.
@@ -654,7 +765,7 @@ __device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) 
 // evict-first; what the L2 keeps is the (optional) prefetched tiles not yet consumed.
 __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
   const int2 d = tbl[j];
-  if (p.tile_tl) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + j) * 3] = (unsigned long long)clock64();
+  stamp_tile(p, j, 0);
   uint8_t *dst = rg.slots + (size_t)slot * SLOT;
   uint64_t *bar = &rg.full[slot];
   sm.issued[slot]++;
@@ -665,25 +776,18 @@ __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2
   tile_copies(p, d, [&](unsigned off, const uint8_t *src, unsigned bytes) { bulk_g2s_hint(dst + off, src, bytes, bar, pol); });
 }
 
-// Bring tile j (modulo the table: past the end come the next token's first tiles)
-// into L2 ahead of its ring copy, so HBM keeps streaming while the warps wait for
-// other CTAs between stages.
-__device__ __forceinline__ void prefetch_tile(const Params &p, const Smem &sm, const int2 *tbl, int j) {
-  if (j >= sm.ntiles) j -= sm.ntiles;
-  if (j < 0 || j >= sm.ntiles) return;
-  tile_copies(p, tbl[j], [&](unsigned, const uint8_t *src, unsigned bytes) { bulk_prefetch_l2(src, bytes); });
-}
-
 // A warp is done reading tile `k` in `slot`; the last of the `nwarps` warps that
-// read it refills the slot with tile k + NSLOT.
+// read it refills the slot with tile k + NSLOT. It refills only when its own wait on
+// the slot succeeded (`landed`): after a failed wait the slot's copy may still be in
+// flight, and a second copy into the same barrier phase would leave the exit drain
+// waiting on the wrong phase. A slot left empty makes the next wait on it give up.
 __device__ __forceinline__ void release_slot(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int slot,
-                                             int k, int nwarps) {
+                                             int k, int nwarps, bool landed) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) {
     if (atomicAdd(&sm.rel[slot], 1) == nwarps - 1) {
       sm.rel[slot] = 0;
-      if (k + NSLOT < sm.ntiles) issue_tile(p, rg, sm, tbl, k + NSLOT, slot);
-      if (p.pf > 0) prefetch_tile(p, sm, tbl, k + NSLOT + p.pf);
+      if (landed && k + NSLOT < sm.ntiles) issue_tile(p, rg, sm, tbl, k + NSLOT, slot);
     }
   }
 }
@@ -734,7 +838,7 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int kind,
     const float ha = __shfl_sync(FULL, sr.hres, (a - r0) & 31);
     const float hb = __shfl_sync(FULL, sr.hres, (b - r0) & 31);
     if (lane == 0) {
-      st_ll(p.hid_ll + a, __fadd_rn(ha, va), tag);
+      if (a != 0 || tag != p.drop_tag) st_ll(p.hid_ll + a, __fadd_rn(ha, va), tag);
       if (hasb) st_ll(p.hid_ll + b, __fadd_rn(hb, vb), tag);
     }
   } else if (kind == ST_GU) {  // a = gate row, vb = up (silu.rs:4-8, elementwise_mul.rs:3-17)
@@ -769,16 +873,15 @@ __device__ __forceinline__ void group_sync(int grp) {
   asm volatile("bar.sync %0, %1;" ::"r"(2 + grp), "n"(NG * 32) : "memory");
 }
 
-// One matvec stage of this CTA. The CTA's tiles alternate between two groups of NG
-// warps (tile k goes to group k & 1), so one group's reductions, epilogues and
-// slot refills overlap the other group's dot products. Within a tile a warp takes
-// two rows at a time (a row pair, or two rows of its input segment when the rows
+// One matvec stage of this CTA. The CTA's tiles rotate over NGRP groups of NG warps
+// (tile k goes to group k % NGRP), so one group's reductions, epilogues and slot
+// refills overlap the other groups' dot products. Within a tile a warp takes four
+// rows at a time (two row pairs, or four rows of its input segment when the rows
 // are split into segments) and reduces them together.
 template <int T>
 __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int kind, int l,
                              const ActRegs<T> &x, float osc, int &slot, unsigned &phase, int &tile_ctr, int pos,
                              const StageRegs &sr, unsigned tag) {
-  constexpr int NW = nwords<T>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = warp / NG, wig = warp % NG;
   const int nseg = stage_nseg(p, kind), rb = stage_rb(p, kind), Tr = p.tile_rows[kind];
@@ -792,59 +895,69 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
   stage_rows(p, kind, l, blockIdx.x, r0, r1);
   const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : kind + 1);
   for (int r = r0; r < r1; r += Tr) {
-    if ((tile_ctr & 1) == grp) {
+    if (tile_ctr % NGRP == grp) {
       const int n = min(Tr, r1 - r);
       const int rows = gu ? 2 * n : n;
       const uint32_t tile = slots + (uint32_t)slot * SLOT;
-      float *red = sm.red[2 * grp + ((tile_ctr >> 1) & 1)];
+      float *red = sm.red[2 * grp + ((tile_ctr / NGRP) & 1)];
       const bool ok = slot_wait(p, rg, sm, slot, tile_ctr, phase);
-      if (p.tile_tl && lead) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + tile_ctr) * 3 + 1] = (unsigned long long)clock64();
+      if (lead) stamp_tile(p, tile_ctr, 1);
       if (lead && r == r0) stamp_now(p, 8 * stage_id + 4);
       if (lead && r + Tr >= r1) stamp_now(p, 8 * stage_id + 5);
       if (ok) {
         if (nseg == 1) {
-          // warp-owned row pairs (2i, 2i+1), or (gate i, up i)
+          // warp-owned row pairs (2i, 2i+1), or (gate i, up i): pairs i and i + NG
+          // together (four rows, one reduction)
           const int npairs = gu ? n : (n + 1) >> 1;
-          for (int i = wig; i < npairs; i += NG) {
-            const int a = gu ? i : 2 * i, b = gu ? n + i : 2 * i + 1;
-            const bool hasb = b < rows;
-            float va = 0.f, vb = 0.f;
+          for (int i = wig; i < npairs; i += 2 * NG) {
+            const int i2 = i + NG;
+            const bool has2 = i2 < npairs;
+            int rw[4];
+            rw[0] = gu ? i : 2 * i;
+            rw[1] = gu ? n + i : 2 * i + 1;
+            rw[2] = gu ? i2 : 2 * i2;
+            rw[3] = gu ? n + i2 : 2 * i2 + 1;
+            const bool hasb = rw[1] < rows, hasb2 = has2 && rw[3] < rows;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
             if (active) {
-              uint32_t wa[NW], wb[NW];
-              lane_load<T>(tile + (uint32_t)a * rb, 0, lane, wa);
-              if (hasb) lane_load<T>(tile + (uint32_t)b * rb, 0, lane, wb);
-              va = lane_dot<T>(wa, x);
-              if (hasb) vb = lane_dot<T>(wb, x);
+              // a missing row reads row rw[0] again (in bounds) and is not used
+              const uint32_t ra[4] = {tile + (uint32_t)rw[0] * rb, tile + (uint32_t)(hasb ? rw[1] : rw[0]) * rb,
+                                      tile + (uint32_t)(has2 ? rw[2] : rw[0]) * rb,
+                                      tile + (uint32_t)(hasb2 ? rw[3] : rw[0]) * rb};
+              quad_dot<T>(ra, 0, lane, x.x, v);
             }
-            const float2 v = warp_sum2(va, vb);
-            const float fa = v.x * osc, fb = v.y * osc;
-            if (gu) finish_rows(p, sm, kind, l, pos, r0, r + i, fa, r + i, fb, true, sr, tag);
-            else finish_rows(p, sm, kind, l, pos, r0, r + a, fa, r + b, fb, hasb, sr, tag);
+            warp_sum4(v);
+            if (gu) {
+              finish_rows(p, sm, kind, l, pos, r0, r + i, v[0] * osc, r + i, v[1] * osc, true, sr, tag);
+              if (has2) finish_rows(p, sm, kind, l, pos, r0, r + i2, v[2] * osc, r + i2, v[3] * osc, true, sr, tag);
+            } else {
+              finish_rows(p, sm, kind, l, pos, r0, r + rw[0], v[0] * osc, r + rw[1], v[1] * osc, hasb, sr, tag);
+              if (has2)
+                finish_rows(p, sm, kind, l, pos, r0, r + rw[2], v[2] * osc, r + rw[3], v[3] * osc, hasb2, sr, tag);
+            }
           }
         } else {
-          // segment-split rows: this warp's segment of rows rs, rs + rpw, ...; the
-          // partial sums meet in shared memory
-          for (int i = rs; i < rows; i += 2 * rpw) {
-            const int a = i, b = i + rpw;
-            const bool hasb = b < rows;
-            float va = 0.f, vb = 0.f;
+          // segment-split rows: this warp's segment of rows rs, rs + rpw, rs + 2 rpw,
+          // rs + 3 rpw, ...; the partial sums meet in shared memory
+          for (int i = rs; i < rows; i += 4 * rpw) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
             if (active) {
-              uint32_t wa[NW], wb[NW];
-              lane_load<T>(tile + (uint32_t)a * rb, seg, lane, wa);
-              if (hasb) lane_load<T>(tile + (uint32_t)b * rb, seg, lane, wb);
-              va = lane_dot<T>(wa, x);
-              if (hasb) vb = lane_dot<T>(wb, x);
+              uint32_t ra[4];
+#pragma unroll
+              for (int q = 0; q < 4; q++) ra[q] = tile + (uint32_t)(i + q * rpw < rows ? i + q * rpw : i) * rb;
+              quad_dot<T>(ra, seg, lane, x.x, v);
             }
-            const float2 v = warp_sum2(va, vb);
+            warp_sum4(v);
             if (lane == 0) {
-              red[a * nseg + seg] = v.x;
-              if (hasb) red[b * nseg + seg] = v.y;
+#pragma unroll
+              for (int q = 0; q < 4; q++)
+                if (i + q * rpw < rows) red[(i + q * rpw) * nseg + seg] = v[q];
             }
           }
         }
       }
-      release_slot(p, rg, sm, tbl, slot, tile_ctr, NG);
-      if (p.tile_tl && lead) p.tile_tl[((size_t)blockIdx.x * p.max_tiles + tile_ctr) * 3 + 2] = (unsigned long long)clock64();
+      release_slot(p, rg, sm, tbl, slot, tile_ctr, NG, ok);
+      if (lead) stamp_tile(p, tile_ctr, 2);
       if (nseg > 1) {
         group_sync(grp);
         // finish the tile's rows: warp wig takes row pairs wig, wig + NG, ...
@@ -879,11 +992,11 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
 // q and the new K/V row from the tagged words of the QKV stage and the older
 // positions from the KV cache; the output goes out tagged for the O stage.
 //
-// Short contexts (head_dim 64, pos < SHORT_CTX): one item per q head. The 8 warps
-// split the cached positions 32 at a time; lane = position for q.k (q broadcast
-// from shared memory, no reductions), lane = dimension for p.V; each warp keeps a
-// running max / sum / accumulator, the warps merge in shared memory, and warp 0
-// adds the current position.
+// Short contexts (head_dim 64, pos < SHORT_CTX): one item per q head. The warps
+// split the cached positions 32 at a time; lane = position for q.k (q broadcast from
+// shared memory, no reductions), lane = dimension for p.V; each warp keeps a running
+// max / sum / accumulator, the warps merge in shared memory, and warp 0 adds the
+// current position.
 constexpr int SHORT_CTX = 512;
 
 template <int DPL>
@@ -909,11 +1022,16 @@ __device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsig
 #pragma unroll
       for (int k = 0; k < HD / 4; k++)
         kr[k] = valid ? ldcg4(kb + (size_t)s * HD + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float vv[32][DPL];
+      constexpr int VJ = 16;  // V rows per batch (fewer registers than all 32 at once)
+      float vv[VJ][DPL];
+      auto load_v = [&](int j0) {
 #pragma unroll
-      for (int j = 0; j < 32; j++)
+        for (int j = 0; j < VJ; j++)
 #pragma unroll
-        for (int i = 0; i < DPL; i++) vv[j][i] = base + j < pos ? __ldcg(vb + (size_t)(base + j) * HD + lane + 32 * i) : 0.f;
+          for (int i = 0; i < DPL; i++)
+            vv[j][i] = base + j0 + j < pos ? __ldcg(vb + (size_t)(base + j0 + j) * HD + lane + 32 * i) : 0.f;
+      };
+      load_v(0);
       float d = 0.f;
 #pragma unroll
       for (int k = 0; k < HD / 4; k++) {
@@ -931,10 +1049,14 @@ __device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsig
 #pragma unroll
       for (int i = 0; i < DPL; i++) acc[i] *= corr;
 #pragma unroll
-      for (int j = 0; j < 32; j++) {
-        const float pjj = __shfl_sync(FULL, pj, j);
+      for (int j0 = 0; j0 < 32; j0 += VJ) {
+        if (j0) load_v(j0);
 #pragma unroll
-        for (int i = 0; i < DPL; i++) acc[i] = fmaf(pjj, vv[j][i], acc[i]);
+        for (int j = 0; j < VJ; j++) {
+          const float pjj = __shfl_sync(FULL, pj, j0 + j);
+#pragma unroll
+          for (int i = 0; i < DPL; i++) acc[i] = fmaf(pjj, vv[j][i], acc[i]);
+        }
       }
       m = mn;
     }
@@ -1025,7 +1147,7 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
     float m = -INFINITY, lsum = 0.f, acc[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; i++) acc[i] = 0.f;
-    constexpr int VJ = DPL >= 4 ? 16 : 32;  // V rows per batch (head_dim 128: two halves, fewer registers)
+    constexpr int VJ = DPL >= 4 ? 8 : 16;  // V rows per batch (fewer registers than all 32 at once)
     for (int base = s0 + warp * 32; base < cached_end; base += NC * 32) {
       const int s = base + lane;
       const bool valid = s < cached_end;
@@ -1196,7 +1318,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   Smem &sm = *reinterpret_cast<Smem *>(tbl_bar + 1);  // 16-byte aligned: 5 + 1 barriers of 8 bytes
   int2 *tbl = reinterpret_cast<int2 *>(&sm + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  stamp_sync(p, p.tl_stride - 6);
+  stamp_sync(p, TL_STRIDE(p) - 6);
   stamp(p, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; s++) {
@@ -1215,7 +1337,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bulk_g2s(tbl, p.tiles + (size_t)blockIdx.x * p.max_tiles, tb, tbl_bar);
     if (mbar_wait(tbl_bar, 0, p.err)) {
       for (int j = 0; j < NSLOT && j < nt; j++) issue_tile(p, rg, sm, tbl, j, j);
-      for (int j = NSLOT; j < NSLOT + p.pf && j < nt; j++) prefetch_tile(p, sm, tbl, j);
     }
   }
   __syncthreads();
@@ -1271,7 +1392,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
   cta_sync();
-  stamp(p, p.tl_stride - 2);
+  stamp(p, TL_STRIDE(p) - 2);
   // ---- greedy argmax: this CTA's rows (kept in shared memory) in order, then the
   // last CTA to finish folds the per-CTA states in row order
   if (warp == 0) {
@@ -1328,8 +1449,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
   }
-  stamp(p, p.tl_stride - 1);
-  stamp_sync(p, p.tl_stride - 4);
+  stamp(p, TL_STRIDE(p) - 1);
+  stamp_sync(p, TL_STRIDE(p) - 4);
 }
 
 // Per-CTA tile tables, built once per context with the same row split the kernel
@@ -1370,12 +1491,15 @@ struct DecodeState {
   unsigned *d_err = nullptr, *d_bar = nullptr, *d_ticket = nullptr, *d_attn_cnt = nullptr;
   int *d_pos = nullptr;
   int n_kv_heads = 0, n_heads = 0, n_layers = 0;
+#ifdef SQ_DECODE_TIMELINE
+  // profiling builds: SQ_DECODE_TIMELINE=<file> writes the stamps of the last launch
   unsigned long long *d_timeline = nullptr;
-  unsigned long long *d_tile_tl = nullptr;  // per-tile stamps of the last launch (with the timeline)
+  unsigned long long *d_tile_tl = nullptr;
   const int2 *d_tiles = nullptr;
-  int max_tiles = 0;  // SQ_DECODE_TIMELINE=<file>: stage stamps of the last launch
+  int max_tiles = 0;
   int tl_stride = 0;
   std::string tl_path;
+#endif
   std::vector<void *> allocs;
 };
 
@@ -1422,15 +1546,10 @@ int decode_prepare(sq_ctx *c) {
   h.tile_rows[dk::ST_GU] = rows_fit(rbE, 2);
   h.tile_rows[dk::ST_DOWN] = rows_fit(rbF, 1);
   h.tile_rows[dk::ST_LM] = rows_fit(rbE, 1);
-  if (const char *tr = getenv("SQ_DECODE_TILE_ROWS")) {  // tuning: caps "qkv,o,gu,down,lm" (even, >= 2)
-    int v[5];
-    if (sscanf(tr, "%d,%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3], &v[4]) == 5)
-      for (int k = 0; k < 5; k++)
-        if (v[k] >= 2) h.tile_rows[k] = std::min(h.tile_rows[k], v[k] & ~1);
-  }
   for (int k = 0; k < 5; k++) {
     const int nseg = k == dk::ST_O ? nQ : (k == dk::ST_DOWN ? nF : nE);
-    ok = ok && h.tile_rows[k] >= 2 && h.tile_rows[k] * (k == dk::ST_GU ? 2 : 1) * nseg <= dk::MAX_TILE_ITEMS;
+    // segment partial sums of a tile (rows x segments) go through shared memory
+    ok = ok && h.tile_rows[k] >= 2 && (nseg == 1 || h.tile_rows[k] * (k == dk::ST_GU ? 2 : 1) * nseg <= dk::MAX_TILE_ITEMS);
   }
   int dev = m->device, nsm = 0;
   SQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
@@ -1507,15 +1626,19 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(alloc((void **)&h.arg_part, (size_t)nsm * sizeof(ArgState)));
   SQ_CUDA(alloc((void **)&h.pos, 4));
   SQ_CUDA(alloc((void **)&st->d_params, sizeof(dk::Params)));
-  h.pf = dk::PF_TILES;
-  if (const char *pf = getenv("SQ_DECODE_L2_PREFETCH")) h.pf = std::max(0, std::min(atoi(pf), 256));  // tuning
-  if (const char *tl = getenv("SQ_DECODE_TIMELINE")) {  // opt-in stage timestamps
+  if (const char *v = getenv("SQ_TEST_DROP_EXCHANGE")) {  // failure-detection tests (see Params::drop_tag)
+    const int n = atoi(v);
+    if (n > 0) h.drop_tag = dk::mk_tag((unsigned)n, 0, dk::TG_POST_O);
+  }
+#ifdef SQ_DECODE_TIMELINE
+  if (const char *tl = getenv("SQ_DECODE_TIMELINE")) {  // stage timestamps of profiling builds
     st->tl_path = tl;
     st->tl_stride = 8 * (5 * cf.n_blocks + 1) + 6;
     SQ_CUDA(alloc((void **)&st->d_timeline, (size_t)nsm * st->tl_stride * 8));
     h.timeline = st->d_timeline;
     h.tl_stride = st->tl_stride;
   }
+#endif
   // tile tables: count pass, then fill (same row split as the kernel)
   SQ_CUDA(alloc((void **)&h.ntiles, (size_t)nsm * sizeof(int)));
   SQ_CUDA(cudaMemcpy(st->d_params, &h, sizeof(dk::Params), cudaMemcpyHostToDevice));
@@ -1525,12 +1648,14 @@ int decode_prepare(sq_ctx *c) {
   SQ_CUDA(cudaMemcpy(counts.data(), h.ntiles, nsm * sizeof(int), cudaMemcpyDeviceToHost));
   h.max_tiles = (*std::max_element(counts.begin(), counts.end()) + 1) & ~1;
   SQ_CUDA(alloc((void **)&h.tiles, (size_t)nsm * h.max_tiles * sizeof(int2)));
+#ifdef SQ_DECODE_TIMELINE
   if (h.timeline) {
     SQ_CUDA(alloc((void **)&h.tile_tl, (size_t)nsm * h.max_tiles * 3 * 8));
     st->d_tile_tl = h.tile_tl;
     st->d_tiles = h.tiles;
     st->max_tiles = h.max_tiles;
   }
+#endif
   SQ_CUDA(cudaMemcpy(st->d_params, &h, sizeof(dk::Params), cudaMemcpyHostToDevice));
   dk::k_build_tiles<<<nsm, 32>>>(st->d_params, h.tiles, h.ntiles, h.max_tiles);
   SQ_CHECK_LAUNCH("build tiles");
@@ -1595,6 +1720,7 @@ int decode_check(sq_ctx *c) {
   if (!st || !st->available) return SQ_OK;
   unsigned err = 0;
   SQ_CUDA(cudaMemcpy(&err, st->d_err, 4, cudaMemcpyDeviceToHost));
+#ifdef SQ_DECODE_TIMELINE
   if (st->d_timeline) {
     std::vector<unsigned long long> tl((size_t)st->grid * st->tl_stride);
     SQ_CUDA(cudaMemcpy(tl.data(), st->d_timeline, tl.size() * 8, cudaMemcpyDeviceToHost));
@@ -1613,6 +1739,7 @@ int decode_check(sq_ctx *c) {
       fclose(f);
     }
   }
+#endif
   if (err) {
     // reset the kernel's flag and counters so the context stays usable
     cudaMemset(st->d_err, 0, 4);

@@ -195,6 +195,7 @@ sq_model::~sq_model() {
   cudaSetDevice(device);
   for (auto &kv : tensors) cudaFree(kv.second.ptr);
   cudaFree(d_inv_freq);
+  tp_allreduce_release(ar);  // every peer's last write into this mailbox preceded its last flag
   nccl_comm_destroy(nccl);
   cudaSetDevice(prev);
 }
@@ -244,6 +245,7 @@ static int model_create(const sq_llama_config *cfg, int device, int acts, int tp
   if (tp_size > 1) {
     SQ_CUDA(cudaSetDevice(device));
     if ((st = nccl_comm_init(nccl_id, tp_rank, tp_size, &m->nccl))) return st;
+    if ((st = tp_allreduce_create(m.get()))) return st;  // collective, like the NCCL init
   }
   *out = m.release();
   return SQ_OK;
@@ -719,8 +721,13 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     } else {
       TRY(launch_linear(s, c->attn, n, Q, L.o, wt, E, c->attn_out, aq, c->xq, ws, wsf));
     }
-    if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));  // row-parallel O: sum the shards
-    if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
+    // row-parallel O: sum the shards, then the residual add (one peer-memory kernel for a decode row)
+    if (tp && n == 1 && m->ar) {
+      TRY(launch_allreduce_add(s, m->ar, c->hidden, c->attn_out));
+    } else {
+      if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));
+      if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
+    }
     if (fused) {
       TRY(launch_matvec_fused(s, gu, wt, pdl));
       TRY(launch_matvec_fused(s, dn, wt, pdl));
@@ -738,8 +745,12 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_silu_mul(s, c->gate, c->up, c->act, (size_t)n * F));
       TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, ws, wsf));
     }
-    if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));  // row-parallel down
-    if (!fused || tp) TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
+    if (tp && n == 1 && m->ar) {  // row-parallel down, likewise
+      TRY(launch_allreduce_add(s, m->ar, c->hidden, c->ffn_out));
+    } else {
+      if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));
+      if (!fused || tp) TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
+    }
   }
   c->seq_len += n;
   if (last) {
@@ -860,6 +871,8 @@ extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *ou
   if (st) return st;
   st = device_wait_status(true, "forward");
   if (st) return st;
+  if (c->m->ar && tp_allreduce_status(c->m->ar, true))
+    return fail(SQ_ERR_TIMEOUT, "forward: a peer's partial sum did not arrive within the tensor-parallel all-reduce's limit");
   if (out_argmax) *out_argmax = (uint32_t)id;
   return SQ_OK;
 }
@@ -937,6 +950,8 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
   if (!st && e3 != cudaSuccess) st = cuda_fail(e3, "decode_steps sync");
   if (!st) st = decode_check(c);
   if (!st) st = device_wait_status(true, "decode_steps");
+  if (!st && c->m->ar && tp_allreduce_status(c->m->ar, true))
+    st = fail(SQ_ERR_TIMEOUT, "decode_steps: a peer's partial sum did not arrive within the tensor-parallel all-reduce's limit");
   c->have_logits = true;
   return st;
 }

@@ -16,6 +16,7 @@ struct DevTensor {
   size_t nbytes = 0;
 };
 struct DecodeState;  // persistent decode kernel resources (decode.cu)
+struct TpAllReduce;  // one-shot NVLink all-reduce of a tensor-parallel model (allreduce.cu)
 void rope_inv_freq(const sq_llama_config &c, std::vector<float> &out);
 int forward_device(sq_ctx *c, const uint32_t *d_ids, int n);
 // NCCL (tp.cpp): loaded on first use
@@ -23,6 +24,15 @@ int nccl_comm_init(const void *id, int rank, int size, void **comm);
 void nccl_comm_destroy(void *comm);
 int nccl_all_reduce_sum(void *comm, float *buf, size_t n, cudaStream_t s);
 int nccl_all_gather_bytes(void *comm, const void *src, void *dst, size_t bytes_per_rank, cudaStream_t s);
+int nccl_all_reduce_min_int(void *comm, int *buf, cudaStream_t s);
+// One-shot all-reduce over NVLink peer memory (allreduce.cu): set up collectively at
+// model creation (m->ar stays null when a rank cannot map its peers: NCCL then serves),
+// launched for one decode row with the residual add fused, error word read after a sync.
+int tp_allreduce_create(sq_model *m);
+void tp_allreduce_release(TpAllReduce *ar);
+cudaError_t launch_allreduce_add(cudaStream_t s, const TpAllReduce *ar, float *hidden, const float *part);
+unsigned tp_allreduce_status(const TpAllReduce *ar, bool clear);
+int tp_allreduce_recover(sq_model *m);  // collective re-synchronization after a timeout
 }  // namespace sq
 
 // LlamaWeights (models/llama/weights.rs:18-47) resolved to device pointers.
@@ -34,6 +44,7 @@ struct sq_model {
   bool finalized = false;
   int tp_rank = 0, tp_size = 1;  // tensor-parallel group (tp.cpp)
   void *nccl = nullptr;          // ncclComm_t when tp_size > 1
+  sq::TpAllReduce *ar = nullptr;  // the decode step's peer-memory all-reduce (null: NCCL's)
   int vocab0 = 0;                // first vocabulary row of this rank's LM-head shard
   std::unordered_map<std::string, sq::DevTensor> tensors;
   struct Layer {

@@ -90,6 +90,11 @@ int nccl_all_reduce_sum(void *comm, float *buf, size_t n, cudaStream_t s) {
   return r == ncclSuccess ? SQ_OK : nccl_fail(r, "ncclAllReduce");
 }
 
+int nccl_all_reduce_min_int(void *comm, int *buf, cudaStream_t s) {
+  const ncclResult_t r = api().all_reduce(buf, buf, 1, ncclInt32, ncclMin, (ncclComm_t)comm, s);
+  return r == ncclSuccess ? SQ_OK : nccl_fail(r, "ncclAllReduce");
+}
+
 int nccl_all_gather_bytes(void *comm, const void *src, void *dst, size_t bytes_per_rank, cudaStream_t s) {
   const ncclResult_t r = api().all_gather(src, dst, bytes_per_rank, ncclUint8, (ncclComm_t)comm, s);
   return r == ncclSuccess ? SQ_OK : nccl_fail(r, "ncclAllGather");

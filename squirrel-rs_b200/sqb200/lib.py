@@ -82,6 +82,7 @@ SIGNATURES = {
     "sq_ctx_stream": (_vp, [_vp]),
     "sq_ctx_launches_per_token": (_i, [_vp, C.POINTER(_i)]),
     "sq_nccl_unique_id": (_i, [_vp, _sz]),
+    "sq_tp_recover": (_i, [_vp]),
     "sq_model_create_tp": (_i, [C.POINTER(LlamaConfig), _i, _i, _i, _i, _vp, C.POINTER(_vp)]),
     "sq_model_load_gguf_tp": (_i, [C.c_char_p, _i, _i, _i, _i, _vp, C.POINTER(_vp)]),
     "sq_tp_shard_tensor": (_i, [C.c_char_p, _i, C.POINTER(C.c_uint64), _i, _i, _i, _vp, _sz, _vp, _sz,
@@ -316,6 +317,11 @@ class Model:
 
     def new_context(self, max_ctx=0):
         return Context(self, max_ctx)
+
+    def tp_recover(self):
+        """sq_tp_recover: collective re-synchronization of a tensor-parallel group's
+        all-reduce after a timeout (every rank calls it; then reset the contexts)."""
+        _check(load().sq_tp_recover(self._h))
 
 
 class Context:

@@ -1,0 +1,120 @@
+"""Failure detection of the persistent decode kernel, without a GPU fault.
+
+Every cross-CTA wait of the decode kernel is bounded (about 2 s of SM clocks); when
+one expires the kernel sets an error word, every other wait sees it and gives up at
+once, the CTAs let their in-flight copies land and return, and the host reports
+SQ_ERR_TIMEOUT and clears the kernel's counters. Here the wait runs out because a
+word is never written: SQ_TEST_DROP_EXCHANGE=n (read when the context is created)
+makes the n-th launch skip one residual word after layer 0's O projection, so the
+gate/up stage polls a word that nothing sets. Nothing traps or hangs; the test then
+checks that the same context decodes the oracle's ids again."""
+import os
+import time
+
+import numpy as np
+import pytest
+
+from golden import make_golden as MG  # tests/golden/make_golden.py
+
+pytestmark = pytest.mark.gpu
+
+
+def test_decode_wait_expires_reports_timeout_and_context_recovers(gpu_lib, monkeypatch):
+    from sqb200 import gguf_synth as G
+    from sqb200 import lib
+    z = np.load(MG.fixture_path("small", "q8_0"))
+    prompt, ids = z["prompt"], z["ids"]
+    monkeypatch.setenv("SQ_TEST_DROP_EXCHANGE", "3")  # the context's third decode launch
+    m = lib.Model(G.ensure_gguf("small", "q8_0"), device=0)
+    ctx = m.new_context(64)
+    monkeypatch.delenv("SQ_TEST_DROP_EXCHANGE")
+    try:
+        assert ctx.launches_per_token == 1  # the persistent kernel serves this model
+        assert ctx.forward(prompt) == ids[0]  # prefill: not a decode launch
+        t0 = time.monotonic()
+        with pytest.raises(lib.KernelError) as e:
+            ctx.decode_steps(5)  # launches 1..5; the third one loses a word
+        assert e.value.kind == "Timeout", e.value
+        assert time.monotonic() - t0 < 60  # one expired wait (~2 s), then every wait gives up at once
+        # the device and the context stay usable: a fresh prefill decodes the oracle's ids
+        ctx.reset()
+        assert ctx.forward(prompt) == ids[0]
+        assert np.array_equal(ctx.decode_steps(len(ids) - 1), ids[1:])
+        lib.wait_status()
+    finally:
+        ctx.close()
+        m.close()
+
+
+def _fault_rank(rank, path, prompt, ids, qin, qout):
+    """Rank 1's third peer all-reduce stores its partial but withholds its flags
+    (SQ_TEST_WITHHOLD_PARTIAL=3, read when its model is created), so rank 0's wait
+    for it expires and rank 0 reports Timeout; both ranks run the whole step (its
+    NCCL calls included), then re-synchronize (sq_tp_recover), reset their contexts
+    and decode the oracle's ids again."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if rank == 1:
+        os.environ["SQ_TEST_WITHHOLD_PARTIAL"] = "3"
+    from sqb200 import lib
+    out = {"rank": rank}
+    try:
+        if rank == 0:
+            uid = lib.nccl_unique_id()
+            qin.put(("uid", uid))
+        else:
+            uid = qout.get(timeout=120)
+        m = lib.Model(path, device=rank, tp_rank=rank, tp_size=2, nccl_id=uid)
+        ctx = m.new_context(64)
+        out["first"] = int(ctx.forward(prompt))  # prefill: NCCL's all-reduces
+        t0 = time.monotonic()
+        try:
+            ctx.decode_steps(2)  # decode rows: the peer all-reduces 1..2 per layer
+            out["fault"] = "none"
+        except lib.KernelError as e:
+            out["fault"] = e.kind
+        out["fault_s"] = time.monotonic() - t0
+        m.tp_recover()
+        ctx.reset()
+        out["ids"] = [int(ctx.forward(prompt))] + [int(i) for i in ctx.decode_steps(len(ids) - 1)]
+        ctx.close()
+        m.close()
+        qin.put(("ok", out))
+    except Exception as e:  # report instead of hanging the parent
+        qin.put(("err", {"rank": rank, "error": repr(e)}))
+
+
+def test_tp_allreduce_wait_expires_reports_timeout_and_group_recovers():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from sqb200 import gguf_synth as G
+    z = np.load(MG.fixture_path("small", "q8_0"))
+    prompt, ids = z["prompt"], [int(i) for i in z["ids"]]
+    path = G.ensure_gguf("small", "q8_0")
+    ctx = mp.get_context("spawn")
+    qin, qout = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_fault_rank, args=(r, path, prompt, ids, qin, qout)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    try:
+        while len(results) < 2:
+            kind, val = qin.get(timeout=300)
+            if kind == "uid":
+                qout.put(val)  # rank 0's NCCL id, relayed to rank 1
+            else:
+                results.append((kind, val))
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    errs = [v for k, v in results if k != "ok"]
+    assert not errs, errs
+    by_rank = {v["rank"]: v for _, v in results}
+    assert by_rank[0]["fault"] == "Timeout", by_rank[0]  # waited for rank 1's withheld flags
+    assert by_rank[1]["fault"] == "none", by_rank[1]  # rank 0's partials all arrived
+    assert by_rank[0]["fault_s"] < 60
+    for r in (0, 1):
+        assert by_rank[r]["ids"] == ids, by_rank[r]

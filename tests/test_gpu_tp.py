@@ -1,11 +1,21 @@
-"""Tensor parallel on two GPUs (one process per GPU, NCCL): the sharded model's
+"""Tensor parallel on 2, 4 and 8 GPUs (one process per GPU): the sharded model's
 greedy ids equal the single-GPU model's and the CPU oracle's, and its gathered
-logits stay within the model tests' tolerance. Skipped with fewer than 2 GPUs."""
+logits stay within the model tests' tolerance. The row-parallel sums of a decode
+row run either on the one-shot peer-memory all-reduce (the default) or on NCCL's
+(SQB200_TP_ALLREDUCE=nccl, read when the model is created); both are checked.
+Sizes with more GPUs than the box has are skipped.
+
+  small (2 kv heads): TP 2 against one GPU and the oracle, Q8_0 and BF16
+  8b (8 kv heads): TP 2 / 4 / 8 against the oracle's pinned ids and logits
+                   (tests/golden/cfg5_8b_q8_0.npz); at TP 8 each rank holds one
+                   kv head, 4 q heads, 1792 FFN rows and 56 blocks of the down rows
+"""
 import os
 
 import numpy as np
 import pytest
 
+from golden import make_golden as MG  # tests/golden/make_golden.py
 from oracle import oracle as O
 
 torch = pytest.importorskip("torch")
@@ -15,32 +25,72 @@ pytestmark = pytest.mark.gpu
 ABS_TOL, REL_TOL = 1e-2, 1e-3
 
 
-def _tp_rank(rank, size, path, prompt, steps, qin, qout):
+def assert_logits_close(got, want):
+    err = float(np.max(np.abs(got - want)))
+    assert err <= ABS_TOL, err
+    assert err / float(np.max(np.abs(want))) <= REL_TOL, err
+
+
+def _tp_rank(rank, size, path, prompt, steps, mode, qin, qout):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if mode == "nccl":
+        os.environ["SQB200_TP_ALLREDUCE"] = "nccl"
     from sqb200 import lib
     try:
         if rank == 0:
             uid = lib.nccl_unique_id()
-            for _ in range(size - 1):
-                qin.put(uid)
+            qin.put(("uid", uid))
         else:
-            uid = qout.get(timeout=60)
+            uid = qout.get(timeout=120)
         m = lib.Model(path, device=rank, tp_rank=rank, tp_size=size, nccl_id=uid)
         ctx = m.new_context(len(prompt) + steps + 4)
         first = ctx.forward(prompt)
-        logits = ctx.logits()  # collective: every rank gathers the vocabulary shards
+        first_logits = ctx.logits()  # collective: every rank gathers the vocabulary shards
         ids = [int(first)] + [int(i) for i in ctx.decode_steps(steps)]
+        last_logits = ctx.logits()
         ctx.close()
         m.close()
-        qin.put(("ok", rank, ids, logits if rank == 0 else None))
+        qin.put(("ok", rank, ids, (first_logits, last_logits) if rank == 0 else None))
     except Exception as e:  # report instead of hanging the parent
         qin.put(("err", rank, repr(e), None))
 
 
+def run_tp(size, path, prompt, steps, mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    qin, qout = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank, args=(r, size, path, prompt, steps, mode, qin, qout)) for r in range(size)]
+    for p in procs:
+        p.start()
+    results = []
+    first = qin.get(timeout=300)
+    if first[0] == "uid":  # rank 0's NCCL id, relayed to the other ranks
+        for _ in range(size - 1):
+            qout.put(first[1])
+    else:
+        results.append(first)
+    while len(results) < size:
+        results.append(qin.get(timeout=900))
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    errs = [r for r in results if r[0] != "ok"]
+    assert not errs, errs
+    ids = {r[1]: r[2] for r in results}
+    assert all(ids[r] == ids[0] for r in ids), "ranks disagree"
+    return ids[0], next(r[3] for r in results if r[1] == 0)
+
+
+def need_gpus(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
 @pytest.mark.parametrize("wt", ["q8_0", "bf16"])
-def test_tp2_matches_single_gpu_and_oracle(wt):
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def test_tp2_matches_single_gpu_and_oracle(wt, mode):
+    need_gpus(2)
     from sqb200 import gguf_synth as G
     from sqb200 import lib
     path = G.ensure_gguf("small", wt)
@@ -56,29 +106,20 @@ def test_tp2_matches_single_gpu_and_oracle(wt):
     om = O.Model(path)
     o_ids, _, _ = om.generate(prompt, steps + 1)
     om.close()
+    ids, (first_logits, _) = run_tp(2, path, prompt, steps, mode)
+    assert ids == s_ids, (ids, s_ids)
+    assert ids == [int(i) for i in o_ids], (ids, list(o_ids))
+    assert_logits_close(first_logits, s_logits)
 
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    qin, qout = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, 2, path, prompt, steps, qin if r == 0 else qin, qout))
-             for r in range(2)]
-    for p in procs:
-        p.start()
-    # rank 0 puts the id for rank 1 on qin; relay it
-    uid = qin.get(timeout=120)
-    qout.put(uid)
-    results = [qin.get(timeout=300) for _ in procs]
-    for p in procs:
-        p.join(timeout=60)
-        if p.is_alive():
-            p.kill()
-    errs = [r for r in results if r[0] != "ok"]
-    assert not errs, errs
-    r0 = next(r for r in results if r[1] == 0)
-    r1 = next(r for r in results if r[1] == 1)
-    assert r0[2] == r1[2], "ranks disagree"
-    assert r0[2] == s_ids, (r0[2], s_ids)
-    assert r0[2] == [int(i) for i in o_ids], (r0[2], list(o_ids))
-    diff = np.abs(r0[3] - s_logits)
-    assert float(diff.max()) <= ABS_TOL, float(diff.max())
-    assert float((diff / np.maximum(np.abs(s_logits), 1.0)).max()) <= REL_TOL
+
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_tp_8b_matches_oracle(size, mode):
+    need_gpus(size)
+    from sqb200 import gguf_synth as G
+    z = np.load(MG.config_fixture_path("cfg5_8b_q8_0"))
+    path = G.ensure_gguf("8b", "q8_0")
+    ids, (first_logits, last_logits) = run_tp(size, path, z["prompt"], len(z["ids"]) - 1, mode)
+    assert ids == [int(i) for i in z["ids"]], (ids, z["ids"].tolist())
+    assert_logits_close(first_logits, z["logits_first"])
+    assert_logits_close(last_logits, z["logits_last"])
