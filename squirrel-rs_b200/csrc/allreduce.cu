@@ -54,9 +54,9 @@ struct TpAllReduce {
   unsigned **d_flags = nullptr;        // device array: flag base of each rank's mailbox
   unsigned *epoch = nullptr, *err = nullptr;  // this rank's per-CTA sequence counters and error word
   // Failure-detection tests only (SQ_TEST_WITHHOLD_PARTIAL=k, read when the model is
-  // created): this rank's k-th all-reduce stores its partial but not its flags, so
-  // the other ranks' waits for it expire. 0 = off.
-  unsigned withhold = 0;
+  // created): the k-th all-reduce this rank launches (or captures) stores its partial
+  // but not its flags, so the other ranks' waits for it expire. 0 = off.
+  unsigned withhold = 0, launches = 0;
 };
 
 namespace {
@@ -73,9 +73,11 @@ __device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterp
 
 __global__ void __launch_bounds__(AR_THREADS) k_allreduce_add(float *hidden, const float *part, float *const *data,
                                                               unsigned *const *flags, unsigned *epoch, unsigned *err,
-                                                              int rank, int world, int E, int nb, unsigned withhold) {
+                                                              int rank, int world, int E, int nb, int withhold) {
   const int c = blockIdx.x, tid = threadIdx.x;
   const int chunk = E / nb, e0 = c * chunk;
+  pdl_wait();     // the partial comes from the kernel before (programmatic launch)
+  pdl_trigger();  // the next kernel may start streaming its weights meanwhile
   __shared__ unsigned s_seq;
   if (tid == 0) s_seq = epoch[c] + 1u;
   __syncthreads();
@@ -88,7 +90,7 @@ __global__ void __launch_bounds__(AR_THREADS) k_allreduce_add(float *hidden, con
     for (int r = 0; r < world; r++) *reinterpret_cast<float4 *>(data[r] + row + 4 * i) = v;
   }
   __syncthreads();  // every thread's stores precede the releases below
-  if (tid < world && seq != withhold) st_release_sys(flags[tid] + ((size_t)slot * world + rank) * nb + c, seq);
+  if (tid < world && !withhold) st_release_sys(flags[tid] + ((size_t)slot * world + rank) * nb + c, seq);
   // 2. wait for every rank's row in this rank's own mailbox
   if (tid < world) {
     const unsigned *f = flags[rank] + ((size_t)slot * world + tid) * nb + c;
@@ -244,10 +246,11 @@ void tp_allreduce_release(TpAllReduce *ar) {
   delete ar;
 }
 
-cudaError_t launch_allreduce_add(cudaStream_t s, const TpAllReduce *ar, float *hidden, const float *part) {
-  k_allreduce_add<<<ar->nb, AR_THREADS, 0, s>>>(hidden, part, ar->d_data, ar->d_flags, ar->epoch, ar->err, ar->rank,
-                                                ar->world, ar->E, ar->nb, ar->withhold);
-  return cudaGetLastError();
+cudaError_t launch_allreduce_add(cudaStream_t s, TpAllReduce *ar, float *hidden, const float *part, bool pdl) {
+  const int withhold = ar->withhold && ++ar->launches == ar->withhold;
+  return launch_ex(k_allreduce_add, dim3(ar->nb), dim3(AR_THREADS), 0, s, pdl, hidden, part,
+                   (float *const *)ar->d_data, (unsigned *const *)ar->d_flags, ar->epoch, ar->err, ar->rank, ar->world,
+                   ar->E, ar->nb, withhold);
 }
 
 // Collective re-synchronization after a timeout: a barrier (every rank's last

@@ -45,16 +45,17 @@ constexpr int NG = 4;                    // warps per group (one per SM sub-part
 constexpr int NGRP = SQ_DECODE_GROUPS;   // groups per CTA: tile k goes to group k % NGRP
 constexpr int NC = NG * NGRP;            // warps per CTA
 constexpr int NTHREADS = NC * 32;
-constexpr int SLOT = 36864;              // bytes per ring slot
+constexpr int SLOT = 36864;              // largest ring slot in bytes (the context's slot: Params::slot_bytes)
 constexpr int NSLOT = 5;
 constexpr int MAX_LAYERS = 128;
 constexpr int MAX_TILE_ITEMS = 64;       // rows x segments per tile
 constexpr int MAX_X = 8192;              // longest stage input staged in shared memory (floats)
-constexpr int MAX_LM_ROWS = 1024;        // LM-head rows per CTA kept in shared memory
+constexpr int MAX_LM_ROWS = 896;         // LM-head rows per CTA kept in shared memory (128256 / 148 = 867)
 constexpr int GROUP = 4;                 // q heads per kv head supported here
 constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
 
-enum { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DOWN = 3, ST_LM = 4 };
+// ST_DOWN2: the second input part of a down projection wider than MAX_X (Params::split)
+enum { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DOWN = 3, ST_LM = 4, ST_DOWN2 = 5 };
 
 struct LayerW {
   const uint8_t *q, *k, *v, *o, *gate, *up, *down;
@@ -65,7 +66,12 @@ struct Params {  // passed by value to the decode kernel: at most the 32 KB of k
   int L, E, Q, KVd, F, V, H, KVH, hd, max_ctx, G;
   int nseg_E, nseg_Q, nseg_F;
   int rb_E, rb_Q, rb_F;        // bytes per weight row with in_dim = E / Q / F
-  int tile_rows[5];            // rows per tile per stage kind (gate/up: per matrix)
+  // FFN inputs wider than the staging buffer (F > MAX_X, e.g. 14336) are taken in two
+  // parts: ST_DOWN over elements [0, xa), ST_DOWN2 over [xa, F), the same output rows;
+  // part 1's sums wait in shared memory for part 2's
+  int split, xa, rb_FA, rb_FB, nseg_FA, nseg_FB;
+  int tile_rows[6];            // rows per tile per stage kind (gate/up: per matrix)
+  int slot_bytes;              // ring slot stride (the largest tile, <= SLOT)
   int max_chunks;
   float eps, attn_scale;
   const uint8_t *embd, *out_w;
@@ -231,7 +237,7 @@ __device__ __forceinline__ void unit_range(int units, int stage, int cta, int G,
 
 // rows of stage `kind` of layer l owned by this CTA, in the stage's row space
 __device__ __forceinline__ void stage_rows(const Params &p, int kind, int l, int cta, int &r0, int &r1) {
-  const int stage = l * 5 + kind;
+  const int stage = l * 5 + (kind == ST_DOWN2 ? ST_DOWN : kind);  // both parts: the same rows
   int u0, u1;
   switch (kind) {
     case ST_QKV:
@@ -241,16 +247,26 @@ __device__ __forceinline__ void stage_rows(const Params &p, int kind, int l, int
       return;
     case ST_O: unit_range(p.E, stage, cta, p.G, r0, r1); return;
     case ST_GU: unit_range(p.F, stage, cta, p.G, r0, r1); return;
-    case ST_DOWN: unit_range(p.E, stage, cta, p.G, r0, r1); return;
+    case ST_DOWN:
+    case ST_DOWN2: unit_range(p.E, stage, cta, p.G, r0, r1); return;
     default: unit_range(p.V, stage, cta, p.G, r0, r1); return;
   }
 }
 
 __device__ __forceinline__ int stage_rb(const Params &p, int kind) {
-  return kind == ST_O ? p.rb_Q : (kind == ST_DOWN ? p.rb_F : p.rb_E);
+  if (kind == ST_DOWN) return p.split ? p.rb_FA : p.rb_F;
+  if (kind == ST_DOWN2) return p.rb_FB;
+  return kind == ST_O ? p.rb_Q : p.rb_E;
 }
 __device__ __forceinline__ int stage_nseg(const Params &p, int kind) {
-  return kind == ST_O ? p.nseg_Q : (kind == ST_DOWN ? p.nseg_F : p.nseg_E);
+  if (kind == ST_DOWN) return p.split ? p.nseg_FA : p.nseg_F;
+  if (kind == ST_DOWN2) return p.nseg_FB;
+  return kind == ST_O ? p.nseg_Q : p.nseg_E;
+}
+__device__ __forceinline__ int stage_in_dim(const Params &p, int kind) {
+  if (kind == ST_DOWN) return p.split ? p.xa : p.F;
+  if (kind == ST_DOWN2) return p.F - p.xa;
+  return kind == ST_O ? p.Q : p.E;
 }
 
 // ---------------------------------------------------------------------------------
@@ -467,8 +483,9 @@ struct Smem {
     AttScratch at;    // attention-stage partials (a different phase of the layer)
   };
   float ssp[NC];      // per-warp partial squared sums of the RMS norm
-  float qh[256];      // one q head (attention over short contexts)
+  float qh[128];      // one q head (head_dim <= 128)
   float lm[MAX_LM_ROWS];
+  float dpart[32];    // split down projection: part 1's sums of this CTA's rows
   int rel[NSLOT];     // warps done with the tile in each slot
   int slot_tile[NSLOT];  // tile index last issued into each slot
   int pad_[3];
@@ -755,6 +772,11 @@ __device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) 
     }
     return (unsigned)(n * rb);
   }
+  if ((kind == ST_DOWN && p.split) || kind == ST_DOWN2) {  // one input part of each row: a copy per row
+    const size_t off = kind == ST_DOWN2 ? (size_t)p.rb_FA : 0;
+    for (int i = 0; i < n; i++) f((unsigned)(i * rb), W.down + (size_t)(r + i) * p.rb_F + off, (unsigned)rb);
+    return (unsigned)(n * rb);
+  }
   const uint8_t *src = kind == ST_O ? W.o : (kind == ST_DOWN ? W.down : p.out_w);
   f(0u, src + (size_t)r * rb, (unsigned)(n * rb));
   return (unsigned)(n * rb);
@@ -766,7 +788,7 @@ __device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) 
 __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
   const int2 d = tbl[j];
   stamp_tile(p, j, 0);
-  uint8_t *dst = rg.slots + (size_t)slot * SLOT;
+  uint8_t *dst = rg.slots + (size_t)slot * p.slot_bytes;
   uint64_t *bar = &rg.full[slot];
   sm.issued[slot]++;
   *(volatile int *)&sm.slot_tile[slot] = j;
@@ -885,7 +907,7 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = warp / NG, wig = warp % NG;
   const int nseg = stage_nseg(p, kind), rb = stage_rb(p, kind), Tr = p.tile_rows[kind];
-  const int in_dim = kind == ST_O ? p.Q : (kind == ST_DOWN ? p.F : p.E);
+  const int in_dim = stage_in_dim(p, kind);
   const bool gu = kind == ST_GU;
   const int seg = wig % nseg, rpw = NG / nseg, rs = wig / nseg;
   const bool active = lane_active<T>(seg, lane, in_dim);
@@ -893,12 +915,12 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
   const bool lead = wig == 0 && lane == 0;  // stamps of the group that has the tile
   int r0, r1;
   stage_rows(p, kind, l, blockIdx.x, r0, r1);
-  const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : kind + 1);
+  const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : (kind == ST_DOWN2 ? ST_DOWN : kind) + 1);
   for (int r = r0; r < r1; r += Tr) {
     if (tile_ctr % NGRP == grp) {
       const int n = min(Tr, r1 - r);
       const int rows = gu ? 2 * n : n;
-      const uint32_t tile = slots + (uint32_t)slot * SLOT;
+      const uint32_t tile = slots + (uint32_t)slot * (uint32_t)p.slot_bytes;
       float *red = sm.red[2 * grp + ((tile_ctr / NGRP) & 1)];
       const bool ok = slot_wait(p, rg, sm, slot, tile_ctr, phase);
       if (lead) stamp_tile(p, tile_ctr, 1);
@@ -973,8 +995,19 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
             }
             va *= osc;
             vb *= osc;
-            if (gu) finish_rows(p, sm, kind, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
-            else finish_rows(p, sm, kind, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
+            if (kind == ST_DOWN && p.split) {  // part 1 of a split down row: kept for part 2
+              if (lane == 0) {
+                sm.dpart[r + a - r0] = va;
+                if (hasb) sm.dpart[r + b - r0] = vb;
+              }
+            } else if (kind == ST_DOWN2) {  // part 2: part 1 + part 2, then the residual
+              finish_rows(p, sm, ST_DOWN, l, pos, r0, r + a, sm.dpart[r + a - r0] + va, r + b,
+                          hasb ? sm.dpart[r + b - r0] + vb : 0.f, hasb, sr, tag);
+            } else if (gu) {
+              finish_rows(p, sm, kind, l, pos, r0, r + i, va, r + i, vb, true, sr, tag);
+            } else {
+              finish_rows(p, sm, kind, l, pos, r0, r + a, va, r + b, vb, hasb, sr, tag);
+            }
           }
         }
       }
@@ -1299,7 +1332,7 @@ __device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l
     sr.s0 = lane < half ? __ldg(p.sin_t + base + lane) : 0.f;
     sr.c1 = lane + 32 < half ? __ldg(p.cos_t + base + 32 + lane) : 0.f;
     sr.s1 = lane + 32 < half ? __ldg(p.sin_t + base + 32 + lane) : 0.f;
-  } else if (kind == ST_O || kind == ST_DOWN) {  // the residual of this CTA's rows (<= 32)
+  } else if (kind == ST_O || kind == ST_DOWN || kind == ST_DOWN2) {  // the residual of this CTA's rows (<= 32)
     int r0, r1;
     stage_rows(p, kind, l, blockIdx.x, r0, r1);
     sr.hres = lane < r1 - r0 ? poll_ll(p, p.hid_ll + r0 + lane, hid_tag) : 0.f;
@@ -1313,7 +1346,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   extern __shared__ __align__(128) uint8_t dsm[];
   Ring rg;
   rg.slots = dsm;
-  rg.full = reinterpret_cast<uint64_t *>(dsm + (size_t)NSLOT * SLOT);
+  rg.full = reinterpret_cast<uint64_t *>(dsm + (size_t)NSLOT * p.slot_bytes);
   uint64_t *tbl_bar = rg.full + NSLOT;
   Smem &sm = *reinterpret_cast<Smem *>(tbl_bar + 1);  // 16-byte aligned: 5 + 1 barriers of 8 bytes
   int2 *tbl = reinterpret_cast<int2 *>(&sm + 1);
@@ -1347,16 +1380,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   unsigned phase = 0;
   ActRegs<T> x;
   StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
-  // One pass per projection stage: QKV, O, gate/up, down of every layer, then the
-  // LM head; a single matvec call site keeps one copy of the tile loop in the
-  // instruction cache for all of them.
-  for (int si = 0; si <= 4 * p.L; si++) {
-    const int l = si >> 2;
-    const int kind = l == p.L ? ST_LM : (si & 3);  // ST_QKV, ST_O, ST_GU, ST_DOWN are 0..3
-    const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : kind + 1);
+  // One pass per projection stage: QKV, O, gate/up, down (in two input parts when
+  // split) of every layer, then the LM head; a single matvec call site keeps one copy
+  // of the tile loop in the instruction cache for all of them.
+  const int spl = p.split ? 5 : 4;  // stages per layer
+  for (int si = 0; si <= spl * p.L; si++) {
+    const int l = si / spl, sk = si - l * spl;
+    const int kind = l == p.L ? ST_LM : (sk == 4 ? ST_DOWN2 : sk);  // ST_QKV, ST_O, ST_GU, ST_DOWN are 0..3
+    const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : (kind == ST_DOWN2 ? ST_DOWN : kind) + 1);
     const LayerW &W = p.layers[l < p.L ? l : 0];
     const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
-    load_stage_regs(p, kind, l, pos, sr, kind == ST_DOWN ? mk_tag(launch, l, TG_POST_O) : hid_in);
+    load_stage_regs(p, kind, l, pos, sr, kind == ST_DOWN || kind == ST_DOWN2 ? mk_tag(launch, l, TG_POST_O) : hid_in);
     if (si > 0) cta_sync();  // every warp is done with the previous input: the staging buffer is rewritten
     float osc;
     unsigned tag_out;
@@ -1371,9 +1405,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       osc = stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q,
                                   8 * stage_id + 1);
       tag_out = mk_tag(launch, l, TG_POST_O);
-    } else if (kind == ST_DOWN) {
-      osc = stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll, mk_tag(launch, l, TG_ACT), nullptr, p.F, p.nseg_F,
-                                  8 * stage_id + 1);
+    } else if (kind == ST_DOWN || kind == ST_DOWN2) {
+      const int x0 = kind == ST_DOWN2 ? p.xa : 0;
+      osc = stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll + x0, mk_tag(launch, l, TG_ACT), nullptr, stage_in_dim(p, kind),
+                                  stage_nseg(p, kind), 8 * stage_id + 1);
       tag_out = mk_tag(launch, l, TG_POST_DOWN);
     } else {  // gate/up after the FFN norm, or the LM head after the final norm (model.rs:72-95)
       const bool lm = kind == ST_LM;
@@ -1460,9 +1495,10 @@ __global__ void k_build_tiles(const Params *__restrict__ pp, int2 *tiles, int *n
   if (threadIdx.x != 0) return;
   const int cta = blockIdx.x;
   int nt = 0;
+  const int spl = p.split ? 5 : 4;  // stages per layer, in the kernel's order
   for (int l = 0; l <= p.L; l++) {
-    const int lo = l < p.L ? ST_QKV : ST_LM, hi = l < p.L ? ST_DOWN : ST_LM;
-    for (int kind = lo; kind <= hi; kind++) {
+    for (int sk = 0; sk < (l < p.L ? spl : 1); sk++) {
+      const int kind = l == p.L ? ST_LM : (sk == 4 ? ST_DOWN2 : sk);
       int r0, r1;
       stage_rows(p, kind, l, cta, r0, r1);
       for (int r = r0; r < r1; r += p.tile_rows[kind]) {
@@ -1527,35 +1563,49 @@ int decode_prepare(sq_ctx *c) {
   // supported shapes: same type everywhere, rows multiple of 16 bytes, <= 8 segments, GQA group 4
   bool ok = m->out_type == wt && m->embd_type == wt && cf.n_blocks <= dk::MAX_LAYERS &&
             cf.n_heads == dk::GROUP * cf.n_kv_heads && (cf.head_dim == 64 || cf.head_dim == 128);
-  const int nE = nseg_for(E), nQ = nseg_for(Q), nF = nseg_for(F);
-  ok = ok && nE && nQ && nF;
+  // an FFN input wider than the staging buffer is taken in two parts of <= MAX_X
+  const int split = F > dk::MAX_X, xa = split ? dk::MAX_X : F, xb = F - xa;
+  const int nE = nseg_for(E), nQ = nseg_for(Q), nF = nseg_for(F), nFA = nseg_for(xa), nFB = split ? nseg_for(xb) : 1;
+  ok = ok && nE && nQ && nFA && nFB && (split || nF);
   ok = ok && m->acts == SQ_ACTS_F32;  // Q8_0 activations run on the op-level kernels
-  for (int d : {E, Q, F}) {
-    ok = ok && (d / QK) % 8 == 0 && ((size_t)(d / QK) * bb) % 16 == 0;  // pairs, 16-byte rows
+  for (int d : {E, Q, xa, split ? xb : xa}) {
+    ok = ok && d > 0 && (d / QK) % 8 == 0 && ((size_t)(d / QK) * bb) % 16 == 0;  // pairs, 16-byte rows and parts
     if (wt == SQ_BF16) ok = ok && d % 2048 == 0;  // BF16 lanes stripe whole 2048-element segments
   }
-  const int rbE = E / QK * bb, rbQ = Q / QK * bb, rbF = F / QK * bb;
+  const int rbE = E / QK * bb, rbQ = Q / QK * bb, rbF = F / QK * bb, rbFA = xa / QK * bb, rbFB = xb / QK * bb;
   auto rows_fit = [&](int rb, int mult) {
     int t = dk::SLOT / (rb * mult);
     if (t >= 2) t &= ~1;
     return t;
   };
   dk::Params h{};
+  h.split = split;
+  h.xa = xa;
+  h.rb_FA = rbFA;
+  h.rb_FB = rbFB;
+  h.nseg_FA = nFA;
+  h.nseg_FB = nFB;
   h.tile_rows[dk::ST_QKV] = rows_fit(rbE, 1);
   h.tile_rows[dk::ST_O] = rows_fit(rbQ, 1);
   h.tile_rows[dk::ST_GU] = rows_fit(rbE, 2);
-  h.tile_rows[dk::ST_DOWN] = rows_fit(rbF, 1);
+  h.tile_rows[dk::ST_DOWN] = rows_fit(split ? rbFA : rbF, 1);
   h.tile_rows[dk::ST_LM] = rows_fit(rbE, 1);
-  for (int k = 0; k < 5; k++) {
-    const int nseg = k == dk::ST_O ? nQ : (k == dk::ST_DOWN ? nF : nE);
+  h.tile_rows[dk::ST_DOWN2] = split ? rows_fit(rbFB, 1) : 2;
+  int slot_bytes = 0;
+  for (int k = 0; k < 6; k++) {
+    const int nseg = k == dk::ST_O ? nQ : (k == dk::ST_DOWN ? (split ? nFA : nF) : (k == dk::ST_DOWN2 ? nFB : nE));
+    const int rb = k == dk::ST_O ? rbQ : (k == dk::ST_DOWN ? (split ? rbFA : rbF) : (k == dk::ST_DOWN2 ? rbFB : rbE));
     // segment partial sums of a tile (rows x segments) go through shared memory
     ok = ok && h.tile_rows[k] >= 2 && (nseg == 1 || h.tile_rows[k] * (k == dk::ST_GU ? 2 : 1) * nseg <= dk::MAX_TILE_ITEMS);
+    if (k != dk::ST_DOWN2 || split) slot_bytes = std::max(slot_bytes, h.tile_rows[k] * rb * (k == dk::ST_GU ? 2 : 1));
   }
+  h.slot_bytes = (slot_bytes + 127) & ~127;  // the largest tile; mbarriers after the ring stay 8-byte aligned
   int dev = m->device, nsm = 0;
   SQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-  // residual rows per CTA live in one register per lane; LM rows per CTA in shared memory
+  // residual rows per CTA live in one register per lane (and part sums in dpart[32]);
+  // LM rows per CTA in shared memory
   ok = ok && (E + nsm - 1) / nsm <= 32 && (cf.vocab_size + nsm - 1) / nsm <= dk::MAX_LM_ROWS;
-  ok = ok && std::max(std::max(E, Q), F) <= dk::MAX_X;  // stage inputs fit the shared staging buffer
+  ok = ok && std::max(std::max(E, Q), std::max(xa, xb)) <= dk::MAX_X;  // stage inputs fit the staging buffer
   if (!ok) return SQ_OK;  // the op-level path serves this model
   void *kern = nullptr;
   if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
@@ -1660,7 +1710,7 @@ int decode_prepare(sq_ctx *c) {
   dk::k_build_tiles<<<nsm, 32>>>(st->d_params, h.tiles, h.ntiles, h.max_tiles);
   SQ_CHECK_LAUNCH("build tiles");
   SQ_CUDA(cudaDeviceSynchronize());
-  const size_t smem = (size_t)dk::NSLOT * dk::SLOT + (dk::NSLOT + 1) * sizeof(uint64_t) + sizeof(dk::Smem) +
+  const size_t smem = (size_t)dk::NSLOT * h.slot_bytes + (dk::NSLOT + 1) * sizeof(uint64_t) + sizeof(dk::Smem) +
                       (size_t)h.max_tiles * sizeof(int2);
   int smem_max = 0;
   SQ_CUDA(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));

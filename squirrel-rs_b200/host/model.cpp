@@ -723,7 +723,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     }
     // row-parallel O: sum the shards, then the residual add (one peer-memory kernel for a decode row)
     if (tp && n == 1 && m->ar) {
-      TRY(launch_allreduce_add(s, m->ar, c->hidden, c->attn_out));
+      TRY(launch_allreduce_add(s, m->ar, c->hidden, c->attn_out, pdl));
     } else {
       if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));
       if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
@@ -746,7 +746,7 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_linear(s, c->act, n, F, L.down, wt, E, c->ffn_out, aq, c->xq, ws, wsf));
     }
     if (tp && n == 1 && m->ar) {  // row-parallel down, likewise
-      TRY(launch_allreduce_add(s, m->ar, c->hidden, c->ffn_out));
+      TRY(launch_allreduce_add(s, m->ar, c->hidden, c->ffn_out, pdl));
     } else {
       if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));
       if (!fused || tp) TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));

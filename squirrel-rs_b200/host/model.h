@@ -30,7 +30,7 @@ int nccl_all_reduce_min_int(void *comm, int *buf, cudaStream_t s);
 // launched for one decode row with the residual add fused, error word read after a sync.
 int tp_allreduce_create(sq_model *m);
 void tp_allreduce_release(TpAllReduce *ar);
-cudaError_t launch_allreduce_add(cudaStream_t s, const TpAllReduce *ar, float *hidden, const float *part);
+cudaError_t launch_allreduce_add(cudaStream_t s, TpAllReduce *ar, float *hidden, const float *part, bool pdl);
 unsigned tp_allreduce_status(const TpAllReduce *ar, bool clear);
 int tp_allreduce_recover(sq_model *m);  // collective re-synchronization after a timeout
 }  // namespace sq

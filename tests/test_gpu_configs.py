@@ -9,8 +9,9 @@ same seeded GGUF and prompt; the GGUF's sha256 is checked first):
                 (split-KV attention inside the decode kernel)
   cfg4_1b_bf16  config 4: an 8192-token BF16 prefill (tensor-core GEMMs and
                 attention), the next id and its logits
-  cfg5_8b_q8_0  config 5's model on one GPU: head_dim 128, FFN 14336, untied LM head,
-                16-token prompt, 8 greedy steps
+  cfg5_8b_q8_0  config 5's model on one GPU: head_dim 128, FFN 14336 (the down
+                projection's input in two parts), untied LM head, 16-token prompt,
+                8 greedy steps through the persistent decode kernel
 
 Bar (north star): identical greedy ids; logits within max-abs 1e-2 and max-abs /
 max|logit| <= 1e-3 after the prompt and after the last step."""
@@ -46,8 +47,7 @@ def test_config_shape_matches_oracle(gpu_lib, name):
         assert int(ctx.forward(prompt)) == int(ids[0])
         assert_logits_close(ctx.logits(), z["logits_first"])
         if len(ids) > 1:
-            if c["spec"] == "1b":
-                assert ctx.launches_per_token == 1  # the persistent decode kernel serves the 1B shape
+            assert ctx.launches_per_token == 1  # the persistent decode kernel serves both shapes
             rest = ctx.decode_steps(len(ids) - 1)
             assert np.array_equal(rest, ids[1:])
             assert_logits_close(ctx.logits(), z["logits_last"])

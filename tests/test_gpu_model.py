@@ -110,6 +110,29 @@ def test_q8_acts_teacher_forced(gpu_lib, models, spec, wt):
     ctx.close()
 
 
+@pytest.mark.parametrize("wt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("spec", ["tiny", "small"])
+def test_q8_acts_free_running(gpu_lib, models, spec, wt):
+    """Q8_0 activations, free-running at the north-star tolerance: the GPU's own greedy
+    ids through sq_decode_steps equal the oracle's W8A8 ids at every step up to the
+    first one whose oracle top-2 margin is within 2 x ABS_TOL (1e-2 of logit error
+    could pick the other token there, and the runs may then diverge). The synthetic
+    models' margins are small, so at least the first three steps must be decidable."""
+    path = G.ensure_gguf(spec, wt)
+    prompt = G.prompt_ids(8, seed=17, high=G.SPECS[spec]["vocab"])
+    ref = O.Model(path, acts_q8=True)
+    ids_ref, _, logits_ref = ref.generate(prompt, 24, want_logits=True)
+    margins = [float(np.diff(np.sort(lg)[-2:])[0]) for lg in logits_ref]
+    decidable = next((i for i, mg in enumerate(margins) if mg <= 2 * ABS_TOL), len(margins))
+    assert decidable >= 3, margins
+    ctx = gpu_model(models, spec, wt, 1).new_context(256)
+    first = ctx.forward(prompt)
+    assert float(np.max(np.abs(ctx.logits() - logits_ref[0]))) <= Q8_ACTS_ABS_TOL
+    ids = np.concatenate([[first], ctx.decode_steps(len(ids_ref) - 1)])
+    assert np.array_equal(ids[:decidable], ids_ref[:decidable]), (ids.tolist(), ids_ref.tolist(), decidable)
+    ctx.close()
+
+
 def test_chunked_prefill_and_decode_steps(gpu_lib, models):
     """A prompt longer than the prefill chunk, then device-chained decode steps."""
     spec, wt = "tiny", "q8_0"
