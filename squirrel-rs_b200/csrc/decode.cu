@@ -784,7 +784,7 @@ __device__ __forceinline__ unsigned tile_copies(const Params &p, int2 d, F &&f) 
 
 // Issue tile j of this CTA's table into `slot`: bulk copies completing on full[slot].
 // The weights are read once per token, so the copies mark their L2 lines
-// evict-first; what the L2 keeps is the (optional) prefetched tiles not yet consumed.
+// evict-first.
 __device__ void issue_tile(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int j, int slot) {
   const int2 d = tbl[j];
   stamp_tile(p, j, 0);
