@@ -278,6 +278,8 @@ int tp_allreduce_recover(sq_model *m) {
   return e == cudaSuccess ? SQ_OK : cuda_fail(e, "tp_recover");
 }
 
+unsigned *tp_allreduce_err_ptr(const TpAllReduce *ar) { return ar ? ar->err : nullptr; }
+
 unsigned tp_allreduce_status(const TpAllReduce *ar, bool clear) {
   if (!ar) return 0;
   unsigned v = 0;

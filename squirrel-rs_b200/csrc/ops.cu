@@ -398,24 +398,36 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     tile_of(t, mi, r0, rows);
     const uint32_t tile = ring + (uint32_t)slot * MV_SLOT + (uint32_t)seg * CB + (uint32_t)lane * PW * 4;
     float *rd = red + slot * MV_REDROWS * nseg;  // partial sums, added by the producer
-    constexpr int RI = T == SQ_Q4_0 ? 4 : 2;  // rows an iteration: independent dot chains
+    constexpr int RI = T == SQ_BF16 ? 2 : 4;  // rows an iteration: independent dot chains
     for (int r = g; r < rows; r += RI * G) {  // rows r, r + G, .. of the tile
       float d[RI];
 #pragma unroll
       for (int q = 0; q < RI; q++) d[q] = 0.f;
-      if (active) {
-        uint32_t wv[RI][PW];
+      if constexpr (T == SQ_Q8_0) {
+        // four rows word by word (the lane's block pair sits at the same odd word
+        // stride as in the decode kernel; `tile` already holds the lane's offset)
+        if (active) {
+          uint32_t ra[4];
 #pragma unroll
-        for (int q = 0; q < RI; q++)
-          if (r + q * G < rows) mv_load_pair<T>(tile + (uint32_t)((r + q * G) * rb), lane, wv[q]);
+          for (int q = 0; q < 4; q++) ra[q] = tile + (uint32_t)((r + q * G < rows ? r + q * G : r) * rb);
+          quad_dot<T>(ra, 0, 0, x2, d);
+        }
+        warp_sum4(d);
+      } else {
+        if (active) {
+          uint32_t wv[RI][PW];
 #pragma unroll
-        for (int q = 0; q < RI; q++)
-          if (r + q * G < rows) d[q] = pair_dot<T>(wv[q], x2);
+          for (int q = 0; q < RI; q++)
+            if (r + q * G < rows) mv_load_pair<T>(tile + (uint32_t)((r + q * G) * rb), lane, wv[q]);
+#pragma unroll
+          for (int q = 0; q < RI; q++)
+            if (r + q * G < rows) d[q] = pair_dot<T>(wv[q], x2);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int q = 0; q < RI; q++) d[q] += __shfl_xor_sync(0xffffffffu, d[q], o);
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int q = 0; q < RI; q++) d[q] += __shfl_xor_sync(0xffffffffu, d[q], o);
       if (lane == 0) {
 #pragma unroll
         for (int q = 0; q < RI; q++) {
@@ -996,6 +1008,35 @@ cudaError_t launch_argmax_fold(cudaStream_t s, const void *states, int n, long l
   return cudaGetLastError();
 }
 size_t argmax_state_bytes() { return sizeof(ArgState); }
+
+unsigned *mv_err_ptr() {
+  static unsigned *ptrs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_mv_err) != cudaSuccess) return nullptr;
+    ptrs[dev] = (unsigned *)p;
+  }
+  return ptrs[dev];
+}
+
+__global__ void k_collect_status(const long long *argmax, const unsigned *e0, const unsigned *e1, const unsigned *e2,
+                                 const unsigned *e3, unsigned long long *out) {
+  if (threadIdx.x != 0) return;
+  out[0] = (unsigned long long)*argmax;
+  out[1] = e0 ? *(volatile const unsigned *)e0 : 0u;
+  out[2] = e1 ? *(volatile const unsigned *)e1 : 0u;
+  out[3] = e2 ? *(volatile const unsigned *)e2 : 0u;
+  out[4] = e3 ? *(volatile const unsigned *)e3 : 0u;
+}
+
+cudaError_t launch_collect_status(cudaStream_t s, const long long *argmax, const unsigned *e0, const unsigned *e1,
+                                  const unsigned *e2, const unsigned *e3, unsigned long long *out) {
+  k_collect_status<<<1, 32, 0, s>>>(argmax, e0, e1, e2, e3, out);
+  return cudaGetLastError();
+}
 
 unsigned matvec_status(bool clear) {
   unsigned v = 0;

@@ -52,6 +52,11 @@ cudaError_t launch_gemm_tc(cudaStream_t s, const float *x, int m, int K, const v
 unsigned gemm_tc_status(bool clear);
 // Non-zero when a bounded wait of the streaming matvec (k_matvec) gave up (read after a sync).
 unsigned matvec_status(bool clear);
+unsigned *mv_err_ptr();  // device address of that error word (current device)
+// One launch that copies the argmax and up to four error words (null: skipped, 0)
+// into out[0..4], so a call ends with one small device-to-host copy.
+cudaError_t launch_collect_status(cudaStream_t s, const long long *argmax, const unsigned *e0, const unsigned *e1,
+                                  const unsigned *e2, const unsigned *e3, unsigned long long *out);
 // Both words of the current device, read (and cleared when `clear`) after a sync:
 // SQ_OK, or SQ_ERR_TIMEOUT with a message naming `what` and the kernels that gave up.
 int device_wait_status(bool clear, const char *what);

@@ -469,6 +469,8 @@ sq_ctx::~sq_ctx() {
   if (step_graph) cudaGraphExecDestroy(step_graph);  // before the buffers (and any NCCL communicator) it uses
   decode_release(this);
   cudaFree(d_out_ids);
+  if (h_ids) cudaFreeHost(h_ids);
+  if (h_status) cudaFreeHost(h_status);
   for (void *p : allocs) cudaFree(p);
   if (stream) cudaStreamDestroy(stream);
   cudaSetDevice(prev);
@@ -530,6 +532,9 @@ extern "C" int sq_ctx_create(sq_model *m, int max_ctx, sq_ctx **out) {
     SQ_CUDA(ctx_alloc(x.get(), (uint8_t **)&x->arg_all, argmax_state_bytes() * m->tp_size));
   }
   SQ_CUDA(ctx_alloc(x.get(), &x->d_tokens, (size_t)R));
+  SQ_CUDA(ctx_alloc(x.get(), &x->d_status, 8));
+  SQ_CUDA(cudaHostAlloc((void **)&x->h_ids, (size_t)max_ctx * sizeof(uint32_t), cudaHostAllocDefault));
+  SQ_CUDA(cudaHostAlloc((void **)&x->h_status, 8 * sizeof(unsigned long long), cudaHostAllocDefault));
   // RoPE table from the C library's sinf/cosf of pos * inv_freq[j] (rope.rs:25-26)
   const int half = c.head_dim / 2;
   std::vector<float> ct((size_t)max_ctx * half), stb((size_t)max_ctx * half);
@@ -846,14 +851,43 @@ static int check_ids(sq_ctx *c, const uint32_t *ids, size_t n) {
   return SQ_OK;
 }
 
+// The end of a model-level call: one launch gathers the argmax and every bounded-wait
+// error word the call's kernels may have set (decode kernel, streaming matvec,
+// tensor-core kernels, peer all-reduce) into one buffer, one copy brings it to pinned
+// host memory, one stream sync. Only when a word is set do the per-kernel status
+// reads (which clear the words and name the kernel) run.
+static int finish_call(sq_ctx *c, const char *what, long long *id) {
+  const unsigned *ar_err = c->m->ar ? tp_allreduce_err_ptr(c->m->ar) : nullptr;
+  SQ_CUDA(launch_collect_status(c->stream, c->d_argmax, decode_err_ptr(c), mv_err_ptr(), tc_err_ptr(), ar_err,
+                                c->d_status));
+  SQ_CUDA(cudaMemcpyAsync(c->h_status, c->d_status, 5 * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                          c->stream));
+  SQ_CUDA(cudaStreamSynchronize(c->stream));
+  const unsigned long long *hs = c->h_status;
+  if (hs[1] || decode_check_always(c)) {
+    const int st = decode_check(c);
+    if (st) return st;
+  }
+  if (hs[2] || hs[3]) {
+    const int st = device_wait_status(true, what);
+    if (st) return st;
+  }
+  if (hs[4] && tp_allreduce_status(c->m->ar, true))
+    return fail(SQ_ERR_TIMEOUT, std::string(what) +
+                                    ": a peer's partial sum did not arrive within the tensor-parallel all-reduce's limit");
+  if (id) *id = (long long)hs[0];
+  return SQ_OK;
+}
+
 extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *out_argmax) {
   if (!c) return fail(SQ_ERR_ARG, "forward: null context");
   int st = check_ids(c, ids, n);
   if (st) return st;
   SQ_CUDA(cudaSetDevice(c->m->device));
+  memcpy(c->h_ids, ids, n * sizeof(uint32_t));  // pinned staging (the previous call's copies have finished)
   for (size_t r0 = 0; r0 < n; r0 += c->ws_rows) {
     const int rows = (int)std::min((size_t)c->ws_rows, n - r0);
-    SQ_CUDA(cudaMemcpyAsync(c->d_tokens, ids + r0, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, c->stream));
+    SQ_CUDA(cudaMemcpyAsync(c->d_tokens, c->h_ids + r0, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, c->stream));
     if (rows == 1 && r0 == 0 && decode_available(c)) {
       st = decode_launch(c, c->d_tokens, nullptr, 0);
     } else if (n == 1) {
@@ -865,14 +899,8 @@ extern "C" int sq_forward(sq_ctx *c, const uint32_t *ids, size_t n, uint32_t *ou
   }
   c->have_logits = true;
   long long id = 0;
-  SQ_CUDA(cudaMemcpyAsync(&id, c->d_argmax, sizeof(long long), cudaMemcpyDeviceToHost, c->stream));
-  SQ_CUDA(cudaStreamSynchronize(c->stream));
-  st = decode_check(c);
+  st = finish_call(c, "forward", &id);
   if (st) return st;
-  st = device_wait_status(true, "forward");
-  if (st) return st;
-  if (c->m->ar && tp_allreduce_status(c->m->ar, true))
-    return fail(SQ_ERR_TIMEOUT, "forward: a peer's partial sum did not arrive within the tensor-parallel all-reduce's limit");
   if (out_argmax) *out_argmax = (uint32_t)id;
   return SQ_OK;
 }
@@ -943,15 +971,16 @@ extern "C" int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids) {
     }
   }
   if (!st) {
-    cudaError_t e2 = cudaMemcpyAsync(out_ids, d_out, n_steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream);
+    cudaError_t e2 = cudaMemcpyAsync(c->h_ids, d_out, n_steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream);
     if (e2 != cudaSuccess) st = cuda_fail(e2, "decode_steps copy");
   }
-  cudaError_t e3 = cudaStreamSynchronize(c->stream);
-  if (!st && e3 != cudaSuccess) st = cuda_fail(e3, "decode_steps sync");
-  if (!st) st = decode_check(c);
-  if (!st) st = device_wait_status(true, "decode_steps");
-  if (!st && c->m->ar && tp_allreduce_status(c->m->ar, true))
-    st = fail(SQ_ERR_TIMEOUT, "decode_steps: a peer's partial sum did not arrive within the tensor-parallel all-reduce's limit");
+  if (!st) st = finish_call(c, "decode_steps", nullptr);  // synchronizes the stream
+  if (st) {
+    cudaStreamSynchronize(c->stream);  // nothing of this call is left running
+    decode_check(c);                   // and the decode kernel's counters are reset
+  } else {
+    memcpy(out_ids, c->h_ids, n_steps * sizeof(uint32_t));
+  }
   c->have_logits = true;
   return st;
 }

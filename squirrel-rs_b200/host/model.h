@@ -32,6 +32,7 @@ int tp_allreduce_create(sq_model *m);
 void tp_allreduce_release(TpAllReduce *ar);
 cudaError_t launch_allreduce_add(cudaStream_t s, TpAllReduce *ar, float *hidden, const float *part, bool pdl);
 unsigned tp_allreduce_status(const TpAllReduce *ar, bool clear);
+unsigned *tp_allreduce_err_ptr(const TpAllReduce *ar);
 int tp_allreduce_recover(sq_model *m);  // collective re-synchronization after a timeout
 }  // namespace sq
 
@@ -92,6 +93,10 @@ struct sq_ctx {
   float *logits_full = nullptr;  // tensor parallel: the gathered vocabulary
   void *arg_local = nullptr, *arg_all = nullptr;  // tensor parallel: per-rank argmax states
   uint32_t *d_out_ids = nullptr;  // ids of sq_decode_steps
+  // pinned host staging: the ids a call copies in or out (max_ctx of them), and the
+  // argmax with the error words every call reads back in one copy
+  uint32_t *h_ids = nullptr;
+  unsigned long long *h_status = nullptr, *d_status = nullptr;
   int out_cap = 0;
   std::vector<void *> allocs;
   ~sq_ctx();

@@ -49,9 +49,10 @@ def test_decode_wait_expires_reports_timeout_and_context_recovers(gpu_lib, monke
 def _fault_rank(rank, path, prompt, ids, qin, qout):
     """Rank 1's third peer all-reduce stores its partial but withholds its flags
     (SQ_TEST_WITHHOLD_PARTIAL=3, read when its model is created), so rank 0's wait
-    for it expires and rank 0 reports Timeout; both ranks run the whole step (its
-    NCCL calls included), then re-synchronize (sq_tp_recover), reset their contexts
-    and decode the oracle's ids again."""
+    for it expires and rank 0 reports Timeout (rank 1, which ran ahead meanwhile,
+    may see its next wait expire too); both ranks run the whole step (its NCCL calls
+    included), then re-synchronize (sq_tp_recover), reset their contexts and decode
+    the oracle's ids again."""
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     if rank == 1:
         os.environ["SQ_TEST_WITHHOLD_PARTIAL"] = "3"
@@ -114,7 +115,8 @@ def test_tp_allreduce_wait_expires_reports_timeout_and_group_recovers():
     assert not errs, errs
     by_rank = {v["rank"]: v for _, v in results}
     assert by_rank[0]["fault"] == "Timeout", by_rank[0]  # waited for rank 1's withheld flags
-    assert by_rank[1]["fault"] == "none", by_rank[1]  # rank 0's partials all arrived
-    assert by_rank[0]["fault_s"] < 60
+    # rank 1 ran ahead while rank 0 waited, so its next wait may expire as well
+    assert by_rank[1]["fault"] in ("none", "Timeout"), by_rank[1]
+    assert by_rank[0]["fault_s"] < 60 and by_rank[1]["fault_s"] < 60
     for r in (0, 1):
         assert by_rank[r]["ids"] == ids, by_rank[r]
