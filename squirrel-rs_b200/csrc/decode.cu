@@ -984,31 +984,33 @@ __device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsig
   }
 }
 
-// Long contexts: split-KV over (q head, chunk) items. Inside an item a lane owns a
-// position (its K row loaded with the warp's other 31 at once; q.k without
-// shuffles), the warp's softmax over its 32 positions, then lane = dimension for
-// p.V with the warp's V rows loaded up front; the 8 warps merge in shared memory
-// into the chunk's partial (max, sum, accumulator). The chunk that holds the token's
-// own position adds it from the tagged words of the QKV stage, and the last CTA to
-// finish a head merges the head's chunks and publishes the head's output.
+// Long contexts, grouped: split-KV over (kv head, chunk) items, so each K / V row a
+// chunk covers is read once for the GROUP q heads that share it (GQA), not once per
+// q head. Warp w takes q heads 2 * (w / 4) and 2 * (w / 4) + 1 of the group and the
+// chunk's 32-position blocks w % 4, w % 4 + 4, ...: a lane owns a position for q.k
+// (its K row in registers, both heads' dots from it), the warp's online softmax per
+// head over its blocks, then lane = dimension for p.V with each V row loaded once
+// for both heads. The four warps of a head merge in shared memory into the chunk's
+// partial per head; the chunk that holds the token's own position adds it from the
+// QKV stage's tagged words; the last CTA to finish a kv head combines the chunks of
+// its four heads (one warp per head) and publishes their outputs.
 template <int DPL>
-__device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsigned tag_in, unsigned tag_out) {
+__device__ void attention_groups(const Params &p, Smem &sm, int l, int pos, unsigned tag_in, unsigned tag_out) {
   constexpr int HD = DPL * 32;
+  static_assert(GROUP == 4 && NC == 8, "two heads x four position lanes of warps");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Lk = pos + 1;
-  int n_chunks = (Lk + NC * 32 - 1) / (NC * 32);
-  const int cap = max(1, (2 * p.G + p.H - 1) / p.H);
-  if (n_chunks > cap) n_chunks = cap;
+  int n_chunks = (Lk + 127) / 128;  // ~128 positions a chunk: four 32-position blocks, one per warp pair
   if (n_chunks > p.max_chunks) n_chunks = p.max_chunks;
   const int CH = (Lk + n_chunks - 1) / n_chunks;
-  const int items = p.H * n_chunks;
+  const int items = p.KVH * n_chunks;
+  const int hp = warp >> 2, bw = warp & 3;  // head pair, block lane of this warp
   for (int item = blockIdx.x; item < items; item += p.G) {
-    const int h = item / n_chunks, c = item % n_chunks, g = h / GROUP;
+    const int g = item / n_chunks, c = item % n_chunks;
     const int s0 = c * CH, s1 = min(Lk, s0 + CH);
     const int cached_end = min(s1, pos);  // positions below pos come from the cache
     const float *kb = p.kc + ((size_t)l * p.KVH + g) * p.max_ctx * HD;
     const float *vb = p.vc + ((size_t)l * p.KVH + g) * p.max_ctx * HD;
-    // this warp's first 32 keys load while q is being fetched
     float4 kr[HD / 4];
     auto load_k = [&](int base) {
       const int s = base + lane;
@@ -1017,80 +1019,94 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
       for (int k = 0; k < HD / 4; k++)
         kr[k] = valid ? ldcg4(kb + (size_t)s * HD + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
     };
-    if (s0 + warp * 32 < cached_end) load_k(s0 + warp * 32);
-    if (warp == 0) {
+    if (s0 + bw * 32 < cached_end) load_k(s0 + bw * 32);
+    if (warp < GROUP) {  // the group's four q heads into shared memory
       const unsigned long long *qa[DPL];
       float qv[DPL];
 #pragma unroll
-      for (int i = 0; i < DPL; i++) qa[i] = p.q_ll + (size_t)h * HD + lane + 32 * i;
+      for (int i = 0; i < DPL; i++) qa[i] = p.q_ll + (size_t)(g * GROUP + warp) * HD + lane + 32 * i;
       poll_ll_n<DPL>(p, qa, tag_in, qv);
 #pragma unroll
-      for (int i = 0; i < DPL; i++) sm.qh[lane + 32 * i] = qv[i];
+      for (int i = 0; i < DPL; i++) sm.at.a[warp][0][lane + 32 * i] = qv[i];  // head j's q in slot [j][0]
     }
     cta_sync();
-    float m = -INFINITY, lsum = 0.f, acc[DPL];
+    const float *q0 = sm.at.a[2 * hp][0], *q1 = sm.at.a[2 * hp + 1][0];
+    float m[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f}, acc[2][DPL];
 #pragma unroll
-    for (int i = 0; i < DPL; i++) acc[i] = 0.f;
-    constexpr int VJ = DPL >= 4 ? 8 : 16;  // V rows per batch (fewer registers than all 32 at once)
-    for (int base = s0 + warp * 32; base < cached_end; base += NC * 32) {
+    for (int i = 0; i < DPL; i++) acc[0][i] = acc[1][i] = 0.f;
+    constexpr int VJ = 8;  // V rows per batch
+    for (int base = s0 + bw * 32; base < cached_end; base += 4 * 32) {
       const int s = base + lane;
       const bool valid = s < cached_end;
-      float vv[VJ][DPL];
-      auto load_v = [&](int j0) {
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < HD / 4; k++) {
+        const float4 a = *reinterpret_cast<const float4 *>(q0 + 4 * k), b = *reinterpret_cast<const float4 *>(q1 + 4 * k);
+        d0 = fmaf(a.x, kr[k].x, d0);
+        d0 = fmaf(a.y, kr[k].y, d0);
+        d0 = fmaf(a.z, kr[k].z, d0);
+        d0 = fmaf(a.w, kr[k].w, d0);
+        d1 = fmaf(b.x, kr[k].x, d1);
+        d1 = fmaf(b.y, kr[k].y, d1);
+        d1 = fmaf(b.z, kr[k].z, d1);
+        d1 = fmaf(b.w, kr[k].w, d1);
+      }
+      if (base + 4 * 32 < cached_end) load_k(base + 4 * 32);  // the next block's keys while this one finishes
+      float pj[2];
+#pragma unroll
+      for (int t = 0; t < 2; t++) {
+        const float sc = valid ? (t ? d1 : d0) * p.attn_scale : -INFINITY;
+        const float mn = fmaxf(m[t], warp_max(sc));
+        const float corr = expf(m[t] - mn);
+        pj[t] = valid ? expf(sc - mn) : 0.f;
+        lsum[t] = fmaf(lsum[t], corr, warp_sum(pj[t]));
+#pragma unroll
+        for (int i = 0; i < DPL; i++) acc[t][i] *= corr;
+        m[t] = mn;
+      }
+#pragma unroll
+      for (int j0 = 0; j0 < 32; j0 += VJ) {
+        float vv[VJ][DPL];
 #pragma unroll
         for (int j = 0; j < VJ; j++)
 #pragma unroll
           for (int i = 0; i < DPL; i++)
             vv[j][i] = base + j0 + j < cached_end ? __ldcg(vb + (size_t)(base + j0 + j) * HD + lane + 32 * i) : 0.f;
-      };
-      load_v(0);
-      float d = 0.f;
-#pragma unroll
-      for (int k = 0; k < HD / 4; k++) {
-        const float4 q4 = *reinterpret_cast<const float4 *>(&sm.qh[4 * k]);
-        d = fmaf(q4.x, kr[k].x, d);
-        d = fmaf(q4.y, kr[k].y, d);
-        d = fmaf(q4.z, kr[k].z, d);
-        d = fmaf(q4.w, kr[k].w, d);
-      }
-      const float sc = valid ? d * p.attn_scale : -INFINITY;
-      const float mn = fmaxf(m, warp_max(sc));
-      const float corr = expf(m - mn);
-      const float pj = valid ? expf(sc - mn) : 0.f;
-      lsum = fmaf(lsum, corr, warp_sum(pj));
-#pragma unroll
-      for (int i = 0; i < DPL; i++) acc[i] *= corr;
-#pragma unroll
-      for (int j0 = 0; j0 < 32; j0 += VJ) {
-        if (j0) load_v(j0);
 #pragma unroll
         for (int j = 0; j < VJ; j++) {
-          const float pjj = __shfl_sync(FULL, pj, j0 + j);
+          const float p0 = __shfl_sync(FULL, pj[0], j0 + j), p1 = __shfl_sync(FULL, pj[1], j0 + j);
 #pragma unroll
-          for (int i = 0; i < DPL; i++) acc[i] = fmaf(pjj, vv[j][i], acc[i]);
+          for (int i = 0; i < DPL; i++) {
+            acc[0][i] = fmaf(p0, vv[j][i], acc[0][i]);
+            acc[1][i] = fmaf(p1, vv[j][i], acc[1][i]);
+          }
         }
       }
-      m = mn;
-      if (base + NC * 32 < cached_end) load_k(base + NC * 32);
     }
-    if (lane == 0) {
-      sm.at.m[warp][0] = m;
-      sm.at.l[warp][0] = lsum;
-    }
-#pragma unroll
-    for (int i = 0; i < DPL; i++) sm.at.a[warp][0][lane + 32 * i] = acc[i];
+    // per-warp partials in slots [warp][2 + t] for local head t (q stays in [j][0] for the merge)
     cta_sync();
-    if (warp == 0) {  // merge the warps, add the token's own position if it is in this chunk
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+      if (lane == 0) {
+        sm.at.m[warp][t] = m[t];
+        sm.at.l[warp][t] = lsum[t];
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; i++) sm.at.a[warp][2 + t][lane + 32 * i] = acc[t][i];
+    }
+    cta_sync();
+    if (warp < GROUP) {  // warp j merges head j of the group over its four warps, adds the token's own position
+      const int j = warp, hpj = j >> 1, t = j & 1, h = g * GROUP + j;
       float M = -INFINITY;
-      for (int w = 0; w < NC; w++) M = fmaxf(M, sm.at.m[w][0]);
+      for (int w = 4 * hpj; w < 4 * hpj + 4; w++) M = fmaxf(M, sm.at.m[w][t]);
       float Ls = 0.f, A[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; i++) A[i] = 0.f;
-      for (int w = 0; w < NC; w++) {
-        const float f = sm.at.l[w][0] > 0.f ? expf(sm.at.m[w][0] - M) : 0.f;
-        Ls = fmaf(sm.at.l[w][0], f, Ls);
+      for (int w = 4 * hpj; w < 4 * hpj + 4; w++) {
+        const float f = sm.at.l[w][t] > 0.f ? expf(sm.at.m[w][t] - M) : 0.f;
+        Ls = fmaf(sm.at.l[w][t], f, Ls);
 #pragma unroll
-        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.at.a[w][0][lane + 32 * i], f, A[i]);
+        for (int i = 0; i < DPL; i++) A[i] = fmaf(sm.at.a[w][2 + t][lane + 32 * i], f, A[i]);
       }
       if (s1 == Lk) {
         const unsigned long long *kva[2 * DPL];
@@ -1102,7 +1118,7 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
         }
         poll_ll_n<2 * DPL>(p, kva, tag_in, kvq);
 #pragma unroll
-        for (int i = 0; i < DPL; i++) d = fmaf(sm.qh[lane + 32 * i], kvq[i], d);
+        for (int i = 0; i < DPL; i++) d = fmaf(sm.at.a[j][0][lane + 32 * i], kvq[i], d);
         const float sc = warp_sum(d) * p.attn_scale;
         const float mn = fmaxf(M, sc);
         const float corr = Ls > 0.f ? expf(M - mn) : 0.f, pp = expf(sc - mn);
@@ -1122,12 +1138,13 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
     }
     cta_sync();
     if (threadIdx.x == 0) {
-      const unsigned old = atomicAdd(p.attn_cnt + (size_t)l * p.H + h, 1u);
+      const unsigned old = atomicAdd(p.attn_cnt + (size_t)l * p.H + g, 1u);
       sm.flag = old == (unsigned)(n_chunks - 1);
     }
     cta_sync();
-    if (sm.flag && warp == 0) {  // the head's last chunk: combine all of them
+    if (sm.flag && warp < GROUP) {  // the kv head's last chunk: warp j combines head j's chunks
       __threadfence();
+      const int h = g * GROUP + warp;
       float M = -INFINITY;
       for (int cc = 0; cc < n_chunks; cc++) {
         const float *pp = p.attn_part + ((size_t)h * p.max_chunks + cc) * (HD + 2);
@@ -1149,9 +1166,9 @@ __device__ void attention_chunks(const Params &p, Smem &sm, int l, int pos, unsi
       const float inv = 1.0f / Ls;
 #pragma unroll
       for (int i = 0; i < DPL; i++) st_ll(p.attn_ll + (size_t)h * HD + lane + 32 * i, A[i] * inv, tag_out);
-      if (lane == 0) p.attn_cnt[(size_t)l * p.H + h] = 0;  // per-layer counter, ready for the next token
     }
     cta_sync();
+    if (sm.flag && threadIdx.x == 0) p.attn_cnt[(size_t)l * p.H + g] = 0;  // ready for the next token
   }
 }
 
@@ -1273,7 +1290,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // ---- attention (waits on q / K / V words, not on a barrier)
       cta_sync();  // shared scratch of the staging buffer is reused below
       if (DPL <= 2 && pos < SHORT_CTX) attention_heads<DPL <= 2 ? DPL : 2>(p, sm, l, pos, tag_out, mk_tag(launch, l, TG_ATTN));
-      else attention_chunks<DPL>(p, sm, l, pos, tag_out, mk_tag(launch, l, TG_ATTN));
+      else attention_groups<DPL>(p, sm, l, pos, tag_out, mk_tag(launch, l, TG_ATTN));
       stamp(p, 8 * (5 * l + 1) + 6);
     }
   }
@@ -1479,7 +1496,8 @@ int decode_prepare(sq_ctx *c) {
   h.rb_E = rbE;
   h.rb_Q = rbQ;
   h.rb_F = rbF;
-  h.max_chunks = std::max(1, (2 * nsm + cf.n_heads - 1) / cf.n_heads);
+  // grouped long-context attention: ~128 positions a chunk, up to one item per CTA
+  h.max_chunks = std::max(1, nsm / cf.n_kv_heads);
   h.eps = cf.rms_eps;
   h.attn_scale = 1.0f / sqrtf((float)cf.head_dim);
   h.embd = (const uint8_t *)m->embd;

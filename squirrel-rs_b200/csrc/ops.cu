@@ -398,36 +398,24 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     tile_of(t, mi, r0, rows);
     const uint32_t tile = ring + (uint32_t)slot * MV_SLOT + (uint32_t)seg * CB + (uint32_t)lane * PW * 4;
     float *rd = red + slot * MV_REDROWS * nseg;  // partial sums, added by the producer
-    constexpr int RI = T == SQ_BF16 ? 2 : 4;  // rows an iteration: independent dot chains
+    constexpr int RI = T == SQ_Q4_0 ? 4 : 2;  // rows an iteration: independent dot chains
     for (int r = g; r < rows; r += RI * G) {  // rows r, r + G, .. of the tile
       float d[RI];
 #pragma unroll
       for (int q = 0; q < RI; q++) d[q] = 0.f;
-      if constexpr (T == SQ_Q8_0) {
-        // four rows word by word (the lane's block pair sits at the same odd word
-        // stride as in the decode kernel; `tile` already holds the lane's offset)
-        if (active) {
-          uint32_t ra[4];
+      if (active) {
+        uint32_t wv[RI][PW];
 #pragma unroll
-          for (int q = 0; q < 4; q++) ra[q] = tile + (uint32_t)((r + q * G < rows ? r + q * G : r) * rb);
-          quad_dot<T>(ra, 0, 0, x2, d);
-        }
-        warp_sum4(d);
-      } else {
-        if (active) {
-          uint32_t wv[RI][PW];
+        for (int q = 0; q < RI; q++)
+          if (r + q * G < rows) mv_load_pair<T>(tile + (uint32_t)((r + q * G) * rb), lane, wv[q]);
 #pragma unroll
-          for (int q = 0; q < RI; q++)
-            if (r + q * G < rows) mv_load_pair<T>(tile + (uint32_t)((r + q * G) * rb), lane, wv[q]);
-#pragma unroll
-          for (int q = 0; q < RI; q++)
-            if (r + q * G < rows) d[q] = pair_dot<T>(wv[q], x2);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int q = 0; q < RI; q++) d[q] += __shfl_xor_sync(0xffffffffu, d[q], o);
+        for (int q = 0; q < RI; q++)
+          if (r + q * G < rows) d[q] = pair_dot<T>(wv[q], x2);
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int q = 0; q < RI; q++) d[q] += __shfl_xor_sync(0xffffffffu, d[q], o);
       if (lane == 0) {
 #pragma unroll
         for (int q = 0; q < RI; q++) {
