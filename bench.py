@@ -168,13 +168,15 @@ def cpu_threads():
 
 def cpu_sample(path, prompt, decode_steps, threads, acts_q8=False):
     """The oracle on the host cores: prefill the prompt, then `decode_steps` timed
-    decode tokens. Returns (tok/s over the decode steps, ids)."""
+    decode tokens. Returns (tok/s over the decode steps, ids, top-2 logit margin of
+    every step)."""
     from oracle import oracle as O
     m = O.Model(path, acts_q8=acts_q8)
-    ids, ms, _ = m.generate(prompt, decode_steps + 1, nthreads=threads)
+    ids, ms, logits = m.generate(prompt, decode_steps + 1, nthreads=threads, want_logits=True)
     m.close()
+    margins = np.diff(np.sort(logits, axis=1)[:, -2:], axis=1)[:, 0]
     dec = ms[1:]
-    return float(len(dec) / (dec.sum() / 1e3)), ids
+    return float(len(dec) / (dec.sum() / 1e3)), ids, margins
 
 
 def cpu_model():
@@ -646,7 +648,7 @@ def run_ours(args):
         th = cpu_threads()
         cplen = plen if spec != "8b" else 8  # 8B on the CPU: a short prompt keeps the sample bounded
         n_cpu = args.cpu_decode_steps if spec != "8b" else 8
-        tps, cpu_ids = cpu_sample(path, prompt[:cplen], n_cpu, th, acts_q8=args.acts == "q8")
+        tps, cpu_ids, margins = cpu_sample(path, prompt[:cplen], n_cpu, th, acts_q8=args.acts == "q8")
         cpu = {"value": tps, "unit": "tok/s", "cores": th, "kind": "port", "cpu_model": cpu_model(),
                "simd": "scalar fallback (x86), compiler autovectorised",
                "sample": f"{cplen}-token prompt prefill untimed, then {n_cpu} timed decode tokens "
@@ -654,7 +656,14 @@ def run_ours(args):
                          f"{th} threads)"}
         if cplen == plen:
             n = min(len(cpu_ids), len(gpu_ids))
-            parity = {"ids_equal": bool(np.array_equal(cpu_ids[:n], gpu_ids[:n])), "n": int(n),
+            rule = "identical ids at every step"
+            if args.acts == "q8":
+                # W8A8: a last-bit difference upstream of the activation quantizer can move
+                # an int8 step, so ids are compared up to the first step whose oracle top-2
+                # margin is within 2 x 1e-2 (the logit tolerance); the runs may diverge there
+                n = min(n, next((i for i, mg in enumerate(margins) if mg <= 2e-2), n))
+                rule = "identical ids up to the first step with oracle top-2 margin <= 2e-2 (W8A8)"
+            parity = {"ids_equal": bool(np.array_equal(cpu_ids[:n], gpu_ids[:n])), "n": int(n), "rule": rule,
                       "e2e_ids_equal": e2e_same, "against": "oracle ids on the same GGUF and prompt"}
     if parity is None:
         want = golden_ids({"1b-q8_0": "cfg1_1b_q8_0"}.get(args.workload, "")) if args.acts == "f32" else None
