@@ -448,12 +448,14 @@ def nccl_allreduce_us(world, n_calls=64, floats=4096, reps=20):
     return float(t.item())
 
 
-def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3, mode="peer"):
+def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3, mode="kernel"):
     """Config 5: the 8B Q8_0 model (128-token prompt) sharded over all ranks (tensor
     parallel, all-reduce after the O and down projections; TP1 on one GPU), `steps`
     greedy decode tokens chained on the device, CUDA events on each rank's context
-    stream, max over ranks. mode "peer": the decode row's all-reduces on the one-shot
-    NVLink peer-memory kernel (the default); "nccl": on NCCL (SQB200_TP_ALLREDUCE).
+    stream, max over ranks. mode "kernel": the persistent decode kernel, the ranks'
+    partial sums exchanged through peer memory inside it (the default); "peer": the
+    op-level step with the one-shot NVLink peer-memory all-reduce kernel; "nccl": the
+    op-level step with NCCL's all-reduce.
     Ids of the group are checked against the oracle's ids of the same model
     (tests/golden/cfg5_8b_q8_0.npz has a 16-token prompt, so the check decodes that
     prompt first)."""
@@ -463,10 +465,13 @@ def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3, mode="peer"):
     if dist:
         dist.barrier()
     path = G.ensure_gguf("8b", "q8_0")
+    # read when the model / context is created
+    os.environ.pop("SQB200_TP_ALLREDUCE", None)
+    os.environ.pop("SQB200_TP_DECODE", None)
+    if mode != "kernel":
+        os.environ["SQB200_TP_DECODE"] = "op"
     if mode == "nccl":
-        os.environ["SQB200_TP_ALLREDUCE"] = "nccl"  # read when the model is created
-    else:
-        os.environ.pop("SQB200_TP_ALLREDUCE", None)
+        os.environ["SQB200_TP_ALLREDUCE"] = "nccl"
     nccl_id = None
     if world > 1:
         from sqb200 import tp as sqtp
@@ -517,13 +522,16 @@ def run_tp(lib, G, rank, world, local, dist, steps=64, warmup=3, mode="peer"):
     ctx.close()
     model.close()
     os.environ.pop("SQB200_TP_ALLREDUCE", None)
+    os.environ.pop("SQB200_TP_DECODE", None)
     ar_us = nccl_allreduce_us(world) if dist and mode == "nccl" else None
     peak, kind = peaks()
     algo = bytes_per_step(cfg, cfg.weight_type, kv0 + (steps - 1) / 2)  # the whole model's bytes
     per_rank = algo / world / (ms / steps / 1e3) / 1e9
     return {"workload": f"8b-q8_0, 128-token prompt, tp{world}", "tp": world,
-            "allreduce": ("peer-memory one-shot kernel (NVLink stores, fused residual add)" if mode == "peer"
-                          else "NCCL") if world > 1 else "none (one GPU)",
+            "allreduce": {"kernel": "inside the persistent decode kernel (partials stored into every rank's "
+                                    "mailbox over NVLink, summed per row in rank order)",
+                          "peer": "op-level step, one-shot peer-memory all-reduce kernel (fused residual add)",
+                          "nccl": "op-level step, NCCL all-reduce"}[mode] if world > 1 else "none (one GPU)",
             "tok_s": steps / (ms / 1e3),
             "ms_per_token": ms / steps, "launches_per_token": lpt,
             "per_rank_gb_s": per_rank, "frac": per_rank / peak, "peak_gb_s": peak, "peak_source": kind,
@@ -681,8 +689,9 @@ def run_ours(args):
     tp_line = None
     if not args.no_extra and not tp:
         tp_line = run_tp(lib, G, rank, world, local, dist)
-        if world > 1:  # the same step with NCCL's all-reduce, for comparison
-            tp_line["nccl"] = run_tp(lib, G, rank, world, local, dist, mode="nccl")
+        if world > 1:  # the op-level step with each all-reduce, for comparison
+            tp_line["op_peer"] = run_tp(lib, G, rank, world, local, dist, mode="peer")
+            tp_line["op_nccl"] = run_tp(lib, G, rank, world, local, dist, mode="nccl")
     if rank == 0:
         conf = workload_config(args, world)
         line = {
@@ -714,7 +723,8 @@ def run_ours(args):
         dist.destroy_process_group()
     bad = [k for k, v in (("decode", parity), ("long_context", long_ctx and long_ctx["parity"]),
                           ("tp", tp_line and tp_line["parity"]),
-                          ("tp nccl", tp_line and tp_line.get("nccl") and tp_line["nccl"]["parity"]))
+                          ("tp op_peer", tp_line and tp_line.get("op_peer") and tp_line["op_peer"]["parity"]),
+                          ("tp op_nccl", tp_line and tp_line.get("op_nccl") and tp_line["op_nccl"]["parity"]))
            if v is not None and not v["ids_equal"]]
     if bad:
         print(f"parity failure: GPU greedy ids differ from the oracle's in {', '.join(bad)}", file=sys.stderr)

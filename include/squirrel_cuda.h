@@ -199,19 +199,22 @@ int sq_decode_steps(sq_ctx *c, int n_steps, uint32_t *out_ids);
  * sq_ctx_logits, sq_tp_recover are collective); each rank's result is the whole
  * model's. Rank 0 makes the id with sq_nccl_unique_id and shares its bytes with
  * the other ranks (e.g. over torch.distributed). NCCL is loaded at first use.
- * The all-reduces of a decode row run on a one-shot kernel over NVLink peer memory
- * (each rank stores its partial into every rank's mailbox, then sums them in rank
- * order with the residual add); prefill rows, and groups whose GPUs cannot map each
- * other's memory, use NCCL's. SQB200_TP_ALLREDUCE=nccl, set when the model is
- * created, selects NCCL's for decode rows too. Contexts of one tensor-parallel
- * model must not run concurrently. */
+ * Decode rows run on the persistent decode kernel, one launch a token on every rank:
+ * the O and down projections store their partial sums into every rank's mailbox
+ * (NVLink peer memory, plain stores) and each CTA sums its own hidden rows over the
+ * ranks in rank order with the residual add; the greedy argmax folds the ranks'
+ * states the same way. SQB200_TP_DECODE=op (read when a context is created) runs
+ * the op-level step instead, whose all-reduces use a one-shot peer-memory kernel,
+ * or NCCL's with SQB200_TP_ALLREDUCE=nccl (read when the model is created). Prefill
+ * rows, and groups whose GPUs cannot map each other's memory, use NCCL's.
+ * Contexts of one tensor-parallel model must not run concurrently. */
 /* ncclGetUniqueId into out (n >= 128 bytes). */
 int sq_nccl_unique_id(void *out, size_t n);
 /* After SQ_ERR_TIMEOUT on any rank (a peer's partial sum did not arrive in time,
  * e.g. because a rank stopped issuing steps), the ranks' all-reduce sequence
  * numbers may differ. Once every rank has stopped issuing work, every rank calls
- * this (collective, over NCCL): it clears the peer-memory all-reduce's mailboxes,
- * sequence numbers and error word. Contexts must then be reset (sq_ctx_reset):
+ * this (collective, over NCCL): it clears the mailboxes (the all-reduce's and the
+ * decode kernel's exchange words), sequence numbers and error word. Contexts must then be reset (sq_ctx_reset):
  * their KV cache past the last good position is undefined. SQ_OK without effect for
  * a model on one GPU or one on NCCL's all-reduce. */
 int sq_tp_recover(sq_model *m);

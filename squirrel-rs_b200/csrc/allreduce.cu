@@ -57,7 +57,21 @@ struct TpAllReduce {
   // created): the k-th all-reduce this rank launches (or captures) stores its partial
   // but not its flags, so the other ranks' waits for it expire. 0 = off.
   unsigned withhold = 0, launches = 0;
+  // the persistent decode kernel's exchange area in every rank's mailbox (after the
+  // all-reduce's data and flags): [2][world][E] tagged words for the O / down
+  // partials, then [world][3] for the ranks' argmax states
+  std::vector<unsigned long long *> dec_box;
+  size_t bytes = 0;
 };
+
+// Bytes of a mailbox: the all-reduce's data and flags, then the decode kernel's area.
+static size_t mailbox_bytes(int world, int E, int nb, size_t *data_b, size_t *flag_b, size_t *dec_b) {
+  auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  *data_b = al((size_t)2 * world * E * sizeof(float));
+  *flag_b = al((size_t)2 * world * nb * sizeof(unsigned));
+  *dec_b = al(((size_t)2 * world * E + (size_t)world * 3) * sizeof(unsigned long long));
+  return *data_b + *flag_b + *dec_b;
+}
 
 namespace {
 
@@ -147,9 +161,9 @@ int tp_allreduce_create(sq_model *m) {
   ar->E = E;
   ar->nb = E >= 4096 ? 8 : E / 512;
   if (const char *v = getenv("SQ_TEST_WITHHOLD_PARTIAL")) ar->withhold = (unsigned)strtoul(v, nullptr, 10);
-  const size_t data_b = align256((size_t)2 * world * E * sizeof(float));
-  const size_t flag_b = align256((size_t)2 * world * ar->nb * sizeof(unsigned));
-  const size_t bytes = data_b + flag_b;
+  size_t data_b = 0, flag_b = 0, dec_b = 0;
+  const size_t bytes = mailbox_bytes(world, E, ar->nb, &data_b, &flag_b, &dec_b);
+  ar->bytes = bytes;
   int ok = 1;
   std::string why;
   cudaIpcMemHandle_t mine{};
@@ -223,6 +237,7 @@ int tp_allreduce_create(sq_model *m) {
   for (int r = 0; r < world; r++) {
     data[r] = (float *)ar->mapped[r];
     flags[r] = (unsigned *)((uint8_t *)ar->mapped[r] + data_b);
+    ar->dec_box.push_back((unsigned long long *)((uint8_t *)ar->mapped[r] + data_b + flag_b));
   }
   if (cudaMalloc((void **)&ar->d_data, world * sizeof(float *)) != cudaSuccess ||
       cudaMalloc((void **)&ar->d_flags, world * sizeof(unsigned *)) != cudaSuccess ||
@@ -266,9 +281,7 @@ int tp_allreduce_recover(sq_model *m) {
   SQ_CUDA(cudaMalloc((void **)&d, sizeof(int)));
   int st = nccl_all_reduce_min_int(m->nccl, d, 0);
   cudaError_t e = st ? cudaSuccess : cudaStreamSynchronize(0);
-  const size_t data_b = align256((size_t)2 * ar->world * ar->E * sizeof(float));
-  const size_t flag_b = align256((size_t)2 * ar->world * ar->nb * sizeof(unsigned));
-  if (!st && e == cudaSuccess) e = cudaMemset(ar->local, 0, data_b + flag_b);
+  if (!st && e == cudaSuccess) e = cudaMemset(ar->local, 0, ar->bytes);
   if (!st && e == cudaSuccess) e = cudaMemset(ar->epoch, 0, align256(ar->nb * sizeof(unsigned)) + 256);
   if (!st && e == cudaSuccess) e = cudaDeviceSynchronize();
   if (!st && e == cudaSuccess) st = nccl_all_reduce_min_int(m->nccl, d, 0);
@@ -279,6 +292,12 @@ int tp_allreduce_recover(sq_model *m) {
 }
 
 unsigned *tp_allreduce_err_ptr(const TpAllReduce *ar) { return ar ? ar->err : nullptr; }
+
+int tp_decode_boxes(const TpAllReduce *ar, unsigned long long **boxes, int max) {
+  if (!ar || (int)ar->dec_box.size() != ar->world || ar->world > max) return 0;
+  for (int r = 0; r < ar->world; r++) boxes[r] = ar->dec_box[r];
+  return ar->world;
+}
 
 unsigned tp_allreduce_status(const TpAllReduce *ar, bool clear) {
   if (!ar) return 0;

@@ -25,6 +25,7 @@
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <string>
@@ -95,9 +96,21 @@ struct Params {  // passed by value to the decode kernel: at most the 32 KB of k
   int max_tiles;
   // Failure-detection tests only (SQ_TEST_DROP_EXCHANGE=n, read when the context is
   // created): in the context's n-th launch the producer of residual word 0 after
-  // layer 0's O projection does not write it, so the gate/up stage's bounded poll
-  // expires and the kernel reports a timeout. 0 = off.
+  // layer 0's O projection (under tensor parallelism: of this rank's partial of that
+  // row) does not write it, so a bounded poll for it expires and the kernel reports
+  // a timeout. 0 = off.
   unsigned drop_tag;
+  // Tensor parallel (tp_world > 1): this rank's shard of the model (local heads, FFN
+  // rows, vocabulary rows; full hidden size). The O and down projections leave
+  // partial sums of every hidden row: a producer stores them, tagged, into row block
+  // [kind][tp_rank] of every rank's exchange area (tp_box[r], peer memory mapped
+  // with CUDA IPC; plain stores, no bulk or TMA access), and after the stage each
+  // CTA sums its own rows over the ranks in rank order, adds the residual and
+  // publishes the result locally, where the next stage's staging reads it. The
+  // greedy argmax folds the ranks' states (area [2][world][E] onwards) in rank
+  // order, which is vocabulary order. tp_box[] is in rank order.
+  int tp_world, tp_rank, vocab_local;
+  unsigned long long *tp_box[8];
   LayerW layers[MAX_LAYERS];
 };
 static_assert(sizeof(Params) + 64 <= 32764, "Params fits the kernel parameter space");
@@ -355,7 +368,7 @@ enum { XS_PLAIN = 0, XS_NORM = 1, XS_EMBED = 2 };
 // every one carries the tag it expects, so receiving the data is the
 // synchronization — no grid barrier, no flag round trip. Tags are
 // launch << 10 | layer << 3 | kind (kind below), so a stale word never matches.
-enum { TG_EMBED = 0, TG_QKV = 1, TG_ATTN = 2, TG_POST_O = 3, TG_ACT = 4, TG_POST_DOWN = 5 };
+enum { TG_EMBED = 0, TG_QKV = 1, TG_ATTN = 2, TG_POST_O = 3, TG_ACT = 4, TG_POST_DOWN = 5, TG_ARG = 6 };
 __host__ __device__ __forceinline__ unsigned mk_tag(unsigned launch, int l, int kind) {
   return (launch << 10) | ((unsigned)l << 3) | (unsigned)kind;
 }
@@ -366,6 +379,17 @@ __device__ __forceinline__ void st_ll(unsigned long long *a, float v, unsigned t
 __device__ __forceinline__ unsigned long long ld_ll(const unsigned long long *a) {
   unsigned long long v;
   asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(a));
+  return v;
+}
+// Tensor-parallel exchange words: stored by any rank (peer memory over NVLink) and
+// read by the owner, so both sides use system scope.
+__device__ __forceinline__ void st_ll_sys(unsigned long long *a, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll_sys(const unsigned long long *a) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
 __device__ __forceinline__ ulonglong2 ld_ll2(const unsigned long long *a) {  // two words, 16-byte aligned
@@ -410,12 +434,12 @@ __device__ __forceinline__ float poll_ll(const Params &p, const unsigned long lo
 }
 // N words at once: every stale word is re-read in the same pass, so a retry costs
 // one L2 round trip however many words are still missing.
-template <int N>
+template <int N, bool SYS = false>
 __device__ __forceinline__ void poll_ll_n(const Params &p, const unsigned long long *const (&a)[N], unsigned tag,
                                           float (&out)[N]) {
   unsigned long long w[N];
 #pragma unroll
-  for (int i = 0; i < N; i++) w[i] = ld_ll(a[i]);
+  for (int i = 0; i < N; i++) w[i] = SYS ? ld_ll_sys(a[i]) : ld_ll(a[i]);
   const long long t0 = clock64();
   for (unsigned it = 0;; it++) {
     bool all = true;
@@ -424,7 +448,7 @@ __device__ __forceinline__ void poll_ll_n(const Params &p, const unsigned long l
     if (all) break;
 #pragma unroll
     for (int i = 0; i < N; i++)
-      if (!ll_ok(w[i], tag)) w[i] = ld_ll(a[i]);
+      if (!ll_ok(w[i], tag)) w[i] = SYS ? ld_ll_sys(a[i]) : ld_ll(a[i]);
     if ((it & 15u) == 15u && poll_expired(p, t0)) break;
   }
 #pragma unroll
@@ -707,6 +731,14 @@ __device__ __forceinline__ void finish_rows(const Params &p, Smem &sm, int kind,
         st_ll(p.kv_ll + p.KVd + vr + 1, vb, tag);
       }
     }
+  } else if ((kind == ST_O || kind == ST_DOWN) && p.tp_world > 1) {  // a row-parallel partial, to every rank
+    if (lane == 0) {
+      const size_t off = ((size_t)(kind == ST_DOWN) * p.tp_world + p.tp_rank) * p.E;
+      for (int d = 0; d < p.tp_world; d++) {
+        if (a != 0 || tag != p.drop_tag) st_ll_sys(p.tp_box[d] + off + a, va, tag);
+        if (hasb) st_ll_sys(p.tp_box[d] + off + b, vb, tag);
+      }
+    }
   } else if (kind == ST_O || kind == ST_DOWN) {  // residual (elementwise_add.rs:47-61)
     const float ha = __shfl_sync(FULL, sr.hres, (a - r0) & 31);
     const float hb = __shfl_sync(FULL, sr.hres, (b - r0) & 31);
@@ -870,6 +902,30 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
     tile_ctr++;
   }
   stamp(p, 8 * stage_id + 6);
+}
+
+// Tensor parallel: after this CTA's O (or down) stage, its hidden rows summed over the
+// ranks' partials in rank order (layers.rs:57 / :76 row-parallel sums), plus the
+// residual (layers.rs:96 / :106), published locally for the next stage's staging.
+// One warp; lane i takes row r0 + i (a CTA owns at most 32 rows).
+__device__ __forceinline__ void tp_reduce_rows(const Params &p, int kind, int l, const StageRegs &sr, unsigned tag) {
+  const int lane = threadIdx.x & 31;
+  int r0, r1;
+  stage_rows(p, kind, l, blockIdx.x, r0, r1);
+  if (r1 <= r0) return;
+  const int a = r0 + lane;
+  const bool mine = lane < r1 - r0;
+  const unsigned long long *box = p.tp_box[p.tp_rank] + (size_t)(kind == ST_O ? 0 : 1) * p.tp_world * p.E;
+  const unsigned long long *w[8];
+#pragma unroll
+  for (int r = 0; r < 8; r++) w[r] = box + (size_t)(r < p.tp_world ? r : 0) * p.E + (mine ? a : r0);
+  float v[8];
+  poll_ll_n<8, true>(p, w, tag, v);
+  float sum = v[0];
+#pragma unroll
+  for (int r = 1; r < 8; r++)
+    if (r < p.tp_world) sum += v[r];
+  if (mine) st_ll(p.hid_ll + a, __fadd_rn(sr.hres, sum), tag);
 }
 
 // Causal GQA attention for one token at position pos (attention.rs:11-70), reading
@@ -1286,6 +1342,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     stamp(p, 8 * stage_id + 2);
     matvec_stage<T>(p, rg, sm, tbl, kind, l, x, osc, slot, phase, tile_ctr, pos, sr, tag_out);
+    if (p.tp_world > 1 && warp == 0 && (kind == ST_O || kind == (p.split ? ST_DOWN2 : ST_DOWN)))
+      tp_reduce_rows(p, kind == ST_O ? ST_O : ST_DOWN, l, sr, tag_out);
     if (kind == ST_QKV) {
       // ---- attention (waits on q / K / V words, not on a barrier)
       cta_sync();  // shared scratch of the staging buffer is reused below
@@ -1331,6 +1389,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if ((lane & (2 * o - 1)) == 0) mine = arg_combine(mine, r);
         }
         if (lane == 0) acc = arg_combine(acc, mine);
+      }
+      if (p.tp_world > 1) {  // this rank's state to every rank, then all ranks' states in rank order
+        acc.v = __shfl_sync(FULL, acc.v, 0);
+        acc.best = __shfl_sync(FULL, acc.best, 0);
+        acc.nan = __shfl_sync(FULL, acc.nan, 0);
+        const unsigned tag = mk_tag(launch, p.L, TG_ARG);
+        const size_t off = (size_t)2 * p.tp_world * p.E + (size_t)p.tp_rank * 3;
+        if (lane < p.tp_world) {
+          unsigned long long *d = p.tp_box[lane] + off;
+          st_ll_sys(d, acc.v, tag);
+          st_ll_sys(d + 1, __int_as_float((int)acc.best), tag);
+          st_ll_sys(d + 2, __int_as_float((int)acc.nan), tag);
+        }
+        ArgState all = arg_empty();
+        if (lane == 0) {
+          const unsigned long long *src = p.tp_box[p.tp_rank] + (size_t)2 * p.tp_world * p.E;
+          for (int r = 0; r < p.tp_world; r++) {
+            const unsigned long long *w3[3] = {src + r * 3, src + r * 3 + 1, src + r * 3 + 2};
+            float v3[3];
+            poll_ll_n<3, true>(p, w3, tag, v3);
+            const long long base = (long long)r * p.vocab_local;
+            const int best = __float_as_int(v3[1]), nan = __float_as_int(v3[2]);
+            ArgState st = {v3[0], best >= 0 ? base + best : -1, nan >= 0 ? base + nan : -1};
+            all = arg_combine(all, st);
+          }
+        }
+        acc = all;
       }
       if (lane == 0) {
         const long long id = arg_result(acc);
@@ -1421,11 +1506,18 @@ static int nseg_for(int in_dim) {
 
 int decode_prepare(sq_ctx *c) {
   const sq_model *m = c->m;
-  const sq_llama_config &cf = m->cfg;
+  const sq_llama_config &cf = m->lc;  // this rank's shard (the whole model on one GPU)
   auto *st = new DecodeState();
   c->dec = st;
   if (getenv("SQ_DISABLE_DECODE_KERNEL")) return SQ_OK;
-  if (m->tp_size > 1) return SQ_OK;  // tensor-parallel contexts run the op-level sequence with NCCL
+  unsigned long long *boxes[8] = {};
+  int tp_world = 1;
+  if (m->tp_size > 1) {  // tensor parallel: the kernel exchanges partial sums through the peer mailboxes
+    if (const char *v = getenv("SQB200_TP_DECODE"))
+      if (strcmp(v, "op") == 0) return SQ_OK;  // the op-level step with its all-reduce kernels (A/B)
+    tp_world = tp_decode_boxes(m->ar, boxes, 8);
+    if (tp_world != m->tp_size) return SQ_OK;  // no peer mailboxes: the op-level step serves this model
+  }
   const int E = cf.embed_dim, Q = cf.n_heads * cf.head_dim, KVd = cf.n_kv_heads * cf.head_dim, F = cf.ffn_dim;
   const int wt = cf.weight_type, bb = block_bytes(wt);
   // supported shapes: same type everywhere, rows multiple of 16 bytes, <= 8 segments, GQA group 4
@@ -1479,6 +1571,10 @@ int decode_prepare(sq_ctx *c) {
   if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
   else if (wt == SQ_Q4_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q4_0, 2>() : pick_kernel<SQ_Q4_0, 4>();
   else kern = cf.head_dim == 64 ? pick_kernel<SQ_BF16, 2>() : pick_kernel<SQ_BF16, 4>();
+  h.tp_world = tp_world;
+  h.tp_rank = m->tp_rank;
+  h.vocab_local = cf.vocab_size;
+  for (int r = 0; r < tp_world && r < 8; r++) h.tp_box[r] = boxes[r];
   h.L = cf.n_blocks;
   h.E = E;
   h.Q = Q;

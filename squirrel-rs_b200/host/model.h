@@ -33,6 +33,9 @@ void tp_allreduce_release(TpAllReduce *ar);
 cudaError_t launch_allreduce_add(cudaStream_t s, TpAllReduce *ar, float *hidden, const float *part, bool pdl);
 unsigned tp_allreduce_status(const TpAllReduce *ar, bool clear);
 unsigned *tp_allreduce_err_ptr(const TpAllReduce *ar);
+// The persistent decode kernel's exchange area of every rank's mailbox (this process's
+// mappings, rank order); returns the number of ranks (0: none).
+int tp_decode_boxes(const TpAllReduce *ar, unsigned long long **boxes, int max);
 int tp_allreduce_recover(sq_model *m);  // collective re-synchronization after a timeout
 }  // namespace sq
 

@@ -46,16 +46,20 @@ def test_decode_wait_expires_reports_timeout_and_context_recovers(gpu_lib, monke
         m.close()
 
 
-def _fault_rank(rank, path, prompt, ids, qin, qout):
-    """Rank 1's third peer all-reduce stores its partial but withholds its flags
-    (SQ_TEST_WITHHOLD_PARTIAL=3, read when its model is created), so rank 0's wait
-    for it expires and rank 0 reports Timeout (rank 1, which ran ahead meanwhile,
-    may see its next wait expire too); both ranks run the whole step (its NCCL calls
-    included), then re-synchronize (sq_tp_recover), reset their contexts and decode
-    the oracle's ids again."""
+def _fault_rank(rank, path, prompt, ids, mode, qin, qout):
+    """Rank 1 leaves one exchange unwritten in its first decode steps: on the
+    persistent kernel ("kernel") its partial of hidden row 0 after layer 0's O
+    projection in its third launch (SQ_TEST_DROP_EXCHANGE=3), on the op-level step
+    ("op") the flags of its third peer all-reduce (SQ_TEST_WITHHOLD_PARTIAL=3). A
+    bounded wait on rank 0 expires and reports Timeout (rank 1's may too: it waits
+    for its own word, or ran ahead while rank 0 waited); both ranks run the whole
+    step, then re-synchronize (sq_tp_recover), reset their contexts and decode the
+    oracle's ids again."""
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    if rank == 1:
-        os.environ["SQ_TEST_WITHHOLD_PARTIAL"] = "3"
+    if mode == "op":
+        os.environ["SQB200_TP_DECODE"] = "op"
+        if rank == 1:
+            os.environ["SQ_TEST_WITHHOLD_PARTIAL"] = "3"
     from sqb200 import lib
     out = {"rank": rank}
     try:
@@ -65,11 +69,15 @@ def _fault_rank(rank, path, prompt, ids, qin, qout):
         else:
             uid = qout.get(timeout=120)
         m = lib.Model(path, device=rank, tp_rank=rank, tp_size=2, nccl_id=uid)
+        if mode == "kernel" and rank == 1:
+            os.environ["SQ_TEST_DROP_EXCHANGE"] = "3"  # read when the context is created
         ctx = m.new_context(64)
+        os.environ.pop("SQ_TEST_DROP_EXCHANGE", None)
+        out["launches_per_token"] = ctx.launches_per_token
         out["first"] = int(ctx.forward(prompt))  # prefill: NCCL's all-reduces
         t0 = time.monotonic()
         try:
-            ctx.decode_steps(2)  # decode rows: the peer all-reduces 1..2 per layer
+            ctx.decode_steps(4)  # decode rows
             out["fault"] = "none"
         except lib.KernelError as e:
             out["fault"] = e.kind
@@ -84,7 +92,8 @@ def _fault_rank(rank, path, prompt, ids, qin, qout):
         qin.put(("err", {"rank": rank, "error": repr(e)}))
 
 
-def test_tp_allreduce_wait_expires_reports_timeout_and_group_recovers():
+@pytest.mark.parametrize("mode", ["kernel", "op"])
+def test_tp_exchange_wait_expires_reports_timeout_and_group_recovers(mode):
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -95,7 +104,7 @@ def test_tp_allreduce_wait_expires_reports_timeout_and_group_recovers():
     path = G.ensure_gguf("small", "q8_0")
     ctx = mp.get_context("spawn")
     qin, qout = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_fault_rank, args=(r, path, prompt, ids, qin, qout)) for r in range(2)]
+    procs = [ctx.Process(target=_fault_rank, args=(r, path, prompt, ids, mode, qin, qout)) for r in range(2)]
     for p in procs:
         p.start()
     results = []
@@ -114,7 +123,9 @@ def test_tp_allreduce_wait_expires_reports_timeout_and_group_recovers():
     errs = [v for k, v in results if k != "ok"]
     assert not errs, errs
     by_rank = {v["rank"]: v for _, v in results}
-    assert by_rank[0]["fault"] == "Timeout", by_rank[0]  # waited for rank 1's withheld flags
+    for v in by_rank.values():  # which decode path ran
+        assert (v["launches_per_token"] == 1) == (mode == "kernel"), v
+    assert by_rank[0]["fault"] == "Timeout", by_rank[0]  # waited for rank 1's missing word
     # rank 1 ran ahead while rank 0 waited, so its next wait may expire as well
     assert by_rank[1]["fault"] in ("none", "Timeout"), by_rank[1]
     assert by_rank[0]["fault_s"] < 60 and by_rank[1]["fault_s"] < 60

@@ -1,8 +1,10 @@
 """Tensor parallel on 2, 4 and 8 GPUs (one process per GPU): the sharded model's
 greedy ids equal the single-GPU model's and the CPU oracle's, and its gathered
-logits stay within the model tests' tolerance. The row-parallel sums of a decode
-row run either on the one-shot peer-memory all-reduce (the default) or on NCCL's
-(SQB200_TP_ALLREDUCE=nccl, read when the model is created); both are checked.
+logits stay within the model tests' tolerance. Decode rows run on the persistent
+kernel with the ranks' partial sums exchanged through peer memory ("kernel", the
+default; shapes the kernel does not serve fall back to the op-level step), or on
+the op-level step (SQB200_TP_DECODE=op) with the one-shot peer-memory all-reduce
+("peer") or NCCL's (SQB200_TP_ALLREDUCE=nccl, "nccl"); all three are checked.
 Sizes with more GPUs than the box has are skipped.
 
   small (2 kv heads): TP 2 against one GPU and the oracle, Q8_0 and BF16
@@ -31,8 +33,10 @@ def assert_logits_close(got, want):
     assert err / float(np.max(np.abs(want))) <= REL_TOL, err
 
 
-def _tp_rank(rank, size, path, prompt, steps, mode, qin, qout):
+def _tp_rank(rank, size, path, prompt, steps, mode, on_kernel, qin, qout):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if mode != "kernel":
+        os.environ["SQB200_TP_DECODE"] = "op"
     if mode == "nccl":
         os.environ["SQB200_TP_ALLREDUCE"] = "nccl"
     from sqb200 import lib
@@ -44,6 +48,9 @@ def _tp_rank(rank, size, path, prompt, steps, mode, qin, qout):
             uid = qout.get(timeout=120)
         m = lib.Model(path, device=rank, tp_rank=rank, tp_size=size, nccl_id=uid)
         ctx = m.new_context(len(prompt) + steps + 4)
+        # which decode path ran: the persistent kernel in "kernel" mode wherever it
+        # serves the shard's shape, the op-level step otherwise
+        assert (ctx.launches_per_token == 1) == (mode == "kernel" and on_kernel), ctx.launches_per_token
         first = ctx.forward(prompt)
         first_logits = ctx.logits()  # collective: every rank gathers the vocabulary shards
         ids = [int(first)] + [int(i) for i in ctx.decode_steps(steps)]
@@ -55,11 +62,11 @@ def _tp_rank(rank, size, path, prompt, steps, mode, qin, qout):
         qin.put(("err", rank, repr(e), None))
 
 
-def run_tp(size, path, prompt, steps, mode):
+def run_tp(size, path, prompt, steps, mode, on_kernel=True):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     qin, qout = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, size, path, prompt, steps, mode, qin, qout)) for r in range(size)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, size, path, prompt, steps, mode, on_kernel, qin, qout)) for r in range(size)]
     for p in procs:
         p.start()
     results = []
@@ -87,7 +94,7 @@ def need_gpus(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("mode", ["kernel", "peer", "nccl"])
 @pytest.mark.parametrize("wt", ["q8_0", "bf16"])
 def test_tp2_matches_single_gpu_and_oracle(wt, mode):
     need_gpus(2)
@@ -98,6 +105,10 @@ def test_tp2_matches_single_gpu_and_oracle(wt, mode):
     steps = 10
     single = lib.Model(path, device=0)
     sctx = single.new_context(len(prompt) + steps + 4)
+    # the persistent kernel takes BF16 rows in whole 2048-element segments: the small
+    # BF16 shape runs the op-level step on one GPU and on two
+    on_kernel = sctx.launches_per_token == 1
+    assert on_kernel == (wt == "q8_0"), sctx.launches_per_token
     s_first = sctx.forward(prompt)
     s_logits = sctx.logits()
     s_ids = [int(s_first)] + [int(i) for i in sctx.decode_steps(steps)]
@@ -106,13 +117,13 @@ def test_tp2_matches_single_gpu_and_oracle(wt, mode):
     om = O.Model(path)
     o_ids, _, _ = om.generate(prompt, steps + 1)
     om.close()
-    ids, (first_logits, _) = run_tp(2, path, prompt, steps, mode)
+    ids, (first_logits, _) = run_tp(2, path, prompt, steps, mode, on_kernel)
     assert ids == s_ids, (ids, s_ids)
     assert ids == [int(i) for i in o_ids], (ids, list(o_ids))
     assert_logits_close(first_logits, s_logits)
 
 
-@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("mode", ["kernel", "peer", "nccl"])
 @pytest.mark.parametrize("size", [2, 4, 8])
 def test_tp_8b_matches_oracle(size, mode):
     need_gpus(size)
