@@ -343,7 +343,7 @@ struct AttScratch {
 struct Smem {
   float red[2 * NGRP][MAX_TILE_ITEMS];  // segment partial sums: two buffers per warp group
   union {
-    float xs[MAX_X];  // the stage input, lane-interleaved (see xs_index)
+    float xs[MAX_X / 2048 * 2176];  // the stage input, lane-interleaved (see xs_index)
     AttScratch at;    // attention-stage partials (a different phase of the layer)
   };
   float ssp[NC];      // per-warp partial squared sums of the RMS norm
@@ -459,12 +459,20 @@ __device__ __forceinline__ void poll_ll_n(const Params &p, const unsigned long l
 // Every CTA needs the whole input vector of a stage (all elements of the residual
 // for a norm, all of attn / act). Reading it once per CTA — not once per warp —
 // keeps the CTAs' simultaneous reads of the same few KB from piling up on a
-// handful of L2 slices. xs stores element e where lane `lane` of a warp reading
-// segment `seg` finds its register i with one conflict-free 16-byte load:
-// xs[seg*2048 + (i/4)*128 + lane*4 + i%4].
+// handful of L2 slices. The layout is the one the dot products read with
+// conflict-free 16-byte loads (lane `lane` of a warp on segment `seg`):
+//  Q8_0: [seg][k][lane] float4, k = 0..16 the step of quad_dot_xs (word k of the
+//        lane's block pair); the lane's element i sits at position i + 2 (i < 32)
+//        or i + 4 of its 68 floats, so step k's four inputs are one float4;
+//  BF16: [seg][i/4][lane] float4 for the lane's element i (quad_dot_xs reads two a
+//        step); Q4_0: the same, loaded once into registers (x_from_smem).
 template <int T>
 __device__ __forceinline__ int xs_index(int e) {
   const int seg = e >> 11, r = e & 2047;
+  if constexpr (T == SQ_Q8_0) {
+    const int ln = r >> 6, i = r & 63, pos = i < 32 ? i + 2 : i + 4;
+    return ((seg * 17 + (pos >> 2)) * 32 + ln) * 4 + (pos & 3);
+  }
   int lane, i;
   if constexpr (T == SQ_BF16) {
     lane = (r & 255) >> 3;
@@ -522,10 +530,18 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
         }
 #pragma unroll
         for (int k = 0; k < 8; k++) ss = fmaf(d[k], d[k], ss);
-        *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(e)]) =
-            make_float4(__fmul_rn(d[0], w0.x), __fmul_rn(d[1], w0.y), __fmul_rn(d[2], w0.z), __fmul_rn(d[3], w0.w));
-        *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(e + 4)]) =
-            make_float4(__fmul_rn(d[4], w1.x), __fmul_rn(d[5], w1.y), __fmul_rn(d[6], w1.z), __fmul_rn(d[7], w1.w));
+        if constexpr (T == SQ_Q8_0) {  // element pairs are contiguous in this layout, quads are not
+          const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int k = 0; k < 8; k += 2)
+            *reinterpret_cast<float2 *>(&sm.xs[xs_index<T>(e + k)]) =
+                make_float2(__fmul_rn(d[k], ww[k]), __fmul_rn(d[k + 1], ww[k + 1]));
+        } else {
+          *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(e)]) =
+              make_float4(__fmul_rn(d[0], w0.x), __fmul_rn(d[1], w0.y), __fmul_rn(d[2], w0.z), __fmul_rn(d[3], w0.w));
+          *reinterpret_cast<float4 *>(&sm.xs[xs_index<T>(e + 4)]) =
+              make_float4(__fmul_rn(d[4], w1.x), __fmul_rn(d[5], w1.y), __fmul_rn(d[6], w1.z), __fmul_rn(d[7], w1.w));
+        }
       }
     }
   } else {
@@ -598,24 +614,113 @@ __device__ __forceinline__ void x_from_smem(f2x (&x2)[32], const Smem &sm, int s
   }
 }
 
-// This warp's activation registers: the 64 f32 inputs its lane meets in every row,
-// as 32 packed pairs.
+// Q4_0 warps hold the 64 f32 inputs their lane meets in every row in registers, as
+// 32 packed pairs. Q8_0 and BF16 read them from the staging buffer in the dot loop
+// (quad_dot_xs): 64 registers fewer, which measured 5 % (1B) and 11 % (8B) faster
+// on Q8_0; the Q4_0 layout would need 2 KB more shared memory than the 8B shapes
+// have to spare.
 template <int T>
 struct ActRegs {
   f2x x[32];
 };
+template <>
+struct ActRegs<SQ_Q8_0> {};
+template <>
+struct ActRegs<SQ_BF16> {};
 
-// Stage a stage's input and load this warp's activation registers (the norm's 1/rms
-// already applied). Returns the factor the stage's dot products take (1 here).
+// Stage a stage's input and load this warp's activation registers, if it keeps
+// them (the norm's 1/rms applied there). Returns the factor the stage's dot
+// products take: 1, or the norm's 1/rms when the inputs stay in shared memory.
 template <int T, int MODE>
 __device__ __forceinline__ float stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
                                          unsigned tag, const float *w, int n, int nseg, int stamp_at,
                                          const uint8_t *emb_row = nullptr, bool write_hidden = false,
                                          unsigned emb_tag = 0u) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, stamp_at);
-  x_from_smem<T>(x.x, sm, (warp % NG) % nseg, lane, n, sc);
-  return 1.0f;
+  if constexpr (T == SQ_Q4_0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    x_from_smem<T>(x.x, sm, (warp % NG) % nseg, lane, n, sc);
+    return 1.0f;
+  } else {
+    (void)x;
+    (void)nseg;
+    return sc;
+  }
+}
+
+// Four rows of one lane's block pair (Q8_0) or eight 16-byte chunks (BF16) against
+// the inputs in the staging buffer: the arithmetic of quad_dot (dot_prod.rs:86-96,
+// 464-472), with each step's inputs fetched by one (Q8_0) or two (BF16) conflict-
+// free 16-byte loads that the four rows share.
+template <int T>
+__device__ __forceinline__ void quad_dot_xs(const uint32_t (&ra)[4], int seg, int lane, uint32_t xs, float (&out)[4]) {
+  if constexpr (T == SQ_Q8_0) {
+    const uint32_t off = (uint32_t)(seg * 32 + lane) * 68u;
+    const uint32_t xa = xs + (uint32_t)((seg * 17 * 32 + lane) * 16);
+    const f2x bias = pk2(-8388736.0f, -8388736.0f);  // 2^23 + 128: sign-flipped int8 under 2^23
+    f2x A[4], B[4];
+    float s0[4], s1[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) A[r] = B[r] = 0ull;
+#pragma unroll
+    for (int k = 0; k < 17; k++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
+      const uint4 xv = lds128(xa + (uint32_t)k * 512u);  // elements 4k-2 .. 4k+1 (block 0) / 4k-4 .. 4k-1
+      const f2x xlo = pk2u(xv.x, xv.y), xhi = pk2u(xv.z, xv.w);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t wx = w[r] ^ 0x80808080u;
+        const f2x lo = fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7540u), __byte_perm(wx, 0x4B000000u, 0x7541u)), bias);
+        const f2x hi = fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7542u), __byte_perm(wx, 0x4B000000u, 0x7543u)), bias);
+        if (k == 0) {  // scale of block 0, quants 0, 1
+          s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
+          A[r] = ffma2(xhi, hi, A[r]);
+        } else if (k < 8) {  // quants 4k-2 .. 4k+1 of block 0
+          A[r] = ffma2(xlo, lo, A[r]);
+          A[r] = ffma2(xhi, hi, A[r]);
+        } else if (k == 8) {  // quants 30, 31 of block 0, scale of block 1
+          A[r] = ffma2(xlo, lo, A[r]);
+          s1[r] = h2f((uint16_t)(w[r] >> 16));
+        } else {  // quants 4k-36 .. 4k-33 of block 1
+          B[r] = ffma2(xlo, lo, B[r]);
+          B[r] = ffma2(xhi, hi, B[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const float2 a = up2(A[r]), b = up2(B[r]);
+      out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
+    }
+  } else {
+    static_assert(T == SQ_BF16, "Q4_0 keeps its inputs in registers (quad_dot)");
+    const uint32_t xa = xs + (uint32_t)(seg * 2048 + lane * 4) * 4u;
+    f2x A[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) A[r] = 0ull;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      uint4 u[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) u[r] = lds128(ra[r] + (uint32_t)(seg * 2048 + k * 256 + lane * 8) * 2u);
+      const uint4 xa4 = lds128(xa + (uint32_t)(2 * k) * 512u), xb4 = lds128(xa + (uint32_t)(2 * k + 1) * 512u);
+      const f2x x0 = pk2u(xa4.x, xa4.y), x1 = pk2u(xa4.z, xa4.w), x2 = pk2u(xb4.x, xb4.y), x3 = pk2u(xb4.z, xb4.w);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        A[r] = ffma2(x0, pk2u(u[r].x << 16, u[r].x & 0xFFFF0000u), A[r]);
+        A[r] = ffma2(x1, pk2u(u[r].y << 16, u[r].y & 0xFFFF0000u), A[r]);
+        A[r] = ffma2(x2, pk2u(u[r].z << 16, u[r].z & 0xFFFF0000u), A[r]);
+        A[r] = ffma2(x3, pk2u(u[r].w << 16, u[r].w & 0xFFFF0000u), A[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const float2 a = up2(A[r]);
+      out[r] = a.x + a.y;
+    }
+  }
 }
 
 // The bulk copies of tile entry d: f(byte offset in the slot, global source, bytes).
@@ -829,7 +934,8 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
               const uint32_t ra[4] = {tile + (uint32_t)rw[0] * rb, tile + (uint32_t)(hasb ? rw[1] : rw[0]) * rb,
                                       tile + (uint32_t)(has2 ? rw[2] : rw[0]) * rb,
                                       tile + (uint32_t)(hasb2 ? rw[3] : rw[0]) * rb};
-              quad_dot<T>(ra, 0, lane, x.x, v);
+              if constexpr (T == SQ_Q4_0) quad_dot<T>(ra, 0, lane, x.x, v);
+              else quad_dot_xs<T>(ra, 0, lane, smem_u32(sm.xs), v);
             }
             warp_sum4(v);
             if (gu) {
@@ -850,7 +956,8 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
               uint32_t ra[4];
 #pragma unroll
               for (int q = 0; q < 4; q++) ra[q] = tile + (uint32_t)(i + q * rpw < rows ? i + q * rpw : i) * rb;
-              quad_dot<T>(ra, seg, lane, x.x, v);
+              if constexpr (T == SQ_Q4_0) quad_dot<T>(ra, seg, lane, x.x, v);
+              else quad_dot_xs<T>(ra, seg, lane, smem_u32(sm.xs), v);
             }
             warp_sum4(v);
             if (lane == 0) {

@@ -5,6 +5,7 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
         if (nseg > 1) finish(t - MV_NS);
         finished = t - MV_NS + 1;
       }
-      if (lane == 0) {
+      if (lane == 0 && t + 1 != a.test_skip) {  // a skipped tile's barrier never completes (tests)
         int mi, r0, rows;
         tile_of(t, mi, r0, rows);
         const unsigned bytes = (unsigned)(rows * rb);
@@ -816,6 +817,19 @@ bool matvec_fused_ok(const MvArgs &a, int wtype) {
   return true;
 }
 
+// Failure-detection tests only: SQ_TEST_SKIP_MATVEC=n (read at the first k_matvec
+// launch of the process) makes the process's n-th k_matvec launch leave its first
+// tile uncopied, so the consumers' bounded wait for it expires, the kernel sets
+// g_mv_err and returns, and the next status check reports a timeout.
+static int mv_test_skip() {
+  static const long n = [] {
+    const char *v = getenv("SQ_TEST_SKIP_MATVEC");
+    return v ? strtol(v, nullptr, 10) : 0L;
+  }();
+  static std::atomic<long> launches{0};
+  return n > 0 && ++launches == n ? 1 : 0;
+}
+
 template <int T, int MODE>
 static cudaError_t matvec_mode_t(cudaStream_t s, const MvArgs &a, bool pdl = false) {
   const size_t mv_smem = mv_smem_bytes<T>(a.in_dim);
@@ -824,7 +838,9 @@ static cudaError_t matvec_mode_t(cudaStream_t s, const MvArgs &a, bool pdl = fal
     cudaFuncSetAttribute(k_matvec<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem);
     attr_set = true;
   }
-  return launch_ex(k_matvec<T, MODE>, dim3(num_sms()), dim3(MV_THREADS), mv_smem, s, pdl, a);
+  MvArgs b = a;
+  b.test_skip = mv_test_skip();
+  return launch_ex(k_matvec<T, MODE>, dim3(num_sms()), dim3(MV_THREADS), mv_smem, s, pdl, b);
 }
 template <int T>
 static cudaError_t matvec_fused_t(cudaStream_t s, const MvArgs &a, bool pdl) {

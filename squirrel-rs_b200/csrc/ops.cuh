@@ -33,6 +33,7 @@ struct MvArgs {
   float *y[3];
   const float *res[3];  // optional residual rows: y[r] = res[r] + dot
   int gate_act;         // n == 2 (gate, up; same rows, no residual): y[1] = silu(gate . x) * (up . x); y[0] unused
+  int test_skip;        // failure-detection tests only (set by the launcher): k > 0 = tile k - 1 is never copied
 };
 bool matvec_fused_ok(const MvArgs &a, int wtype);
 // pdl: launched with programmatic stream serialization (the kernel streams its first

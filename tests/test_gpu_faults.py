@@ -1,4 +1,6 @@
-"""Failure detection of the persistent decode kernel, without a GPU fault.
+"""Failure detection of the bounded device waits, without a GPU fault: the
+persistent decode kernel (one GPU and tensor parallel), the peer all-reduce and the
+streaming matvec.
 
 Every cross-CTA wait of the decode kernel is bounded (about 2 s of SM clocks); when
 one expires the kernel sets an error word, every other wait sees it and gives up at
@@ -44,6 +46,65 @@ def test_decode_wait_expires_reports_timeout_and_context_recovers(gpu_lib, monke
     finally:
         ctx.close()
         m.close()
+
+
+def _matvec_child(q):
+    """A fresh process (the launch count starts at zero): its second k_matvec launch
+    leaves its first tile uncopied (SQ_TEST_SKIP_MATVEC=2)."""
+    os.environ["SQ_TEST_SKIP_MATVEC"] = "2"
+    try:
+        import torch
+        from oracle import oracle as O
+        from sqb200 import gguf_synth as G
+        from sqb200 import lib
+        rng = np.random.default_rng(7)
+        k, n = 2048, 512
+        x = torch.from_numpy(rng.standard_normal((1, k)).astype(np.float32)).cuda()
+        w = torch.from_numpy(G.quantize((rng.standard_normal(n * k) * 0.02).astype(np.float32), O.Q8_0)).cuda()
+        first = lib.linear(x, w, O.Q8_0, n)  # launch 1
+        torch.cuda.synchronize()
+        lib.wait_status()
+        t0 = time.monotonic()
+        lib.linear(x, w, O.Q8_0, n)  # launch 2: the consumers' wait for tile 0 runs out
+        torch.cuda.synchronize()
+        try:
+            lib.wait_status()
+            kind = "none"
+        except lib.KernelError as e:
+            kind = e.kind
+        took = time.monotonic() - t0
+        again = lib.linear(x, w, O.Q8_0, n)  # launch 3: a normal call after the error was cleared
+        torch.cuda.synchronize()
+        lib.wait_status()
+        same = bool(torch.equal(first, again))
+        q.put(("ok", kind, took, same))
+    except Exception as e:  # report instead of hanging the parent
+        q.put(("err", repr(e), 0.0, False))
+
+
+def test_matvec_wait_expires_reports_timeout_and_next_call_is_correct():
+    """The streaming matvec's bounded waits (k_matvec): a tile whose copy is never
+    issued makes the consumers' wait expire (and the producer's wait for their
+    release, and its drain of that slot); the kernel returns, sq_wait_status reports
+    Timeout, and the next call on the same device gives the first call's bits."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_matvec_child, args=(q,))
+    p.start()
+    try:
+        status, kind, took, same = q.get(timeout=300)
+    finally:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert status == "ok", kind
+    assert kind == "Timeout", kind
+    assert took < 60, took  # three bounded waits of ~2 s
+    assert same
 
 
 def _fault_rank(rank, path, prompt, ids, mode, qin, qout):
