@@ -17,6 +17,7 @@ LM head, device argmax fed back as the next input).
   parity: the GPU's greedy ids against the oracle's on the same prompt (the run
           exits 1 when they differ)
   long_context: config 3 (1B Q4_0, 2048-token prompt, decode at KV 2048-2304)
+  w8a8  : config 1's model under Q8_0 activations (the reference's aarch64 scheme)
   sweep : config 2 (isolated matvec, five shapes x three weight types)
   tp    : config 5 (8B Q8_0) tensor parallel over all ranks (TP1 on one GPU)
   prefill: config 4 (1B BF16 prefill of 512 / 2048 / 8192 tokens)
@@ -425,6 +426,60 @@ def run_long_context(lib, G, device, steps=256):
             "parity": parity}
 
 
+def run_w8a8(lib, G, device, steps=64):
+    """Config 1's model under Q8_0 activations (the reference's aarch64 scheme,
+    matmul.rs:89-100) on the persistent kernel's integer block dots: `steps` greedy
+    tokens after the 32-token prompt, chained on the device and timed by CUDA events.
+    Parity first, teacher-forced on the oracle's ids (tests/golden/cfg1_1b_q8_0_a8.npz):
+    the GPU's id must equal the oracle's at every step whose oracle top-2 margin exceeds
+    twice the scheme's last-bit noise at this shape (0.17: reordering the oracle's own
+    RMSNorm sum moves its logits that much)."""
+    import torch
+    model = lib.Model(G.ensure_gguf("1b", "q8_0"), device=device, acts=lib.ACTS_Q8)
+    cfg = model.config
+    prompt = G.prompt_ids(32, seed=1234)
+    ctx = model.new_context(32 + steps + 32)
+    parity = None
+    fx = os.path.join(ROOT, "tests", "golden", "cfg1_1b_q8_0_a8.npz")
+    if os.path.exists(fx):
+        z = np.load(fx)
+        ok, n = True, 0
+        nxt = int(ctx.forward(prompt))
+        for i, want in enumerate(z["ids"]):
+            if i > 0:
+                nxt = int(ctx.forward(np.array([z["ids"][i - 1]], np.uint32)))
+            if z["margins"][i] > 2 * 0.17:
+                ok, n = ok and nxt == int(want), n + 1
+        parity = {"ids_equal": ok, "n": n, "rule": "teacher-forced; ids compared where the oracle's top-2 "
+                  "margin exceeds 2 x 0.17 (the scheme's last-bit noise at this shape)",
+                  "against": "oracle ids, tests/golden/cfg1_1b_q8_0_a8.npz"}
+        ctx.reset()
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    ctx.forward(prompt)
+    ctx.decode_steps(3)  # warm-up
+    ctx.reset()
+    ctx.forward(prompt)
+    kv0 = ctx.seq_len
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    ctx.decode_steps(steps)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    lpt = ctx.launches_per_token
+    peak, kind = peaks()
+    algo = bytes_per_step(cfg, cfg.weight_type, kv0 + (steps - 1) / 2)
+    achieved = algo / (ms / steps / 1e3) / 1e9
+    ctx.close()
+    model.close()
+    return {"workload": "1b-q8_0, acts q8 (W8A8), 32-token prompt", "tok_s": steps / (ms / 1e3),
+            "ms_per_token": ms / steps, "launches_per_token": lpt,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": kind, "algorithmic_bytes_per_step": algo},
+            "parity": parity}
+
+
 def nccl_allreduce_us(world, n_calls=64, floats=4096, reps=20):
     """Device time of the TP step's collectives alone: `n_calls` all-reduces (sum) of
     `floats` f32 (the 8B hidden size: one after O and one after down in each of the
@@ -680,11 +735,13 @@ def run_ours(args):
             parity = {"ids_equal": bool(np.array_equal(want[:n], gpu_ids[:n])), "n": int(n),
                       "e2e_ids_equal": e2e_same, "against": "oracle ids, tests/golden/cfg1_1b_q8_0.npz"}
     single = rank == 0 and world == 1
-    prefill = long_ctx = sweep = None
+    prefill = long_ctx = sweep = w8a8 = None
     if single and args.prefill and spec == "1b":
         prefill = run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], local)
     if single and not args.no_extra:
         long_ctx = run_long_context(lib, G, local)
+        if args.acts == "f32":
+            w8a8 = run_w8a8(lib, G, local)
         sweep = run_sweep(lib, local)
     tp_line = None
     if not args.no_extra and not tp:
@@ -714,6 +771,7 @@ def run_ours(args):
             "first_ids": [int(i) for i in gpu_ids[:9]],
             "prefill": prefill,
             "long_context": long_ctx,
+            "w8a8": w8a8,
             "sweep": sweep,
             "tp": tp_line,
         }
@@ -722,6 +780,7 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     bad = [k for k, v in (("decode", parity), ("long_context", long_ctx and long_ctx["parity"]),
+                          ("w8a8", w8a8 and w8a8["parity"]),
                           ("tp", tp_line and tp_line["parity"]),
                           ("tp op_peer", tp_line and tp_line.get("op_peer") and tp_line["op_peer"]["parity"]),
                           ("tp op_nccl", tp_line and tp_line.get("op_nccl") and tp_line["op_nccl"]["parity"]))

@@ -206,125 +206,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
   return v;
 }
 
-// Four weight rows at a time. The lane's partial dot products of rows at shared
-// addresses ra[0..3] with its 64 activations (x2[j] = elements 2j, 2j+1): Q8_0 /
-// Q4_0 one 68 / 36-byte block pair of segment `seg` (4-byte words at an odd word
-// stride between lanes: conflict-free), BF16 eight 16-byte chunks. The loop runs
-// word by word with the four rows innermost, so each step has four independent
-// load -> convert -> FMA chains and the weights never sit in registers longer than
-// one step. Per block the products are summed first and scaled once, as the
-// reference does (dot_prod.rs:86-96, 255-270; BF16 one running sum, :464-472).
-template <int T>
-__device__ __forceinline__ void quad_dot(const uint32_t (&ra)[4], int seg, int lane, const f2x (&x2)[32],
-                                         float (&out)[4]) {
-  if constexpr (T == SQ_Q8_0) {
-    const uint32_t off = (uint32_t)(seg * 32 + lane) * 68u;
-    const f2x bias = pk2(-8388736.0f, -8388736.0f);  // 2^23 + 128: sign-flipped int8 under 2^23
-    f2x A[4], B[4];
-    float s0[4], s1[4];
-#pragma unroll
-    for (int r = 0; r < 4; r++) A[r] = B[r] = 0ull;
-#pragma unroll
-    for (int k = 0; k < 17; k++) {
-      uint32_t w[4];
-#pragma unroll
-      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t wx = w[r] ^ 0x80808080u;
-        const f2x lo = fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7540u), __byte_perm(wx, 0x4B000000u, 0x7541u)), bias);
-        const f2x hi = fadd2(pk2u(__byte_perm(wx, 0x4B000000u, 0x7542u), __byte_perm(wx, 0x4B000000u, 0x7543u)), bias);
-        if (k == 0) {  // scale of block 0, quants 0, 1
-          s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
-          A[r] = ffma2(x2[0], hi, A[r]);
-        } else if (k < 8) {  // quants 4k-2 .. 4k+1 of block 0
-          A[r] = ffma2(x2[2 * k - 1], lo, A[r]);
-          A[r] = ffma2(x2[2 * k], hi, A[r]);
-        } else if (k == 8) {  // quants 30, 31 of block 0, scale of block 1
-          A[r] = ffma2(x2[15], lo, A[r]);
-          s1[r] = h2f((uint16_t)(w[r] >> 16));
-        } else {  // quants 4k-36 .. 4k-33 of block 1
-          B[r] = ffma2(x2[2 * k - 2], lo, B[r]);
-          B[r] = ffma2(x2[2 * k - 1], hi, B[r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-      const float2 a = up2(A[r]), b = up2(B[r]);
-      out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
-    }
-  } else if constexpr (T == SQ_Q4_0) {
-    const uint32_t off = (uint32_t)(seg * 32 + lane) * 36u;
-    const f2x bias = pk2(-8388616.0f, -8388616.0f);  // 2^23 + 8: nibble q under 2^23, value q - 8
-    f2x A[4], B[4];
-    float s0[4], s1[4];
-#pragma unroll
-    for (int r = 0; r < 4; r++) A[r] = B[r] = 0ull;
-#pragma unroll
-    for (int k = 0; k < 9; k++) {
-      uint32_t w[4];
-#pragma unroll
-      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        // low nibbles are elements j, high nibbles elements j + 16 of their block
-        const uint32_t nl = w[r] & 0x0F0F0F0Fu, nh = (w[r] >> 4) & 0x0F0F0F0Fu;
-        const f2x l01 = fadd2(pk2u(__byte_perm(nl, 0x4B000000u, 0x7540u), __byte_perm(nl, 0x4B000000u, 0x7541u)), bias);
-        const f2x l23 = fadd2(pk2u(__byte_perm(nl, 0x4B000000u, 0x7542u), __byte_perm(nl, 0x4B000000u, 0x7543u)), bias);
-        const f2x h01 = fadd2(pk2u(__byte_perm(nh, 0x4B000000u, 0x7540u), __byte_perm(nh, 0x4B000000u, 0x7541u)), bias);
-        const f2x h23 = fadd2(pk2u(__byte_perm(nh, 0x4B000000u, 0x7542u), __byte_perm(nh, 0x4B000000u, 0x7543u)), bias);
-        if (k == 0) {  // scale of block 0, its bytes 0, 1
-          s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
-          A[r] = ffma2(x2[0], l23, A[r]);
-          A[r] = ffma2(x2[8], h23, A[r]);
-        } else if (k < 4) {  // bytes 4k-2 .. 4k+1 of block 0
-          A[r] = ffma2(x2[2 * k - 1], l01, A[r]);
-          A[r] = ffma2(x2[2 * k], l23, A[r]);
-          A[r] = ffma2(x2[2 * k + 7], h01, A[r]);
-          A[r] = ffma2(x2[2 * k + 8], h23, A[r]);
-        } else if (k == 4) {  // bytes 14, 15 of block 0, scale of block 1
-          A[r] = ffma2(x2[7], l01, A[r]);
-          A[r] = ffma2(x2[15], h01, A[r]);
-          s1[r] = h2f((uint16_t)(w[r] >> 16));
-        } else {  // bytes 4k-20 .. 4k-17 of block 1
-          B[r] = ffma2(x2[2 * k + 6], l01, B[r]);
-          B[r] = ffma2(x2[2 * k + 7], l23, B[r]);
-          B[r] = ffma2(x2[2 * k + 14], h01, B[r]);
-          B[r] = ffma2(x2[2 * k + 15], h23, B[r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-      const float2 a = up2(A[r]), b = up2(B[r]);
-      out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
-    }
-  } else {
-    f2x A[4];
-#pragma unroll
-    for (int r = 0; r < 4; r++) A[r] = 0ull;
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-      uint4 u[4];
-#pragma unroll
-      for (int r = 0; r < 4; r++) u[r] = lds128(ra[r] + (uint32_t)(seg * 2048 + k * 256 + lane * 8) * 2u);
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        A[r] = ffma2(x2[4 * k], pk2u(u[r].x << 16, u[r].x & 0xFFFF0000u), A[r]);
-        A[r] = ffma2(x2[4 * k + 1], pk2u(u[r].y << 16, u[r].y & 0xFFFF0000u), A[r]);
-        A[r] = ffma2(x2[4 * k + 2], pk2u(u[r].z << 16, u[r].z & 0xFFFF0000u), A[r]);
-        A[r] = ffma2(x2[4 * k + 3], pk2u(u[r].w << 16, u[r].w & 0xFFFF0000u), A[r]);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-      const float2 a = up2(A[r]);
-      out[r] = a.x + a.y;
-    }
-  }
-}
-
 // Sum four values over the warp: a butterfly that halves the values it carries at
 // each of the first two steps (6 shuffles in all, against 4 x 5 for four separate
 // sums), then every lane gets all four totals.

@@ -6,19 +6,20 @@
 // attention, O + residual, RMSNorm + gate/up + SiLU*up, down + residual], final
 // RMSNorm, LM head, argmax — and feeds the argmax back as the next token id.
 //
-// Layout: one CTA of NC warps (NGRP groups of four) per SM. Every weight row the CTA owns for the whole
-// token streams through a ring of NSLOT shared-memory slots with 1-D bulk async
-// copies (cp.async.bulk ... mbarrier::complete_tx): the last warp to finish with a
-// slot immediately refills it with the tile NSLOT positions ahead in the CTA's tile
-// table (built once per context), so NSLOT tiles are always in flight — also while
-// the warps wait at a grid barrier. The warps decode the GGUF blocks straight from
-// shared memory (native 34/18/64-byte layout) against activations held in
-// registers, two weight rows per warp at a time, and finish each row inside the
-// warp (RoPE, residual add, SiLU*up, logits). They meet the other CTAs at grid
-// barriers only where the math needs a whole vector (after QKV, attention, O,
-// gate/up, down).
+// Layout: one CTA of NC warps (NGRP groups of four) per SM. Every weight row the
+// CTA owns for the whole token streams through a ring of NSLOT shared-memory slots
+// with 1-D bulk async copies (cp.async.bulk ... mbarrier::complete_tx): the last
+// warp to finish with a slot immediately refills it with the tile NSLOT positions
+// ahead in the CTA's tile table (built once per context), so NSLOT tiles are always
+// in flight, also while the warps wait for another stage's output. The warps decode
+// the GGUF blocks straight from shared memory (native 34/18/64-byte layout) against
+// the stage input, staged once per CTA in shared memory (f32, or quantized to Q8_0
+// blocks for W8A8 contexts), four weight rows per warp at a time, and finish each
+// row inside the warp (RoPE, residual add, SiLU*up, logits). CTAs hand vectors to
+// each other as tagged words that the consumers poll (no grid barrier): after QKV,
+// attention, O, gate/up and down.
 //
-// Every wait (mbarrier, grid barrier) is bounded by a clock limit; on expiry the
+// Every wait (mbarrier, exchange word) is bounded by a clock limit; on expiry the
 // kernel records an error, drains its in-flight copies and returns, and the host
 // reports SQ_ERR_TIMEOUT.
 #include <cuda_runtime.h>
@@ -340,10 +341,20 @@ struct AttScratch {
   float a[NC][GROUP][128];
 };
 
+// The stage input of a W8A8 context (SQ_ACTS_Q8): int8 activations laid out word for
+// word against the weight words the integer dot products read (see stage_q), and the
+// f32 value of each block's f16 scale.
+struct QStage {
+  uint32_t xq[MAX_X / 2048 * 18 * 32];  // Q8_0 weights: [seg][17][lane]; Q4_0: [seg][9][low / high][lane]
+  float2 xsc[MAX_X / 64];               // scales of the two blocks of each lane's pair
+  int2 xsum[MAX_X / 64];                // Q4_0: sums of the quants of the two blocks
+};
+
 struct Smem {
   float red[2 * NGRP][MAX_TILE_ITEMS];  // segment partial sums: two buffers per warp group
   union {
     float xs[MAX_X / 2048 * 2176];  // the stage input, lane-interleaved (see xs_index)
+    QStage qs;                      // the quantized stage input (W8A8)
     AttScratch at;    // attention-stage partials (a different phase of the layer)
   };
   float ssp[NC];      // per-warp partial squared sums of the RMS norm
@@ -459,19 +470,42 @@ __device__ __forceinline__ void poll_ll_n(const Params &p, const unsigned long l
 // Every CTA needs the whole input vector of a stage (all elements of the residual
 // for a norm, all of attn / act). Reading it once per CTA — not once per warp —
 // keeps the CTAs' simultaneous reads of the same few KB from piling up on a
-// handful of L2 slices. The layout is the one the dot products read with
-// conflict-free 16-byte loads (lane `lane` of a warp on segment `seg`):
-//  Q8_0: [seg][k][lane] float4, k = 0..16 the step of quad_dot_xs (word k of the
-//        lane's block pair); the lane's element i sits at position i + 2 (i < 32)
-//        or i + 4 of its 68 floats, so step k's four inputs are one float4;
-//  BF16: [seg][i/4][lane] float4 for the lane's element i (quad_dot_xs reads two a
-//        step); Q4_0: the same, loaded once into registers (x_from_smem).
+// handful of L2 slices. The layout is the one the dot products read, with
+// conflict-free 16-byte loads that the four rows of a step share (lane `lane` of a
+// warp on segment `seg`, its 64 elements i of the segment's 2048):
+//  Q8_0: [seg][k 0..16][lane] float4: step k of quad_dot_xs (word k of the lane's
+//        68-byte block pair) takes slot k; the lane's element i sits at position
+//        i + 2 (i < 32) or i + 4 of its 68 floats, so the two scales' positions are
+//        padding. (Sharing one slot between steps 0 and 8, as Q4_0 does, measured
+//        4 % slower on Q8_0: the staging index arithmetic sits on every stage's
+//        critical path.)
+//  Q4_0: [seg][slot 0..7][low / high][lane] float4: word k of the 36-byte pair
+//        holds bytes whose low nibbles are elements j and high nibbles j + 16, so a
+//        step loads both halves of slot k (k 1..3), k - 1 (k 5..8), or slot 0
+//        (bytes 14, 15, 0, 1 of block 0), shared by steps 0 and 4;
+//  BF16: [seg][i / 4][lane] float4 for the lane's element i = 8k .. 8k+7 of step k.
+// Element pairs (2j, 2j + 1) are adjacent in every layout.
 template <int T>
 __device__ __forceinline__ int xs_index(int e) {
   const int seg = e >> 11, r = e & 2047;
   if constexpr (T == SQ_Q8_0) {
     const int ln = r >> 6, i = r & 63, pos = i < 32 ? i + 2 : i + 4;
     return ((seg * 17 + (pos >> 2)) * 32 + ln) * 4 + (pos & 3);
+  }
+  if constexpr (T == SQ_Q4_0) {
+    const int ln = r >> 6, i = r & 63, j = i & 31, byte = j & 15, half = j >> 4;
+    int slot, c;
+    if (i >= 32) {
+      slot = 4 + (byte >> 2);
+      c = byte & 3;
+    } else if (byte < 2 || byte >= 14) {
+      slot = 0;
+      c = byte < 2 ? byte + 2 : byte - 14;
+    } else {
+      slot = (byte + 2) >> 2;
+      c = (byte + 2) & 3;
+    }
+    return (((seg * 8 + slot) * 2 + half) * 32 + ln) * 4 + c;
   }
   int lane, i;
   if constexpr (T == SQ_BF16) {
@@ -530,7 +564,7 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
         }
 #pragma unroll
         for (int k = 0; k < 8; k++) ss = fmaf(d[k], d[k], ss);
-        if constexpr (T == SQ_Q8_0) {  // element pairs are contiguous in this layout, quads are not
+        if constexpr (T != SQ_BF16) {  // element pairs are adjacent in these layouts, quads are not
           const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
           for (int k = 0; k < 8; k += 2)
@@ -599,59 +633,196 @@ __device__ float stage_x(const Params &p, Smem &sm, const unsigned long long *v,
   return 1.0f / __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
 }
 
-// This warp's activation registers from the staged input, times `scale` (1/rms
-// for a norm: (h*w) * (1/rms), one rounding from the reference's (h*w)/rms).
+// Byte offset in QStage::xq of activation element j (0..31) of block h (0, 1) of a
+// lane's block pair, for the weight type the dots read. Q8_0: the pair is 17 words
+// (scale, 32 quants, scale, 32 quants), so element j of block h lines up with byte
+// 2 + 34h + j of the weight words. Q4_0: 9 words (scale, 16 bytes, scale, 16 bytes);
+// byte 2 + 18h + (j & 15) holds element j in its low nibble (j < 16) or high nibble,
+// so the low and high elements go to two word planes. Positions under a scale stay 0.
 template <int T>
-__device__ __forceinline__ void x_from_smem(f2x (&x2)[32], const Smem &sm, int seg, int lane, int n, float scale) {
-  const bool act = lane_active<T>(seg, lane, n);
-  const f2x sc = pk2(scale, scale);
-#pragma unroll
-  for (int k = 0; k < 16; k++) {
-    const float4 f = act ? *reinterpret_cast<const float4 *>(&sm.xs[(seg << 11) + (k << 7) + (lane << 2)])
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    x2[2 * k] = fmul2(pk2(f.x, f.y), sc);
-    x2[2 * k + 1] = fmul2(pk2(f.z, f.w), sc);
-  }
-}
-
-// Q4_0 warps hold the 64 f32 inputs their lane meets in every row in registers, as
-// 32 packed pairs. Q8_0 and BF16 read them from the staging buffer in the dot loop
-// (quad_dot_xs): 64 registers fewer, which measured 5 % (1B) and 11 % (8B) faster
-// on Q8_0; the Q4_0 layout would need 2 KB more shared memory than the 8B shapes
-// have to spare.
-template <int T>
-struct ActRegs {
-  f2x x[32];
-};
-template <>
-struct ActRegs<SQ_Q8_0> {};
-template <>
-struct ActRegs<SQ_BF16> {};
-
-// Stage a stage's input and load this warp's activation registers, if it keeps
-// them (the norm's 1/rms applied there). Returns the factor the stage's dot
-// products take: 1, or the norm's 1/rms when the inputs stay in shared memory.
-template <int T, int MODE>
-__device__ __forceinline__ float stage_in(const Params &p, Smem &sm, ActRegs<T> &x, const unsigned long long *v,
-                                         unsigned tag, const float *w, int n, int nseg, int stamp_at,
-                                         const uint8_t *emb_row = nullptr, bool write_hidden = false,
-                                         unsigned emb_tag = 0u) {
-  const float sc = stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, stamp_at);
-  if constexpr (T == SQ_Q4_0) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    x_from_smem<T>(x.x, sm, (warp % NG) % nseg, lane, n, sc);
-    return 1.0f;
+__device__ __forceinline__ uint32_t xq_byte(int seg, int lane, int h, int j) {
+  if constexpr (T == SQ_Q8_0) {
+    const int pos = 2 + 34 * h + j;
+    return (uint32_t)(((seg * 17 + (pos >> 2)) * 32 + lane) * 4 + (pos & 3));
   } else {
-    (void)x;
-    (void)nseg;
-    return sc;
+    const int pos = 2 + 18 * h + (j & 15);
+    return (uint32_t)((((seg * 9 + (pos >> 2)) * 2 + (j >> 4)) * 32 + lane) * 4 + (pos & 3));
   }
 }
 
-// Four rows of one lane's block pair (Q8_0) or eight 16-byte chunks (BF16) against
-// the inputs in the staging buffer: the arithmetic of quad_dot (dot_prod.rs:86-96,
-// 464-472), with each step's inputs fetched by one (Q8_0) or two (BF16) conflict-
-// free 16-byte loads that the four rows share.
+__device__ __forceinline__ void sts16(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"((unsigned short)v) : "memory");
+}
+
+// W8A8 (SQ_ACTS_Q8): the stage's n-element input quantized to Q8_0 blocks
+// (quantize_row_q8_0, dot_prod.rs:21-31) into sm.qs, after the RMS norm for XS_NORM /
+// XS_EMBED in the reference's form y = (h*w) / rms (rms_norm.rs:40-56; the squared
+// sum in a fixed order of our own). Every linear quantizes its input this way
+// (matmul.rs:89-100). Thread t takes eight consecutive elements (a quarter block) per
+// pass; the four threads of a block meet through shuffles for its absolute maximum
+// and (Q4_0) the sum of its quants. Returns 1: the norm is applied before quantizing.
+template <int T, int MODE>
+__device__ float stage_q(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag, const float *w, int n,
+                         const uint8_t *emb_row, bool write_hidden, unsigned emb_tag, int stamp_at) {
+  constexpr int MAXG = MAX_X / 8 / NTHREADS;  // passes of eight elements a thread
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = n / 8;  // n is a multiple of 256 (host check): whole warps take part in a pass
+  float x[MAXG][8];
+  float ss = 0.f;
+  if constexpr (MODE == XS_EMBED) {
+#pragma unroll
+    for (int k = 0; k < MAXG; k++) {
+      const int g = k * NTHREADS + tid;
+      if (g < ng) {
+        const int e = g * 8, b = e >> 5, j0 = e & 31;
+        const uint8_t *blk = emb_row + (size_t)b * (T == SQ_Q8_0 ? Q8_BYTES : Q4_BYTES);
+        const float sc = h2f(ld_u16(blk));
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if constexpr (T == SQ_Q8_0) {
+            x[k][i] = sc * (float)(int8_t)__ldg(blk + 2 + j0 + i);
+          } else {
+            const uint8_t byte = __ldg(blk + 2 + ((j0 + i) & 15));
+            x[k][i] = sc * (float)((j0 < 16 ? (byte & 0x0F) : (byte >> 4)) - 8);
+          }
+        }
+        if (write_hidden) {
+#pragma unroll
+          for (int i = 0; i < 8; i++) st_ll(p.hid_ll + e + i, x[k][i], emb_tag);
+        }
+      }
+    }
+  } else {
+    ulonglong2 c[MAXG][4];
+#pragma unroll
+    for (int k = 0; k < MAXG; k++) {
+      const int g = k * NTHREADS + tid;
+#pragma unroll
+      for (int i = 0; i < 4; i++) c[k][i] = g < ng ? ld_ll2(v + 8 * g + 2 * i) : make_ulonglong2(0ull, 0ull);
+    }
+    const long long t0 = clock64();
+    for (unsigned it = 0;; it++) {  // re-read all stale pairs together
+      bool all = true;
+#pragma unroll
+      for (int k = 0; k < MAXG; k++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          if (k * NTHREADS + tid < ng && !(ll_ok(c[k][i].x, tag) && ll_ok(c[k][i].y, tag))) all = false;
+      if (all) break;
+#pragma unroll
+      for (int k = 0; k < MAXG; k++) {
+        const int g = k * NTHREADS + tid;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          if (g < ng && !(ll_ok(c[k][i].x, tag) && ll_ok(c[k][i].y, tag))) c[k][i] = ld_ll2(v + 8 * g + 2 * i);
+      }
+      if ((it & 15u) == 15u && poll_expired(p, t0)) break;
+    }
+#pragma unroll
+    for (int k = 0; k < MAXG; k++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        x[k][2 * i] = ll_val(c[k][i].x);
+        x[k][2 * i + 1] = ll_val(c[k][i].y);
+      }
+  }
+  if (stamp_at >= 0) stamp(p, stamp_at);
+  float rms = 1.0f;
+  if constexpr (MODE != XS_PLAIN) {
+#pragma unroll
+    for (int k = 0; k < MAXG; k++)
+      if (k * NTHREADS + tid < ng) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss = fmaf(x[k][i], x[k][i], ss);
+      }
+    ss = warp_sum(ss);
+    if (lane == 0) sm.ssp[warp] = ss;
+    cta_sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NC; k++) tot += sm.ssp[k];
+    rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), p.eps));
+  }
+  const uint32_t xq = smem_u32(sm.qs.xq);
+  float *xsc = reinterpret_cast<float *>(sm.qs.xsc);
+  int *xsum = reinterpret_cast<int *>(sm.qs.xsum);
+#pragma unroll
+  for (int k = 0; k < MAXG; k++) {
+    const int g = k * NTHREADS + tid;
+    if (g >= ng) continue;  // warp-uniform (ng is a multiple of 32), so the shuffles below see whole warps
+    float y[8];
+    if constexpr (MODE != XS_PLAIN) {
+      const float4 w0 = ldnc4(w + 8 * g), w1 = ldnc4(w + 8 * g + 4);
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++) y[i] = __fdiv_rn(__fmul_rn(x[k][i], ww[i]), rms);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; i++) y[i] = x[k][i];
+    }
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(y[i]));
+    am = fmaxf(am, __shfl_xor_sync(FULL, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(FULL, am, 2));
+    const float scale = __fdiv_rn(am, 127.0f);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    int q[8], qs = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float r = roundf(__fmul_rn(y[i], inv));  // ties away from zero, like f32::round
+      q[i] = (r != r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+      qs += q[i];
+    }
+    const int b = g >> 2, qq = g & 3;  // block of the stage input, quarter of the block
+    const int seg = b >> 6, ln = (b >> 1) & 31, h = b & 1;
+#pragma unroll
+    for (int i = 0; i < 8; i += 2)
+      sts16(xq + xq_byte<T>(seg, ln, h, 8 * qq + i), (uint32_t)(q[i] & 0xFF) | ((uint32_t)(q[i + 1] & 0xFF) << 8));
+    if constexpr (T == SQ_Q8_0) {
+      if (qq == 0) sts16(xq + xq_byte<T>(seg, ln, h, -2), 0u);  // under the block's scale
+    } else {
+      if ((qq & 1) == 0) {  // this plane (low for qq 0, high for qq 2) under the block's scale (byte 18h)
+        const int pos = 18 * h;
+        sts16(xq + (uint32_t)((((seg * 9 + (pos >> 2)) * 2 + (qq >> 1)) * 32 + ln) * 4 + (pos & 3)), 0u);
+      }
+      qs += __shfl_xor_sync(FULL, qs, 1);
+      qs += __shfl_xor_sync(FULL, qs, 2);
+      if (qq == 0) xsum[b] = qs;
+    }
+    if (qq == 0) xsc[b] = __half2float(__float2half_rn(scale));
+  }
+  cta_sync();
+  if (stamp_at >= 0) stamp(p, stamp_at + 2);
+  return 1.0f;
+}
+
+// Stage a stage's input into the staging buffer, where the dot products read it.
+// Returns the factor the stage's dot products take: the norm's 1/rms (1 for a plain
+// input), applied to each row's sum (the reference scales the input, (h*w)/rms:
+// one rounding apart). W8A8 contexts (AQ) stage the quantized input instead.
+template <int T, int MODE, bool AQ>
+__device__ __forceinline__ float stage_in(const Params &p, Smem &sm, const unsigned long long *v, unsigned tag,
+                                         const float *w, int n, int stamp_at, const uint8_t *emb_row = nullptr,
+                                         bool write_hidden = false, unsigned emb_tag = 0u) {
+  if constexpr (AQ) return stage_q<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, stamp_at);
+  else return stage_x<T, MODE>(p, sm, v, tag, w, n, emb_row, write_hidden, emb_tag, stamp_at);
+}
+
+// Q4_0 step k of a lane's block pair: the staging slot holding its inputs.
+__host__ __device__ constexpr int xs_slot_q4(int k) { return k == 0 || k == 4 ? 0 : (k < 4 ? k : k - 1); }
+
+// Four weight rows at a time: the lane's partial dot products of rows at shared
+// addresses ra[0..3] with its 64 inputs in the staging buffer (xs, layout at
+// xs_index). Q8_0 / Q4_0 one 68 / 36-byte block pair of segment `seg` (4-byte words
+// at an odd word stride between lanes: conflict-free), BF16 eight 16-byte chunks.
+// The loop runs word by word with the four rows innermost: each step loads its
+// inputs once (one or two 16-byte loads the four rows share) and has four
+// independent load -> convert -> FMA chains. int8 / nibble -> f32 by byte permute
+// into a float magic constant, packed f32x2 adds and FMAs. Per block the products
+// are summed first and scaled once, as the reference does (dot_prod.rs:86-96,
+// 255-270; BF16 one running sum, :464-472). Keeping the inputs here instead of in 64
+// registers a lane measured 5 % (1B) and 11 % (8B) faster on Q8_0.
 template <int T>
 __device__ __forceinline__ void quad_dot_xs(const uint32_t (&ra)[4], int seg, int lane, uint32_t xs, float (&out)[4]) {
   if constexpr (T == SQ_Q8_0) {
@@ -694,8 +865,56 @@ __device__ __forceinline__ void quad_dot_xs(const uint32_t (&ra)[4], int seg, in
       const float2 a = up2(A[r]), b = up2(B[r]);
       out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
     }
+  } else if constexpr (T == SQ_Q4_0) {
+    const uint32_t off = (uint32_t)(seg * 32 + lane) * 36u;
+    const uint32_t xa = xs + (uint32_t)((seg * 16 * 32 + lane) * 16);  // [slot][half][lane] float4
+    const f2x bias = pk2(-8388616.0f, -8388616.0f);  // 2^23 + 8: nibble q under 2^23, value q - 8
+    f2x A[4], B[4];
+    float s0[4], s1[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) A[r] = B[r] = 0ull;
+#pragma unroll
+    for (int k = 0; k < 9; k++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
+      const uint32_t sa = xa + (uint32_t)xs_slot_q4(k) * 1024u;
+      const uint4 xl = lds128(sa), xh = lds128(sa + 512u);  // low-nibble and high-nibble elements
+      const f2x l01x = pk2u(xl.x, xl.y), l23x = pk2u(xl.z, xl.w), h01x = pk2u(xh.x, xh.y), h23x = pk2u(xh.z, xh.w);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t nl = w[r] & 0x0F0F0F0Fu, nh = (w[r] >> 4) & 0x0F0F0F0Fu;
+        const f2x l01 = fadd2(pk2u(__byte_perm(nl, 0x4B000000u, 0x7540u), __byte_perm(nl, 0x4B000000u, 0x7541u)), bias);
+        const f2x l23 = fadd2(pk2u(__byte_perm(nl, 0x4B000000u, 0x7542u), __byte_perm(nl, 0x4B000000u, 0x7543u)), bias);
+        const f2x h01 = fadd2(pk2u(__byte_perm(nh, 0x4B000000u, 0x7540u), __byte_perm(nh, 0x4B000000u, 0x7541u)), bias);
+        const f2x h23 = fadd2(pk2u(__byte_perm(nh, 0x4B000000u, 0x7542u), __byte_perm(nh, 0x4B000000u, 0x7543u)), bias);
+        if (k == 0) {  // scale of block 0, its bytes 0, 1 (slot 0's upper halves)
+          s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
+          A[r] = ffma2(l23x, l23, A[r]);
+          A[r] = ffma2(h23x, h23, A[r]);
+        } else if (k < 4) {  // bytes 4k-2 .. 4k+1 of block 0
+          A[r] = ffma2(l01x, l01, A[r]);
+          A[r] = ffma2(l23x, l23, A[r]);
+          A[r] = ffma2(h01x, h01, A[r]);
+          A[r] = ffma2(h23x, h23, A[r]);
+        } else if (k == 4) {  // bytes 14, 15 of block 0 (slot 0's lower halves), scale of block 1
+          A[r] = ffma2(l01x, l01, A[r]);
+          A[r] = ffma2(h01x, h01, A[r]);
+          s1[r] = h2f((uint16_t)(w[r] >> 16));
+        } else {  // bytes 4k-20 .. 4k-17 of block 1
+          B[r] = ffma2(l01x, l01, B[r]);
+          B[r] = ffma2(l23x, l23, B[r]);
+          B[r] = ffma2(h01x, h01, B[r]);
+          B[r] = ffma2(h23x, h23, B[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const float2 a = up2(A[r]), b = up2(B[r]);
+      out[r] = fmaf(a.x + a.y, s0[r], (b.x + b.y) * s1[r]);
+    }
   } else {
-    static_assert(T == SQ_BF16, "Q4_0 keeps its inputs in registers (quad_dot)");
     const uint32_t xa = xs + (uint32_t)(seg * 2048 + lane * 4) * 4u;
     f2x A[4];
 #pragma unroll
@@ -721,6 +940,83 @@ __device__ __forceinline__ void quad_dot_xs(const uint32_t (&ra)[4], int seg, in
       out[r] = a.x + a.y;
     }
   }
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {  // signed bytes x signed bytes
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsigned bytes x signed bytes
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// W8A8 block dots, four weight rows at a time: the lane's block pair of segment seg
+// of rows ra[0..3] against the quantized input in sm.qs (stage_q). Each weight word
+// meets the activation word built against it (zeros under the scales), so a step is
+// one dp4a a row (Q8_0) or two on the word's low and high nibbles (Q4_0, quants
+// q in 0..15: the block's sum is fixed up by -8 x the sum of the activation quants).
+// Per block the integer sum is scaled as the reference does, (isum * d_a) * d_w
+// (dot_q8_0_q8_0_scalar / dot_q8_0_q4_0_scalar, dot_prod.rs:378-403).
+template <int T>
+__device__ __forceinline__ void quad_dot_q(const uint32_t (&ra)[4], int seg, int lane, const QStage &qs,
+                                           float (&out)[4]) {
+  const uint32_t xq = smem_u32(qs.xq);
+  int i0[4] = {0, 0, 0, 0}, i1[4] = {0, 0, 0, 0};
+  float s0[4], s1[4];
+  if constexpr (T == SQ_Q8_0) {
+    const uint32_t off = (uint32_t)(seg * 32 + lane) * 68u;
+    const uint32_t xa = xq + (uint32_t)((seg * 17 * 32 + lane) * 4);
+#pragma unroll
+    for (int k = 0; k < 17; k++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
+      const uint32_t a = lds32(xa + (uint32_t)k * 128u);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        if (k <= 8) i0[r] = dp4a_ss(w[r], a, i0[r]);  // word 8: block 0's last two quants, block 1's scale
+        else i1[r] = dp4a_ss(w[r], a, i1[r]);
+        if (k == 0) s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
+        if (k == 8) s1[r] = h2f((uint16_t)(w[r] >> 16));
+      }
+    }
+  } else {
+    const uint32_t off = (uint32_t)(seg * 32 + lane) * 36u;
+    const uint32_t xa = xq + (uint32_t)((seg * 9 * 2 * 32 + lane) * 4);
+#pragma unroll
+    for (int k = 0; k < 9; k++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) w[r] = lds32(ra[r] + off + 4u * k);
+      const uint32_t alo = lds32(xa + (uint32_t)(2 * k) * 128u), ahi = lds32(xa + (uint32_t)(2 * k + 1) * 128u);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t lo = w[r] & 0x0F0F0F0Fu, hi = (w[r] >> 4) & 0x0F0F0F0Fu;
+        if (k <= 4) {  // word 4: block 0's bytes 14, 15 and block 1's scale
+          i0[r] = dp4a_us(lo, alo, i0[r]);
+          i0[r] = dp4a_us(hi, ahi, i0[r]);
+        } else {
+          i1[r] = dp4a_us(lo, alo, i1[r]);
+          i1[r] = dp4a_us(hi, ahi, i1[r]);
+        }
+        if (k == 0) s0[r] = h2f((uint16_t)(w[r] & 0xFFFFu));
+        if (k == 4) s1[r] = h2f((uint16_t)(w[r] >> 16));
+      }
+    }
+    const int2 qsum = qs.xsum[seg * 32 + lane];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      i0[r] -= 8 * qsum.x;
+      i1[r] -= 8 * qsum.y;
+    }
+  }
+  const float2 da = qs.xsc[seg * 32 + lane];
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+    out[r] = __fadd_rn(__fmul_rn(__fmul_rn((float)i0[r], da.x), s0[r]), __fmul_rn(__fmul_rn((float)i1[r], da.y), s1[r]));
 }
 
 // The bulk copies of tile entry d: f(byte offset in the slot, global source, bytes).
@@ -799,6 +1095,7 @@ __device__ __forceinline__ void release_slot(const Params &p, const Ring &rg, Sm
 // residual of this CTA's rows of the O / down stages).
 struct StageRegs {
   float c0, c1, s0, s1, hres;
+  unsigned long long hw;  // the residual's tagged word as loaded, before its tag is checked
 };
 
 // Finish output row(s) of a stage (warp-uniform arguments; lane 0 stores).
@@ -888,9 +1185,9 @@ __device__ __forceinline__ void group_sync(int grp) {
 // refills overlap the other groups' dot products. Within a tile a warp takes four
 // rows at a time (two row pairs, or four rows of its input segment when the rows
 // are split into segments) and reduces them together.
-template <int T>
+template <int T, bool AQ>
 __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Smem &sm, const int2 *tbl, int kind, int l,
-                             const ActRegs<T> &x, float osc, int &slot, unsigned &phase, int &tile_ctr, int pos,
+                             float osc, int &slot, unsigned &phase, int &tile_ctr, int pos,
                              const StageRegs &sr, unsigned tag) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = warp / NG, wig = warp % NG;
@@ -934,7 +1231,7 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
               const uint32_t ra[4] = {tile + (uint32_t)rw[0] * rb, tile + (uint32_t)(hasb ? rw[1] : rw[0]) * rb,
                                       tile + (uint32_t)(has2 ? rw[2] : rw[0]) * rb,
                                       tile + (uint32_t)(hasb2 ? rw[3] : rw[0]) * rb};
-              if constexpr (T == SQ_Q4_0) quad_dot<T>(ra, 0, lane, x.x, v);
+              if constexpr (AQ) quad_dot_q<T>(ra, 0, lane, sm.qs, v);
               else quad_dot_xs<T>(ra, 0, lane, smem_u32(sm.xs), v);
             }
             warp_sum4(v);
@@ -956,7 +1253,7 @@ __device__ __forceinline__ void matvec_stage(const Params &p, const Ring &rg, Sm
               uint32_t ra[4];
 #pragma unroll
               for (int q = 0; q < 4; q++) ra[q] = tile + (uint32_t)(i + q * rpw < rows ? i + q * rpw : i) * rb;
-              if constexpr (T == SQ_Q4_0) quad_dot<T>(ra, seg, lane, x.x, v);
+              if constexpr (AQ) quad_dot_q<T>(ra, seg, lane, sm.qs, v);
               else quad_dot_xs<T>(ra, seg, lane, smem_u32(sm.xs), v);
             }
             warp_sum4(v);
@@ -1069,7 +1366,7 @@ __device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsig
 #pragma unroll
       for (int k = 0; k < HD / 4; k++)
         kr[k] = valid ? ldcg4(kb + (size_t)s * HD + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
-      constexpr int VJ = 16;  // V rows per batch (fewer registers than all 32 at once)
+      constexpr int VJ = 64 / DPL;  // V rows per batch (64 registers): in flight with q.K and the softmax
       float vv[VJ][DPL];
       auto load_v = [&](int j0) {
 #pragma unroll
@@ -1157,15 +1454,22 @@ __device__ void attention_heads(const Params &p, Smem &sm, int l, int pos, unsig
 // partial per head; the chunk that holds the token's own position adds it from the
 // QKV stage's tagged words; the last CTA to finish a kv head combines the chunks of
 // its four heads (one warp per head) and publishes their outputs.
+// Chunks of the (kv head, chunk) attention items at key length Lk: ~128 positions a
+// chunk (four 32-position blocks, one per warp pair), at most max_chunks per head.
+__device__ __forceinline__ void attn_chunking(const Params &p, int Lk, int &n_chunks, int &CH) {
+  n_chunks = (Lk + 127) / 128;
+  if (n_chunks > p.max_chunks) n_chunks = p.max_chunks;
+  CH = (Lk + n_chunks - 1) / n_chunks;
+}
+
 template <int DPL>
 __device__ void attention_groups(const Params &p, Smem &sm, int l, int pos, unsigned tag_in, unsigned tag_out) {
   constexpr int HD = DPL * 32;
-  static_assert(GROUP == 4 && NC == 8, "two heads x four position lanes of warps");
+  static_assert(GROUP == 4 && NC >= 8, "two heads x four position lanes of warps (warps past 8 only keep step)");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Lk = pos + 1;
-  int n_chunks = (Lk + 127) / 128;  // ~128 positions a chunk: four 32-position blocks, one per warp pair
-  if (n_chunks > p.max_chunks) n_chunks = p.max_chunks;
-  const int CH = (Lk + n_chunks - 1) / n_chunks;
+  int n_chunks, CH;
+  attn_chunking(p, Lk, n_chunks, CH);
   const int items = p.KVH * n_chunks;
   const int hp = warp >> 2, bw = warp & 3;  // head pair, block lane of this warp
   for (int item = blockIdx.x; item < items; item += p.G) {
@@ -1197,10 +1501,22 @@ __device__ void attention_groups(const Params &p, Smem &sm, int l, int pos, unsi
     float m[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f}, acc[2][DPL];
 #pragma unroll
     for (int i = 0; i < DPL; i++) acc[0][i] = acc[1][i] = 0.f;
-    constexpr int VJ = 8;  // V rows per batch
+    // V rows per batch: head_dim 64 all 32 rows of the block (64 registers), loaded
+    // before q.K so that they are in flight with it and the softmax; head_dim 128
+    // (whose keys already take 128 registers) 8 rows at a time after the softmax
+    constexpr int VJ = DPL <= 2 ? 32 : 8;
     for (int base = s0 + bw * 32; base < cached_end; base += 4 * 32) {
       const int s = base + lane;
       const bool valid = s < cached_end;
+      float vv[VJ][DPL];
+      auto load_v = [&](int j0) {
+#pragma unroll
+        for (int j = 0; j < VJ; j++)
+#pragma unroll
+          for (int i = 0; i < DPL; i++)
+            vv[j][i] = base + j0 + j < cached_end ? __ldcg(vb + (size_t)(base + j0 + j) * HD + lane + 32 * i) : 0.f;
+      };
+      if constexpr (DPL <= 2) load_v(0);
       float d0 = 0.f, d1 = 0.f;
 #pragma unroll
       for (int k = 0; k < HD / 4; k++) {
@@ -1229,12 +1545,7 @@ __device__ void attention_groups(const Params &p, Smem &sm, int l, int pos, unsi
       }
 #pragma unroll
       for (int j0 = 0; j0 < 32; j0 += VJ) {
-        float vv[VJ][DPL];
-#pragma unroll
-        for (int j = 0; j < VJ; j++)
-#pragma unroll
-          for (int i = 0; i < DPL; i++)
-            vv[j][i] = base + j0 + j < cached_end ? __ldcg(vb + (size_t)(base + j0 + j) * HD + lane + 32 * i) : 0.f;
+        if (j0 > 0 || DPL > 2) load_v(j0);
 #pragma unroll
         for (int j = 0; j < VJ; j++) {
           const float p0 = __shfl_sync(FULL, pj[0], j0 + j), p1 = __shfl_sync(FULL, pj[1], j0 + j);
@@ -1353,8 +1664,7 @@ __device__ ArgState warp_argmax_smem(const float *v, int n, long long base) {
   return s;
 }
 
-__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr,
-                                                unsigned hid_tag) {
+__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr) {
   const int lane = threadIdx.x & 31;
   if (kind == ST_QKV) {
     const int half = p.hd >> 1;
@@ -1366,11 +1676,24 @@ __device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l
   } else if (kind == ST_O || kind == ST_DOWN || kind == ST_DOWN2) {  // the residual of this CTA's rows (<= 32)
     int r0, r1;
     stage_rows(p, kind, l, blockIdx.x, r0, r1);
-    sr.hres = lane < r1 - r0 ? poll_ll(p, p.hid_ll + r0 + lane, hid_tag) : 0.f;
+    // issued now, checked after the staging (resolve_hres): the load's round trip
+    // overlaps the stage input's instead of adding to it
+    sr.hw = lane < r1 - r0 ? ld_ll(p.hid_ll + r0 + lane) : 0ull;
   }
 }
 
-template <int T, int DPL>
+// The residual word loaded by load_stage_regs: its value once it carries hid_tag (it
+// nearly always does: the residual was published a stage or more ago).
+__device__ __forceinline__ void resolve_hres(const Params &p, int kind, int l, StageRegs &sr, unsigned hid_tag) {
+  if (kind != ST_O && kind != ST_DOWN && kind != ST_DOWN2) return;
+  const int lane = threadIdx.x & 31;
+  int r0, r1;
+  stage_rows(p, kind, l, blockIdx.x, r0, r1);
+  if (lane < r1 - r0 && !ll_ok(sr.hw, hid_tag)) sr.hw = ll_wait(p, p.hid_ll + r0 + lane, hid_tag);
+  sr.hres = lane < r1 - r0 ? ll_val(sr.hw) : 0.f;
+}
+
+template <int T, int DPL, bool AQ>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_decode(const __grid_constant__ Params p, const uint32_t *tok_in, uint32_t *tok_out, uint32_t *out_ids,
              int step) {
@@ -1409,8 +1732,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const unsigned launch = *p.launch;
   int slot = 0, tile_ctr = 0;
   unsigned phase = 0;
-  ActRegs<T> x;
-  StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
+  StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f, 0ull};
   // One pass per projection stage: QKV, O, gate/up, down (in two input parts when
   // split) of every layer, then the LM head; a single matvec call site keeps one copy
   // of the tile loop in the instruction cache for all of them.
@@ -1421,34 +1743,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : (kind == ST_DOWN2 ? ST_DOWN : kind) + 1);
     const LayerW &W = p.layers[l < p.L ? l : 0];
     const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
-    load_stage_regs(p, kind, l, pos, sr, kind == ST_DOWN || kind == ST_DOWN2 ? mk_tag(launch, l, TG_POST_O) : hid_in);
+    const unsigned res_tag = kind == ST_DOWN || kind == ST_DOWN2 ? mk_tag(launch, l, TG_POST_O) : hid_in;
+    load_stage_regs(p, kind, l, pos, sr);
     if (si > 0) cta_sync();  // every warp is done with the previous input: the staging buffer is rewritten
     float osc;
     unsigned tag_out;
     if (kind == ST_QKV) {
       if (l == 0)
-        osc = stage_in<T, XS_EMBED>(p, sm, x, nullptr, 0u, W.attn_norm, p.E, p.nseg_E, 8 * stage_id + 1,
+        osc = stage_in<T, XS_EMBED, AQ>(p, sm, nullptr, 0u, W.attn_norm, p.E, 8 * stage_id + 1,
                                     p.embd + (size_t)tok * p.rb_E, blockIdx.x == 0, hid_in);
       else
-        osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, hid_in, W.attn_norm, p.E, p.nseg_E, 8 * stage_id + 1);
+        osc = stage_in<T, XS_NORM, AQ>(p, sm, p.hid_ll, hid_in, W.attn_norm, p.E, 8 * stage_id + 1);
       tag_out = mk_tag(launch, l, TG_QKV);
     } else if (kind == ST_O) {
-      osc = stage_in<T, XS_PLAIN>(p, sm, x, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, p.nseg_Q,
-                                  8 * stage_id + 1);
+      osc = stage_in<T, XS_PLAIN, AQ>(p, sm, p.attn_ll, mk_tag(launch, l, TG_ATTN), nullptr, p.Q, 8 * stage_id + 1);
       tag_out = mk_tag(launch, l, TG_POST_O);
     } else if (kind == ST_DOWN || kind == ST_DOWN2) {
       const int x0 = kind == ST_DOWN2 ? p.xa : 0;
-      osc = stage_in<T, XS_PLAIN>(p, sm, x, p.act_ll + x0, mk_tag(launch, l, TG_ACT), nullptr, stage_in_dim(p, kind),
-                                  stage_nseg(p, kind), 8 * stage_id + 1);
+      osc = stage_in<T, XS_PLAIN, AQ>(p, sm, p.act_ll + x0, mk_tag(launch, l, TG_ACT), nullptr, stage_in_dim(p, kind),
+                                  8 * stage_id + 1);
       tag_out = mk_tag(launch, l, TG_POST_DOWN);
     } else {  // gate/up after the FFN norm, or the LM head after the final norm (model.rs:72-95)
       const bool lm = kind == ST_LM;
-      osc = stage_in<T, XS_NORM>(p, sm, x, p.hid_ll, lm ? mk_tag(launch, p.L - 1, TG_POST_DOWN) : mk_tag(launch, l, TG_POST_O),
-                                 lm ? p.out_norm : W.ffn_norm, p.E, p.nseg_E, 8 * stage_id + 1);
+      osc = stage_in<T, XS_NORM, AQ>(p, sm, p.hid_ll, lm ? mk_tag(launch, p.L - 1, TG_POST_DOWN) : mk_tag(launch, l, TG_POST_O),
+                                 lm ? p.out_norm : W.ffn_norm, p.E, 8 * stage_id + 1);
       tag_out = lm ? 0u : mk_tag(launch, l, TG_ACT);
     }
+    resolve_hres(p, kind, l, sr, res_tag);
     stamp(p, 8 * stage_id + 2);
-    matvec_stage<T>(p, rg, sm, tbl, kind, l, x, osc, slot, phase, tile_ctr, pos, sr, tag_out);
+    matvec_stage<T, AQ>(p, rg, sm, tbl, kind, l, osc, slot, phase, tile_ctr, pos, sr, tag_out);
     if (p.tp_world > 1 && warp == 0 && (kind == ST_O || kind == (p.split ? ST_DOWN2 : ST_DOWN)))
       tp_reduce_rows(p, kind == ST_O ? ST_O : ST_DOWN, l, sr, tag_out);
     if (kind == ST_QKV) {
@@ -1599,9 +1922,9 @@ struct DecodeState {
   std::vector<void *> allocs;
 };
 
-template <int T, int DPL>
+template <int T, int DPL, bool AQ = false>
 static void *pick_kernel() {
-  return (void *)dk::k_decode<T, DPL>;
+  return (void *)dk::k_decode<T, DPL, AQ>;
 }
 
 static int nseg_for(int in_dim) {
@@ -1634,7 +1957,9 @@ int decode_prepare(sq_ctx *c) {
   const int split = F > dk::MAX_X, xa = split ? dk::MAX_X : F, xb = F - xa;
   const int nE = nseg_for(E), nQ = nseg_for(Q), nF = nseg_for(F), nFA = nseg_for(xa), nFB = split ? nseg_for(xb) : 1;
   ok = ok && nE && nQ && nFA && nFB && (split || nF);
-  ok = ok && m->acts == SQ_ACTS_F32;  // Q8_0 activations run on the op-level kernels
+  // W8A8 (Q8_0 activations) for Q8_0 / Q4_0 weights; BF16 weights keep f32 activations
+  // under either setting, as the reference's BF16 linear does (matmul.rs:106-108)
+  const bool aq = m->acts == SQ_ACTS_Q8 && wt != SQ_BF16;
   for (int d : {E, Q, xa, split ? xb : xa}) {
     ok = ok && d > 0 && (d / QK) % 8 == 0 && ((size_t)(d / QK) * bb) % 16 == 0;  // pairs, 16-byte rows and parts
     if (wt == SQ_BF16) ok = ok && d % 2048 == 0;  // BF16 lanes stripe whole 2048-element segments
@@ -1675,7 +2000,11 @@ int decode_prepare(sq_ctx *c) {
   ok = ok && std::max(std::max(E, Q), std::max(xa, xb)) <= dk::MAX_X;  // stage inputs fit the staging buffer
   if (!ok) return SQ_OK;  // the op-level path serves this model
   void *kern = nullptr;
-  if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
+  if (wt == SQ_Q8_0 && aq)
+    kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2, true>() : pick_kernel<SQ_Q8_0, 4, true>();
+  else if (wt == SQ_Q4_0 && aq)
+    kern = cf.head_dim == 64 ? pick_kernel<SQ_Q4_0, 2, true>() : pick_kernel<SQ_Q4_0, 4, true>();
+  else if (wt == SQ_Q8_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q8_0, 2>() : pick_kernel<SQ_Q8_0, 4>();
   else if (wt == SQ_Q4_0) kern = cf.head_dim == 64 ? pick_kernel<SQ_Q4_0, 2>() : pick_kernel<SQ_Q4_0, 4>();
   else kern = cf.head_dim == 64 ? pick_kernel<SQ_BF16, 2>() : pick_kernel<SQ_BF16, 4>();
   h.tp_world = tp_world;

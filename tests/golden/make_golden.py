@@ -42,6 +42,10 @@ CONFIG_CASES = {
     "cfg4_1b_bf16": dict(spec="1b", wt="bf16", prompt=8192, steps=1),
     # config 5's shape on one GPU: 16-token prompt, then greedy decode
     "cfg5_8b_q8_0": dict(spec="8b", wt="q8_0", prompt=16, steps=9),
+    # config 1's model under the aarch64 scheme (Q8_0 activations, integer block dots);
+    # the top-2 logit margin of every step is pinned too (the GPU test, teacher-forced,
+    # compares ids only at steps whose margin exceeds the scheme's last-bit noise)
+    "cfg1_1b_q8_0_a8": dict(spec="1b", wt="q8_0", prompt=32, steps=17, acts_q8=True),
 }
 CONFIG_PROMPT_SEED = 1234
 
@@ -68,12 +72,13 @@ def compute_config(name):
     c = CONFIG_CASES[name]
     path = G.ensure_gguf(c["spec"], c["wt"])
     prompt = G.prompt_ids(c["prompt"], seed=CONFIG_PROMPT_SEED)
-    m = O.Model(path)
+    m = O.Model(path, acts_q8=c.get("acts_q8", False))
     ids, _, logits = m.generate(prompt, c["steps"], want_logits=True)
     m.close()
+    margins = [float(np.diff(np.sort(lg)[-2:])[0]) for lg in logits]
     return dict(prompt=np.asarray(prompt, np.uint32), ids=np.asarray(ids, np.uint32),
                 logits_first=np.asarray(logits[0], np.float32), logits_last=np.asarray(logits[-1], np.float32),
-                gguf_sha256=np.array(sha256(path)))
+                margins=np.asarray(margins, np.float32), gguf_sha256=np.array(sha256(path)))
 
 
 def compute(spec, wt, acts_q8=False):

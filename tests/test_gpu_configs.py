@@ -31,7 +31,7 @@ def assert_logits_close(got, want):
     assert err / float(np.max(np.abs(want))) <= REL_TOL, err
 
 
-@pytest.mark.parametrize("name", list(MG.CONFIG_CASES))
+@pytest.mark.parametrize("name", [n for n, c in MG.CONFIG_CASES.items() if not c.get("acts_q8")])
 def test_config_shape_matches_oracle(gpu_lib, name):
     from sqb200 import gguf_synth as G
     from sqb200 import lib
@@ -51,6 +51,52 @@ def test_config_shape_matches_oracle(gpu_lib, name):
             rest = ctx.decode_steps(len(ids) - 1)
             assert np.array_equal(rest, ids[1:])
             assert_logits_close(ctx.logits(), z["logits_last"])
+        lib.wait_status()
+    finally:
+        ctx.close()
+        m.close()
+
+
+# W8A8 at the 1B shape is chaotic in the last bit: summing the oracle's own RMSNorm
+# squares in another order (256 strided partials, then in sequence) moves its logits
+# after this prompt by 0.167 max-abs and its greedy ids from step 1 on. So the bound
+# here is that noise floor with margin, and ids are compared only where the oracle's
+# top-2 margin exceeds twice it. The small models, where the noise is far smaller,
+# are held to 5e-2 every step (tests/test_gpu_model.py).
+W8A8_1B_NOISE = 0.17
+W8A8_1B_TOL = 1.5 * W8A8_1B_NOISE
+
+
+@pytest.mark.parametrize("name", [n for n, c in MG.CONFIG_CASES.items() if c.get("acts_q8")])
+def test_config_shape_w8a8(gpu_lib, name):
+    """Config 1's model under Q8_0 activations (the reference's aarch64 scheme,
+    matmul.rs:89-100), decoded by the persistent kernel's integer block dots,
+    teacher-forced: every step feeds the oracle's id through the one-token forward (the
+    persistent kernel). The GPU's greedy id must equal the oracle's wherever the
+    oracle's top-2 margin exceeds 2 x W8A8_1B_NOISE, and the logits after the prompt
+    and after the last step must be within W8A8_1B_TOL."""
+    from sqb200 import gguf_synth as G
+    from sqb200 import lib
+    c = MG.CONFIG_CASES[name]
+    z = np.load(MG.config_fixture_path(name))
+    path = G.ensure_gguf(c["spec"], c["wt"])
+    assert MG.sha256(path) == str(z["gguf_sha256"])
+    prompt, ids, margins = z["prompt"], z["ids"], z["margins"]
+    m = lib.Model(path, device=0, acts=lib.ACTS_Q8)
+    ctx = m.new_context(len(prompt) + len(ids) + 8)
+    try:
+        nxt = int(ctx.forward(prompt))
+        assert float(np.max(np.abs(ctx.logits() - z["logits_first"]))) <= W8A8_1B_TOL
+        assert ctx.launches_per_token == 1  # the persistent kernel serves W8A8 too
+        checked = 0
+        for i in range(len(ids)):
+            if i > 0:
+                nxt = int(ctx.forward(np.array([ids[i - 1]], np.uint32)))
+            if margins[i] > 2 * W8A8_1B_NOISE:
+                assert nxt == int(ids[i]), (i, nxt, int(ids[i]), float(margins[i]))
+                checked += 1
+        assert checked >= 2, margins
+        assert float(np.max(np.abs(ctx.logits() - z["logits_last"]))) <= W8A8_1B_TOL
         lib.wait_status()
     finally:
         ctx.close()
