@@ -20,7 +20,8 @@ LM head, device argmax fed back as the next input).
   w8a8  : config 1's model under Q8_0 activations (the reference's aarch64 scheme)
   sweep : config 2 (isolated matvec, five shapes x three weight types)
   tp    : config 5 (8B Q8_0) tensor parallel over all ranks (TP1 on one GPU)
-  prefill: config 4 (1B BF16 prefill of 512 / 2048 / 8192 tokens)
+  prefill: config 4 (1B BF16 prefill of 512 / 2048 / 8192 tokens), and under "q4_0"
+          config 3's 2048-token Q4_0 prompt (quantized-row tensor-core GEMM)
 
 `--impl reference` times that CPU restatement alone on this workload (the Rust
 reference cannot be built here: no Rust toolchain).
@@ -301,7 +302,7 @@ def run_prefill(lib, G, lengths, device, wtype="bf16"):
                                     "mma_tflops_issued": mma / (ms / 1e3) / 1e12}}
         ctx.close()
     model.close()
-    return {"workload": f"1b-{wtype} prefill" + (" (config 3)" if wtype == "bf16" else ""),
+    return {"workload": f"1b-{wtype} prefill" + (" (config 4)" if wtype == "bf16" else ""),
             "dtype": f"f32 activations, {wtype} weights; bf16 MMA terms", "lengths": out}
 
 
@@ -738,6 +739,8 @@ def run_ours(args):
     prefill = long_ctx = sweep = w8a8 = None
     if single and args.prefill and spec == "1b":
         prefill = run_prefill(lib, G, [int(v) for v in args.prefill.split(",")], local)
+        # config 3's 2048-token Q4_0 prompt on the quantized-row tensor-core GEMM
+        prefill["q4_0"] = run_prefill(lib, G, [2048], local, wtype="q4_0")
     if single and not args.no_extra:
         long_ctx = run_long_context(lib, G, local)
         if args.acts == "f32":

@@ -669,6 +669,7 @@ __device__ float stage_q(const Params &p, Smem &sm, const unsigned long long *v,
   const int ng = n / 8;  // n is a multiple of 256 (host check): whole warps take part in a pass
   float x[MAXG][8];
   float ss = 0.f;
+
   if constexpr (MODE == XS_EMBED) {
 #pragma unroll
     for (int k = 0; k < MAXG; k++) {
@@ -1095,7 +1096,6 @@ __device__ __forceinline__ void release_slot(const Params &p, const Ring &rg, Sm
 // residual of this CTA's rows of the O / down stages).
 struct StageRegs {
   float c0, c1, s0, s1, hres;
-  unsigned long long hw;  // the residual's tagged word as loaded, before its tag is checked
 };
 
 // Finish output row(s) of a stage (warp-uniform arguments; lane 0 stores).
@@ -1664,7 +1664,8 @@ __device__ ArgState warp_argmax_smem(const float *v, int n, long long base) {
   return s;
 }
 
-__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr) {
+__device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l, int pos, StageRegs &sr,
+                                                unsigned hid_tag) {
   const int lane = threadIdx.x & 31;
   if (kind == ST_QKV) {
     const int half = p.hd >> 1;
@@ -1676,21 +1677,8 @@ __device__ __forceinline__ void load_stage_regs(const Params &p, int kind, int l
   } else if (kind == ST_O || kind == ST_DOWN || kind == ST_DOWN2) {  // the residual of this CTA's rows (<= 32)
     int r0, r1;
     stage_rows(p, kind, l, blockIdx.x, r0, r1);
-    // issued now, checked after the staging (resolve_hres): the load's round trip
-    // overlaps the stage input's instead of adding to it
-    sr.hw = lane < r1 - r0 ? ld_ll(p.hid_ll + r0 + lane) : 0ull;
+    sr.hres = lane < r1 - r0 ? poll_ll(p, p.hid_ll + r0 + lane, hid_tag) : 0.f;
   }
-}
-
-// The residual word loaded by load_stage_regs: its value once it carries hid_tag (it
-// nearly always does: the residual was published a stage or more ago).
-__device__ __forceinline__ void resolve_hres(const Params &p, int kind, int l, StageRegs &sr, unsigned hid_tag) {
-  if (kind != ST_O && kind != ST_DOWN && kind != ST_DOWN2) return;
-  const int lane = threadIdx.x & 31;
-  int r0, r1;
-  stage_rows(p, kind, l, blockIdx.x, r0, r1);
-  if (lane < r1 - r0 && !ll_ok(sr.hw, hid_tag)) sr.hw = ll_wait(p, p.hid_ll + r0 + lane, hid_tag);
-  sr.hres = lane < r1 - r0 ? ll_val(sr.hw) : 0.f;
 }
 
 template <int T, int DPL, bool AQ>
@@ -1732,7 +1720,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const unsigned launch = *p.launch;
   int slot = 0, tile_ctr = 0;
   unsigned phase = 0;
-  StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f, 0ull};
+  StageRegs sr = {0.f, 0.f, 0.f, 0.f, 0.f};
   // One pass per projection stage: QKV, O, gate/up, down (in two input parts when
   // split) of every layer, then the LM head; a single matvec call site keeps one copy
   // of the tile loop in the instruction cache for all of them.
@@ -1743,8 +1731,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int stage_id = kind == ST_LM ? 5 * p.L : 5 * l + (kind == ST_QKV ? 0 : (kind == ST_DOWN2 ? ST_DOWN : kind) + 1);
     const LayerW &W = p.layers[l < p.L ? l : 0];
     const unsigned hid_in = l == 0 ? mk_tag(launch, 0, TG_EMBED) : mk_tag(launch, l - 1, TG_POST_DOWN);
-    const unsigned res_tag = kind == ST_DOWN || kind == ST_DOWN2 ? mk_tag(launch, l, TG_POST_O) : hid_in;
-    load_stage_regs(p, kind, l, pos, sr);
+    load_stage_regs(p, kind, l, pos, sr, kind == ST_DOWN || kind == ST_DOWN2 ? mk_tag(launch, l, TG_POST_O) : hid_in);
     if (si > 0) cta_sync();  // every warp is done with the previous input: the staging buffer is rewritten
     float osc;
     unsigned tag_out;
@@ -1769,7 +1756,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                  lm ? p.out_norm : W.ffn_norm, p.E, 8 * stage_id + 1);
       tag_out = lm ? 0u : mk_tag(launch, l, TG_ACT);
     }
-    resolve_hres(p, kind, l, sr, res_tag);
     stamp(p, 8 * stage_id + 2);
     matvec_stage<T, AQ>(p, rg, sm, tbl, kind, l, osc, slot, phase, tile_ctr, pos, sr, tag_out);
     if (p.tp_world > 1 && warp == 0 && (kind == ST_O || kind == (p.split ? ST_DOWN2 : ST_DOWN)))

@@ -7,7 +7,8 @@ the op-level step (SQB200_TP_DECODE=op) with the one-shot peer-memory all-reduce
 ("peer") or NCCL's (SQB200_TP_ALLREDUCE=nccl, "nccl"); all three are checked.
 Sizes with more GPUs than the box has are skipped.
 
-  small (2 kv heads): TP 2 against one GPU and the oracle, Q8_0 and BF16
+  small (2 kv heads): TP 2 against one GPU and the oracle, Q8_0 and BF16; W8A8
+                     (Q8_0 activations) TP 2 against the oracle's W8A8 ids
   8b (8 kv heads): TP 2 / 4 / 8 against the oracle's pinned ids and logits
                    (tests/golden/cfg5_8b_q8_0.npz); at TP 8 each rank holds one
                    kv head, 4 q heads, 1792 FFN rows and 56 blocks of the down rows
@@ -33,7 +34,7 @@ def assert_logits_close(got, want):
     assert err / float(np.max(np.abs(want))) <= REL_TOL, err
 
 
-def _tp_rank(rank, size, path, prompt, steps, mode, on_kernel, qin, qout):
+def _tp_rank(rank, size, path, prompt, steps, mode, on_kernel, qin, qout, acts=0):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     if mode != "kernel":
         os.environ["SQB200_TP_DECODE"] = "op"
@@ -46,7 +47,7 @@ def _tp_rank(rank, size, path, prompt, steps, mode, on_kernel, qin, qout):
             qin.put(("uid", uid))
         else:
             uid = qout.get(timeout=120)
-        m = lib.Model(path, device=rank, tp_rank=rank, tp_size=size, nccl_id=uid)
+        m = lib.Model(path, device=rank, acts=acts, tp_rank=rank, tp_size=size, nccl_id=uid)
         ctx = m.new_context(len(prompt) + steps + 4)
         # which decode path ran: the persistent kernel in "kernel" mode wherever it
         # serves the shard's shape, the op-level step otherwise
@@ -62,11 +63,12 @@ def _tp_rank(rank, size, path, prompt, steps, mode, on_kernel, qin, qout):
         qin.put(("err", rank, repr(e), None))
 
 
-def run_tp(size, path, prompt, steps, mode, on_kernel=True):
+def run_tp(size, path, prompt, steps, mode, on_kernel=True, acts=0):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     qin, qout = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, size, path, prompt, steps, mode, on_kernel, qin, qout)) for r in range(size)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, size, path, prompt, steps, mode, on_kernel, qin, qout, acts))
+             for r in range(size)]
     for p in procs:
         p.start()
     results = []
@@ -134,3 +136,28 @@ def test_tp_8b_matches_oracle(size, mode):
     assert ids == [int(i) for i in z["ids"]], (ids, z["ids"].tolist())
     assert_logits_close(first_logits, z["logits_first"])
     assert_logits_close(last_logits, z["logits_last"])
+
+
+Q8_ACTS_ABS_TOL = 5e-2
+
+
+def test_tp2_w8a8_matches_oracle():
+    """Q8_0 activations (the reference's aarch64 scheme) on two GPUs through the
+    persistent kernel: every rank quantizes its stage inputs as one GPU does, the row-
+    parallel partial sums are exchanged as in f32 contexts. Greedy ids equal the
+    oracle's W8A8 ids at every step up to the first whose oracle top-2 margin is
+    within 2 x ABS_TOL; logits after the prompt within Q8_ACTS_ABS_TOL."""
+    need_gpus(2)
+    from sqb200 import gguf_synth as G
+    path = G.ensure_gguf("small", "q8_0")
+    prompt = G.prompt_ids(8, seed=17, high=G.SPECS["small"]["vocab"])
+    steps = 12
+    om = O.Model(path, acts_q8=True)
+    o_ids, _, o_logits = om.generate(prompt, steps + 1, want_logits=True)
+    om.close()
+    margins = [float(np.diff(np.sort(lg)[-2:])[0]) for lg in o_logits]
+    decidable = next((i for i, mg in enumerate(margins) if mg <= 2 * ABS_TOL), len(margins))
+    assert decidable >= 3, margins
+    ids, (first_logits, _) = run_tp(2, path, prompt, steps, "kernel", True, acts=1)
+    assert ids[:decidable] == [int(i) for i in o_ids[:decidable]], (ids, list(o_ids), decidable)
+    assert float(np.max(np.abs(first_logits - o_logits[0]))) <= Q8_ACTS_ABS_TOL
