@@ -101,3 +101,29 @@ def test_config_shape_w8a8(gpu_lib, name):
     finally:
         ctx.close()
         m.close()
+
+
+def test_1b_bf16_decode_matches_oracle(gpu_lib):
+    """The 1B shape with BF16 weights through the persistent decode kernel (its down
+    projection split by input segment across CTAs, like the Q8_0 / Q4_0 configs), against
+    the oracle run live on a short prompt: identical greedy ids, logits within the bar."""
+    from oracle import oracle as O
+    from sqb200 import gguf_synth as G
+    from sqb200 import lib
+    path = G.ensure_gguf("1b", "bf16")
+    prompt = G.prompt_ids(12, seed=MG.CONFIG_PROMPT_SEED)
+    ref = O.Model(path)
+    want, _, want_logits = ref.generate(prompt, 5, want_logits=True)
+    ref.close()
+    m = lib.Model(path, device=0)
+    ctx = m.new_context(64)
+    try:
+        first = int(ctx.forward(prompt))
+        assert ctx.launches_per_token == 1
+        got = np.concatenate([[first], ctx.decode_steps(4)])
+        assert np.array_equal(got, want), (got.tolist(), list(want))
+        assert_logits_close(ctx.logits(), want_logits[-1])
+        lib.wait_status()
+    finally:
+        ctx.close()
+        m.close()
