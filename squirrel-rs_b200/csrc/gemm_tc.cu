@@ -70,11 +70,21 @@ struct TcCfg {
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-// grid: (ceil(N/128), ceil(m/BN), splits). kb_per: K blocks of 64 per split.
+// Up to three weight matrices that share one input (q / k / v, gate / up): one launch
+// covers all their 128-row tiles, tile x of matrix i for blockIdx.x in [t[i], t[i+1]).
+struct TcW {
+  CUtensorMap map[3];
+  float *y[3];
+  int N[3];
+  int t[4];  // first tile of each matrix; t[3] = the grid's x extent
+};
+
+// grid: (tiles of all matrices, ceil(m/BN), splits). kb_per: K blocks of 64 per split
+// (split-K only with one matrix).
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int m, int N,
-              int nkb, int kb_per, float *__restrict__ y, float *__restrict__ part, unsigned *err) {
+    k_gemm_tc(const __grid_constant__ TcW W, const __grid_constant__ CUtensorMap tx, int m, int nkb, int kb_per,
+              float *__restrict__ part, unsigned *err) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = su32(smem_raw);
@@ -88,7 +98,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f0 = blockIdx.x * TC_M, t0 = blockIdx.y * BN;
+  const int bx = blockIdx.x, mi = bx < W.t[1] ? 0 : (bx < W.t[2] ? 1 : 2);  // this tile's matrix
+  const CUtensorMap *tw = &W.map[mi];
+  const int N = W.N[mi];
+  float *__restrict__ y = W.y[mi];
+  const int f0 = (bx - W.t[mi]) * TC_M, t0 = blockIdx.y * BN;
   const int kb0 = blockIdx.z * kb_per;
   const int nk = min(nkb, kb0 + kb_per) - kb0;  // >= 1 (the host sizes the splits)
 
@@ -100,7 +114,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bar_init(done, TC_TERMS);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    prefetch_map(&tw);
+    prefetch_map(tw);
     prefetch_map(&tx);
   }
   __syncwarp();
@@ -121,7 +135,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t a = base + (uint32_t)s * C::STAGE;
           const int k = (kb0 + i) * TC_KB;
           bar_expect_tx(full(s), (unsigned)C::STAGE);
-          tma_load_2d(a, &tw, k, f0, full(s));
+          tma_load_2d(a, tw, k, f0, full(s));
 #pragma unroll
           for (int t = 0; t < TC_TERMS; t++)
             tma_load_3d(a + C::A_BYTES + (uint32_t)t * C::B_BYTES, &tx, k, t0, t, full(s));
@@ -315,9 +329,13 @@ __device__ __forceinline__ void convert_step(uint32_t row, int sub, uint32_t dst
 // grid: (ceil(N/128), ceil(m/BN), splits); ch_per: 256-element chunks per split.
 template <int T, int BN>
 __global__ void __launch_bounds__(Q_THREADS, 1)
-    k_gemm_tcq(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int m, int N,
-               int nch, int ch_per, float *__restrict__ y, float *__restrict__ part, unsigned *err) {
+    k_gemm_tcq(const __grid_constant__ TcW W, const __grid_constant__ CUtensorMap tx, int m, int nch, int ch_per,
+               float *__restrict__ part, unsigned *err) {
   using C = QCfg<T, BN>;
+  const int bx = blockIdx.x, mi = bx < W.t[1] ? 0 : (bx < W.t[2] ? 1 : 2);  // this tile's matrix
+  const CUtensorMap *tw = &W.map[mi];
+  const int N = W.N[mi];
+  float *__restrict__ y = W.y[mi];
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw0 = su32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
@@ -328,7 +346,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f0 = blockIdx.x * TC_M, t0 = blockIdx.y * BN;
+  const int f0 = (bx - W.t[mi]) * TC_M, t0 = blockIdx.y * BN;
   const int c0 = blockIdx.z * ch_per;
   const int nc = min(nch, c0 + ch_per) - c0;  // >= 1
   const int nsub = 4 * nc;                    // 64-element steps
@@ -341,7 +359,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    prefetch_map(&tw);
+    prefetch_map(tw);
     prefetch_map(&tx);
   }
   __syncwarp();
@@ -360,7 +378,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         const int rb = c & 1;
         if (c >= 2 && !bar_wait(bar(QB_RAWEMPTY + rb), (unsigned)((c >> 1) - 1) & 1u, err, abort_flag)) return false;
         bar_expect_tx(bar(QB_RAWFULL + rb), (unsigned)C::RAW);
-        tma_load_2d(base + C::OFF_RAW + rb * C::RAW, &tw, (c0 + c) * (C::CB / 2), f0, bar(QB_RAWFULL + rb));
+        tma_load_2d(base + C::OFF_RAW + rb * C::RAW, tw, (c0 + c) * (C::CB / 2), f0, bar(QB_RAWFULL + rb));
         raw_issued = c + 1;
         return true;
       };
@@ -568,44 +586,65 @@ bool encode(CUtensorMap *map, const void *ptr, int rank, const cuuint64_t *dims,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// nmat (1-3) weight matrices of K columns against the same activation terms; splits
+// > 1 only with one matrix.
 template <int BN>
-cudaError_t run_tc(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const void *w, int N, float *y,
-                   int splits, float *part) {
+cudaError_t run_tc(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, int nmat, const void *const *w,
+                   const int *N, float *const *y, int splits, float *part) {
   using C = TcCfg<BN>;
-  CUtensorMap tw, tx;
-  const cuuint64_t wd[2] = {(cuuint64_t)K, (cuuint64_t)N}, ws_[1] = {(cuuint64_t)K * 2};
+  TcW W{};
+  CUtensorMap tx;
+  const cuuint64_t ws_[1] = {(cuuint64_t)K * 2};
   const cuuint32_t wb[2] = {TC_KB, TC_M};
+  W.t[0] = 0;
+  for (int i = 0; i < 3; i++) {
+    const int j = i < nmat ? i : nmat - 1;  // unused entries repeat the last matrix (never selected)
+    const cuuint64_t wd[2] = {(cuuint64_t)K, (cuuint64_t)N[j]};
+    if (!encode(&W.map[i], w[j], 2, wd, ws_, wb)) return cudaErrorInvalidValue;
+    W.y[i] = y[j];
+    W.N[i] = N[j];
+    W.t[i + 1] = W.t[i] + (i < nmat ? (N[i] + TC_M - 1) / TC_M : 0);
+  }
   const cuuint64_t xd[3] = {(cuuint64_t)K, (cuuint64_t)m, TC_TERMS},
                    xst[2] = {(cuuint64_t)K * 2, (cuuint64_t)m * K * 2};
   const cuuint32_t xb[3] = {TC_KB, BN, 1};
-  if (!encode(&tw, w, 2, wd, ws_, wb) || !encode(&tx, xs, 3, xd, xst, xb)) return cudaErrorInvalidValue;
+  if (!encode(&tx, xs, 3, xd, xst, xb)) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nkb = (K + TC_KB - 1) / TC_KB;
+  if (nmat > 1) splits = 1;
   const int kb_per = (nkb + splits - 1) / splits;
   splits = (nkb + kb_per - 1) / kb_per;  // every split gets at least one block
-  const dim3 grid((N + TC_M - 1) / TC_M, (m + BN - 1) / BN, splits);
-  k_gemm_tc<BN><<<grid, TC_THREADS, C::SMEM, s>>>(tw, tx, m, N, nkb, kb_per, y, splits > 1 ? part : nullptr,
-                                                  tc_err_ptr());
+  const dim3 grid(W.t[3], (m + BN - 1) / BN, splits);
+  k_gemm_tc<BN><<<grid, TC_THREADS, C::SMEM, s>>>(W, tx, m, nkb, kb_per, splits > 1 ? part : nullptr, tc_err_ptr());
   e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
-  const size_t n = (size_t)m * N;
-  k_split_sum_tc<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(part, splits, n, y);
+  const size_t n = (size_t)m * N[0];
+  k_split_sum_tc<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(part, splits, n, y[0]);
   return cudaGetLastError();
 }
 
 template <int T, int BN>
-cudaError_t run_tcq(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const void *w, int N, float *y,
-                    int splits, float *part) {
+cudaError_t run_tcq(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, int nmat, const void *const *w,
+                    const int *N, float *const *y, int splits, float *part) {
   using C = QCfg<T, BN>;
-  CUtensorMap tw, tx;
+  TcW W{};
+  CUtensorMap tx;
   const cuuint64_t rowbytes = (cuuint64_t)(K / QK) * C::BB;
-  const cuuint64_t wd[2] = {rowbytes / 2, (cuuint64_t)N}, wst[1] = {rowbytes};
+  const cuuint64_t wst[1] = {rowbytes};
   const cuuint32_t wb[2] = {(cuuint32_t)(C::CB / 2), TC_M}, es[2] = {1, 1};
-  if (g_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(w), wd, wst, wb, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
+  W.t[0] = 0;
+  for (int i = 0; i < 3; i++) {
+    const int j = i < nmat ? i : nmat - 1;  // unused entries repeat the last matrix (never selected)
+    const cuuint64_t wd[2] = {rowbytes / 2, (cuuint64_t)N[j]};
+    if (g_encode(&W.map[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(w[j]), wd, wst, wb, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    W.y[i] = y[j];
+    W.N[i] = N[j];
+    W.t[i + 1] = W.t[i] + (i < nmat ? (N[i] + TC_M - 1) / TC_M : 0);
+  }
   const cuuint64_t xd[3] = {(cuuint64_t)K, (cuuint64_t)m, TC_TERMS},
                    xst[2] = {(cuuint64_t)K * 2, (cuuint64_t)m * K * 2};
   const cuuint32_t xb[3] = {TC_KB, BN, 1};
@@ -613,24 +652,25 @@ cudaError_t run_tcq(cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const
   cudaError_t e = cudaFuncSetAttribute(k_gemm_tcq<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nch = K / Q_CHUNK;
+  if (nmat > 1) splits = 1;
   const int ch_per = (nch + splits - 1) / splits;
   splits = (nch + ch_per - 1) / ch_per;
-  const dim3 grid((N + TC_M - 1) / TC_M, (m + BN - 1) / BN, splits);
-  k_gemm_tcq<T, BN><<<grid, Q_THREADS, C::SMEM, s>>>(tw, tx, m, N, nch, ch_per, y, splits > 1 ? part : nullptr,
+  const dim3 grid(W.t[3], (m + BN - 1) / BN, splits);
+  k_gemm_tcq<T, BN><<<grid, Q_THREADS, C::SMEM, s>>>(W, tx, m, nch, ch_per, splits > 1 ? part : nullptr,
                                                      tc_err_ptr());
   e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
-  const size_t n = (size_t)m * N;
-  k_split_sum_tc<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(part, splits, n, y);
+  const size_t n = (size_t)m * N[0];
+  k_split_sum_tc<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(part, splits, n, y[0]);
   return cudaGetLastError();
 }
 
 template <int T>
 cudaError_t run_tcq_bn(int bn, cudaStream_t s, const __nv_bfloat16 *xs, int m, int K, const void *w, int N, float *y,
                        int splits, float *part) {
-  if (bn == 32) return run_tcq<T, 32>(s, xs, m, K, w, N, y, splits, part);
-  if (bn == 64) return run_tcq<T, 64>(s, xs, m, K, w, N, y, splits, part);
-  return run_tcq<T, 128>(s, xs, m, K, w, N, y, splits, part);
+  if (bn == 32) return run_tcq<T, 32>(s, xs, m, K, 1, &w, &N, &y, splits, part);
+  if (bn == 64) return run_tcq<T, 64>(s, xs, m, K, 1, &w, &N, &y, splits, part);
+  return run_tcq<T, 128>(s, xs, m, K, 1, &w, &N, &y, splits, part);
 }
 
 }  // namespace
@@ -693,7 +733,32 @@ cudaError_t launch_gemm_tc_terms(cudaStream_t s, int m, int K, const void *w, in
     splits = std::min(splits, std::max(1, nkb / 4));  // at least 4 K blocks per split
     while (splits > 1 && (size_t)splits * m * N > part_floats) splits--;
   }
-  return wide ? run_tc<128>(s, xs, m, K, w, N, y, splits, part) : run_tc<64>(s, xs, m, K, w, N, y, splits, part);
+  return wide ? run_tc<128>(s, xs, m, K, 1, &w, &N, &y, splits, part)
+              : run_tc<64>(s, xs, m, K, 1, &w, &N, &y, splits, part);
+}
+
+cudaError_t launch_gemm_tc_terms_multi(cudaStream_t s, int m, int K, int nmat, const void *const *w, int wtype,
+                                       const int *N, float *const *y, float *ws, size_t ws_floats) {
+  // one launch over every matrix's tiles when the kernel takes them without a K split
+  // (enough tiles of 128 weight rows x 128 activation rows for the SMs); otherwise one
+  // launch per matrix
+  long long tiles = 0;
+  bool ok = nmat >= 1 && nmat <= 3;
+  for (int i = 0; i < nmat && ok; i++) {
+    ok = gemm_tc_supported(m, K, ws, w[i], wtype, ws, ws_floats);
+    tiles += (long long)((N[i] + TC_M - 1) / TC_M) * ((m + 127) / 128);
+  }
+  if (ok && tiles >= g_sms_tc) {
+    const __nv_bfloat16 *xs = reinterpret_cast<const __nv_bfloat16 *>(ws);
+    if (wtype == SQ_BF16) return run_tc<128>(s, xs, m, K, nmat, w, N, y, 1, nullptr);
+    if (wtype == SQ_Q8_0) return run_tcq<SQ_Q8_0, 128>(s, xs, m, K, nmat, w, N, y, 1, nullptr);
+    return run_tcq<SQ_Q4_0, 128>(s, xs, m, K, nmat, w, N, y, 1, nullptr);
+  }
+  for (int i = 0; i < nmat; i++) {
+    const cudaError_t e = launch_gemm_tc_terms(s, m, K, w[i], wtype, N[i], y[i], ws, ws_floats);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 bool gemm_tc_enabled() {

@@ -77,6 +77,11 @@ cudaError_t launch_attn_tc(cudaStream_t s, const float *q, const float *k, const
 // written by launch_rms_norm_terms / launch_silu_mul_terms / launch_split_terms.
 cudaError_t launch_gemm_tc_terms(cudaStream_t s, int m, int K, const void *w, int wtype, int N, float *y, float *ws,
                                  size_t ws_floats);
+// The same for nmat (1-3) weight matrices that share the input terms (q / k / v,
+// gate / up): one launch over all their tiles when the kernel takes them without a K
+// split, else one launch per matrix.
+cudaError_t launch_gemm_tc_terms_multi(cudaStream_t s, int m, int K, int nmat, const void *const *w, int wtype,
+                                       const int *N, float *const *y, float *ws, size_t ws_floats);
 cudaError_t launch_split_terms(cudaStream_t s, const float *x, int m, int K, float *ws);
 // RMSNorm / SiLU.mul writing only the three bf16 terms of their output ([3][rows][dim]).
 bool rms_norm_terms_ok(const float *x, const float *w, int dim);

@@ -693,9 +693,10 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_matvec_fused(s, qkv, wt, pdl));
     } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.attn_norm, ws, n, E, cf.rms_eps));
-      TRY(launch_gemm_tc_terms(s, n, E, L.q, wt, Q, c->q, ws, wsf));
-      TRY(launch_gemm_tc_terms(s, n, E, L.k, wt, KVd, c->k, ws, wsf));
-      TRY(launch_gemm_tc_terms(s, n, E, L.v, wt, KVd, c->v, ws, wsf));
+      const void *wqkv[3] = {L.q, L.k, L.v};
+      const int nqkv[3] = {Q, KVd, KVd};
+      float *yqkv[3] = {c->q, c->k, c->v};
+      TRY(launch_gemm_tc_terms_multi(s, n, E, 3, wqkv, wt, nqkv, yqkv, ws, wsf));
     } else {
       TRY(launch_rms_norm(s, c->hidden, L.attn_norm, c->normed, n, E, cf.rms_eps));
       if (aq) TRY(launch_quantize_q8_0(s, c->normed, (size_t)n * E, c->xq));  // shared quantization
@@ -738,8 +739,10 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_matvec_fused(s, dn, wt, pdl));
     } else if (tcl) {
       TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
-      TRY(launch_gemm_tc_terms(s, n, E, L.gate, wt, F, c->gate, ws, wsf));
-      TRY(launch_gemm_tc_terms(s, n, E, L.up, wt, F, c->up, ws, wsf));
+      const void *wgu[2] = {L.gate, L.up};
+      const int ngu[2] = {F, F};
+      float *ygu[2] = {c->gate, c->up};
+      TRY(launch_gemm_tc_terms_multi(s, n, E, 2, wgu, wt, ngu, ygu, ws, wsf));
       TRY(launch_silu_mul_terms(s, c->gate, c->up, ws, (size_t)n * F));
       TRY(launch_gemm_tc_terms(s, n, F, L.down, wt, E, c->ffn_out, ws, wsf));
     } else {
