@@ -571,12 +571,14 @@ __device__ __forceinline__ void store_terms4(__nv_bfloat16 *terms, size_t plane,
 }
 
 // y (may be null) and / or the three bf16 terms of the output (terms may be null;
-// plane = rows * dim).
-__global__ void __launch_bounds__(256) k_rms_norm_v(const float *__restrict__ x, const float *__restrict__ w,
-                                                    float *y, int dim, float eps, __nv_bfloat16 *terms,
-                                                    size_t plane) {
+// plane = rows * dim). add (may be null): the residual add first, x += add
+// (elementwise_add.rs:47-61), written back to x, then the norm of the sum.
+__global__ void __launch_bounds__(256) k_rms_norm_v(float *x, const float *__restrict__ w, float *y, int dim,
+                                                    float eps, __nv_bfloat16 *terms, size_t plane,
+                                                    const float *__restrict__ add) {
   __shared__ float red[8];
-  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * dim);
+  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)blockIdx.x * dim);
+  const float4 *ar = add ? reinterpret_cast<const float4 *>(add + (size_t)blockIdx.x * dim) : nullptr;
   const float4 *wr = reinterpret_cast<const float4 *>(w);
   float4 *yr = reinterpret_cast<float4 *>(y + (size_t)blockIdx.x * dim);
   const int nv = dim / 4;
@@ -586,6 +588,18 @@ __global__ void __launch_bounds__(256) k_rms_norm_v(const float *__restrict__ x,
     const int i = threadIdx.x + k * 256;
     v[k] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     g[k] = i < nv ? __ldg(wr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (add) {
+#pragma unroll
+    for (int k = 0; k < RMS_V; k++) {
+      const int i = threadIdx.x + k * 256;
+      if (i < nv) {
+        const float4 a = ar[i];
+        v[k] = make_float4(__fadd_rn(v[k].x, a.x), __fadd_rn(v[k].y, a.y), __fadd_rn(v[k].z, a.z),
+                           __fadd_rn(v[k].w, a.w));
+        xr[i] = v[k];
+      }
+    }
   }
   float ss = 0.f;
 #pragma unroll
@@ -945,7 +959,7 @@ cudaError_t launch_rms_norm(cudaStream_t s, const float *x, const float *w, floa
                             float eps) {
   if (dim % 4 == 0 && dim <= RMS_V * 4 * 256 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
       ((uintptr_t)y & 15) == 0)
-    k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, y, dim, eps, nullptr, 0);
+    k_rms_norm_v<<<rows, 256, 0, s>>>(const_cast<float *>(x), w, y, dim, eps, nullptr, 0, nullptr);
   else
     k_rms_norm<<<rows, 256, 0, s>>>(x, w, y, dim, eps);
   return cudaGetLastError();
@@ -983,7 +997,14 @@ bool rms_norm_terms_ok(const float *x, const float *w, int dim) {
 cudaError_t launch_rms_norm_terms(cudaStream_t s, const float *x, const float *w, void *terms, int rows, int dim,
                                   float eps) {
   if (!rms_norm_terms_ok(x, w, dim) || ((uintptr_t)terms & 15)) return cudaErrorNotSupported;
-  k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, nullptr, dim, eps, (__nv_bfloat16 *)terms, (size_t)rows * dim);
+  k_rms_norm_v<<<rows, 256, 0, s>>>(const_cast<float *>(x), w, nullptr, dim, eps, (__nv_bfloat16 *)terms,
+                                    (size_t)rows * dim, nullptr);
+  return cudaGetLastError();
+}
+cudaError_t launch_add_rms_norm_terms(cudaStream_t s, float *x, const float *add, const float *w, void *terms,
+                                      int rows, int dim, float eps) {
+  if (!rms_norm_terms_ok(x, w, dim) || ((uintptr_t)terms & 15) || ((uintptr_t)add & 15)) return cudaErrorNotSupported;
+  k_rms_norm_v<<<rows, 256, 0, s>>>(x, w, nullptr, dim, eps, (__nv_bfloat16 *)terms, (size_t)rows * dim, add);
   return cudaGetLastError();
 }
 cudaError_t launch_silu_mul_terms(cudaStream_t s, const float *g, const float *u, void *terms, size_t n) {

@@ -87,6 +87,9 @@ cudaError_t launch_split_terms(cudaStream_t s, const float *x, int m, int K, flo
 bool rms_norm_terms_ok(const float *x, const float *w, int dim);
 cudaError_t launch_rms_norm_terms(cudaStream_t s, const float *x, const float *w, void *terms, int rows, int dim,
                                   float eps);
+// The residual add x += add first (written back to x), then the same norm of the sum.
+cudaError_t launch_add_rms_norm_terms(cudaStream_t s, float *x, const float *add, const float *w, void *terms,
+                                      int rows, int dim, float eps);
 cudaError_t launch_silu_mul_terms(cudaStream_t s, const float *g, const float *u, void *terms, size_t n);
 cudaError_t launch_quantize_q8_0(cudaStream_t s, const float *x, size_t n, void *out);
 cudaError_t launch_embed(cudaStream_t s, const uint32_t *tokens, int n, const void *w, int wtype,

@@ -671,6 +671,9 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
   TRY(launch_embed(s, d_ids, n, m->embd, m->embd_type, E, m->cfg.vocab_size, c->hidden));  // replicated table
   float *ws = c->gemm_ws;
   const size_t wsf = c->gemm_ws_floats;
+  // tensor-core layers on one GPU defer each residual add (elementwise_add.rs:47-61)
+  // into the next RMSNorm's pass over the hidden rows (one read and write fewer)
+  const float *pending = nullptr;
   for (int l = 0; l < cf.n_blocks; l++) {
     const auto &L = m->layers[l];
     float *kc = c->kc + l * layer_kv, *vc = c->vc + l * layer_kv;
@@ -689,10 +692,16 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
     // the one-row step's kernels start while their predecessor finishes (each waits
     // for it before touching activations)
     const bool pdl = fused && pdl_enabled();
+    if (pending && !tcl) {  // a deferred residual add that this layer's norm does not take
+      TRY(launch_add(s, c->hidden, pending, (size_t)n * E));
+      pending = nullptr;
+    }
     if (fused) {
       TRY(launch_matvec_fused(s, qkv, wt, pdl));
     } else if (tcl) {
-      TRY(launch_rms_norm_terms(s, c->hidden, L.attn_norm, ws, n, E, cf.rms_eps));
+      if (pending) TRY(launch_add_rms_norm_terms(s, c->hidden, pending, L.attn_norm, ws, n, E, cf.rms_eps));
+      else TRY(launch_rms_norm_terms(s, c->hidden, L.attn_norm, ws, n, E, cf.rms_eps));
+      pending = nullptr;
       const void *wqkv[3] = {L.q, L.k, L.v};
       const int nqkv[3] = {Q, KVd, KVd};
       float *yqkv[3] = {c->q, c->k, c->v};
@@ -732,13 +741,16 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_allreduce_add(s, m->ar, c->hidden, c->attn_out, pdl));
     } else {
       if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->attn_out, (size_t)n * E, s));
-      if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
+      if (tcl && !tp) pending = c->attn_out;  // added by the FFN norm below
+      else if (!fused || tp) TRY(launch_add(s, c->hidden, c->attn_out, (size_t)n * E));
     }
     if (fused) {
       TRY(launch_matvec_fused(s, gu, wt, pdl));
       TRY(launch_matvec_fused(s, dn, wt, pdl));
     } else if (tcl) {
-      TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
+      if (pending) TRY(launch_add_rms_norm_terms(s, c->hidden, pending, L.ffn_norm, ws, n, E, cf.rms_eps));
+      else TRY(launch_rms_norm_terms(s, c->hidden, L.ffn_norm, ws, n, E, cf.rms_eps));
+      pending = nullptr;
       const void *wgu[2] = {L.gate, L.up};
       const int ngu[2] = {F, F};
       float *ygu[2] = {c->gate, c->up};
@@ -757,9 +769,11 @@ static int forward_rows(sq_ctx *c, const uint32_t *d_ids, int n, bool last, cons
       TRY(launch_allreduce_add(s, m->ar, c->hidden, c->ffn_out, pdl));
     } else {
       if (tp) TRY_ST(nccl_all_reduce_sum(m->nccl, c->ffn_out, (size_t)n * E, s));
-      if (!fused || tp) TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
+      if (tcl && !tp) pending = c->ffn_out;  // added by the next layer's attention norm
+      else if (!fused || tp) TRY(launch_add(s, c->hidden, c->ffn_out, (size_t)n * E));
     }
   }
+  if (pending) TRY(launch_add(s, c->hidden, pending, (size_t)n * E));  // the last layer's
   c->seq_len += n;
   if (last) {
     // final norm of the last row only: rows are normalized independently (model.rs:72-87)
